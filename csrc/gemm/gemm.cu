@@ -1,0 +1,558 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-gen tensor cores.
+//
+//   C[M,N] = alpha * sum_k A(m,k) * B(n,k)      (fp32 accumulate in TMEM)
+//
+// Operands are staged by TMA (tiled, 128-byte swizzle, one CTA per load, local
+// memory only) into a STAGES-deep shared-memory ring; one elected thread issues
+// tcgen05.mma (kind::f16, M=128, N=BN, K=16) into a double-buffered TMEM
+// accumulator; four epilogue warps drain TMEM with tcgen05.ld and apply the
+// epilogue while the next tile's MMAs run.
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
+// issuer, warps 2..5 = epilogue (warp w reads TMEM lanes 32*(w%4) .. +31).
+//
+// Either operand may be K-major (row-major [rows, K]) or MN-major (row-major
+// [K, rows]); that covers y = x W^T (fwd), dx = dy W (dgrad) and dW = dy^T x
+// (wgrad) without transposes.  Epilogues: bf16 store, fp32 store, fp32
+// accumulate (gradient accumulation into fp32 master grads), SwiGLU (gate|up
+// weight halves fused into one 256-wide tile, writes silu(g)*u and optionally
+// g|u for backward), and SwiGLU-backward (dact -> d[g|u]).
+//
+// Replaces the reference's nn.Linear/cuBLAS projections
+// (tinytron/model/modules/attn.py:141-145, mlp.py:27-29,45, gpt.py:60,109) and the
+// SiLU*up elementwise op (mlp.py:45).
+#include "common/ptx.cuh"
+#include "common/host_utils.h"
+
+namespace tt {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int NUM_THREADS = 192;
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_DSWIGLU = 4 };
+
+struct Params {
+  int M, N, K;                 // output rows, output cols, reduction length
+  void* C;                     // output (bf16 or fp32), row stride ldc elements
+  int ldc;
+  const __nv_bfloat16* aux;    // DSWIGLU: g|u pre-activations [M, 2N]
+  int ld_aux;
+  __nv_bfloat16* aux_out;      // SWIGLU: optional g|u store [M, 2N]; DSWIGLU: d(g|u) [M, 2N]
+  int ld_aux_out;
+  float alpha;
+  const float* alpha_ptr;      // optional device scalar multiplied into alpha
+  int b_row_offset2;           // SWIGLU: first row of the "up" half inside B
+  int* status;                 // device status word for bounded waits
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  // Grouped order: 16 M-blocks share each sweep over N, so concurrently running
+  // CTAs reuse both A rows and B rows from L2.
+  constexpr int GROUP = 16;
+  const int group_tiles = GROUP * num_n;
+  const int g = tile / group_tiles;
+  const int first_m = g * GROUP;
+  const int gm = min(num_m - first_m, GROUP);
+  const int in = tile - g * group_tiles;
+  mb = first_m + in % gm;
+  nb = in / gm;
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Store n (<= 32) fp32 values as bf16 starting at dst; vectorised when a full aligned run.
+template <int NV>
+__device__ __forceinline__ void store_bf16(__nv_bfloat16* dst, const float (&v)[NV], int n_valid) {
+  if (n_valid >= NV) {
+    uint32_t packed[NV / 2];
+#pragma unroll
+    for (int i = 0; i < NV / 2; ++i) packed[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int i = 0; i < NV / 8; ++i)
+      d4[i] = make_uint4(packed[4 * i], packed[4 * i + 1], packed[4 * i + 2], packed[4 * i + 3]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      if (i < n_valid) dst[i] = __float2bfloat16_rn(v[i]);
+  }
+}
+
+template <int NV>
+__device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&v)[NV], int n_valid) {
+  if (n_valid >= NV) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+    for (int i = 0; i < NV / 8; ++i) {
+      uint4 q = s4[i];
+      float2 a = unpack_bf16x2(q.x), b = unpack_bf16x2(q.y), c = unpack_bf16x2(q.z), d = unpack_bf16x2(q.w);
+      v[8 * i + 0] = a.x; v[8 * i + 1] = a.y; v[8 * i + 2] = b.x; v[8 * i + 3] = b.y;
+      v[8 * i + 4] = c.x; v[8 * i + 5] = c.y; v[8 * i + 6] = d.x; v[8 * i + 7] = d.y;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = (i < n_valid) ? __bfloat162float(src[i]) : 0.0f;
+  }
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr uint32_t A_BYTES = BM * BK * 2;
+  constexpr uint32_t B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN, A_MN, B_MN);
+  constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
+  static_assert(EPI != EPI_SWIGLU || (BN == 256 && !B_MN), "SwiGLU epilogue needs BN=256, K-major B");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_ptr(smem_raw, 1024);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t pending = 0;        // bit s: stage s has an issued load
+      uint32_t pending_phase = 0;  // bit s: parity of that load's fill
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_2d(a_dst + c * (BK * 128), &tmA, &full[stage], mb * BM + c * 64, kb * BK);
+          }
+          if constexpr (EPI == EPI_SWIGLU) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * (BN / 2));
+            tma_load_2d(b_dst + (BN / 2) * 128, &tmB, &full[stage], kb * BK, p.b_row_offset2 + nb * (BN / 2));
+          } else if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(b_dst + c * (BK * 128), &tmB, &full[stage], nb * BN + c * 64, kb * BK);
+          }
+          pending |= (1u << stage);
+          pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Wait (bounded) until every load this thread issued has landed, so no
+      // copy is still writing shared memory when the CTA exits.
+      for (int s = 0; s < STAGES; ++s)
+        if (pending & (1u << s)) mbar_wait(&full[s], (pending_phase >> s) & 1u, p.status, kTimeoutOther);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------ MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_base + j * 2048, BK * 128, 1024)
+                                     : sdesc_sw128(a_base + j * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_base + j * 2048, BK * 128, 1024)
+                                     : sdesc_sw128(b_base + j * 32, 16, 1024);
+            umma_f16_ss(d_tmem, ad, bd, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);  // stage is free once these MMAs retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[acc]);  // accumulator ready once the tile's MMAs retire
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      // Drain: every MMA issued above must retire before TMEM is released.
+      umma_commit(done_bar);
+      mbar_wait(done_bar, 0, p.status, kTimeoutOther);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;
+    const int row_in_tile = q * 32 + lane;
+    float alpha = p.alpha;
+    if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
+      tc_fence_after();
+      const int row = mb * BM + row_in_tile;
+      const bool row_ok = row < p.M;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c0, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c0;
+          if (row_ok && col0 < p.N) {
+            const int nv = min(32, p.N - col0);
+            float v[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+            if constexpr (EPI == EPI_BF16) {
+              store_bf16<32>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, v, nv);
+            } else {
+              float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
+              if (nv == 32) {
+                float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                  if constexpr (EPI == EPI_F32_ACC) {
+                    const float4 c = d4[i];
+                    o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+                  }
+                  d4[i] = o;
+                }
+              } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                  if (i < nv) {
+                    if constexpr (EPI == EPI_F32_ACC) dst[i] += v[i];
+                    else dst[i] = v[i];
+                  }
+                }
+              }
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < OUT_BN; c0 += 16) {
+          uint32_t g[16], u[16];
+          tmem_ld16(t_row + c0, g);
+          tmem_ld16(t_row + OUT_BN + c0, u);
+          tmem_ld_wait();
+          const int col0 = nb * OUT_BN + c0;
+          if (row_ok && col0 < p.N) {
+            const int nv = min(16, p.N - col0);
+            float gv[16], uv[16], o[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              gv[i] = __uint_as_float(g[i]);
+              uv[i] = __uint_as_float(u[i]);
+              o[i] = silu_f(gv[i]) * uv[i];
+            }
+            store_bf16<16>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, o, nv);
+            if (p.aux_out != nullptr) {
+              __nv_bfloat16* base = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
+              store_bf16<16>(base + col0, gv, nv);
+              store_bf16<16>(base + p.N + col0, uv, nv);
+            }
+          }
+        }
+      } else if constexpr (EPI == EPI_DSWIGLU) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld16(t_row + c0, r);
+          tmem_ld_wait();
+          const int col0 = nb * BN + c0;
+          if (row_ok && col0 < p.N) {
+            const int nv = min(16, p.N - col0);
+            const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
+            float gv[16], uv[16], dg[16], du[16];
+            load_bf16<16>(a + col0, gv, nv);
+            load_bf16<16>(a + p.N + col0, uv, nv);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float d = __uint_as_float(r[i]) * alpha;
+              const float s = 1.0f / (1.0f + __expf(-gv[i]));
+              du[i] = d * gv[i] * s;
+              dg[i] = d * uv[i] * s * (1.0f + gv[i] * (1.0f - s));
+            }
+            __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
+            store_bf16<16>(o + col0, dg, nv);
+            store_bf16<16>(o + p.N + col0, du, nv);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------- host
+
+template <int BN, int STAGES>
+constexpr size_t smem_bytes() {
+  return static_cast<size_t>(STAGES) * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+void launch_cfg(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
+  constexpr size_t smem = smem_bytes<BN, STAGES>();
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  const int num_tiles = ((p.M + BM - 1) / BM) * ((p.N + OUT_BN - 1) / OUT_BN);
+  const int grid = std::max(1, std::min(num_tiles, num_sms(device)));
+  kern<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_bn(int bn, const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
+  if constexpr (EPI == EPI_SWIGLU) {
+    launch_cfg<256, 4, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+  } else {
+    if (bn == 256)
+      launch_cfg<256, 4, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+    else
+      launch_cfg<128, 6, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+  }
+}
+
+// Pick the N tile: prefer 256 unless 128 gives clearly fewer idle SM-slots.
+static int choose_bn(int M, int N, int device) {
+  const int sms = num_sms(device);
+  auto eff = [&](int bn) {
+    const long tiles = static_cast<long>((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const long waves = (tiles + sms - 1) / sms;
+    const double util = static_cast<double>(tiles) / static_cast<double>(waves * sms);
+    const double colwaste = static_cast<double>(N) / static_cast<double>(((N + bn - 1) / bn) * bn);
+    return util * colwaste * (bn == 256 ? 1.0 : 0.93);  // 128-wide tiles re-read A twice as often
+  };
+  return eff(256) >= eff(128) ? 256 : 128;
+}
+
+static CUtensorMap operand_map(const torch::Tensor& t, bool mn_major, int rows_box) {
+  // K-major operand: tensor [rows, K] (row stride t.stride(0)); box {BK, rows_box}.
+  // MN-major operand: tensor [K, rows] ; box {64, BK}.
+  const uint64_t inner = static_cast<uint64_t>(t.size(1));
+  const uint64_t outer = static_cast<uint64_t>(t.size(0));
+  const uint64_t stride = static_cast<uint64_t>(t.stride(0)) * 2;
+  TT_CHECK(t.stride(1) == 1, "GEMM operands must have unit inner stride");
+  if (!mn_major) return make_tmap_2d_bf16(t.data_ptr(), inner, outer, stride, BK, rows_box);
+  return make_tmap_2d_bf16(t.data_ptr(), inner, outer, stride, 64, BK);
+}
+
+template <int EPI>
+static void dispatch(bool a_mn, bool b_mn, int bn, const Params& p, const CUtensorMap& ta, const CUtensorMap& tb,
+                     int device, cudaStream_t st) {
+  if (!a_mn && !b_mn)
+    launch_bn<false, false, EPI>(bn, p, ta, tb, device, st);
+  else if (!a_mn && b_mn)
+    launch_bn<false, true, EPI>(bn, p, ta, tb, device, st);
+  else if (a_mn && b_mn)
+    launch_bn<true, true, EPI>(bn, p, ta, tb, device, st);
+  else
+    launch_bn<true, false, EPI>(bn, p, ta, tb, device, st);
+}
+
+static Params base_params(int M, int N, int K, const torch::Tensor& out, double alpha,
+                          const c10::optional<torch::Tensor>& alpha_t, int device) {
+  Params p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.C = out.data_ptr();
+  p.ldc = static_cast<int>(out.stride(0));
+  p.alpha = static_cast<float>(alpha);
+  p.alpha_ptr = nullptr;
+  if (alpha_t.has_value()) {
+    TT_CHECK(alpha_t->is_cuda() && alpha_t->scalar_type() == torch::kFloat32 && alpha_t->numel() == 1,
+             "alpha tensor must be a 1-element float32 CUDA tensor");
+    p.alpha_ptr = alpha_t->data_ptr<float>();
+  }
+  p.status = device_status_ptr(device);
+  return p;
+}
+
+}  // namespace gemm
+
+// C (+)= alpha * op(A) op(B)^T.
+//   a: [M, K] (K-major) or [K, M] (a_mn);  b: [N, K] (K-major) or [K, N] (b_mn)
+//   c: [M, N] bf16 (overwritten) or fp32 (overwritten, or accumulated if `accumulate`).
+void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, bool accumulate, double alpha,
+             c10::optional<torch::Tensor> alpha_t, int64_t bn) {
+  using namespace gemm;
+  check_cuda_bf16(a, "a");
+  check_cuda_bf16(b, "b");
+  TT_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm expects 2-D tensors");
+  const int M = static_cast<int>(a_mn ? a.size(1) : a.size(0));
+  const int K = static_cast<int>(a_mn ? a.size(0) : a.size(1));
+  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0));
+  const int Kb = static_cast<int>(b_mn ? b.size(0) : b.size(1));
+  TT_CHECK(K == Kb, "gemm: reduction dims differ");
+  TT_CHECK(c.size(0) == M && c.size(1) == N && c.stride(1) == 1, "gemm: bad output shape/stride");
+  TT_CHECK(c.is_cuda() && c.device() == a.device() && b.device() == a.device(), "gemm: device mismatch");
+  const bool out_bf16 = c.scalar_type() == torch::kBFloat16;
+  TT_CHECK(out_bf16 || c.scalar_type() == torch::kFloat32, "gemm: output must be bf16 or fp32");
+  TT_CHECK(!(accumulate && out_bf16), "gemm: accumulate needs an fp32 output");
+  TT_CHECK(c.stride(0) % (out_bf16 ? 8 : 4) == 0 && reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
+           "gemm: output rows must be 16-byte aligned");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  if (K == 0) {
+    if (!accumulate) c.zero_();
+    return;
+  }
+  const int use_bn = (bn == 128 || bn == 256) ? static_cast<int>(bn) : choose_bn(M, N, device);
+  const CUtensorMap ta = operand_map(a, a_mn, BM);
+  const CUtensorMap tb = operand_map(b, b_mn, use_bn);
+  Params p = base_params(M, N, K, c, alpha, alpha_t, device);
+  cudaStream_t st = cur_stream();
+  if (out_bf16)
+    dispatch<EPI_BF16>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
+  else if (accumulate)
+    dispatch<EPI_F32_ACC>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
+  else
+    dispatch<EPI_F32>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
+}
+
+// out[M, I] = silu(x Wg^T) * (x Wu^T) with w_gu = [Wg; Wu] ([2I, K], K-major).
+// If gu_out is given, also stores the pre-activations g|u ([M, 2I]) for backward.
+void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10::optional<torch::Tensor> gu_out) {
+  using namespace gemm;
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w_gu, "w_gu");
+  check_cuda_bf16(out, "out");
+  const int M = static_cast<int>(x.size(0));
+  const int K = static_cast<int>(x.size(1));
+  TT_CHECK(w_gu.size(1) == K && w_gu.size(0) % 2 == 0, "swiglu: weight must be [2I, K]");
+  const int I = static_cast<int>(w_gu.size(0) / 2);
+  TT_CHECK(out.size(0) == M && out.size(1) == I && out.stride(1) == 1 && out.stride(0) % 8 == 0,
+           "swiglu: bad output");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int device = x.get_device();
+  const CUtensorMap ta = operand_map(x, false, BM);
+  const CUtensorMap tb = make_tmap_2d_bf16(w_gu.data_ptr(), static_cast<uint64_t>(K), static_cast<uint64_t>(2 * I),
+                                           static_cast<uint64_t>(w_gu.stride(0)) * 2, BK, 128);
+  Params p = base_params(M, I, K, out, 1.0, c10::nullopt, device);
+  p.b_row_offset2 = I;
+  if (gu_out.has_value()) {
+    check_cuda_bf16(*gu_out, "gu_out");
+    TT_CHECK(gu_out->size(0) == M && gu_out->size(1) == 2 * I && gu_out->stride(0) % 8 == 0, "swiglu: bad gu_out");
+    p.aux_out = reinterpret_cast<__nv_bfloat16*>(gu_out->data_ptr());
+    p.ld_aux_out = static_cast<int>(gu_out->stride(0));
+  }
+  TT_CHECK(I % 8 == 0, "swiglu: intermediate size must be a multiple of 8");
+  launch_bn<false, false, EPI_SWIGLU>(256, p, ta, tb, device, cur_stream());
+}
+
+// d(g|u)[M, 2I] from dy[M, D], w_down[D, I] and the saved pre-activations gu[M, 2I]:
+//   dact = dy @ w_down ; dg = dact * u * silu'(g) ; du = dact * silu(g)
+void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu, double alpha) {
+  using namespace gemm;
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(w_down, "w_down");
+  check_cuda_bf16(gu, "gu");
+  check_cuda_bf16(dgu, "dgu");
+  const int M = static_cast<int>(dy.size(0));
+  const int D = static_cast<int>(dy.size(1));
+  TT_CHECK(w_down.size(0) == D, "dswiglu: w_down must be [D, I]");
+  const int I = static_cast<int>(w_down.size(1));
+  TT_CHECK(gu.size(0) == M && gu.size(1) == 2 * I && dgu.size(0) == M && dgu.size(1) == 2 * I, "dswiglu: bad shapes");
+  TT_CHECK(I % 64 == 0, "dswiglu: intermediate size must be a multiple of 64");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  const int device = dy.get_device();
+  const int bn = choose_bn(M, I, device);
+  const CUtensorMap ta = operand_map(dy, false, BM);
+  const CUtensorMap tb = operand_map(w_down, true, bn);
+  Params p = base_params(M, I, D, dgu, alpha, c10::nullopt, device);
+  p.C = nullptr;
+  p.aux = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr());
+  p.ld_aux = static_cast<int>(gu.stride(0));
+  p.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
+  p.ld_aux_out = static_cast<int>(dgu.stride(0));
+  launch_bn<false, true, EPI_DSWIGLU>(bn, p, ta, tb, device, cur_stream());
+}
+
+}  // namespace tt

@@ -1,0 +1,88 @@
+"""tcgen05 GEMM vs a PyTorch fp32 reference of the same op (all operand majors, epilogues)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def ext():
+    from tinytron_b200.ops import _ext
+
+    return _ext.load()
+
+
+def _operands(M, N, K, a_mn, b_mn, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    A = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    B = torch.randn(N, K, device="cuda", generator=g).bfloat16()
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    return A, B, a, b
+
+
+def _check(out, ref, tol):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err / scale < tol, f"rel err {err / scale:.3e}"
+
+
+SHAPES = [(128, 256, 64), (256, 512, 128), (296, 200, 136), (1024, 3072, 2048), (136, 1000, 72), (512, 128, 5504)]
+
+
+@pytest.mark.parametrize("M,N,K", SHAPES)
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
+@pytest.mark.parametrize("bn", [0, 128])
+def test_gemm_bf16_out(M, N, K, a_mn, b_mn, bn):
+    A, B, a, b = _operands(M, N, K, a_mn, b_mn)
+    c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ext().gemm(a, b, c, a_mn, b_mn, False, 1.0, None, bn)
+    ref = A.float() @ B.float().t()
+    _check(c, ref, 1e-2)
+    assert ext().status_read(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 384), (1000, 264, 520)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
+def test_gemm_fp32_accumulate_alpha(M, N, K, a_mn, b_mn):
+    A, B, a, b = _operands(M, N, K, a_mn, b_mn, seed=1)
+    c0 = torch.randn(M, N, device="cuda")
+    c = c0.clone()
+    alpha_t = torch.tensor([0.5], device="cuda")
+    ext().gemm(a, b, c, a_mn, b_mn, True, 2.0, alpha_t, 0)
+    ref = c0 + (A.float() @ B.float().t())
+    _check(c, ref, 1e-5)
+    c2 = torch.empty(M, N, device="cuda")
+    ext().gemm(a, b, c2, a_mn, b_mn, False, 0.25, None, 0)
+    _check(c2, 0.25 * (A.float() @ B.float().t()), 1e-5)
+
+
+@pytest.mark.parametrize("M,I,K", [(256, 256, 128), (300, 5504 // 8, 256), (1024, 1408, 2048)])
+def test_gemm_swiglu(M, I, K):
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
+    w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.05).bfloat16()
+    out = torch.empty(M, I, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    ext().gemm_swiglu(x, w, out, gu)
+    pre = x.float() @ w.float().t()
+    gate, up = pre[:, :I], pre[:, I:]
+    ref = torch.nn.functional.silu(gate) * up
+    _check(out, ref, 1e-2)
+    _check(gu, pre, 1e-2)
+
+
+@pytest.mark.parametrize("M,D,I", [(256, 256, 256), (300, 128, 704), (1024, 2048, 1408)])
+def test_gemm_dswiglu(M, D, I):
+    g = torch.Generator(device="cuda").manual_seed(3)
+    dy = torch.randn(M, D, device="cuda", generator=g).bfloat16()
+    wd = (torch.randn(D, I, device="cuda", generator=g) * 0.05).bfloat16()
+    gu = torch.randn(M, 2 * I, device="cuda", generator=g).bfloat16()
+    dgu = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    ext().gemm_dswiglu(dy, wd, gu, dgu, 1.0)
+    dact = dy.float() @ wd.float()
+    gate, up = gu[:, :I].float(), gu[:, I:].float()
+    s = torch.sigmoid(gate)
+    ref_dg = dact * up * s * (1 + gate * (1 - s))
+    ref_du = dact * gate * s
+    _check(dgu[:, :I], ref_dg, 2e-2)
+    _check(dgu[:, I:], ref_du, 2e-2)
