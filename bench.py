@@ -1,0 +1,340 @@
+"""Headline benchmark: train tokens/s (whole job) + MFU for the dense ~1.3B GPT
+(24L, d2048, 16q/4kv heads, SwiGLU 5504, vocab 50304, seq 4096), micro-batch 4
+per GPU, grad-accum 4, DDP + ZeRO-1 AdamW, bf16 compute with fp32 masters.
+
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+
+For N > 1 launch with torch.distributed.run (one rank per GPU, NCCL).  Rank 0
+prints one JSON line.  ``value`` is device-timed (CUDA events on the launching
+stream, barrier + synchronize on both sides, max over ranks) with inputs already
+on the device; ``e2e`` runs the same steps through the public Trainer API with
+every step's inputs copied from pinned host memory and the loss read back.
+Inputs (weights, activations, 1.6 GB logits) are far larger than the 126 MB L2,
+so no explicit L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import socket
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+MODEL_FLAGS = ["--num_layer", "24", "--hidden_size", "2048", "--num_attention_heads", "16",
+               "--num_key_value_heads", "4", "--intermediate_size", "5504", "--vocab_size", "50304",
+               "--block_size", "4096", "--init_std", "0.02"]
+MICRO_BATCH, SEQ, GA = 4, 4096, 4
+METRIC = "train_tokens_per_sec_per_box"
+MODEL_NAME = "dense-1.3B (24L d2048 16q/4kv I5504 V50304)"
+
+
+def _free_port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _train_argv(n_gpus: int, steps: int, log_dir: str) -> list[str]:
+    return ["--use_mock_data", "--deterministic", "--mock_data_num_samples", str(MICRO_BATCH * GA * n_gpus * (steps + 2)),
+            "--log_dir", log_dir, "--total_batch_size", str(MICRO_BATCH * SEQ * GA * n_gpus),
+            "--batch_size", str(MICRO_BATCH), "--seq_len", str(SEQ), "--max_steps", str(steps + 1),
+            "--warmup_steps", "1", "--max_lr", "3e-4", "--min_lr", "3e-5", "--weight_decay", "0.1",
+            "--sep_size", "1", "--use_distributed_optimizer", *MODEL_FLAGS]
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle sampling during the timed region (rank 0, all GPUs)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, enabled: bool):
+        self.enabled = enabled
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        if self.enabled:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            try:
+                self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader",
+                                              "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            except Exception:
+                self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self, n_gpus: int) -> dict:
+        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        if not self.path or not os.path.exists(self.path):
+            return out
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                idx, sm, smax = int(parts[0]), float(parts[1].split()[0]), float(parts[2].split()[0])
+            except ValueError:
+                continue
+            if idx >= n_gpus:
+                continue
+            rows.append((sm, smax, parts[5:9]))
+        if not rows:
+            return out
+        loaded = [r for r in rows if r[0] > 600] or rows
+        out["sm_mhz"] = statistics.median(r[0] for r in loaded)
+        out["sm_max_mhz"] = max(r[1] for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in loaded:
+            for name, val in zip(names, r[2]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        out["reasons"] = sorted(reasons)
+        out["samples"] = len(loaded)
+        return out
+
+
+def _setup_dist(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}; launch N>1 with torch.distributed.run")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    os.environ.setdefault("RANK", "0")
+    os.environ.setdefault("LOCAL_RANK", "0")
+    os.environ.setdefault("WORLD_SIZE", "1")
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", str(_free_port()))
+    torch.cuda.set_device(local)
+    return rank, local, world
+
+
+def _max_over_ranks(x: float) -> float:
+    import torch
+    import torch.distributed as dist
+
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return x
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _timed(step_fn, steps: int, start_step: int) -> float:
+    """ms for `steps` calls, CUDA events, barrier + sync on both sides, max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(steps):
+        step_fn(start_step + i)
+    e.record()
+    torch.cuda.synchronize()
+    if dist.is_initialized():
+        dist.barrier()
+    return _max_over_ranks(s.elapsed_time(e))
+
+
+def _count_launches(step_fn, step: int, own_marker: str) -> tuple[int, int]:
+    """(our kernels, all kernels) launched by one step, from the torch profiler (untimed)."""
+    import torch
+
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+        step_fn(step)
+        torch.cuda.synchronize()
+    ours = total = 0
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            total += 1
+            if own_marker and own_marker in ev.name:
+                ours += 1
+    return ours, total
+
+
+def _make_device_batches(vocab: int, n: int, seed: int):
+    import torch
+
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    out = []
+    for _ in range(n):
+        data = torch.randint(0, vocab, (MICRO_BATCH, SEQ + 1), generator=g)
+        out.append({"input_ids": data[:, :SEQ].contiguous(), "labels": data[:, 1:].contiguous()})
+    return out
+
+
+def run(args, impl: str):
+    import torch
+    import torch.distributed as dist
+
+    rank, local, world = _setup_dist(args.gpus)
+    log_dir = tempfile.mkdtemp(prefix=f"tt_bench_{impl}_")
+    total_steps = args.warmup + 2 * args.steps + 2
+    if impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        try:
+            from tinytron.training import Trainer, build_config, parse_args  # the unmodified reference
+        except Exception as exc:  # pragma: no cover
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable": f"reference import failed: {exc}"}))
+            return
+        argv = _train_argv(world, total_steps, log_dir) + ["--debug"]
+        if args.ref_compile:
+            argv.append("--use_compile")
+        cfg = build_config(parse_args(argv))
+        trainer = Trainer(cfg)
+        # the reference's padded-bmm MoE path is forced only for MoE configs; dense here.
+        own_marker = ""
+    else:
+        sys.path.insert(0, ROOT)
+        from tinytron_b200.ops import _ext
+        from tinytron_b200.training import build_config, parse_args
+        from tinytron_b200.training.trainer import Trainer
+
+        _ext.load()
+        cfg = build_config(parse_args(_train_argv(world, total_steps, log_dir)))
+        trainer = Trainer(cfg)
+        own_marker = "tt::"
+    trainer.model.train()
+    ga = trainer.training_info["grad_accum_steps"]
+    assert ga == GA, ga
+
+    # ---- device-resident inputs (the `value` measurement)
+    dev_batches = [{k: v.cuda() for k, v in b.items()} for b in _make_device_batches(50304, ga, seed=1234 + rank)]
+    state = {"i": 0}
+
+    def next_dev():
+        b = dev_batches[state["i"] % ga]
+        state["i"] += 1
+        return b
+
+    host_batches = [{k: v.pin_memory() for k, v in b.items()} for b in _make_device_batches(50304, ga, seed=99 + rank)]
+
+    def next_host():
+        b = host_batches[state["i"] % ga]
+        state["i"] += 1
+        return b
+
+    def step_fn(step):
+        trainer.one_step_results = {}
+        trainer._one_training_step(trainer.config, step)
+
+    losses = []
+
+    def e2e_step_fn(step):
+        trainer.one_step_results = {}
+        trainer._one_training_step(trainer.config, step)
+        losses.append(float(trainer.one_step_results["loss"].item()))  # device -> host read of the result
+
+    trainer._next_train_batch = next_dev
+    for w in range(args.warmup):
+        step_fn(w)
+    torch.cuda.synchronize()
+    with ClockSampler(rank == 0 and not args.no_clocks) as clk:
+        ms = _timed(step_fn, args.steps, args.warmup)
+    clocks = clk.summary(world)
+
+    trainer._next_train_batch = next_host
+    e2e_ms = _timed(e2e_step_fn, args.steps, args.warmup + args.steps)
+    h2d = ga * MICRO_BATCH * SEQ * 8 * 2  # int64 input_ids + labels per rank per step
+    d2h = 4
+
+    trainer._next_train_batch = next_dev
+    launches, all_kernels = _count_launches(step_fn, args.warmup + 2 * args.steps, own_marker)
+
+    tokens_per_step = MICRO_BATCH * SEQ * ga * world
+    value = tokens_per_step / (ms / args.steps / 1e3)
+    e2e_value = tokens_per_step / (e2e_ms / args.steps / 1e3)
+    sys.path.insert(0, ROOT)
+    from tinytron_b200.models.presets import get_preset
+    from tinytron_b200.utils.flops import training_flops_per_microstep
+
+    flops_step = training_flops_per_microstep(get_preset("b200-dense-1.3b"), MICRO_BATCH, SEQ) * ga * world
+    achieved = flops_step / (ms / args.steps / 1e3)
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    measured_peak = float(peaks.get("bf16_tflops", 1590.0)) * 1e12
+    out = {
+        "metric": METRIC,
+        "value": round(value, 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic uniform random tokens (seeded), random-init weights N(0,0.02)",
+        "config": {"model": MODEL_NAME, "global_batch": MICRO_BATCH * GA * world, "seq_len": SEQ,
+                   "micro_batch": MICRO_BATCH, "grad_accum": GA, "parallelism": f"dp{world}" + ("+zero1"),
+                   "optimizer": "AdamW (ZeRO-1)", "l2": "inputs larger than L2 (no flush needed)"},
+        "mfu": round(achieved / (world * 2.25e15), 4),
+        "mfu_of_measured_cublas_peak": round(achieved / (world * measured_peak), 4),
+        "model_tflops_per_gpu": round(achieved / world / 1e12, 1),
+        "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": round(e2e_ms / args.steps, 3)},
+        "gpu_launches": launches * args.steps,
+        "kernels_per_step": {"ours": launches, "all": all_kernels},
+        "clocks": clocks,
+        "final_loss": losses[-1] if losses else None,
+    }
+    if impl == "reference":
+        out["impl"] = "reference"
+        out.pop("gpu_launches")
+        out["config"]["reference_flags"] = "mock data, deterministic, ZeRO-1, " + (
+            "--use_compile" if args.ref_compile else "eager")
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if hasattr(trainer, "close"):
+        trainer.close()
+    elif dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--ref-compile", action="store_true", help="reference arm: pass --use_compile")
+    ap.add_argument("--no-clocks", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    run(args, args.impl)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,78 @@
+"""CPU fp32 parity of the framework's model against the reference model (same weights)."""
+import pytest
+import torch
+
+import ref_oracle
+from tinytron_b200.models import GPT, ModelConfig
+
+pytestmark = pytest.mark.skipif(not ref_oracle.available(), reason="reference not installed under baseline/_ref")
+
+
+def _cfgs():
+    dense = ModelConfig(block_size=64, vocab_size=256, num_layer=2, num_attention_heads=4, num_key_value_heads=2,
+                        hidden_size=64, intermediate_size=96, init_std=0.02, seed=7)
+    moe = ModelConfig(block_size=64, vocab_size=256, num_layer=2, num_attention_heads=4, num_key_value_heads=2,
+                      hidden_size=64, intermediate_size=96, init_std=0.02, seed=7, use_moe=True, num_experts=4,
+                      num_experts_per_tok=2, moe_intermediate_size=48, moe_balance_loss_weight=0.01)
+    return {"dense": dense, "moe": moe}
+
+
+@pytest.fixture(scope="module")
+def ref():
+    ref_oracle.ensure_gloo_world1()
+    with ref_oracle.cpu_reference() as tt:
+        from tinytron.distributed import parallel_state
+        from tinytron.training.config import ParallelConfig
+
+        parallel_state.initialize_model_parallel(ParallelConfig(sep_size=1))
+        yield tt
+
+
+@pytest.mark.parametrize("kind", ["dense", "moe"])
+def test_forward_backward_matches_reference(ref, kind):
+    from tinytron.model import GPT as RefGPT
+    from tinytron.model.config import ModelConfig as RefCfg
+
+    cfg = _cfgs()[kind]
+    ref_cfg = RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+    torch.manual_seed(0)
+    rm = RefGPT(ref_cfg)
+    ours = GPT(cfg, device="cpu")
+    missing, unexpected = ours.load_state_dict(rm.state_dict(), strict=True)
+    assert not missing and not unexpected
+    x = torch.randint(0, cfg.vocab_size, (2, 32))
+    y = torch.randint(0, cfg.vocab_size, (2, 32))
+    y[0, :5] = -100
+    _, rl, rll = rm(x, y)
+    rl.backward()
+    _, ol, oll = ours(x, y)
+    ol.backward()
+    assert torch.allclose(ol, rl, atol=1e-5, rtol=1e-5), (ol.item(), rl.item())
+    assert torch.allclose(oll, rll, atol=1e-5, rtol=1e-5)
+    rg = {n: p.grad for n, p in rm.named_parameters()}
+    for n, p in ours.named_parameters():
+        assert p.grad is not None, n
+        assert torch.allclose(p.grad, rg[n], atol=1e-5, rtol=1e-4), n
+    # logits path (no targets)
+    assert torch.allclose(ours(x), rm(x), atol=1e-5, rtol=1e-5)
+    # clip_grad_norm semantics
+    assert torch.allclose(ours.clip_grad_norm(0.5), rm.clip_grad_norm(0.5), atol=1e-5, rtol=1e-5)
+
+
+def test_kv_cache_decode_matches_reference(ref):
+    from tinytron.model import GPT as RefGPT
+    from tinytron.model.config import ModelConfig as RefCfg
+
+    cfg = _cfgs()["dense"]
+    rm = RefGPT(RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})).eval()
+    ours = GPT(cfg, device="cpu").eval()
+    ours.load_state_dict(rm.state_dict())
+    x = torch.randint(0, cfg.vocab_size, (2, 10))
+    with torch.no_grad():
+        rl, rkv = rm(x, use_cache=True)
+        ol, okv = ours(x, use_cache=True)
+        assert torch.allclose(ol, rl, atol=1e-5)
+        nxt = torch.randint(0, cfg.vocab_size, (2, 1))
+        rl2, _ = rm(nxt, use_cache=True, past_key_values=rkv, position_offset=10)
+        ol2, _ = ours(nxt, use_cache=True, past_key_values=okv, position_offset=10)
+        assert torch.allclose(ol2, rl2, atol=1e-5)

@@ -1,0 +1,91 @@
+"""CPU training parity: framework Trainer (fp32 CPU path, flat ZeRO-1 AdamW) vs the
+reference model + torch AdamW + reference LR schedule, same weights and batches
+(BASELINE config 1 shape, shortened)."""
+import math
+import os
+
+import pytest
+import torch
+
+import ref_oracle
+from tinytron_b200.training import build_config, parse_args
+
+
+def _args(tmp_path, steps=6, extra=()):
+    argv = ["--use_mock_data", "--deterministic", "--mock_data_num_samples", "64", "--log_dir", str(tmp_path),
+            "--total_batch_size", str(4 * 64), "--batch_size", "4", "--seq_len", "64", "--max_steps", str(steps),
+            "--warmup_steps", "2", "--max_lr", "3e-4", "--min_lr", "3e-5", "--weight_decay", "0.1",
+            "--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--vocab_size", "256", "--block_size", "64", "--init_std", "0.02",
+            "--backend", "gloo", *extra]
+    return parse_args(argv)
+
+
+def test_trainer_runs_and_loss_decreases(tmp_path, monkeypatch):
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR"):
+        monkeypatch.delenv(k, raising=False)
+    from tinytron_b200.training.trainer import Trainer
+
+    cfg = build_config(_args(tmp_path, steps=12, extra=["--max_lr", "3e-3", "--mock_data_num_samples", "4"]))
+    tr = Trainer(cfg)
+    tr.train()
+    losses = [tr.results[s]["loss"].item() for s in sorted(tr.results)]
+    assert losses[-1] < losses[0] - 0.05, losses
+
+
+@pytest.mark.skipif(not ref_oracle.available(), reason="reference not installed under baseline/_ref")
+def test_trainer_matches_reference_loop(tmp_path, monkeypatch):
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR"):
+        monkeypatch.delenv(k, raising=False)
+    from tinytron_b200.training.trainer import Trainer
+
+    steps = 6
+    cfg = build_config(_args(tmp_path, steps=steps))
+    tr = Trainer(cfg)
+    init_sd = {k: v.detach().clone() for k, v in tr.raw_model.state_dict().items()}
+    batches = []
+    orig = tr._next_train_batch
+
+    def rec():
+        b = orig()
+        batches.append({k: v.clone() for k, v in b.items()})
+        return b
+
+    tr._next_train_batch = rec
+    ours = []
+    for s in range(steps):
+        tr.train_step(s)
+        ours.append(tr.one_step_results["loss"].item())
+
+    ref_oracle.ensure_gloo_world1(port=29612)
+    with ref_oracle.cpu_reference():
+        from tinytron.distributed import parallel_state
+        from tinytron.model import GPT as RefGPT
+        from tinytron.model.config import ModelConfig as RefCfg
+        from tinytron.training.config import ParallelConfig
+
+        parallel_state.initialize_model_parallel(ParallelConfig(sep_size=1))
+        rcfg = RefCfg(**{k: v for k, v in cfg.model.__dict__.items() if k in RefCfg.__dataclass_fields__})
+        rm = RefGPT(rcfg)
+        rm.load_state_dict(init_sd)
+        opt = torch.optim.AdamW(rm.parameters(), lr=3e-4, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8)
+
+        def lr_at(it, max_steps=steps, warm=2, max_lr=3e-4, min_lr=3e-5):
+            if it < warm:
+                return max_lr * (it + 1) / warm
+            r = (it - warm) / (max_steps - warm)
+            return min_lr + 0.5 * (1 + math.cos(math.pi * r)) * (max_lr - min_lr)
+
+        ref = []
+        for s in range(steps):
+            opt.zero_grad()
+            b = batches[s]
+            _, loss, ll = rm(b["input_ids"], b["labels"])
+            loss.backward()
+            rm.clip_grad_norm(1.0)
+            for g in opt.param_groups:
+                g["lr"] = lr_at(s)
+            opt.step()
+            ref.append(ll.item())
+    for a, b in zip(ours, ref):
+        assert abs(a - b) < 1e-4 * max(1.0, abs(b)), (ours, ref)

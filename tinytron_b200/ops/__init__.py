@@ -1,0 +1,112 @@
+"""Functional ops used by the model.  Each op has exactly one GPU implementation
+(sm_100a kernels from the in-tree extension, via ``functional``) and a CPU
+implementation that restates the reference's PyTorch math in fp32 (the CPU oracle
+and the CPU training path).  The device of the input selects the implementation;
+there is no fallback between them on the GPU.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from .rope import rope_reference
+
+
+def _cuda_fn():
+    from . import functional
+
+    return functional
+
+
+def check_status(device=None, clear: bool = True) -> int:
+    """Read the device status word written by bounded device-side waits; raise on error."""
+    from . import _ext
+
+    dev = torch.cuda.current_device() if device is None else torch.device(device).index or 0
+    code = int(_ext.load().status_read(dev))
+    if code != 0:
+        if clear:
+            _ext.load().status_clear(dev)
+        raise RuntimeError(f"tinytron_b200 device wait timed out (status code {code}) on cuda:{dev}")
+    return code
+
+
+def _cat_w(weights):
+    return weights[0] if len(weights) == 1 else torch.cat(list(weights), 0)
+
+
+def linear(x: torch.Tensor, *weights: torch.Tensor) -> torch.Tensor:
+    """y = x @ cat(weights)^T (several weights sharing the input fuse into one GEMM)."""
+    if x.is_cuda:
+        return _cuda_fn().LinearFn.apply(x, *weights)
+    return F.linear(x, _cat_w(weights))
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    if x.is_cuda:
+        return _cuda_fn().RMSNormFn.apply(x, weight, eps)
+    dt = x.dtype
+    xf = x.to(torch.float32)
+    xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return weight * xf.to(dt)
+
+
+def add_rmsnorm(x: torch.Tensor, delta: torch.Tensor | None, weight: torch.Tensor, eps: float):
+    """(x + delta, rmsnorm(x + delta)); with delta None returns (x, rmsnorm(x))."""
+    if delta is None:
+        return x, rmsnorm(x, weight, eps)
+    if x.is_cuda:
+        return _cuda_fn().AddRMSNormFn.apply(x, delta, weight, eps)
+    x = x + delta
+    return x, rmsnorm(x, weight, eps)
+
+
+def swiglu_mlp(x: torch.Tensor, w_gate: torch.Tensor, w_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    if x.is_cuda:
+        return _cuda_fn().SwiGLUMLPFn.apply(x, w_gate, w_up, w_down)
+    return F.linear(F.silu(F.linear(x, w_gate)) * F.linear(x, w_up), w_down)
+
+
+def rotary_attention(qkv: torch.Tensor, B: int, T: int, Hq: int, Hkv: int, D: int, pos_offset: int = 0,
+                     theta: float = 10000.0, causal: bool = True) -> torch.Tensor:
+    """qkv [B*T, (Hq+2Hkv)*D] -> o [B*T, Hq*D]; RoPE positions pos_offset + t."""
+    if qkv.is_cuda:
+        return _cuda_fn().RotaryAttentionFn.apply(qkv, B, T, Hq, Hkv, D, pos_offset, theta, causal)
+    x = qkv.view(B, T, Hq + 2 * Hkv, D).transpose(1, 2)
+    q, k, v = x[:, :Hq], x[:, Hq:Hq + Hkv], x[:, Hq + Hkv:]
+    pos = torch.arange(pos_offset, pos_offset + T, device=qkv.device).unsqueeze(0)
+    q, k = rope_reference(q, k, pos, theta)
+    if Hkv != Hq:
+        k = k.repeat_interleave(Hq // Hkv, dim=1)
+        v = v.repeat_interleave(Hq // Hkv, dim=1)
+    o = F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+    return o.transpose(1, 2).reshape(B * T, Hq * D)
+
+
+def embedding(idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    if weight.is_cuda:
+        return _cuda_fn().EmbeddingFn.apply(idx, weight)
+    return F.embedding(idx, weight)
+
+
+def lm_head_ce_sum(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100):
+    """Sum of token cross-entropies over valid targets of logits = h @ weight^T."""
+    if h.is_cuda:
+        return _cuda_fn().LMHeadCrossEntropyFn.apply(h, weight, targets, ignore_index)
+    logits = F.linear(h, weight)
+    per = F.cross_entropy(logits.view(-1, logits.size(-1)).float(), targets.reshape(-1), ignore_index=ignore_index,
+                          reduction="none")
+    valid = (targets.reshape(-1) != ignore_index).to(per.dtype)
+    return (per * valid).sum()
+
+
+def lm_logits(h: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    if h.is_cuda:
+        return _cuda_fn().lm_logits(h, weight)
+    return F.linear(h, weight)
+
+
+def attention_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

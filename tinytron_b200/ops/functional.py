@@ -1,0 +1,317 @@
+"""Autograd functions for the sm_100a path.  Every op here launches the in-tree
+CUDA extension (no PyTorch/cuBLAS fallback on the GPU); see ``tinytron_b200.ops``
+for the device dispatch and the CPU reference path.
+
+Dtype contract (matches the reference's fp32-master + bf16-autocast numerics):
+  * residual stream, norms, embedding table, master weights, weight grads: fp32
+  * projection inputs/outputs, attention operands, logits: bf16
+  * weight gradients accumulate in fp32 inside the GEMM epilogue.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _ext
+from .rope import rope_tables
+from .weights import adjacent_views, bf16_of, concat_rows, main_grad_of, notify_grad_ready
+
+
+def C():
+    return _ext.load()
+
+
+def _bf16(x: torch.Tensor) -> torch.Tensor:
+    x = x if x.dtype == torch.bfloat16 else x.to(torch.bfloat16)
+    return x if x.is_contiguous() else x.contiguous()
+
+
+# ----------------------------------------------------------------------------- GEMM helpers
+def gemm_nt(a: torch.Tensor, w16: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """a [M, K] @ w16[N, K]^T."""
+    out = torch.empty(a.shape[0], w16.shape[0], device=a.device, dtype=out_dtype)
+    C().gemm(a, w16, out, False, False, False, 1.0, None, 0)
+    return out
+
+
+def gemm_nn(a: torch.Tensor, w16: torch.Tensor, alpha_t=None) -> torch.Tensor:
+    """a [M, N] @ w16[N, K]  (dgrad)."""
+    out = torch.empty(a.shape[0], w16.shape[1], device=a.device, dtype=torch.bfloat16)
+    C().gemm(a, w16, out, False, True, False, 1.0, alpha_t, 0)
+    return out
+
+
+def weight_grads(weights, dy2d: torch.Tensor, x2d: torch.Tensor, alpha_t=None):
+    """Gradients of y = x @ cat(weights)^T w.r.t. each weight: dW = dy^T x.
+
+    Accumulates into ``main_grad`` (one GEMM when the main grads are adjacent) and
+    returns Nones, or returns fresh fp32 grads for autograd when there is no main_grad.
+    """
+    mgs = [main_grad_of(w) for w in weights]
+    if all(m is not None for m in mgs):
+        if len(mgs) == 1 or adjacent_views(mgs):
+            C().gemm(dy2d, x2d, concat_rows(mgs), True, True, True, 1.0, alpha_t, 0)
+        else:
+            tmp = torch.empty(dy2d.shape[1], x2d.shape[1], device=dy2d.device, dtype=torch.float32)
+            C().gemm(dy2d, x2d, tmp, True, True, False, 1.0, alpha_t, 0)
+            r = 0
+            for m in mgs:
+                m.add_(tmp[r:r + m.shape[0]])
+                r += m.shape[0]
+        notify_grad_ready(weights)
+        return [None] * len(weights)
+    tmp = torch.empty(dy2d.shape[1], x2d.shape[1], device=dy2d.device, dtype=torch.float32)
+    C().gemm(dy2d, x2d, tmp, True, True, False, 1.0, alpha_t, 0)
+    out, r = [], 0
+    for w in weights:
+        out.append(tmp[r:r + w.shape[0]].view_as(w))
+        r += w.shape[0]
+    return out
+
+
+# ----------------------------------------------------------------------------- Linear
+class LinearFn(torch.autograd.Function):
+    """y = x @ cat(weights)^T  (several weights sharing an input are fused into one GEMM)."""
+
+    @staticmethod
+    def forward(ctx, x, *weights):
+        shape = x.shape
+        x2d = _bf16(x.reshape(-1, shape[-1]))
+        w16 = concat_rows([bf16_of(w) for w in weights])
+        y = gemm_nt(x2d, w16)
+        ctx.save_for_backward(x2d, w16)
+        ctx.weights = weights
+        ctx.in_shape = shape
+        ctx.x_dtype = x.dtype
+        return y.view(*shape[:-1], w16.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, w16 = ctx.saved_tensors
+        dy2d = _bf16(dy.reshape(-1, dy.shape[-1]))
+        dx = None
+        if ctx.needs_input_grad[0]:
+            dx = gemm_nn(dy2d, w16).view(ctx.in_shape)
+            if ctx.x_dtype != torch.bfloat16:
+                dx = dx.to(ctx.x_dtype)
+        grads = weight_grads(ctx.weights, dy2d, x2d)
+        return (dx, *grads)
+
+
+# ----------------------------------------------------------------------------- SwiGLU MLP
+class SwiGLUMLPFn(torch.autograd.Function):
+    """down(silu(gate(x)) * up(x)); gate|up run as one tcgen05 GEMM with the SwiGLU
+    epilogue, the backward's SwiGLU derivative runs in the down-proj dgrad epilogue."""
+
+    @staticmethod
+    def forward(ctx, x, w_gate, w_up, w_down):
+        shape = x.shape
+        x2d = _bf16(x.reshape(-1, shape[-1]))
+        M = x2d.shape[0]
+        w_gu = concat_rows([bf16_of(w_gate), bf16_of(w_up)])
+        wd = bf16_of(w_down)
+        I = w_gate.shape[0]
+        act = torch.empty(M, I, device=x.device, dtype=torch.bfloat16)
+        gu = torch.empty(M, 2 * I, device=x.device, dtype=torch.bfloat16)
+        C().gemm_swiglu(x2d, w_gu, act, gu)
+        y = gemm_nt(act, wd)
+        ctx.save_for_backward(x2d, act, gu, w_gu, wd)
+        ctx.weights = (w_gate, w_up, w_down)
+        ctx.in_shape = shape
+        return y.view(*shape[:-1], wd.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2d, act, gu, w_gu, wd = ctx.saved_tensors
+        w_gate, w_up, w_down = ctx.weights
+        dy2d = _bf16(dy.reshape(-1, dy.shape[-1]))
+        dgu = torch.empty_like(gu)
+        C().gemm_dswiglu(dy2d, wd, gu, dgu, 1.0)
+        (g_down,) = weight_grads([w_down], dy2d, act)
+        dx = gemm_nn(dgu, w_gu).view(ctx.in_shape)
+        g_gate, g_up = weight_grads([w_gate, w_up], dgu, x2d)
+        return dx, g_gate, g_up, g_down
+
+
+# ----------------------------------------------------------------------------- norms
+def _norm_weight_grad(w, dw_buf_needed: bool):
+    mg = main_grad_of(w)
+    if mg is not None:
+        return mg, True
+    return torch.zeros_like(w, dtype=torch.float32), False
+
+
+class RMSNormFn(torch.autograd.Function):
+    """h = bf16(w * rmsnorm(x)), x fp32 [.., D]."""
+
+    @staticmethod
+    def forward(ctx, x, w, eps):
+        shape = x.shape
+        x2d = x.reshape(-1, shape[-1]).contiguous().float()
+        M, D = x2d.shape
+        h = torch.empty(M, D, device=x.device, dtype=torch.bfloat16)
+        rstd = torch.empty(M, device=x.device, dtype=torch.float32)
+        C().add_rmsnorm_fwd(x2d, None, w, None, h, rstd, eps)
+        ctx.save_for_backward(x2d, rstd, w)
+        ctx.shape = shape
+        return h.view(shape)
+
+    @staticmethod
+    def backward(ctx, gh):
+        x2d, rstd, w = ctx.saved_tensors
+        M, D = x2d.shape
+        gh2d = _bf16(gh.reshape(M, D))
+        gx = torch.empty(M, D, device=x2d.device, dtype=torch.float32)
+        dw, is_main = _norm_weight_grad(w, True)
+        scratch = torch.empty(C().rmsnorm_bwd_scratch_numel(M, D), device=x2d.device, dtype=torch.float32)
+        C().rmsnorm_bwd(gh2d, x2d, rstd, w, None, gx, None, dw, True, scratch)
+        if is_main:
+            notify_grad_ready([w])
+        return gx.view(ctx.shape), (None if is_main else dw), None
+
+
+class AddRMSNormFn(torch.autograd.Function):
+    """x_out = x + delta (fp32 residual += bf16 branch output); h = bf16(w * rmsnorm(x_out))."""
+
+    @staticmethod
+    def forward(ctx, x, delta, w, eps):
+        shape = x.shape
+        x2d = x.reshape(-1, shape[-1])
+        M, D = x2d.shape
+        d2d = _bf16(delta.reshape(M, D))
+        x_out = torch.empty(M, D, device=x.device, dtype=torch.float32)
+        h = torch.empty(M, D, device=x.device, dtype=torch.bfloat16)
+        rstd = torch.empty(M, device=x.device, dtype=torch.float32)
+        C().add_rmsnorm_fwd(x2d.contiguous(), d2d, w, x_out, h, rstd, eps)
+        ctx.save_for_backward(x_out, rstd, w)
+        ctx.shape = shape
+        ctx.delta_dtype = delta.dtype
+        return x_out.view(shape), h.view(shape)
+
+    @staticmethod
+    def backward(ctx, g_xout, gh):
+        x_out, rstd, w = ctx.saved_tensors
+        M, D = x_out.shape
+        dw, is_main = _norm_weight_grad(w, True)
+        gx = torch.empty(M, D, device=x_out.device, dtype=torch.float32)
+        g_delta = torch.empty(M, D, device=x_out.device, dtype=torch.bfloat16)
+        scratch = torch.empty(C().rmsnorm_bwd_scratch_numel(M, D), device=x_out.device, dtype=torch.float32)
+        gres = None if g_xout is None else g_xout.reshape(M, D).float().contiguous()
+        if gh is None:
+            gh = torch.zeros(M, D, device=x_out.device, dtype=torch.bfloat16)
+        C().rmsnorm_bwd(_bf16(gh.reshape(M, D)), x_out, rstd, w, gres, gx, g_delta, dw, True, scratch)
+        if is_main:
+            notify_grad_ready([w])
+        gd = g_delta.view(ctx.shape)
+        if ctx.delta_dtype != torch.bfloat16:
+            gd = gx.view(ctx.shape).to(ctx.delta_dtype)
+        return gx.view(ctx.shape), gd, (None if is_main else dw), None
+
+
+# ----------------------------------------------------------------------------- attention
+class RotaryAttentionFn(torch.autograd.Function):
+    """RoPE (in place on q|k of the packed qkv buffer) + causal flash attention.
+
+    qkv: [B*T, (Hq + 2*Hkv) * D] bf16 straight from the fused QKV projection.
+    Returns o: [B*T, Hq*D] bf16 (c_proj input layout)."""
+
+    @staticmethod
+    def forward(ctx, qkv, B, T, Hq, Hkv, D, pos_offset, theta, causal):
+        qkv = qkv.contiguous()
+        cos, sin = rope_tables(D, theta, T + pos_offset, qkv.device)
+        C().rope_inplace(qkv, cos, sin, T, pos_offset, Hq + Hkv, D, False)
+        o = torch.empty(B * T, Hq * D, device=qkv.device, dtype=torch.bfloat16)
+        lse = torch.empty(B, Hq, T, device=qkv.device, dtype=torch.float32)
+        scale = 1.0 / math.sqrt(D)
+        C().attn_fwd(qkv, qkv, qkv, 0, Hq * D, (Hq + Hkv) * D, B, T, T, Hq, Hkv, D, o, lse, scale, causal, 0)
+        ctx.save_for_backward(qkv, o, lse)
+        ctx.cfg = (B, T, Hq, Hkv, D, pos_offset, theta, causal, scale)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, o, lse = ctx.saved_tensors
+        B, T, Hq, Hkv, D, pos_offset, theta, causal, scale = ctx.cfg
+        do = _bf16(do)
+        dqkv = torch.empty_like(qkv)
+        dq_acc = torch.empty(B * T, Hq * D, device=qkv.device, dtype=torch.float32)
+        delta = torch.empty(B, Hq, T, device=qkv.device, dtype=torch.float32)
+        C().attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * D, (Hq + Hkv) * D, lse, B, T, Hq, Hkv, D, dqkv, 0, dqkv, Hq * D,
+                     dqkv, (Hq + Hkv) * D, dq_acc, delta, scale, causal)
+        cos, sin = rope_tables(D, theta, T + pos_offset, qkv.device)
+        C().rope_inplace(dqkv, cos, sin, T, pos_offset, Hq + Hkv, D, True)
+        return dqkv, None, None, None, None, None, None, None, None
+
+
+def attention_fwd_only(q, k, v, q_col0, k_col0, v_col0, B, T, Tk, Hq, Hkv, D, causal, causal_offset, out=None,
+                       want_lse=False):
+    """Forward-only flash attention over token-major buffers (inference / prefill)."""
+    o = out if out is not None else torch.empty(B * T, Hq * D, device=q.device, dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device=q.device, dtype=torch.float32) if want_lse else None
+    C().attn_fwd(q, k, v, q_col0, k_col0, v_col0, B, T, Tk, Hq, Hkv, D, o, lse, 1.0 / math.sqrt(D), causal,
+                 causal_offset)
+    return o, lse
+
+
+# ----------------------------------------------------------------------------- embedding
+class EmbeddingFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, idx, weight):
+        idx_flat = idx.reshape(-1).contiguous()
+        out = torch.empty(idx_flat.numel(), weight.shape[1], device=weight.device, dtype=torch.float32)
+        C().embedding_fwd(idx_flat, weight.detach().contiguous(), out)
+        ctx.save_for_backward(idx_flat)
+        ctx.weight = weight
+        return out.view(*idx.shape, weight.shape[1])
+
+    @staticmethod
+    def backward(ctx, g):
+        (idx_flat,) = ctx.saved_tensors
+        w = ctx.weight
+        g2d = g.reshape(-1, w.shape[1]).float().contiguous()
+        mg = main_grad_of(w)
+        if mg is not None:
+            C().embedding_bwd(idx_flat, g2d, mg)
+            notify_grad_ready([w])
+            return None, None
+        gw = torch.zeros(w.shape, device=w.device, dtype=torch.float32)
+        C().embedding_bwd(idx_flat, g2d, gw)
+        return None, gw
+
+
+# ----------------------------------------------------------------------------- LM head + CE
+class LMHeadCrossEntropyFn(torch.autograd.Function):
+    """Sum over valid tokens of CE(h @ W^T, targets).
+
+    The CE kernel overwrites the bf16 logits with (softmax - onehot) in place, so
+    backward is two GEMMs scaled by the incoming scalar gradient read on device."""
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, ignore_index):
+        h2d = _bf16(h.reshape(-1, h.shape[-1]))
+        w16 = bf16_of(weight)
+        logits = gemm_nt(h2d, w16)
+        loss_rows = torch.empty(h2d.shape[0], device=h.device, dtype=torch.float32)
+        C().cross_entropy_fwd(logits, targets.reshape(-1).contiguous(), loss_rows, None, ignore_index, True)
+        ctx.save_for_backward(h2d, logits, w16)
+        ctx.weight = weight
+        ctx.h_shape = h.shape
+        ctx.h_dtype = h.dtype
+        return loss_rows.sum()
+
+    @staticmethod
+    def backward(ctx, g_loss):
+        h2d, grad_logits, w16 = ctx.saved_tensors
+        alpha = g_loss.detach().reshape(1).float().contiguous()
+        dh = gemm_nn(grad_logits, w16, alpha_t=alpha).view(ctx.h_shape)
+        if ctx.h_dtype != torch.bfloat16:
+            dh = dh.to(ctx.h_dtype)
+        (gw,) = weight_grads([ctx.weight], grad_logits, h2d, alpha_t=alpha)
+        return dh, gw, None, None
+
+
+def lm_logits(h: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    """Forward-only logits (bf16) for inference."""
+    h2d = _bf16(h.reshape(-1, h.shape[-1]))
+    return gemm_nt(h2d, bf16_of(weight)).view(*h.shape[:-1], weight.shape[0])
