@@ -1,0 +1,167 @@
+"""Multi-rank semantics on CPU (gloo): SEP training (Ulysses attention + expert-parallel
+MoE), head-parallel KV-cache decode and DP + ZeRO-1 must reproduce single-process
+results for the same weights and data."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from tinytron_b200.models import GPT, ModelConfig
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _entry(rank, world, port, fn, args):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK"):
+        os.environ.pop(k, None)
+    torch.set_num_threads(1)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        fn(rank, world, *args)
+    finally:
+        from tinytron_b200.parallel import parallel_state
+
+        parallel_state.destroy_model_parallel()
+        dist.destroy_process_group()
+
+
+def spawn(fn, world, *args):
+    mp.spawn(_entry, args=(world, _port(), fn, args), nprocs=world, join=True)
+
+
+def cfg(**kw):
+    base = dict(block_size=64, vocab_size=128, num_layer=2, num_attention_heads=4, num_key_value_heads=2,
+                hidden_size=64, intermediate_size=96, init_std=0.02, seed=11)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def data(B=2, T=32, V=128, seed=5):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randint(0, V, (B, T), generator=g)
+    y = torch.randint(0, V, (B, T), generator=g)
+    return x, y
+
+
+# ---------------------------------------------------------------- SEP training
+def _sep_worker(rank, world, c, out_dir):
+    from tinytron_b200.models.gpt import EXPERT_LOCAL_PARAM_SUFFIXES
+    from tinytron_b200.parallel import allreduce_non_expert_grads_across_sp, parallel_state
+
+    parallel_state.initialize_model_parallel(sep_size=world)
+    torch.manual_seed(0)
+    m = GPT(c, device="cpu")
+    x, y = data(V=c.vocab_size)
+    T = x.size(1) // world
+    _, loss, ll = m(x[:, rank * T:(rank + 1) * T], y[:, rank * T:(rank + 1) * T])
+    loss.backward()
+    allreduce_non_expert_grads_across_sp(m, parallel_state.get_sp_group(), world, EXPERT_LOCAL_PARAM_SUFFIXES)
+    torch.save({"ll": ll.item(), "grads": {n: p.grad.clone() for n, p in m.named_parameters()}},
+               os.path.join(out_dir, f"r{rank}.pt"))
+
+
+@pytest.mark.parametrize("kv,moe", [(2, False), (1, False), (2, True)])
+def test_sep2_training_matches_single_rank(kv, moe):
+    extra = dict(use_moe=True, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32,
+                 moe_balance_loss_weight=0.01) if moe else {}
+    c = cfg(num_key_value_heads=kv, **extra)
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_sep_worker, 2, c, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    full = GPT(c, device="cpu")
+    x, y = data(V=c.vocab_size)
+    _, loss, ll = full(x, y)
+    loss.backward()
+    for r in range(2):
+        assert abs(res[r]["ll"] - ll.item()) < 1e-5
+        for n, p in full.named_parameters():
+            g = res[r]["grads"][n]
+            if n.endswith(("experts_gate_weights", "experts_up_weights", "experts_down_weights")):
+                ref = p.grad[r * 2:(r + 1) * 2]
+            else:
+                ref = p.grad
+            assert torch.allclose(g, ref, atol=2e-5, rtol=1e-3), (r, n, (g - ref).abs().max())
+
+
+# ---------------------------------------------------------------- head-parallel decode
+def _decode_worker(rank, world, c, out_dir):
+    from tinytron_b200.parallel import parallel_state
+
+    parallel_state.initialize_model_parallel(sep_size=world)
+    m = GPT(c, device="cpu").eval()
+    x, _ = data(B=2, T=12, V=c.vocab_size)
+    with torch.no_grad():
+        l1, kv = m(x, use_cache=True)
+        nxt = x[:, :1]
+        l2, _ = m(nxt, use_cache=True, past_key_values=kv, position_offset=12)
+    torch.save({"l1": l1, "l2": l2}, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+@pytest.mark.parametrize("kv", [2, 1])
+def test_sep2_head_parallel_decode_matches_single_rank(kv):
+    c = cfg(num_key_value_heads=kv)
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_decode_worker, 2, c, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    m = GPT(c, device="cpu").eval()
+    x, _ = data(B=2, T=12, V=c.vocab_size)
+    with torch.no_grad():
+        l1, kv_ = m(x, use_cache=True)
+        l2, _ = m(x[:, :1], use_cache=True, past_key_values=kv_, position_offset=12)
+    for r in range(2):
+        assert torch.allclose(res[r]["l1"], l1, atol=1e-5)
+        assert torch.allclose(res[r]["l2"], l2, atol=1e-5)
+
+
+# ---------------------------------------------------------------- DP + ZeRO-1
+def _dp_worker(rank, world, c, out_dir):
+    from tinytron_b200.parallel import parallel_state
+    from tinytron_b200.parallel.buffers import FlatParams
+    from tinytron_b200.parallel.zero1 import FlatZeRO1
+
+    parallel_state.initialize_model_parallel(sep_size=1)
+    m = GPT(c, device="cpu")
+    flat = FlatParams(m, pad_to_multiple=64 * world, with_bf16=False)
+    opt = FlatZeRO1(flat, dp_group=parallel_state.get_dp_group(), lr=1e-2, weight_decay=0.1)
+    x, y = data(B=4, V=c.vocab_size)
+    for step in range(3):
+        flat.zero_grad()
+        _, loss, _ = m(x[rank * 2:(rank + 1) * 2], y[rank * 2:(rank + 1) * 2])
+        loss.backward()
+        for p in flat.params:
+            p.__dict__["main_grad"].add_(p.grad)
+            p.grad = None
+        opt.reduce_gradients()
+        norm, coef = opt.grad_norm_and_coef(1.0)
+        opt.step(grad_scale=coef)
+    torch.save({n: p.detach().clone() for n, p in m.named_parameters()}, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_dp2_zero1_matches_single_rank_adamw():
+    c = cfg()
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_dp_worker, 2, c, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    m = GPT(c, device="cpu")
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-2, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8)
+    x, y = data(B=4, V=c.vocab_size)
+    for step in range(3):
+        opt.zero_grad()
+        _, loss, _ = m(x, y)
+        loss.backward()
+        m.clip_grad_norm(1.0)
+        opt.step()
+    for n, p in m.named_parameters():
+        for r in range(2):
+            assert torch.allclose(res[r][n], p.detach(), atol=2e-5, rtol=1e-4), (n, r)

@@ -1,0 +1,152 @@
+"""KV-cache inference engine (reference: tinytron/inference/engine.py:16-261).
+
+Same constructor and ``generate`` signature/return values as the reference.
+Differences that matter for speed:
+  * prefill computes logits only for the last position (the reference materialises
+    [B, T, V] logits and slices the last row);
+  * the EOS stop test is evaluated on the device and read back every
+    ``eos_check_interval`` steps; the returned sequences are cut at the exact step
+    where every sequence had produced EOS, so the output equals the per-step check;
+  * with SEP > 1, SEP rank 0 samples and broadcasts the tokens (as the reference).
+"""
+from __future__ import annotations
+
+import time
+from contextlib import nullcontext
+
+import torch
+import torch.distributed as dist
+
+from tinytron_b200.models import GPT
+from tinytron_b200.parallel import parallel_state
+
+from .cache import PagedKVCache
+from .checkpoint import load_model_state_dict_for_inference
+from .sampler import sample_next_token, sample_next_token_with_log_prob
+
+
+class InferenceEngine:
+    def __init__(self, model_config, checkpoint_path: str | None = None, device: str = "cuda",
+                 dtype: torch.dtype = torch.bfloat16, use_paged_kv_cache: bool = True, kv_cache_page_size: int = 128,
+                 eos_check_interval: int = 8):
+        self.device = torch.device(device)
+        if self.device.type == "cuda":
+            if self.device.index is None:
+                self.device = torch.device("cuda", torch.cuda.current_device())
+            torch.cuda.set_device(self.device)
+        self.model_config = model_config
+        self.use_paged_kv_cache = use_paged_kv_cache
+        self.kv_cache_page_size = kv_cache_page_size
+        self.eos_check_interval = max(1, int(eos_check_interval))
+        self.model = GPT(model_config, device=self.device)
+        if checkpoint_path:
+            self.model.load_state_dict(load_model_state_dict_for_inference(checkpoint_path, model_config))
+        self.model.eval()
+        self.dtype = dtype
+
+    # ------------------------------------------------------------------ SEP-synced sampling
+    def _sep(self):
+        g = parallel_state.get_sp_group_or_none()
+        if g is None or not dist.is_initialized() or parallel_state.get_sep_world_size() <= 1:
+            return None
+        return g, parallel_state.get_sep_rank(), parallel_state.get_sep_global_rank(0)
+
+    def _sample_next_token_synced(self, logits, temperature=1.0, top_k=None, top_p=None):
+        sep = self._sep()
+        if sep is None:
+            return sample_next_token(logits, temperature=temperature, top_k=top_k, top_p=top_p)
+        g, r, src = sep
+        tok = sample_next_token(logits, temperature, top_k, top_p) if r == 0 else \
+            torch.empty(logits.size(0), dtype=torch.long, device=logits.device)
+        dist.broadcast(tok, src=src, group=g)
+        return tok
+
+    def _sample_next_token_with_log_prob_synced(self, logits, temperature=1.0, top_k=None, top_p=None):
+        sep = self._sep()
+        if sep is None:
+            return sample_next_token_with_log_prob(logits, temperature=temperature, top_k=top_k, top_p=top_p)
+        g, r, src = sep
+        if r == 0:
+            tok, lp = sample_next_token_with_log_prob(logits, temperature, top_k, top_p)
+        else:
+            tok = torch.empty(logits.size(0), dtype=torch.long, device=logits.device)
+            lp = torch.empty(logits.size(0), dtype=torch.float32, device=logits.device)
+        dist.broadcast(tok, src=src, group=g)
+        dist.broadcast(lp, src=src, group=g)
+        return tok, lp
+
+    def new_cache(self, batch_size: int, max_seq_len: int | None = None):
+        if self.use_paged_kv_cache:
+            return PagedKVCache.from_model_config(self.model_config, batch_size, self.kv_cache_page_size, self.device,
+                                                  self.dtype, max_seq_len=max_seq_len)
+        return PagedKVCache.contiguous(self.model_config, batch_size, self.device, self.dtype, max_seq_len=max_seq_len)
+
+    # ------------------------------------------------------------------ generation
+    @torch.no_grad()
+    def generate(self, input_ids: torch.Tensor, max_new_tokens: int, temperature: float = 1.0, top_k=None,
+                 top_p=None, eos_token_id: int | None = None, return_stats: bool = False,
+                 return_logprobs: bool = False):
+        if input_ids.dim() != 2:
+            raise ValueError(f"input_ids must be [B, T], got shape={tuple(input_ids.shape)}")
+        prompt = input_ids.to(self.device)
+        B, P = prompt.shape
+        total = P + max_new_tokens
+        if total > self.model_config.block_size:
+            raise ValueError(f"Requested total sequence length {total} exceeds block_size {self.model_config.block_size}")
+        tokens = torch.empty(B, total, dtype=prompt.dtype, device=self.device)
+        tokens[:, :P] = prompt
+        cache = self.new_cache(B, max_seq_len=total)
+        cuda = self.device.type == "cuda"
+        sync = torch.cuda.synchronize if cuda else (lambda *a: None)
+        logp_steps = []
+        finished = torch.zeros(B, dtype=torch.bool, device=self.device)
+        all_done = []
+        sync()
+        t0 = time.perf_counter()
+        logits, cache = self.model._forward_cached(prompt, cache, True, 0, last_only=True)
+        sync()
+        t1 = time.perf_counter()
+        cur = P
+        steps = 0
+        stop_at = None
+        for i in range(max_new_tokens):
+            last = logits[:, -1, :]
+            if return_logprobs:
+                nxt, lp = self._sample_next_token_with_log_prob_synced(last, temperature, top_k, top_p)
+                logp_steps.append(lp)
+            else:
+                nxt = self._sample_next_token_synced(last, temperature, top_k, top_p)
+            tokens[:, cur] = nxt
+            cur += 1
+            steps += 1
+            if eos_token_id is not None:
+                finished |= nxt == eos_token_id
+                all_done.append(finished.all())
+                if steps % self.eos_check_interval == 0 or i == max_new_tokens - 1:
+                    flags = torch.stack(all_done[-self.eos_check_interval:]).tolist()
+                    if any(flags):
+                        stop_at = steps - len(flags) + flags.index(True) + 1
+                        break
+            if i == max_new_tokens - 1:
+                break
+            logits, cache = self.model._forward_cached(nxt.unsqueeze(-1), cache, True, cur - 1, last_only=True)
+        sync()
+        t2 = time.perf_counter()
+        if stop_at is not None:
+            steps = stop_at
+            cur = P + stop_at
+            logp_steps = logp_steps[:stop_at]
+        tokens = tokens[:, :cur]
+        if not return_stats and not return_logprobs:
+            return tokens
+        extras = {}
+        if return_stats:
+            dt_p, dt_d = max(t1 - t0, 1e-9), max(t2 - t1, 1e-9)
+            extras.update({"prefill_tokens_per_sec": B * P / dt_p,
+                           "decode_tokens_per_sec": (B * steps / dt_d) if steps else 0.0,
+                           "prefill_tokens": float(B * P), "decode_tokens": float(B * steps)})
+        if return_logprobs:
+            lp = torch.stack(logp_steps, 1) if logp_steps else torch.empty(B, 0, device=self.device)
+            extras.update({"prompt_len": float(P), "decode_steps": float(steps), "token_log_probs": lp,
+                           "response_mask": torch.ones_like(lp, dtype=torch.float32)})
+        return tokens, extras

@@ -1,0 +1,39 @@
+"""Sampling (reference: tinytron/inference/sampler.py:6-61): temperature, top-k,
+top-p (nucleus, always keeping the most likely token), multinomial draw, and the
+log-prob of the drawn token under the filtered distribution."""
+from __future__ import annotations
+
+import torch
+
+
+def filter_logits(logits: torch.Tensor, temperature: float = 1.0, top_k: int | None = None,
+                  top_p: float | None = None) -> torch.Tensor:
+    if temperature <= 0:
+        raise ValueError("temperature must be > 0")
+    logits = logits.float()
+    if temperature != 1.0:
+        logits = logits / temperature
+    if top_k is not None and top_k > 0:
+        kth = torch.topk(logits, k=min(top_k, logits.size(-1)), dim=-1).values[:, -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    if top_p is not None and 0 < top_p < 1.0:
+        sorted_logits, order = torch.sort(logits, descending=True, dim=-1)
+        cum = torch.softmax(sorted_logits, dim=-1).cumsum(dim=-1)
+        drop = cum > top_p
+        drop[..., 0] = False
+        kept = sorted_logits.masked_fill(drop, float("-inf"))
+        logits = torch.full_like(logits, float("-inf")).scatter_(-1, order, kept)
+    return logits
+
+
+def sample_next_token(logits, temperature: float = 1.0, top_k=None, top_p=None) -> torch.Tensor:
+    if top_k == 1 and temperature > 0:  # greedy: identical result without a multinomial draw
+        return logits.argmax(dim=-1)
+    probs = torch.softmax(filter_logits(logits, temperature, top_k, top_p), dim=-1)
+    return torch.multinomial(probs, num_samples=1).squeeze(-1)
+
+
+def sample_next_token_with_log_prob(logits, temperature: float = 1.0, top_k=None, top_p=None):
+    lp = torch.log_softmax(filter_logits(logits, temperature, top_k, top_p), dim=-1)
+    tok = lp.argmax(dim=-1) if top_k == 1 else torch.multinomial(lp.exp(), num_samples=1).squeeze(-1)
+    return tok, lp.gather(-1, tok.unsqueeze(-1)).squeeze(-1)

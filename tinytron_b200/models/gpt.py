@@ -108,6 +108,8 @@ class GPT(nn.Module):
                 pending = blk.mlp(h)
         x, h = ops.add_rmsnorm(x, pending, self.lnf.weight, self.eps)
         if targets is None:
+            if torch.is_grad_enabled():  # differentiable logits (e.g. RL policy log-probs)
+                return ops.linear(h, self.lm_head.weight)
             return ops.lm_logits(h, self.lm_head.weight)
         loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index)
         loss, logging_loss = self.loss_fn.reduce(loss_sum, valid.sum())

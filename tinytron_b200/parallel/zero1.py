@@ -158,7 +158,12 @@ class FlatZeRO1:
         if self.sp > 1 and self.flat.dense_numel > 0:
             dist.all_reduce(g[:self.flat.dense_numel], op=dist.ReduceOp.SUM, group=self.sp_group)
         if self.dp > 1:
-            dist.reduce_scatter_tensor(g[self.lo:self.hi], g, op=dist.ReduceOp.AVG, group=self.dp_group)
+            if dist.get_backend(self.dp_group) == "nccl":
+                dist.reduce_scatter_tensor(g[self.lo:self.hi], g, op=dist.ReduceOp.AVG, group=self.dp_group)
+            else:  # gloo: no AVG and no aliasing of output into input
+                out = torch.empty(self.shard, dtype=g.dtype, device=g.device)
+                dist.reduce_scatter_tensor(out, g, op=dist.ReduceOp.SUM, group=self.dp_group)
+                g[self.lo:self.hi].copy_(out.div_(self.dp))
 
     # ---------------------------------------------------------------- norm
     @torch.no_grad()
@@ -214,7 +219,10 @@ class FlatZeRO1:
             if self.flat.bf16 is not None:
                 self.flat.bf16[lo:hi].copy_(p)
         if self.dp > 1:
-            dist.all_gather_into_tensor(self.flat.data, self.flat.data[lo:hi], group=self.dp_group)
+            if dist.get_backend(self.dp_group) == "nccl":
+                dist.all_gather_into_tensor(self.flat.data, self.flat.data[lo:hi], group=self.dp_group)
+            else:
+                dist.all_gather_into_tensor(self.flat.data, self.flat.data[lo:hi].clone(), group=self.dp_group)
             if self.flat.bf16 is not None:
                 # shadow of the shards other ranks updated
                 if lo > 0:
