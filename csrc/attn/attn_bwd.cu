@@ -217,9 +217,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         sm.delta[buf][t] = (q < p.T) ? p.delta[idx] : 0.0f;
       }
       mbar_arrive(&sm.stage_bar[buf]);
-      if (!mbar_wait(&sm.stage_bar[buf], (it >> 1) & 1, p.status, kTimeoutOther)) { ok = false; break; }
+      if (!mbar_wait_warp(&sm.stage_bar[buf], (it >> 1) & 1, p.status, kTimeoutOther)) { ok = false; break; }
       // ---- P^T = exp2(S^T * scale_log2 - lse2[q]) (0 for masked / padded queries)
-      if (!mbar_wait(&sm.s_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
+      if (!mbar_wait_warp(&sm.s_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
       float pv[BLOCK_B];
 #pragma unroll
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         if ((diag && i < r) || key_pad) e = 0.0f;  // causal: query qt*128+i < key kt*128+r
         pv[i] = e;
       }
-      if (it > 0 && !mbar_wait(&sm.ps_free, ph ^ 1u, p.status, kTimeoutAccEmpty)) { ok = false; break; }
+      if (it > 0 && !mbar_wait_warp(&sm.ps_free, ph ^ 1u, p.status, kTimeoutAccEmpty)) { ok = false; break; }
 #pragma unroll
       for (int c = 0; c < BLOCK_B; c += 8) {
         const uint4 v = make_uint4(pack_bf16x2(pv[c], pv[c + 1]), pack_bf16x2(pv[c + 2], pv[c + 3]),
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&sm.p_ready);
       // ---- dS^T = P^T * (dP^T - delta[q]) * scale
-      if (!mbar_wait(&sm.dp_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
+      if (!mbar_wait_warp(&sm.dp_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
 #pragma unroll
       for (int c = 0; c < BLOCK_B; c += 32) {
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       tc_fence_before();
       mbar_arrive(&sm.ds_ready);
       // ---- dQ partial (lane = query row) -> fp32 atomics
-      if (!mbar_wait(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
+      if (!mbar_wait_warp(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
       const int q = qt * BLOCK_B + r;
       float* dst = p.dq_acc + static_cast<size_t>(row0 + q) * (p.Hq * D) + static_cast<size_t>(h) * D;
@@ -292,7 +292,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_arrive(&sm.dq_empty);
     }
     // ---- dK, dV (lane = key row) -> bf16
-    if (ok && n_iter > 0 && mbar_wait(&sm.dq_full, (n_iter - 1) & 1, p.status, kTimeoutAccFull)) {
+    if (ok && n_iter > 0 && mbar_wait_warp(&sm.dq_full, (n_iter - 1) & 1, p.status, kTimeoutAccFull)) {
       tc_fence_after();
       const bool key_ok = key < p.T;
       __nv_bfloat16* dkrow = p.dk + static_cast<size_t>(row0 + key) * p.ld_dk + p.dk_col0 + static_cast<size_t>(g) * D;

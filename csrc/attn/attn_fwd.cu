@@ -206,7 +206,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     bool ok = true;
     for (int j = 0; j < n_kt; ++j) {
       const int s = j & 1;
-      if (!mbar_wait(&sm.s_full[s], (j >> 1) & 1, p.status, kTimeoutAccFull)) {
+      if (!mbar_wait_warp(&sm.s_full[s], (j >> 1) & 1, p.status, kTimeoutAccFull)) {
         ok = false;
         break;
       }
@@ -254,13 +254,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       l = l * alpha + rs;
       // P buffer and O are free once the previous PV MMA retired.
       if (j > 0) {
-        if (!mbar_wait(&sm.pv_done, (j - 1) & 1, p.status, kTimeoutAccFull)) {
+        if (!mbar_wait_warp(&sm.pv_done, (j - 1) & 1, p.status, kTimeoutAccFull)) {
           ok = false;
           break;
         }
         tc_fence_after();
       }
-      if (rescale) {
+      // tcgen05.ld/st are warp-collective: if any lane of the warp must rescale its O row,
+      // the whole warp runs the loop (alpha == 1 for rows that did not change).
+      if (__any_sync(0xffffffffu, rescale)) {
+        if (!rescale) alpha = 1.0f;
 #pragma unroll
         for (int c = 0; c < D; c += 16) {
           uint32_t ov[16];
@@ -284,7 +287,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_arrive(&sm.p_full);
     }
     // ------------------------------------------------ epilogue: O / l, LSE
-    if (ok && n_kt > 0 && mbar_wait(&sm.pv_done, (n_kt - 1) & 1, p.status, kTimeoutAccFull)) {
+    if (ok && n_kt > 0 && mbar_wait_warp(&sm.pv_done, (n_kt - 1) & 1, p.status, kTimeoutAccFull)) {
       tc_fence_after();
       const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
       const bool row_ok = q_idx < p.T;

@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
-      if (!mbar_wait(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
+      if (!mbar_wait_warp(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
       tc_fence_after();
       const int row = mb * BM + row_in_tile;
       const bool row_ok = row < p.M;
