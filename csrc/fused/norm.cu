@@ -9,6 +9,7 @@
 //           g_delta = bf16(g);  dw partial sums per row-group, reduced deterministically.
 #include "common/host_utils.h"
 #include "common/ptx.cuh"
+#include "fused/rmsnorm_bwd_noalloc.h"
 
 namespace tt {
 namespace {
@@ -209,3 +210,56 @@ void rmsnorm_bwd(torch::Tensor gh, torch::Tensor x, torch::Tensor rstd, torch::T
 int64_t rmsnorm_bwd_scratch_numel(int64_t M, int64_t D) { return ((M + BWD_ROWS - 1) / BWD_ROWS) * D; }
 
 }  // namespace tt
+
+// ----------------------------------------------------------------------------------------------
+// Allocation-free variant of rmsnorm_bwd (see fused/rmsnorm_bwd_noalloc.h). Same kernels; the
+// weight-gradient partials live in a file-scope device array instead of a caller-provided
+// buffer. Host code must not hand the array's name to a kernel (on the host it is only a
+// stand-in for the symbol): its device address is looked up once per device below.
+static __device__ __align__(256) float tt_rmsnorm_noalloc_scratch[TT_RMSNORM_NOALLOC_MAX_SCRATCH];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[64] = {nullptr};
+
+float* noalloc_scratch_for_current_device(int* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    *err = 3;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, tt_rmsnorm_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      *err = 3;
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int tt_rmsnorm_bwd_noalloc(
+    const __nv_bfloat16* gh, const float* x, const float* rstd, const float* w, const float* g_res, float* gx,
+    __nv_bfloat16* g_delta, float* dw, int M, int D, int accumulate_dw, cudaStream_t stream) {
+  using namespace tt;
+  if (gh == nullptr || x == nullptr || rstd == nullptr || w == nullptr || dw == nullptr || M < 0 || D <= 0 ||
+      D % EPT != 0 || D / EPT > 1024)
+    return 1;
+  if (M == 0) return 0;
+  const long long G = (static_cast<long long>(M) + BWD_ROWS - 1) / BWD_ROWS;
+  if (G * D > TT_RMSNORM_NOALLOC_MAX_SCRATCH) return 2;
+  int err = 0;
+  float* scratch = noalloc_scratch_for_current_device(&err);
+  if (scratch == nullptr) return err ? err : 3;
+  rmsnorm_bwd_kernel<<<static_cast<unsigned>(G), norm_threads(D), 0, stream>>>(gh, x, rstd, w, g_res, gx, g_delta,
+                                                                            scratch, M, D);
+  if (cudaGetLastError() != cudaSuccess) return 4;
+  reduce_rows_kernel<<<static_cast<unsigned>((D + 255) / 256), 256, 0, stream>>>(scratch, dw, static_cast<int>(G), D,
+                                                                                accumulate_dw ? 1 : 0);
+  if (cudaGetLastError() != cudaSuccess) return 4;
+  return 0;
+}
+
