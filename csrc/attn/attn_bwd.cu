@@ -1,4 +1,6 @@
 // Flash-attention backward on sm_100a tensor cores (tcgen05 + TMEM), GQA-native.
+// Pipelined: Q/dO tiles double-buffered, P^T kept in TMEM as the A operand of the dV
+// MMA, the next S^T issued while the compute warps form dS (see the kernel comment).
 //
 // Replaces the autograd backward of SDPA + repeat_interleave used by the reference
 // (tinytron/model/modules/attn.py:66-83, 420).  One CTA owns a 128-key tile of one
@@ -7,13 +9,14 @@
 // once, unexpanded.  Per (q head, q tile) iteration, five tcgen05 MMAs:
 //   S^T  = K Q^T        (TMEM, lanes = keys)
 //   dP^T = V dO^T       (TMEM, lanes = keys)
-//   dV  += P^T dO       (P^T written to smem by the softmax threads)
+//   dV  += P^T dO       (P^T written back into TMEM over S^T, read as the A operand)
 //   dK  += dS^T Q       (dS^T written to smem)
 //   dQp  = dS K         (TMEM, lanes = queries; same smem dS^T buffer read MN-major)
 // dQp is added into an fp32 accumulator with vector atomics; a final kernel
 // converts it to bf16.  Inputs/outputs are token-major (packed qkv layout).
 #include "common/host_utils.h"
 #include "common/ptx.cuh"
+#include "common/fast_exp2.cuh"
 
 namespace tt {
 namespace attn {
@@ -41,16 +44,20 @@ struct BwdSmem {
   static constexpr int TILE = BLOCK_B * D * 2;
   alignas(1024) uint8_t k[TILE];
   alignas(1024) uint8_t v[TILE];
-  alignas(1024) uint8_t q[TILE];
-  alignas(1024) uint8_t dout[TILE];
-  alignas(1024) uint8_t pt[BLOCK_B * BLOCK_B * 2];
-  alignas(1024) uint8_t dst[BLOCK_B * BLOCK_B * 2];
+  alignas(1024) uint8_t q[2][TILE];
+  alignas(1024) uint8_t dout[2][TILE];
+  alignas(1024) uint8_t dst[BLOCK_B * BLOCK_B * 2];  // dS^T [keys][queries], 128B-swizzled
   float lse2[2][BLOCK_B];
   float delta[2][BLOCK_B];
-  uint64_t kv_full, qdo_full, qdo_empty, s_full, dp_full, dp_empty, p_ready, ds_ready, ps_free, dq_full, dq_empty,
-      done, stage_bar[2];
+  uint64_t kv_full, qdo_full[2], qdo_empty[2], s_full, p_ready, dp_full, ds_ready, ds_free, dq_full, dq_empty, done,
+      stage_bar[2];
   uint32_t tmem_slot;
 };
+// Bytes the layout actually uses (sizeof rounds up to the 1 KB member alignment).
+template <int D>
+constexpr uint32_t bwd_smem_bytes() {
+  return static_cast<uint32_t>(offsetof(BwdSmem<D>, tmem_slot) + sizeof(uint32_t));
+}
 
 __device__ __forceinline__ uint32_t sw128(int row, int col, int rows) {
   const int chunk = col >> 6;
@@ -58,6 +65,10 @@ __device__ __forceinline__ uint32_t sw128(int row, int col, int rows) {
   return static_cast<uint32_t>(chunk * rows * 128 + row * 128 + ((unit ^ (row & 7)) << 4) + ((col & 7) << 1));
 }
 
+// Iteration pipeline (it = (q head in group, q tile)), MMAs issued in this order by one thread:
+//   S^T(0), dP^T(0); per it: dV += P^T(it) dO [P^T from TMEM] ; S^T(it+1) ;
+//   dK += dS^T Q, dQ = dS K [into the dP^T columns] ; dP^T(it+1)
+// so the next scores are computed while the compute warps form dS(it).
 template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -65,7 +76,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                     const BwdParams p) {
   constexpr uint32_t TILE = BwdSmem<D>::TILE;
   constexpr uint32_t ID_SQ = idesc_bf16_f32(BLOCK_B, BLOCK_B, false, false);  // S^T, dP^T
-  constexpr uint32_t ID_KV = idesc_bf16_f32(BLOCK_B, D, false, true);         // dV, dK
+  constexpr uint32_t ID_KV = idesc_bf16_f32(BLOCK_B, D, false, true);         // dV (A from TMEM), dK
   constexpr uint32_t ID_DQ = idesc_bf16_f32(BLOCK_B, D, true, true);          // dQ
   constexpr uint32_t S_COL = 0, DP_COL = BLOCK_B, DV_COL = 2 * BLOCK_B, DK_COL = 2 * BLOCK_B + D;
   constexpr uint32_t TMEM_COLS = 512;
@@ -73,6 +84,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   extern __shared__ uint8_t smem_raw[];
   BwdSmem<D>& sm = *reinterpret_cast<BwdSmem<D>*>(align_ptr(smem_raw, 1024));
+  // The D=128 layout needs all but ~0.9 KB of the 227 KB limit, so the launch does not
+  // reserve a full 1 KB for aligning the base; check that the aligned layout fits.
+  if (static_cast<uint32_t>(reinterpret_cast<uint8_t*>(&sm) - smem_raw) + bwd_smem_bytes<D>() > dynamic_smem_size()) {
+    if (threadIdx.x == 0) atomicCAS(p.status, 0, static_cast<int>(kSmemTooSmall));
+    return;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + BLOCK_B - 1) / BLOCK_B;
   const int kt = static_cast<int>(blockIdx.x);  // low kt = most work; launched first
@@ -90,19 +107,19 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     tma_prefetch_desc(&tmV);
     tma_prefetch_desc(&tmDO);
     mbar_init(&sm.kv_full, 1);
-    mbar_init(&sm.qdo_full, 1);
-    mbar_init(&sm.qdo_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sm.qdo_full[i], 1);
+      mbar_init(&sm.qdo_empty[i], 1);
+      mbar_init(&sm.stage_bar[i], 128);
+    }
     mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.dp_empty, 128);
     mbar_init(&sm.p_ready, 128);
+    mbar_init(&sm.dp_full, 1);
     mbar_init(&sm.ds_ready, 128);
-    mbar_init(&sm.ps_free, 1);
+    mbar_init(&sm.ds_free, 1);
     mbar_init(&sm.dq_full, 1);
     mbar_init(&sm.dq_empty, 128);
     mbar_init(&sm.done, 1);
-    mbar_init(&sm.stage_bar[0], 128);
-    mbar_init(&sm.stage_bar[1], 128);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -116,7 +133,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_iter > 0) {
-      // ------------------------------------------------ producer
+      // ------------------------------------------------ producer (Q/dO double-buffered)
       mbar_arrive_expect_tx(&sm.kv_full, 2 * TILE);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
@@ -124,32 +141,29 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tma_load_2d(sm.v + c * BLOCK_B * 128, &tmV, &sm.kv_full, p.v_col0 + g * D + c * 64, row0 + kt * BLOCK_B);
       }
       for (int it = 0; it < n_iter; ++it) {
+        const int s = it & 1;
         const int h = g * group + it / per_head;
         const int qt = qt0 + it % per_head;
-        if (!mbar_wait(&sm.qdo_empty, (it & 1) ^ 1u, p.status, kTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&sm.qdo_full, 2 * TILE);
+        if (!mbar_wait(&sm.qdo_empty[s], ((it >> 1) & 1) ^ 1u, p.status, kTimeoutEmpty)) break;
+        mbar_arrive_expect_tx(&sm.qdo_full[s], 2 * TILE);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_2d(sm.q + c * BLOCK_B * 128, &tmQ, &sm.qdo_full, p.q_col0 + h * D + c * 64, row0 + qt * BLOCK_B);
-          tma_load_2d(sm.dout + c * BLOCK_B * 128, &tmDO, &sm.qdo_full, p.do_col0 + h * D + c * 64,
+          tma_load_2d(sm.q[s] + c * BLOCK_B * 128, &tmQ, &sm.qdo_full[s], p.q_col0 + h * D + c * 64,
+                      row0 + qt * BLOCK_B);
+          tma_load_2d(sm.dout[s] + c * BLOCK_B * 128, &tmDO, &sm.qdo_full[s], p.do_col0 + h * D + c * 64,
                       row0 + qt * BLOCK_B);
         }
       }
       mbar_wait(&sm.kv_full, 0, p.status, kTimeoutOther);
-      mbar_wait(&sm.qdo_full, (n_iter - 1) & 1, p.status, kTimeoutOther);
+      for (int it = max(0, n_iter - 2); it < n_iter; ++it)
+        mbar_wait(&sm.qdo_full[it & 1], (it >> 1) & 1, p.status, kTimeoutOther);
     }
   } else if (warp == 1) {
     if (lane == 0 && n_iter > 0) {
       // ------------------------------------------------ MMA issuer
-      const uint32_t k_b = smem_u32(sm.k), v_b = smem_u32(sm.v), q_b = smem_u32(sm.q), do_b = smem_u32(sm.dout);
-      const uint32_t pt_b = smem_u32(sm.pt), ds_b = smem_u32(sm.dst);
-      bool ok = mbar_wait(&sm.kv_full, 0, p.status, kTimeoutFull);
-      for (int it = 0; ok && it < n_iter; ++it) {
-        const uint32_t ph = it & 1;
-        if (!mbar_wait(&sm.qdo_full, ph, p.status, kTimeoutFull)) break;
-        if (!mbar_wait(&sm.dq_empty, ph ^ 1u, p.status, kTimeoutAccEmpty)) break;
-        tc_fence_after();
-        // S^T = K Q^T
+      const uint32_t k_b = smem_u32(sm.k), v_b = smem_u32(sm.v), ds_b = smem_u32(sm.dst);
+      auto s_mma = [&](int it) {  // S^T = K Q^T
+        const uint32_t q_b = smem_u32(sm.q[it & 1]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BLOCK_B * 128) + (kk & 3) * 32;
@@ -157,9 +171,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       kk > 0 ? 1u : 0u);
         }
         umma_commit(&sm.s_full);
-        if (!mbar_wait(&sm.dp_empty, ph ^ 1u, p.status, kTimeoutAccEmpty)) break;
-        tc_fence_after();
-        // dP^T = V dO^T
+      };
+      auto dp_mma = [&](int it) {  // dP^T = V dO^T
+        const uint32_t do_b = smem_u32(sm.dout[it & 1]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BLOCK_B * 128) + (kk & 3) * 32;
@@ -167,16 +181,31 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       kk > 0 ? 1u : 0u);
         }
         umma_commit(&sm.dp_full);
-        // dV += P^T dO
+      };
+      bool ok = mbar_wait(&sm.kv_full, 0, p.status, kTimeoutFull) &&
+                mbar_wait(&sm.qdo_full[0], 0, p.status, kTimeoutFull);
+      if (ok) {
+        tc_fence_after();
+        s_mma(0);
+        dp_mma(0);
+      }
+      for (int it = 0; ok && it < n_iter; ++it) {
+        const uint32_t ph = it & 1;
+        const bool next = it + 1 < n_iter;
+        const uint32_t q_b = smem_u32(sm.q[it & 1]), do_b = smem_u32(sm.dout[it & 1]);
+        // dV += P^T dO   (P^T in TMEM over the S^T columns, 8 columns per 16 queries)
         if (!mbar_wait(&sm.p_ready, ph, p.status, kTimeoutFull)) break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < BLOCK_B / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (BLOCK_B * 128) + (kk & 3) * 32;
-          umma_f16_ss(tmem + DV_COL, sdesc_sw128(pt_b + a_off, 16, 1024),
-                      sdesc_sw128(do_b + kk * 2048, BLOCK_B * 128, 1024), ID_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BLOCK_B / 16; ++kk)
+          umma_f16_ts(tmem + DV_COL, tmem + S_COL + kk * 8, sdesc_sw128(do_b + kk * 2048, BLOCK_B * 128, 1024),
+                      ID_KV, (it > 0 || kk > 0) ? 1u : 0u);
+        if (next) {  // next scores, in order after the dV MMA that reads P^T from the same columns
+          if (!mbar_wait(&sm.qdo_full[(it + 1) & 1], ((it + 1) >> 1) & 1, p.status, kTimeoutFull)) break;
+          tc_fence_after();
+          s_mma(it + 1);
         }
-        // dK += dS^T Q ; dQp = dS K
+        // dK += dS^T Q ; dQ = dS K (into the consumed dP^T columns)
         if (!mbar_wait(&sm.ds_ready, ph, p.status, kTimeoutFull)) break;
         tc_fence_after();
 #pragma unroll
@@ -186,31 +215,36 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                       sdesc_sw128(q_b + kk * 2048, BLOCK_B * 128, 1024), ID_KV, (it > 0 || kk > 0) ? 1u : 0u);
         }
 #pragma unroll
-        for (int kk = 0; kk < BLOCK_B / 16; ++kk) {
-          umma_f16_ss(tmem + S_COL, sdesc_sw128(ds_b + kk * 2048, BLOCK_B * 128, 1024),
+        for (int kk = 0; kk < BLOCK_B / 16; ++kk)
+          umma_f16_ss(tmem + DP_COL, sdesc_sw128(ds_b + kk * 2048, BLOCK_B * 128, 1024),
                       sdesc_sw128(k_b + kk * 2048, BLOCK_B * 128, 1024), ID_DQ, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(&sm.qdo_empty);
-        umma_commit(&sm.ps_free);
         umma_commit(&sm.dq_full);
+        umma_commit(&sm.qdo_empty[it & 1]);
+        umma_commit(&sm.ds_free);
+        if (next) {
+          if (!mbar_wait(&sm.dq_empty, ph, p.status, kTimeoutAccEmpty)) break;
+          tc_fence_after();
+          dp_mma(it + 1);
+        }
       }
       umma_commit(&sm.done);
       mbar_wait(&sm.done, 0, p.status, kTimeoutOther);
     }
   } else {
-    // ------------------------------------------------ compute threads (warps 2..5)
+    // ------------------------------------------------ compute warps 2..5 (one TMEM lane each)
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // TMEM lane: key row (S/dP phases), query row (dQ phase)
+    const int r = quarter * 32 + lane;  // key row (S/dP phases), query row (dQ phase)
     const int t = threadIdx.x - 64;     // 0..127
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int key = kt * BLOCK_B + r;
+    const float key_scale = (key < p.T) ? 1.0f : 0.0f;  // keys past the end were masked in forward
     bool ok = n_iter > 0;
     for (int it = 0; ok && it < n_iter; ++it) {
       const uint32_t ph = it & 1;
       const int h = g * group + it / per_head;
       const int qt = qt0 + it % per_head;
       const int buf = it & 1;
-      {  // stage this q tile's LSE (log2 domain) and Delta in shared memory
+      {  // this q tile's LSE (log2 domain) and Delta, staged in shared memory
         const int q = qt * BLOCK_B + t;
         const size_t idx = (static_cast<size_t>(b) * p.Hq + h) * p.T + q;
         sm.lse2[buf][t] = (q < p.T) ? p.lse[idx] * 1.4426950408889634f : INFINITY;
@@ -218,81 +252,94 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       }
       mbar_arrive(&sm.stage_bar[buf]);
       if (!mbar_wait_warp(&sm.stage_bar[buf], (it >> 1) & 1, p.status, kTimeoutOther)) { ok = false; break; }
-      // ---- P^T = exp2(S^T * scale_log2 - lse2[q]) (0 for masked / padded queries)
+      // ---- P^T row = 2^(S^T*scale_log2 - lse2[q]) ; causal diagonal: queries < key are 0
       if (!mbar_wait_warp(&sm.s_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
       float pv[BLOCK_B];
-#pragma unroll
-      for (int c = 0; c < BLOCK_B; c += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_addr + S_COL + c, rr);
+      {
+        uint32_t raw[BLOCK_B];
+        tmem_ld32(tmem + lane_addr + S_COL + 0, *reinterpret_cast<uint32_t(*)[32]>(&raw[0]));
+        tmem_ld32(tmem + lane_addr + S_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[32]));
+        tmem_ld32(tmem + lane_addr + S_COL + 64, *reinterpret_cast<uint32_t(*)[32]>(&raw[64]));
+        tmem_ld32(tmem + lane_addr + S_COL + 96, *reinterpret_cast<uint32_t(*)[32]>(&raw[96]));
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pv[c + i] = __uint_as_float(rr[i]);
+        for (int i = 0; i < BLOCK_B; ++i)
+          pv[i] = ex2_mufu(fmaf(__uint_as_float(raw[i]), p.scale_log2, -sm.lse2[buf][i])) * key_scale;
       }
-      const bool diag = p.causal && qt == kt;
-      const bool key_pad = key >= p.T;  // rows past the sequence end were masked in forward
+      if (p.causal && qt == kt) {
 #pragma unroll
-      for (int i = 0; i < BLOCK_B; ++i) {
-        float e = exp2f(pv[i] * p.scale_log2 - sm.lse2[buf][i]);
-        if ((diag && i < r) || key_pad) e = 0.0f;  // causal: query qt*128+i < key kt*128+r
-        pv[i] = e;
+        for (int i = 0; i < BLOCK_B; ++i) pv[i] = (i < r) ? 0.0f : pv[i];
       }
-      if (it > 0 && !mbar_wait_warp(&sm.ps_free, ph ^ 1u, p.status, kTimeoutAccEmpty)) { ok = false; break; }
 #pragma unroll
-      for (int c = 0; c < BLOCK_B; c += 8) {
-        const uint4 v = make_uint4(pack_bf16x2(pv[c], pv[c + 1]), pack_bf16x2(pv[c + 2], pv[c + 3]),
-                                   pack_bf16x2(pv[c + 4], pv[c + 5]), pack_bf16x2(pv[c + 6], pv[c + 7]));
-        *reinterpret_cast<uint4*>(sm.pt + sw128(r, c, BLOCK_B)) = v;
+      for (int c = 0; c < BLOCK_B; c += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(pv[c + 2 * i], pv[c + 2 * i + 1]);
+        tmem_st16(tmem + lane_addr + S_COL + (c >> 1), pk);
       }
-      fence_proxy_async();
+      tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.p_ready);
-      // ---- dS^T = P^T * (dP^T - delta[q]) * scale
+      // ---- dS^T = P^T * (dP^T - delta[q]) * scale  -> shared memory (A of dK, MN-major A of dQ)
       if (!mbar_wait_warp(&sm.dp_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
+      if (it > 0 && !mbar_wait_warp(&sm.ds_free, ph ^ 1u, p.status, kTimeoutAccEmpty)) { ok = false; break; }
       tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < BLOCK_B; c += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_addr + DP_COL + c, rr);
+      {
+        uint32_t bufA[32], bufB[32];
+        tmem_ld32(tmem + lane_addr + DP_COL, bufA);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) pv[c + i] = pv[c + i] * (__uint_as_float(rr[i]) - sm.delta[buf][c + i]) * p.scale;
-      }
-      tc_fence_before();
-      mbar_arrive(&sm.dp_empty);
+        for (int c = 0; c < 4; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? bufB : bufA;
+          uint32_t(&nxt)[32] = (c & 1) ? bufA : bufB;
+          if (c < 3) tmem_ld32(tmem + lane_addr + DP_COL + (c + 1) * 32, nxt);
+          float ds[32];
 #pragma unroll
-      for (int c = 0; c < BLOCK_B; c += 8) {
-        const uint4 v = make_uint4(pack_bf16x2(pv[c], pv[c + 1]), pack_bf16x2(pv[c + 2], pv[c + 3]),
-                                   pack_bf16x2(pv[c + 4], pv[c + 5]), pack_bf16x2(pv[c + 6], pv[c + 7]));
-        *reinterpret_cast<uint4*>(sm.dst + sw128(r, c, BLOCK_B)) = v;
+          for (int i = 0; i < 32; ++i)
+            ds[i] = pv[c * 32 + i] * (__uint_as_float(cur[i]) - sm.delta[buf][c * 32 + i]) * p.scale;
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const uint4 w = make_uint4(pack_bf16x2(ds[8 * u], ds[8 * u + 1]), pack_bf16x2(ds[8 * u + 2], ds[8 * u + 3]),
+                                       pack_bf16x2(ds[8 * u + 4], ds[8 * u + 5]),
+                                       pack_bf16x2(ds[8 * u + 6], ds[8 * u + 7]));
+            *reinterpret_cast<uint4*>(sm.dst + sw128(r, c * 32 + 8 * u, BLOCK_B)) = w;
+          }
+          if (c < 3) tmem_ld_wait();
+        }
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(&sm.ds_ready);
-      // ---- dQ partial (lane = query row) -> fp32 atomics
+      // ---- dQ partial (lane = query row) -> fp32 vector atomics
       if (!mbar_wait_warp(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
       const int q = qt * BLOCK_B + r;
       float* dst = p.dq_acc + static_cast<size_t>(row0 + q) * (p.Hq * D) + static_cast<size_t>(h) * D;
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_addr + S_COL + c, rr);
+      {
+        uint32_t bufA[32], bufB[32];
+        tmem_ld32(tmem + lane_addr + DP_COL, bufA);
         tmem_ld_wait();
-        if (q < p.T) {
 #pragma unroll
-          for (int i = 0; i < 8; ++i)
-            atomicAdd(reinterpret_cast<float4*>(dst + c) + i,
-                      make_float4(__uint_as_float(rr[4 * i]), __uint_as_float(rr[4 * i + 1]),
-                                  __uint_as_float(rr[4 * i + 2]), __uint_as_float(rr[4 * i + 3])));
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? bufB : bufA;
+          uint32_t(&nxt)[32] = (c & 1) ? bufA : bufB;
+          if (c + 1 < D / 32) tmem_ld32(tmem + lane_addr + DP_COL + (c + 1) * 32, nxt);
+          if (q < p.T) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              atomicAdd(reinterpret_cast<float4*>(dst + c * 32) + i,
+                        make_float4(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1]),
+                                    __uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3])));
+          }
+          if (c + 1 < D / 32) tmem_ld_wait();
         }
       }
       tc_fence_before();
       mbar_arrive(&sm.dq_empty);
     }
     // ---- dK, dV (lane = key row) -> bf16
-    if (ok && n_iter > 0 && mbar_wait_warp(&sm.dq_full, (n_iter - 1) & 1, p.status, kTimeoutAccFull)) {
+    if (ok && n_iter > 0 && mbar_wait_warp(&sm.done, 0, p.status, kTimeoutAccFull)) {
       tc_fence_after();
       const bool key_ok = key < p.T;
       __nv_bfloat16* dkrow = p.dk + static_cast<size_t>(row0 + key) * p.ld_dk + p.dk_col0 + static_cast<size_t>(g) * D;
@@ -315,16 +362,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                              pack_bf16x2(__uint_as_float(rr[8 * i + 4]), __uint_as_float(rr[8 * i + 5])),
                              pack_bf16x2(__uint_as_float(rr[8 * i + 6]), __uint_as_float(rr[8 * i + 7])));
           }
-        }
-      }
-    } else if (n_iter == 0) {
-      // No query can see these keys: their gradients are zero.
-      if (key < p.T) {
-        __nv_bfloat16* dkrow = p.dk + static_cast<size_t>(row0 + key) * p.ld_dk + p.dk_col0 + static_cast<size_t>(g) * D;
-        __nv_bfloat16* dvrow = p.dv + static_cast<size_t>(row0 + key) * p.ld_dv + p.dv_col0 + static_cast<size_t>(g) * D;
-        for (int c = 0; c < D; c += 8) {
-          reinterpret_cast<uint4*>(dkrow + c)[0] = make_uint4(0, 0, 0, 0);
-          reinterpret_cast<uint4*>(dvrow + c)[0] = make_uint4(0, 0, 0, 0);
         }
       }
     }
@@ -439,11 +476,11 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   const CUtensorMap tq = attn_head_map(q), tk = attn_head_map(k), tv = attn_head_map(v), tdo = attn_head_map(dout);
   dim3 grid(static_cast<unsigned>((T + BLOCK_B - 1) / BLOCK_B), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
   if (D == 128) {
-    const size_t smem = sizeof(BwdSmem<128>) + 1024;
+    const size_t smem = std::min<size_t>(bwd_smem_bytes<128>() + 1024, size_t(232448));
     TT_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attn_bwd_kernel<128><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, p);
   } else {
-    const size_t smem = sizeof(BwdSmem<64>) + 1024;
+    const size_t smem = std::min<size_t>(bwd_smem_bytes<64>() + 1024, size_t(232448));
     TT_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attn_bwd_kernel<64><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, p);
   }

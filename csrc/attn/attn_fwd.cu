@@ -10,23 +10,33 @@
 // written token-major [tokens, Hq*D] (the c_proj input layout); LSE (natural log)
 // is written [B, Hq, T] for the backward pass.
 //
-// One CTA = one (batch, q head, 128-query tile).  Warp roles (192 threads):
-//   warp 0: TMA producer (Q once; K/V tiles through a 2-deep ring)
-//   warp 1: TMEM owner + MMA issuer: S = Q K^T into a double-buffered TMEM S,
-//           O += P V into TMEM O (P from shared memory)
-//   warps 2-5: softmax, one query row per thread (TMEM lane), online softmax in
-//           fp32 with exp2; O is rescaled in TMEM only when the running row max
-//           grows by more than 2^8 (otherwise the stale max is kept, which is
-//           exact because the final normalisation uses the same reference max).
+// One CTA = one (batch, q head, pair of 128-query tiles).  Warp roles (384 threads):
+//   TMA producer: both Q tiles once; K/V tiles through a 2-deep ring, each
+//           K/V tile serving both query tiles.
+//   MMA issuer: ping-ponging the two query tiles: while one
+//           softmax warpgroup works on its scores the tensor core runs the other
+//           tile's S = Q K^T or O += P V.  P is written back into TMEM over the
+//           consumed S columns (bf16 pairs) and fed to tcgen05.mma as the A operand
+//           straight from TMEM, so it never touches shared memory.
+//   warps 4-7 / 8-11: softmax warpgroup of query tile 0 / 1, one query row per thread
+//           (TMEM lane): the thread's 128 scores come from TMEM in one round trip and
+//           stay in registers for max, exp (ex2.approx, softmax scale folded into one
+//           FMA), row sum and bf16 packing; O is rescaled in TMEM only when the
+//           running row max grows by more than 2^8 (the stale max is exact because the
+//           final normalisation uses the same reference max).
+//   warp 0: TMA producer; warp 1: TMEM owner + MMA issuer; warps 2-3 idle.
 #include "common/host_utils.h"
+#include <cstdlib>
 #include "common/ptx.cuh"
+#include "common/fast_exp2.cuh"
 
 namespace tt {
 namespace attn {
 
 constexpr int BLOCK = 128;
-constexpr int THREADS = 192;
+constexpr int THREADS = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
+constexpr int kDefaultVariant = 0;
 
 struct FwdParams {
   int B, T, Tk, Hq, Hkv;
@@ -38,31 +48,47 @@ struct FwdParams {
   int causal;
   int causal_offset;  // query i attends keys j <= i + causal_offset
   int* status;
+  int handoff;    // 1: the two softmax warpgroups take turns per tile (TT_ATTN_HANDOFF=1; off by default,
+                  //    measured slower: 0.53 vs 0.43 ms at B4 T4096 Hq16 Hkv4 d128 causal)
+  int skip_math;  // diagnostics (TT_ATTN_SKIP_MATH=1): publish an all-zero P, to time the pipeline alone
 };
 
 template <int D>
 struct FwdSmem {
   static constexpr int TILE_BYTES = BLOCK * D * 2;
-  alignas(1024) uint8_t q[TILE_BYTES];
+  alignas(1024) uint8_t q[2][TILE_BYTES];
   alignas(1024) uint8_t k[2][TILE_BYTES];
   alignas(1024) uint8_t v[2][TILE_BYTES];
-  alignas(1024) uint8_t p[BLOCK * BLOCK * 2];
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
-  uint64_t s_full[2], s_empty[2];
-  uint64_t p_full, pv_done, done;
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t turn[2];  // softmax hand-off: turn[x] completes when the other warpgroup finished a tile
+  uint64_t done;
   uint32_t tmem_slot;
 };
 
-// Byte offset of element (row, col) inside a [rows][ncols] K-major bf16 tile stored as
-// (ncols/64) chunks of [rows][128 B] with the 128-byte swizzle (matches TMA SWIZZLE_128B).
-__device__ __forceinline__ uint32_t sw128_offset(int row, int col, int rows) {
-  const int chunk = col >> 6;
-  const int unit = (col & 63) >> 3;
-  return static_cast<uint32_t>(chunk * rows * 128 + row * 128 + ((unit ^ (row & 7)) << 4) + ((col & 7) << 1));
+__device__ __forceinline__ float ex2_ftz(float x) { return ex2_mufu(x); }
+
+// Number of 128-key tiles query tile `qt` must visit.
+__device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int qt) {
+  if (qt * BLOCK >= p.T) return 0;
+  const int n_all = (p.Tk + BLOCK - 1) / BLOCK;
+  if (!p.causal) return n_all;
+  const int last_q = min(qt * BLOCK + BLOCK - 1, p.T - 1) + p.causal_offset;
+  return max(0, min(n_all, last_q / BLOCK + 1));
 }
 
-template <int D>
+// VARIANT selects the softmax arithmetic mix: bit 0 = half of the exponentials on the FMA
+// pipe (exp2_poly), bit 1 = bf16 packing with integer ops instead of the conversion unit.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  // round-to-nearest (ties away from zero) of non-negative finite values, then keep the
+  // high halves: (hi16(hi) << 16) | hi16(lo)
+  const uint32_t a = __float_as_uint(lo) + 0x8000u;
+  const uint32_t b = __float_as_uint(hi) + 0x8000u;
+  return __byte_perm(a, b, 0x7632);
+}
+
+template <int D, int VARIANT>
 __global__ void __launch_bounds__(THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const FwdParams p) {
@@ -70,9 +96,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   constexpr uint32_t TILE_BYTES = FwdSmem<D>::TILE_BYTES;
   constexpr uint32_t IDESC_QK = idesc_bf16_f32(BLOCK, BLOCK, false, false);
   constexpr uint32_t IDESC_PV = idesc_bf16_f32(BLOCK, D, false, true);
-  constexpr uint32_t S_COL[2] = {0, BLOCK};
-  constexpr uint32_t O_COL = 2 * BLOCK;
   constexpr uint32_t TMEM_COLS = 512;
+  // TMEM: S/P of tile x at cols [128x, 128x+128) (P = bf16 pairs in the first 64 cols),
+  //       O of tile x at cols [256 + x*D, 256 + (x+1)*D).
+  auto S_COL = [](int x) { return static_cast<uint32_t>(x * BLOCK); };
+  auto O_COL = [](int x) { return static_cast<uint32_t>(2 * BLOCK + x * D); };
 
   extern __shared__ uint8_t smem_raw[];
   FwdSmem<D>& sm = *reinterpret_cast<FwdSmem<D>*>(align_ptr(smem_raw, 1024));
@@ -80,18 +108,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int n_qt = (p.T + BLOCK - 1) / BLOCK;
-  const int qt = n_qt - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
+  const int n_pairs = (n_qt + 1) / 2;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
   const int h = blockIdx.y;
   const int b = blockIdx.z;
   const int g = h / (p.Hq / p.Hkv);
-  const int q_row0 = b * p.T + qt * BLOCK;
   const int k_row0 = b * p.Tk;
-  const int n_kt_all = (p.Tk + BLOCK - 1) / BLOCK;
-  int n_kt = n_kt_all;
-  if (p.causal) {
-    const int last_q = min(qt * BLOCK + BLOCK - 1, p.T - 1) + p.causal_offset;
-    n_kt = min(n_kt_all, last_q / BLOCK + 1);
-  }
+  int n_x[2];
+  n_x[0] = kv_tiles_for(p, 2 * pair);
+  n_x[1] = kv_tiles_for(p, 2 * pair + 1);
+  const int n_max = max(n_x[0], n_x[1]);
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmQ);
@@ -104,10 +130,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_init(&sm.v_full[i], 1);
       mbar_init(&sm.v_empty[i], 1);
       mbar_init(&sm.s_full[i], 1);
-      mbar_init(&sm.s_empty[i], 128);
+      mbar_init(&sm.p_full[i], 128);
+      mbar_init(&sm.o_done[i], 1);
+      mbar_init(&sm.turn[i], 128);
     }
-    mbar_init(&sm.p_full, 128);
-    mbar_init(&sm.pv_done, 1);
     mbar_init(&sm.done, 1);
     fence_barrier_init();
   }
@@ -121,181 +147,266 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = sm.tmem_slot;
 
   if (warp == 0) {
-    if (lane == 0 && n_kt > 0) {
-      // ------------------------------------------------ producer
-      mbar_arrive_expect_tx(&sm.q_full, TILE_BYTES);
+    if (lane == 0 && n_max > 0) {
+      // ------------------------------------------------ TMA producer
+      mbar_arrive_expect_tx(&sm.q_full, 2 * TILE_BYTES);
 #pragma unroll
-      for (int c = 0; c < D / 64; ++c)
-        tma_load_2d(sm.q + c * BLOCK * 128, &tmQ, &sm.q_full, p.q_col0 + h * D + c * 64, q_row0);
-      for (int j = 0; j < n_kt; ++j) {
+      for (int x = 0; x < 2; ++x)
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+          tma_load_2d(sm.q[x] + c * BLOCK * 128, &tmQ, &sm.q_full, p.q_col0 + h * D + c * 64,
+                      b * p.T + (2 * pair + x) * BLOCK);
+      for (int j = 0; j < n_max; ++j) {
         const int s = j & 1;
         const uint32_t ph = (j >> 1) & 1;
         if (!mbar_wait(&sm.k_empty[s], ph ^ 1u, p.status, kTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&sm.k_full[s], TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(sm.k[s] + c * BLOCK * 128, &tmK, &sm.k_full[s], p.k_col0 + g * D + c * 64,
-                      k_row0 + j * BLOCK);
+          tma_load_2d(sm.k[s] + c * BLOCK * 128, &tmK, &sm.k_full[s], p.k_col0 + g * D + c * 64, k_row0 + j * BLOCK);
         if (!mbar_wait(&sm.v_empty[s], ph ^ 1u, p.status, kTimeoutEmpty)) break;
         mbar_arrive_expect_tx(&sm.v_full[s], TILE_BYTES);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
-          tma_load_2d(sm.v[s] + c * BLOCK * 128, &tmV, &sm.v_full[s], p.v_col0 + g * D + c * 64,
-                      k_row0 + j * BLOCK);
+          tma_load_2d(sm.v[s] + c * BLOCK * 128, &tmV, &sm.v_full[s], p.v_col0 + g * D + c * 64, k_row0 + j * BLOCK);
       }
-      // Let every issued copy land before the CTA can exit.
       mbar_wait(&sm.q_full, 0, p.status, kTimeoutOther);
-      for (int j = max(0, n_kt - 2); j < n_kt; ++j) {
+      for (int j = max(0, n_max - 2); j < n_max; ++j) {
         mbar_wait(&sm.k_full[j & 1], (j >> 1) & 1, p.status, kTimeoutOther);
         mbar_wait(&sm.v_full[j & 1], (j >> 1) & 1, p.status, kTimeoutOther);
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && n_kt > 0) {
-      // ------------------------------------------------ MMA issuer
-      const uint32_t q_base = smem_u32(sm.q);
-      const uint32_t p_base = smem_u32(sm.p);
-      bool ok = mbar_wait(&sm.q_full, 0, p.status, kTimeoutFull);
-      auto issue_qk = [&](int j) -> bool {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!mbar_wait(&sm.s_empty[s], ph ^ 1u, p.status, kTimeoutAccEmpty)) return false;
-        if (!mbar_wait(&sm.k_full[s], ph, p.status, kTimeoutFull)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(sm.k[s]);
+    if (lane == 0 && n_max > 0) {
+      // ------------------------------------------------ MMA issuer (ping-pong over the two q tiles)
+      auto qk = [&](int x, int j) {
+        const uint32_t q_base = smem_u32(sm.q[x]);
+        const uint32_t k_base = smem_u32(sm.k[j & 1]);
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (kk >> 2) * (BLOCK * 128) + (kk & 3) * 32;
-          umma_f16_ss(tmem + S_COL[s], sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024),
+          umma_f16_ss(tmem + S_COL(x), sdesc_sw128(q_base + off, 16, 1024), sdesc_sw128(k_base + off, 16, 1024),
                       IDESC_QK, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&sm.k_empty[s]);
-        umma_commit(&sm.s_full[s]);
-        return true;
+        umma_commit(&sm.s_full[x]);
       };
-      if (ok) ok = issue_qk(0);
-      for (int j = 0; ok && j < n_kt; ++j) {
-        if (j + 1 < n_kt && !issue_qk(j + 1)) break;
-        const int s = j & 1;
-        if (!mbar_wait(&sm.p_full, j & 1, p.status, kTimeoutFull)) break;
-        if (!mbar_wait(&sm.v_full[s], (j >> 1) & 1, p.status, kTimeoutFull)) break;
-        tc_fence_after();
-        const uint32_t v_base = smem_u32(sm.v[s]);
+      auto pv = [&](int x, int j) {
+        const uint32_t v_base = smem_u32(sm.v[j & 1]);
 #pragma unroll
-        for (int kk = 0; kk < BLOCK / 16; ++kk) {
-          const uint32_t a_off = (kk >> 2) * (BLOCK * 128) + (kk & 3) * 32;
-          const uint32_t b_off = kk * 16 * 128;
-          umma_f16_ss(tmem + O_COL, sdesc_sw128(p_base + a_off, 16, 1024),
-                      sdesc_sw128(v_base + b_off, BLOCK * 128, 1024), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < BLOCK / 16; ++kk)  // P (A operand) read from TMEM: 8 columns per 16 keys
+          umma_f16_ts(tmem + O_COL(x), tmem + S_COL(x) + kk * 8, sdesc_sw128(v_base + kk * 2048, BLOCK * 128, 1024),
+                      IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&sm.o_done[x]);
+      };
+      bool ok = mbar_wait(&sm.q_full, 0, p.status, kTimeoutFull) &&
+                mbar_wait(&sm.k_full[0], 0, p.status, kTimeoutFull);
+      if (ok) {
+        tc_fence_after();
+        for (int x = 0; x < 2; ++x)
+          if (n_x[x] > 0) qk(x, 0);
+        umma_commit(&sm.k_empty[0]);
+      }
+      for (int j = 0; ok && j < n_max; ++j) {
+        const bool next = j + 1 < n_max;
+        if (!mbar_wait(&sm.v_full[j & 1], (j >> 1) & 1, p.status, kTimeoutFull)) break;
+        if (next && !mbar_wait(&sm.k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.status, kTimeoutFull)) break;
+        tc_fence_after();
+        for (int x = 0; x < 2; ++x) {
+          if (j < n_x[x]) {
+            if (!mbar_wait(&sm.p_full[x], j & 1, p.status, kTimeoutFull)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            pv(x, j);
+          }
+          if (j + 1 < n_x[x]) qk(x, j + 1);  // in-order after PV(x, j), which read P from these columns
         }
-        umma_commit(&sm.v_empty[s]);
-        umma_commit(&sm.pv_done);
+        if (!ok) break;
+        umma_commit(&sm.v_empty[j & 1]);
+        if (next) umma_commit(&sm.k_empty[(j + 1) & 1]);
       }
       umma_commit(&sm.done);
       mbar_wait(&sm.done, 0, p.status, kTimeoutOther);
     }
-  } else {
-    // ------------------------------------------------ softmax (warps 2..5)
+  } else if (warp >= 4) {
+    // ------------------------------------------------ softmax warpgroups: x = 0 (warps 4-7), 1 (warps 8-11)
+    const int x = (warp - 4) >> 2;
     const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;                 // query row within the tile == TMEM lane
-    const int q_idx = qt * BLOCK + r;                  // query position within the sequence
+    const int r = quarter * 32 + lane;
+    const int qt = 2 * pair + x;
+    const int q_idx = qt * BLOCK + r;
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
-    const int q_lim = q_idx + p.causal_offset;          // last key this row may attend (causal)
-    float m_ref = -INFINITY;
+    const uint32_t s_addr = tmem + lane_addr + S_COL(x);
+    const uint32_t o_addr = tmem + lane_addr + O_COL(x);
+    const int q_lim = q_idx + p.causal_offset;
+    const int n = n_x[x];
+    const float sl2 = p.scale_log2;
+    float m_ref = -INFINITY;  // running max in the scaled log2 domain
     float l = 0.0f;
     bool ok = true;
-    for (int j = 0; j < n_kt; ++j) {
-      const int s = j & 1;
-      if (!mbar_wait_warp(&sm.s_full[s], (j >> 1) & 1, p.status, kTimeoutAccFull)) {
+    const int n_other = n_x[x ^ 1];
+    for (int j = 0; j < n; ++j) {
+      // With hand-off the two warpgroups alternate (A(j), B(j), A(j+1), ...) so one computes exponentials
+      // while the tensor core serves the other, instead of both sharing the MUFU at once.
+      const bool wait_turn = p.handoff && ((x == 0) ? (j >= 1 && j - 1 < n_other) : (j < n_other));
+      const int turn_idx = (x == 0) ? j - 1 : j;
+      if (wait_turn && !mbar_wait_warp(&sm.turn[x], turn_idx & 1, p.status, kTimeoutOther)) {
+        ok = false;
+        break;
+      }
+      if (!mbar_wait_warp(&sm.s_full[x], j & 1, p.status, kTimeoutAccFull)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      float sv[BLOCK];
+      if (p.skip_math) {  // pipeline-only timing: publish an all-zero P
+        uint32_t z[16];
 #pragma unroll
-      for (int c = 0; c < BLOCK; c += 32) {
-        uint32_t rr[32];
-        tmem_ld32(tmem + lane_addr + S_COL[s] + c, rr);
-        tmem_ld_wait();
+        for (int i = 0; i < 16; ++i) z[i] = 0u;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(rr[i]);
+        for (int c = 0; c < 4; ++c) tmem_st16(s_addr + c * 16, z);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&sm.p_full[x]);
+        if (p.handoff && j < n_other) mbar_arrive(&sm.turn[x ^ 1]);
+        l = 1.0f;
+        m_ref = 0.0f;
+        continue;
       }
-      tc_fence_before();
-      mbar_arrive(&sm.s_empty[s]);
-      // mask + scale into log2 domain
       const int key0 = j * BLOCK;
       const bool need_mask = (key0 + BLOCK > p.Tk) || (p.causal && key0 + BLOCK - 1 > q_lim);
-      float mx = -INFINITY;
-#pragma unroll
-      for (int i = 0; i < BLOCK; ++i) {
-        float x = sv[i] * p.scale_log2;
+      // Scores are read in 4 chunks of 32 columns, double-buffered so each chunk's TMEM
+      // load overlaps the previous chunk's math.
+      auto load_chunk = [&](int c, uint32_t (&buf)[32]) { tmem_ld32(s_addr + c * 32, buf); };
+      auto masked = [&](uint32_t raw, int col) -> float {
+        float v = __uint_as_float(raw);
         if (need_mask) {
-          const int key = key0 + i;
-          if (key >= p.Tk || (p.causal && key > q_lim)) x = -INFINITY;
+          const int key = key0 + col;
+          if (key >= p.Tk || (p.causal && key > q_lim)) v = -INFINITY;
         }
-        sv[i] = x;
-        mx = fmaxf(mx, x);
+        return v;
+      };
+      if (m_ref == -INFINITY) {  // first visible tile of this row: establish the reference max
+        float mx = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t buf[32];
+          load_chunk(c, buf);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, masked(buf[i], c * 32 + i));
+        }
+        if (mx != -INFINITY) m_ref = mx * sl2;
       }
+      // Exp pass against the current reference max, P written to TMEM chunk by chunk. If
+      // the tile's max exceeds the reference by more than 2^8, the written P (and the
+      // row sum) are rescaled by 2^(m_old - m_new) afterwards (rare), which equals
+      // recomputing with the new reference (exponents are clamped at 2^126 first).
       float alpha = 1.0f;
       bool rescale = false;
-      if (mx > m_ref + RESCALE_THRESHOLD || (m_ref == -INFINITY && mx != -INFINITY)) {
-        alpha = (m_ref == -INFINITY) ? 0.0f : exp2f(m_ref - mx);
-        rescale = (j > 0);
-        m_ref = mx;
-      }
-      const float mref = (m_ref == -INFINITY) ? 0.0f : m_ref;
-      float rs = 0.0f;
+      const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      {
+        uint32_t bufA[32], bufB[32];
+        load_chunk(0, bufA);
+        tmem_ld_wait();
 #pragma unroll
-      for (int i = 0; i < BLOCK; ++i) {
-        const float e = exp2f(sv[i] - mref);
-        sv[i] = e;
-        rs += e;
+        for (int c = 0; c < 4; ++c) {
+          uint32_t(&cur)[32] = (c & 1) ? bufB : bufA;
+          uint32_t(&nxt)[32] = (c & 1) ? bufA : bufB;
+          if (c < 3) load_chunk(c + 1, nxt);
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(cur[i]);
+          if (need_mask) {  // uniform per tile: only diagonal / tail tiles take this path
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int key = key0 + c * 32 + i;
+              v[i] = (key >= p.Tk || (p.causal && key > q_lim)) ? -INFINITY : v[i];
+            }
+          }
+          // independent chains: 4 partial maxima / sums, exponentials issued back to back
+          float e[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = fminf(fmaf(v[i], sl2, neg_m), 126.0f);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = ((VARIANT & 1) && (i & 1)) ? exp2_poly(e[i]) : ex2_mufu(e[i]);
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            mq[0] = fmaxf(mq[0], v[i]);
+            mq[1] = fmaxf(mq[1], v[i + 1]);
+            mq[2] = fmaxf(mq[2], v[i + 2]);
+            mq[3] = fmaxf(mq[3], v[i + 3]);
+            sq[0] += e[i];
+            sq[1] += e[i + 1];
+            sq[2] += e[i + 2];
+            sq[3] += e[i + 3];
+          }
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            pk[i] = (VARIANT & 2) ? pack_bf16x2_int(e[2 * i], e[2 * i + 1]) : pack_bf16x2(e[2 * i], e[2 * i + 1]);
+          tmem_st16(s_addr + c * 16, pk);
+          if (c < 3) tmem_ld_wait();
+        }
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
+      const float rs0 = sq[0] + sq[1], rs1 = sq[2] + sq[3];
+      float rs = rs0 + rs1;
+      const float mx_s = mx * sl2;
+      float pfix = 1.0f;
+      if (mx_s > m_ref + RESCALE_THRESHOLD) {
+        pfix = ex2_ftz(m_ref - mx_s);
+        alpha = pfix;
+        rescale = j > 0;
+        rs *= pfix;
+        m_ref = mx_s;
+      }
+      if (__any_sync(0xffffffffu, pfix != 1.0f)) {  // rare, warp-collective fix-up of P
+        tmem_st_wait();
+#pragma unroll
+        for (int c = 0; c < BLOCK / 2; c += 16) {
+          uint32_t pv[16];
+          tmem_ld16(s_addr + c, pv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float2 f = unpack_bf16x2(pv[i]);
+            pv[i] = pack_bf16x2(f.x * pfix, f.y * pfix);
+          }
+          tmem_st16(s_addr + c, pv);
+        }
       }
       l = l * alpha + rs;
-      // P buffer and O are free once the previous PV MMA retired.
-      if (j > 0) {
-        if (!mbar_wait_warp(&sm.pv_done, (j - 1) & 1, p.status, kTimeoutAccFull)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-      }
-      // tcgen05.ld/st are warp-collective: if any lane of the warp must rescale its O row,
-      // the whole warp runs the loop (alpha == 1 for rows that did not change).
-      if (__any_sync(0xffffffffu, rescale)) {
+      if (__any_sync(0xffffffffu, rescale)) {  // warp-collective O rescale (alpha = 1 for unchanged rows)
         if (!rescale) alpha = 1.0f;
 #pragma unroll
         for (int c = 0; c < D; c += 16) {
           uint32_t ov[16];
-          tmem_ld16(tmem + lane_addr + O_COL + c, ov);
+          tmem_ld16(o_addr + c, ov);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
-          tmem_st16(tmem + lane_addr + O_COL + c, ov);
+          tmem_st16(o_addr + c, ov);
         }
-        tmem_st_wait();
       }
-      // P row -> shared memory (bf16, K-major, 128B swizzle)
-#pragma unroll
-      for (int c = 0; c < BLOCK; c += 8) {
-        const uint4 v = make_uint4(pack_bf16x2(sv[c], sv[c + 1]), pack_bf16x2(sv[c + 2], sv[c + 3]),
-                                   pack_bf16x2(sv[c + 4], sv[c + 5]), pack_bf16x2(sv[c + 6], sv[c + 7]));
-        *reinterpret_cast<uint4*>(sm.p + sw128_offset(r, c, BLOCK)) = v;
-      }
-      fence_proxy_async();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(&sm.p_full);
+      mbar_arrive(&sm.p_full[x]);
+      if (p.handoff && j < n_other) mbar_arrive(&sm.turn[x ^ 1]);
     }
     // ------------------------------------------------ epilogue: O / l, LSE
-    if (ok && n_kt > 0 && mbar_wait_warp(&sm.pv_done, (n_kt - 1) & 1, p.status, kTimeoutAccFull)) {
+    if (ok && n > 0 && mbar_wait_warp(&sm.o_done[x], (n - 1) & 1, p.status, kTimeoutAccFull)) {
       tc_fence_after();
       const float inv_l = (l > 0.0f) ? 1.0f / l : 0.0f;
       const bool row_ok = q_idx < p.T;
-      __nv_bfloat16* orow = p.o + static_cast<size_t>(q_row0 + r) * p.ld_o + static_cast<size_t>(h) * D;
+      __nv_bfloat16* orow = p.o + static_cast<size_t>(b * p.T + q_idx) * p.ld_o + static_cast<size_t>(h) * D;
 #pragma unroll
       for (int c = 0; c < D; c += 32) {
         uint32_t ov[32];
-        tmem_ld32(tmem + lane_addr + O_COL + c, ov);
+        tmem_ld32(o_addr + c, ov);
         tmem_ld_wait();
         if (row_ok) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
@@ -366,16 +477,29 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t q_col0,
   p.causal = causal ? 1 : 0;
   p.causal_offset = static_cast<int>(causal_offset);
   p.status = device_status_ptr(q.get_device());
+  {
+    static const int handoff = [] { const char* e = std::getenv("TT_ATTN_HANDOFF"); return e ? std::atoi(e) : 0; }();
+    static const int skip = [] { const char* e = std::getenv("TT_ATTN_SKIP_MATH"); return e ? std::atoi(e) : 0; }();
+    p.handoff = handoff;
+    p.skip_math = skip;
+  }
   const CUtensorMap tq = head_map(q), tk = head_map(k), tv = head_map(v);
-  dim3 grid(static_cast<unsigned>((T + BLOCK - 1) / BLOCK), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  dim3 grid(static_cast<unsigned>(((T + BLOCK - 1) / BLOCK + 1) / 2), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  static const int variant = [] { const char* e = std::getenv("TT_ATTN_VARIANT"); return e ? std::atoi(e) : kDefaultVariant; }();
+  auto launch = [&](auto kern, size_t smem) {
+    TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    kern<<<grid, THREADS, smem, cur_stream()>>>(tq, tk, tv, p);
+  };
   if (D == 128) {
     const size_t smem = sizeof(FwdSmem<128>) + 1024;
-    TT_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attn_fwd_kernel<128><<<grid, THREADS, smem, cur_stream()>>>(tq, tk, tv, p);
+    switch (variant) {
+      case 1: launch(attn_fwd_kernel<128, 1>, smem); break;
+      case 2: launch(attn_fwd_kernel<128, 2>, smem); break;
+      case 3: launch(attn_fwd_kernel<128, 3>, smem); break;
+      default: launch(attn_fwd_kernel<128, 0>, smem); break;
+    }
   } else {
-    const size_t smem = sizeof(FwdSmem<64>) + 1024;
-    TT_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attn_fwd_kernel<64><<<grid, THREADS, smem, cur_stream()>>>(tq, tk, tv, p);
+    launch(attn_fwd_kernel<64, 0>, sizeof(FwdSmem<64>) + 1024);
   }
   TT_CUDA_CHECK(cudaGetLastError());
 }

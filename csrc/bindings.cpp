@@ -6,6 +6,23 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
              c10::optional<torch::Tensor> alpha_t, int64_t bn);
 void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10::optional<torch::Tensor> gu_out);
 void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu, double alpha);
+void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2);
+void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, torch::Tensor gu_out,
+                        torch::Tensor grp_off, int64_t n_groups);
+void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
+                         torch::Tensor grp_off, int64_t n_groups);
+void moe_topk_softmax_op(torch::Tensor logits, int64_t k, torch::Tensor w, torch::Tensor sel);
+void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor sel, torch::Tensor dlogits);
+int64_t moe_row_capacity(int64_t P, int64_t E);
+void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair);
+void moe_gather_rows_op(torch::Tensor x, torch::Tensor row_pair, torch::Tensor grp_off, int64_t k, torch::Tensor out);
+void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k,
+                    torch::Tensor out);
+void moe_combine_bwd_op(torch::Tensor dout, torch::Tensor y_rows, torch::Tensor row_pair, torch::Tensor w,
+                        torch::Tensor grp_off, int64_t k, torch::Tensor dy_rows, torch::Tensor dw);
+void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
+                       bool accumulate);
 int64_t status_read(int64_t device);
 void status_clear(int64_t device);
 void add_rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w,
@@ -33,6 +50,7 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
               int64_t Hkv, int64_t D, torch::Tensor dq, int64_t dq_col0, torch::Tensor dk, int64_t dk_col0,
               torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor delta, double scale,
               bool causal);
+void exp2_poly_op(torch::Tensor x, torch::Tensor y);
 }  // namespace tt
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -40,6 +58,23 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tt::gemm_op, "C (+)= alpha * op(A) op(B)^T on tcgen05", py::arg("a"), py::arg("b"), py::arg("c"),
         py::arg("a_mn") = false, py::arg("b_mn") = false, py::arg("accumulate") = false, py::arg("alpha") = 1.0,
         py::arg("alpha_t") = py::none(), py::arg("bn") = 0);
+  m.def("moe_gemm", &tt::moe_gemm_op, "grouped GEMM over expert row segments (bf16 out)", py::arg("a"),
+        py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("b_mn"), py::arg("b_grp_rows"),
+        py::arg("b_split_k") = 0, py::arg("b_off2") = 0);
+  m.def("moe_gemm_swiglu", &tt::moe_gemm_swiglu_op, "grouped gate|up GEMM with SwiGLU epilogue", py::arg("x"),
+        py::arg("w_gu"), py::arg("out"), py::arg("gu_out"), py::arg("grp_off"), py::arg("n_groups"));
+  m.def("moe_gemm_dswiglu", &tt::moe_gemm_dswiglu_op, "grouped down-proj dgrad with SwiGLU backward epilogue",
+        py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("dgu"), py::arg("grp_off"), py::arg("n_groups"));
+  m.def("moe_gemm_wgrad", &tt::moe_gemm_wgrad_op, "per-expert weight gradient over token segments (fp32)",
+        py::arg("a"), py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("accumulate"));
+  m.def("moe_topk_softmax", &tt::moe_topk_softmax_op, "router top-k + softmax over the selected logits");
+  m.def("moe_topk_softmax_bwd", &tt::moe_topk_softmax_bwd_op, "backward of moe_topk_softmax");
+  m.def("moe_row_capacity", &tt::moe_row_capacity, "padded expert-row capacity for P pairs and E experts");
+  m.def("moe_layout", &tt::moe_layout_op, "expert segments (128-row aligned, stable) for the grouped GEMMs");
+  m.def("moe_gather_rows", &tt::moe_gather_rows_op, "x_rows[r] = x[token of row r], zero pad rows");
+  m.def("moe_combine", &tt::moe_combine_op, "out[t] = sum_j w[t,j] y_rows[slot[t,j]]", py::arg("y_rows"),
+        py::arg("slot"), py::arg("w"), py::arg("k"), py::arg("out"));
+  m.def("moe_combine_bwd", &tt::moe_combine_bwd_op, "backward of moe_combine (dy_rows, dw)");
   m.def("gemm_swiglu", &tt::gemm_swiglu_op, "silu(x Wg^T) * (x Wu^T) with fused gate|up weight", py::arg("x"),
         py::arg("w_gu"), py::arg("out"), py::arg("gu_out") = py::none());
   m.def("gemm_dswiglu", &tt::gemm_dswiglu_op, "SwiGLU backward fused into the down-proj dgrad", py::arg("dy"),
@@ -56,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &tt::adamw_step, "fused AdamW over flat fp32 buffers (+ bf16 shadow)");
   m.def("sumsq", &tt::sumsq);
   m.def("clip_coef", &tt::clip_coef);
+  m.def("exp2_poly", &tt::exp2_poly_op, "2^x via the FMA-pipe polynomial (test hook)");
   m.def("attn_fwd", &tt::attn_fwd, "flash attention forward (tcgen05, GQA-native)");
   m.def("attn_bwd", &tt::attn_bwd, "flash attention backward (tcgen05, GQA-native, dQ via fp32 atomics)");
 }

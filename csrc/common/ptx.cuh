@@ -26,10 +26,18 @@ enum StatusCode : int {
   kTimeoutAccEmpty = 4, // MMA warp waited too long for the epilogue
   kTimeoutPeer = 5,     // wait on a peer GPU's flag expired
   kTimeoutOther = 6,
+  kSmemTooSmall = 7,    // dynamic shared memory after 1024-byte alignment is smaller than the layout
+  kBadIndex = 8,        // an index input was out of range (the entry was skipped)
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t dynamic_smem_size() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {

@@ -12,6 +12,7 @@
 //   * Sum of squares / clip coefficient for global-norm clipping (gpt.py:143-163).
 #include "common/host_utils.h"
 #include "common/ptx.cuh"
+#include "common/fast_exp2.cuh"
 
 namespace tt {
 namespace {
@@ -263,7 +264,25 @@ __global__ void clip_coef_kernel(const float* __restrict__ sumsq, float* __restr
   coef_out[0] = fminf(max_norm / (nrm + 1e-6f), 1.0f);
 }
 
+__global__ void exp2_poly_kernel(const float* __restrict__ x, float* __restrict__ y, long long n) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = exp2_poly(x[i]);
+}
+
 }  // namespace
+
+// Elementwise 2^x with the FMA-pipe polynomial used inside the attention kernels (for testing).
+void exp2_poly_op(torch::Tensor x, torch::Tensor y) {
+  TT_CHECK(x.scalar_type() == torch::kFloat32 && y.scalar_type() == torch::kFloat32 && x.is_contiguous() &&
+               y.is_contiguous() && x.numel() == y.numel(),
+           "exp2_poly: fp32 contiguous tensors of equal size");
+  const long long n = x.numel();
+  if (n == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  exp2_poly_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, cur_stream()>>>(x.data_ptr<float>(),
+                                                                                   y.data_ptr<float>(), n);
+  TT_CUDA_CHECK(cudaGetLastError());
+}
 
 void rope_inplace(torch::Tensor qkv, torch::Tensor cos_t, torch::Tensor sin_t, int64_t T, int64_t pos_offset,
                   int64_t n_heads, int64_t head_dim, bool inverse) {

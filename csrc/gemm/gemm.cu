@@ -18,9 +18,17 @@
 // weight halves fused into one 256-wide tile, writes silu(g)*u and optionally
 // g|u for backward), and SwiGLU-backward (dact -> d[g|u]).
 //
+// Grouped mode (MoE experts): the token operand's rows are grouped by expert in
+// segments [grp_off[e], grp_off[e+1]) that start on multiples of 128 (padding rows
+// are zero).  GROUP_M: C_rows = A_rows B_e^T with each 128-row tile's expert found
+// from grp_off (forward and dgrad); GROUP_K: C_e (+)= A_e^T B_e with the reduction
+// running over expert e's token segment only (weight gradients).  grp_off lives on
+// the device, so routing never synchronises with the host.
+//
 // Replaces the reference's nn.Linear/cuBLAS projections
 // (tinytron/model/modules/attn.py:141-145, mlp.py:27-29,45, gpt.py:60,109) and the
-// SiLU*up elementwise op (mlp.py:45).
+// SiLU*up elementwise op (mlp.py:45); grouped mode replaces the expert GEMMs
+// (F.grouped_mm / bmm, mlp.py:157-187).
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
 
@@ -32,6 +40,7 @@ constexpr int BK = 64;
 constexpr int NUM_THREADS = 192;
 
 enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_DSWIGLU = 4 };
+enum Group : int { GROUP_NONE = 0, GROUP_M = 1, GROUP_K = 2 };
 
 struct Params {
   int M, N, K;                 // output rows, output cols, reduction length
@@ -45,6 +54,20 @@ struct Params {
   const float* alpha_ptr;      // optional device scalar multiplied into alpha
   int b_row_offset2;           // SWIGLU: first row of the "up" half inside B
   int* status;                 // device status word for bounded waits
+  // Grouped mode only.
+  const int* grp_off;          // [n_groups + 1] segment starts (multiples of BM), device
+  int n_groups;
+  int b_grp_rows;              // GROUP_M: per-group offset of B rows (K-major) or K coordinate (MN-major)
+  int b_split_kb;              // GROUP_M, MN-major B: k-blocks >= this come from rows b_off2 + ...
+  int b_off2;
+  int c_grp_rows;              // GROUP_K: per-group row offset of C
+};
+
+struct TileInfo {
+  int mb, nb;  // tile coordinates (rows of A / C, columns of C)
+  int grp;     // group (expert) of the tile
+  int kb0;     // first k-block (GROUP_K: start of the group's token segment)
+  int nk;      // number of k-blocks (GROUP_K: 0 for an empty group -> tile skipped)
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -58,6 +81,35 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int in = tile - g * group_tiles;
   mb = first_m + in % gm;
   nb = in / gm;
+}
+
+template <int GROUP>
+__device__ __forceinline__ TileInfo decode_tile(int tile, int num_m, int num_n, int num_k, const Params& p) {
+  TileInfo t;
+  t.grp = 0;
+  t.kb0 = 0;
+  t.nk = num_k;
+  if constexpr (GROUP == GROUP_K) {
+    const int per = num_m * num_n;
+    t.grp = tile / per;
+    tile_coords(tile - t.grp * per, num_m, num_n, t.mb, t.nb);
+    const int r0 = __ldg(p.grp_off + t.grp), r1 = __ldg(p.grp_off + t.grp + 1);
+    t.kb0 = r0 / BK;
+    t.nk = (r1 - r0) / BK;
+  } else {
+    tile_coords(tile, num_m, num_n, t.mb, t.nb);
+    if constexpr (GROUP == GROUP_M) {  // last group starting at or before the tile's first row
+      const int row = t.mb * BM;
+      int lo = 0, hi = p.n_groups - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (__ldg(p.grp_off + mid) <= row) lo = mid;
+        else hi = mid - 1;
+      }
+      t.grp = lo;
+    }
+  }
+  return t;
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
@@ -97,7 +149,7 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&v)[N
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int GROUP>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   constexpr uint32_t A_BYTES = BM * BK * 2;
@@ -107,6 +159,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   static_assert(BN == 128 || BN == 256, "BN must be 128 or 256");
   static_assert(EPI != EPI_SWIGLU || (BN == 256 && !B_MN), "SwiGLU epilogue needs BN=256, K-major B");
+  static_assert(GROUP != GROUP_K || (A_MN && B_MN), "GROUP_K reduces over token rows: both operands MN-major");
+  static_assert(GROUP != GROUP_M || !A_MN, "GROUP_M: A holds the grouped token rows, K-major");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_ptr(smem_raw, 1024);
@@ -121,9 +175,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM;
+  // GROUP_M: the row count is the padded token total, known only on the device.
+  const int M = (GROUP == GROUP_M) ? __ldg(p.grp_off + p.n_groups) : p.M;
+  const int num_m = (M + BM - 1) / BM;
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
-  const int num_tiles = num_m * num_n;
+  const int num_tiles = num_m * num_n * (GROUP == GROUP_K ? p.n_groups : 1);
   const int num_k = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -158,9 +214,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t pending_phase = 0;  // bit s: parity of that load's fill
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
-        int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < num_k; ++kb) {
+        const TileInfo t = decode_tile<GROUP>(tile, num_m, num_n, num_k, p);
+        const int mb = t.mb, nb = t.nb;
+        const int b_rows0 = (GROUP == GROUP_M) ? t.grp * p.b_grp_rows : 0;
+        for (int kb = 0; kb < t.nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
             ok = false;
             break;
@@ -168,22 +225,26 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           mbar_arrive_expect_tx(&full[stage], A_BYTES + B_BYTES);
           uint8_t* a_dst = sA + stage * A_BYTES;
           uint8_t* b_dst = sB + stage * B_BYTES;
+          const int kc = (t.kb0 + kb) * BK;  // k coordinate (token row for GROUP_K)
           if constexpr (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, mb * BM);
+            tma_load_2d(a_dst, &tmA, &full[stage], kc, mb * BM);
           } else {
 #pragma unroll
             for (int c = 0; c < BM / 64; ++c)
-              tma_load_2d(a_dst + c * (BK * 128), &tmA, &full[stage], mb * BM + c * 64, kb * BK);
+              tma_load_2d(a_dst + c * (BK * 128), &tmA, &full[stage], mb * BM + c * 64, kc);
           }
           if constexpr (EPI == EPI_SWIGLU) {
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * (BN / 2));
-            tma_load_2d(b_dst + (BN / 2) * 128, &tmB, &full[stage], kb * BK, p.b_row_offset2 + nb * (BN / 2));
+            tma_load_2d(b_dst, &tmB, &full[stage], kc, b_rows0 + nb * (BN / 2));
+            tma_load_2d(b_dst + (BN / 2) * 128, &tmB, &full[stage], kc, p.b_row_offset2 + b_rows0 + nb * (BN / 2));
           } else if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * BN);
+            tma_load_2d(b_dst, &tmB, &full[stage], kc, b_rows0 + nb * BN);
           } else {
+            int kb_b = kc;
+            if constexpr (GROUP == GROUP_M)
+              kb_b = (kb < p.b_split_kb) ? b_rows0 + kb * BK : p.b_off2 + b_rows0 + (kb - p.b_split_kb) * BK;
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
-              tma_load_2d(b_dst + c * (BK * 128), &tmB, &full[stage], nb * BN + c * 64, kb * BK);
+              tma_load_2d(b_dst + c * (BK * 128), &tmB, &full[stage], nb * BN + c * 64, kb_b);
           }
           pending |= (1u << stage);
           pending_phase = (pending_phase & ~(1u << stage)) | (phase << stage);
@@ -207,10 +268,12 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        const int nk = decode_tile<GROUP>(tile, num_m, num_n, num_k, p).nk;
+        if (nk == 0) continue;  // empty group (GROUP_K): no accumulator used
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1u, p.status, kTimeoutAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kTimeoutFull)) {
             ok = false;
             break;
@@ -252,12 +315,14 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      const TileInfo t = decode_tile<GROUP>(tile, num_m, num_n, num_k, p);
+      if (t.nk == 0) continue;
+      const int nb = t.nb;
       if (!mbar_wait_warp(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
       tc_fence_after();
-      const int row = mb * BM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const int row_local = t.mb * BM + row_in_tile;
+      const bool row_ok = row_local < M;
+      const int row = (GROUP == GROUP_K) ? t.grp * p.c_grp_rows + row_local : row_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
 
       if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_ACC) {
@@ -372,27 +437,29 @@ constexpr size_t smem_bytes() {
   return static_cast<size_t>(STAGES) * (BM * BK * 2 + BN * BK * 2) + 1024 + 256;
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI>
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, int GROUP = GROUP_NONE>
 void launch_cfg(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
   constexpr size_t smem = smem_bytes<BN, STAGES>();
-  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI>;
+  auto kern = gemm_kernel<BN, STAGES, A_MN, B_MN, EPI, GROUP>;
   TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
-  const int num_tiles = ((p.M + BM - 1) / BM) * ((p.N + OUT_BN - 1) / OUT_BN);
-  const int grid = std::max(1, std::min(num_tiles, num_sms(device)));
+  // GROUP_M: p.M is the row capacity (an upper bound of the device-side total).
+  const long num_tiles = static_cast<long>((p.M + BM - 1) / BM) * ((p.N + OUT_BN - 1) / OUT_BN) *
+                         (GROUP == GROUP_K ? p.n_groups : 1);
+  const int grid = static_cast<int>(std::max(1L, std::min(num_tiles, static_cast<long>(num_sms(device)))));
   kern<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int GROUP = GROUP_NONE>
 void launch_bn(int bn, const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
   if constexpr (EPI == EPI_SWIGLU) {
-    launch_cfg<256, 4, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+    launch_cfg<256, 4, A_MN, B_MN, EPI, GROUP>(p, ta, tb, device, st);
   } else {
     if (bn == 256)
-      launch_cfg<256, 4, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+      launch_cfg<256, 4, A_MN, B_MN, EPI, GROUP>(p, ta, tb, device, st);
     else
-      launch_cfg<128, 6, A_MN, B_MN, EPI>(p, ta, tb, device, st);
+      launch_cfg<128, 6, A_MN, B_MN, EPI, GROUP>(p, ta, tb, device, st);
   }
 }
 
@@ -553,6 +620,144 @@ void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, t
   p.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
   p.ld_aux_out = static_cast<int>(dgu.stride(0));
   launch_bn<false, true, EPI_DSWIGLU>(bn, p, ta, tb, device, cur_stream());
+}
+
+// ---------------------------------------------------------------------------- grouped (MoE) GEMMs
+namespace gemm {
+static void check_grp(const torch::Tensor& grp_off, int64_t n_groups, const torch::Tensor& like) {
+  TT_CHECK(grp_off.is_cuda() && grp_off.scalar_type() == torch::kInt32 && grp_off.numel() == n_groups + 1,
+           "grouped gemm: grp_off must be int32 CUDA [n_groups + 1]");
+  TT_CHECK(grp_off.device() == like.device(), "grouped gemm: grp_off on another device");
+  TT_CHECK(n_groups >= 1, "grouped gemm: n_groups >= 1");
+}
+}  // namespace gemm
+
+// C_rows[cap, N] (bf16) = A_rows[cap, K] . B_e^T for the expert e owning each 128-row tile.
+//   b K-major: [n_groups * b_grp_rows, K], expert e's rows start at e * b_grp_rows.
+//   b MN-major: [rows, N] indexed by k; k-blocks < b_split_k/64 at e*b_grp_rows + k, the rest at
+//   b_off2 + e*b_grp_rows + (k - b_split_k) (gate|up weights stored as two stacked tensors).
+void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2) {
+  using namespace gemm;
+  check_cuda_bf16(a, "a");
+  check_cuda_bf16(b, "b");
+  check_cuda_bf16(c, "c");
+  check_grp(grp_off, n_groups, a);
+  const int M = static_cast<int>(a.size(0));
+  const int K = static_cast<int>(a.size(1));
+  const int N = static_cast<int>(c.size(1));
+  TT_CHECK(c.size(0) == M && c.stride(1) == 1 && c.stride(0) % 8 == 0, "moe_gemm: bad output");
+  TT_CHECK(b_mn ? b.size(1) == N : b.size(1) == K, "moe_gemm: B shape");
+  TT_CHECK(b_split_k % BK == 0 && b_grp_rows % (b_mn ? BK : 1) == 0, "moe_gemm: group offsets must be 64-aligned");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  const int bn = choose_bn(M, N, device);
+  const CUtensorMap ta = operand_map(a, false, BM);
+  const CUtensorMap tb = operand_map(b, b_mn, bn);
+  Params p = base_params(M, N, K, c, 1.0, c10::nullopt, device);
+  p.grp_off = grp_off.data_ptr<int>();
+  p.n_groups = static_cast<int>(n_groups);
+  p.b_grp_rows = static_cast<int>(b_grp_rows);
+  p.b_split_kb = b_split_k > 0 ? static_cast<int>(b_split_k / BK) : (1 << 30);
+  p.b_off2 = static_cast<int>(b_off2);
+  if (b_mn)
+    launch_bn<false, true, EPI_BF16, GROUP_M>(bn, p, ta, tb, device, cur_stream());
+  else
+    launch_bn<false, false, EPI_BF16, GROUP_M>(bn, p, ta, tb, device, cur_stream());
+}
+
+// act[cap, I] = silu(x_e Wg_e^T) * (x_e Wu_e^T) per expert; w_gu = [Wg (n_groups*I rows); Wu (same)].
+void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, torch::Tensor gu_out,
+                        torch::Tensor grp_off, int64_t n_groups) {
+  using namespace gemm;
+  check_cuda_bf16(x, "x");
+  check_cuda_bf16(w_gu, "w_gu");
+  check_cuda_bf16(out, "out");
+  check_cuda_bf16(gu_out, "gu_out");
+  check_grp(grp_off, n_groups, x);
+  const int M = static_cast<int>(x.size(0));
+  const int K = static_cast<int>(x.size(1));
+  const int I = static_cast<int>(out.size(1));
+  TT_CHECK(w_gu.size(0) == 2 * n_groups * I && w_gu.size(1) == K, "moe_swiglu: w_gu must be [2*E*I, K]");
+  TT_CHECK(out.size(0) == M && out.stride(0) % 8 == 0 && gu_out.size(0) == M && gu_out.size(1) == 2 * I &&
+               gu_out.stride(0) % 8 == 0 && I % 8 == 0, "moe_swiglu: bad outputs");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int device = x.get_device();
+  const CUtensorMap ta = operand_map(x, false, BM);
+  const CUtensorMap tb = make_tmap_2d_bf16(w_gu.data_ptr(), static_cast<uint64_t>(K), static_cast<uint64_t>(w_gu.size(0)),
+                                           static_cast<uint64_t>(w_gu.stride(0)) * 2, BK, 128);
+  Params p = base_params(M, I, K, out, 1.0, c10::nullopt, device);
+  p.b_row_offset2 = static_cast<int>(n_groups * I);
+  p.aux_out = reinterpret_cast<__nv_bfloat16*>(gu_out.data_ptr());
+  p.ld_aux_out = static_cast<int>(gu_out.stride(0));
+  p.grp_off = grp_off.data_ptr<int>();
+  p.n_groups = static_cast<int>(n_groups);
+  p.b_grp_rows = I;
+  launch_bn<false, false, EPI_SWIGLU, GROUP_M>(256, p, ta, tb, device, cur_stream());
+}
+
+// d(g|u)[cap, 2I] from dy_rows[cap, D], w_down [n_groups*D, I] and the saved g|u.
+void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
+                         torch::Tensor grp_off, int64_t n_groups) {
+  using namespace gemm;
+  check_cuda_bf16(dy, "dy");
+  check_cuda_bf16(w_down, "w_down");
+  check_cuda_bf16(gu, "gu");
+  check_cuda_bf16(dgu, "dgu");
+  check_grp(grp_off, n_groups, dy);
+  const int M = static_cast<int>(dy.size(0));
+  const int D = static_cast<int>(dy.size(1));
+  const int I = static_cast<int>(w_down.size(1));
+  TT_CHECK(w_down.size(0) == n_groups * D && D % BK == 0, "moe_dswiglu: w_down must be [E*D, I], D % 64 == 0");
+  TT_CHECK(gu.size(0) == M && gu.size(1) == 2 * I && dgu.size(0) == M && dgu.size(1) == 2 * I && I % 64 == 0,
+           "moe_dswiglu: bad shapes");
+  if (M == 0) return;
+  const c10::cuda::CUDAGuard guard(dy.device());
+  const int device = dy.get_device();
+  const int bn = choose_bn(M, I, device);
+  const CUtensorMap ta = operand_map(dy, false, BM);
+  const CUtensorMap tb = operand_map(w_down, true, bn);
+  Params p = base_params(M, I, D, dgu, 1.0, c10::nullopt, device);
+  p.C = nullptr;
+  p.aux = reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr());
+  p.ld_aux = static_cast<int>(gu.stride(0));
+  p.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
+  p.ld_aux_out = static_cast<int>(dgu.stride(0));
+  p.grp_off = grp_off.data_ptr<int>();
+  p.n_groups = static_cast<int>(n_groups);
+  p.b_grp_rows = D;
+  p.b_split_kb = 1 << 30;
+  launch_bn<false, true, EPI_DSWIGLU, GROUP_M>(bn, p, ta, tb, device, cur_stream());
+}
+
+// Per-expert weight gradient: C[e*M:(e+1)*M, N] (+)= A_e^T B_e with A [cap, M], B [cap, N]
+// (token rows; the reduction covers expert e's segment only).  C is fp32.
+void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
+                       bool accumulate) {
+  using namespace gemm;
+  check_cuda_bf16(a, "a");
+  check_cuda_bf16(b, "b");
+  check_grp(grp_off, n_groups, a);
+  const int M = static_cast<int>(a.size(1));
+  const int N = static_cast<int>(b.size(1));
+  const int K = static_cast<int>(a.size(0));
+  TT_CHECK(b.size(0) == K, "moe_wgrad: token rows differ");
+  TT_CHECK(c.scalar_type() == torch::kFloat32 && c.size(0) == n_groups * M && c.size(1) == N && c.stride(1) == 1 &&
+               c.stride(0) % 4 == 0, "moe_wgrad: C must be fp32 [E*M, N]");
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  if (!accumulate) c.zero_();  // empty experts' tiles are skipped
+  if (K == 0) return;
+  const int bn = choose_bn(M, N, device);
+  const CUtensorMap ta = operand_map(a, true, BM);
+  const CUtensorMap tb = operand_map(b, true, bn);
+  Params p = base_params(M, N, K, c, 1.0, c10::nullopt, device);
+  p.grp_off = grp_off.data_ptr<int>();
+  p.n_groups = static_cast<int>(n_groups);
+  p.c_grp_rows = M;
+  launch_bn<true, true, EPI_F32_ACC, GROUP_K>(bn, p, ta, tb, device, cur_stream());
 }
 
 }  // namespace tt

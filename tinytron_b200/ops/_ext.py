@@ -25,6 +25,7 @@ SOURCES = [
     "fused/elementwise.cu",
     "attn/attn_fwd.cu",
     "attn/attn_bwd.cu",
+    "moe/moe.cu",
 ]
 
 CUDA_FLAGS = [

@@ -91,14 +91,94 @@ def bench_gemm(shapes=None):
     return rows
 
 
+def bench_attention(B=4, T=4096, Hq=16, Hkv=4, d=128, iters=10):
+    """Causal GQA flash attention fwd/bwd (packed qkv) vs torch SDPA (expanded kv, as the reference)."""
+    import math
+
+    import torch.nn.functional as F
+
+    from tinytron_b200.ops import _ext
+
+    C = _ext.load()
+    W = (Hq + 2 * Hkv) * d
+    qkv = torch.randn(B * T, W, device="cuda").bfloat16()
+    o = torch.empty(B * T, Hq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device="cuda")
+    sc = 1 / math.sqrt(d)
+    fwd = lambda: C.attn_fwd(qkv, qkv, qkv, 0, Hq * d, (Hq + Hkv) * d, B, T, T, Hq, Hkv, d, o, lse, sc, True, 0)
+    t_fwd = time_fn(fwd, iters=iters)
+    do = torch.randn_like(o)
+    dqkv = torch.empty_like(qkv)
+    dq_acc = torch.empty(B * T, Hq * d, device="cuda")
+    delta = torch.empty(B, Hq, T, device="cuda")
+    bwd = lambda: C.attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d, dqkv, 0, dqkv,
+                             Hq * d, dqkv, (Hq + Hkv) * d, dq_acc, delta, sc, True)
+    t_bwd = time_fn(bwd, iters=iters)
+    x = qkv.view(B, T, Hq + 2 * Hkv, d).transpose(1, 2)
+    q = x[:, :Hq].contiguous().requires_grad_(True)
+    k = x[:, Hq:Hq + Hkv].repeat_interleave(Hq // Hkv, 1).contiguous().requires_grad_(True)
+    v = x[:, Hq + Hkv:].repeat_interleave(Hq // Hkv, 1).contiguous().requires_grad_(True)
+    ref_f = lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    t_ref_f = time_fn(lambda: ref_f(), iters=iters)
+    out = ref_f()
+    g = torch.randn_like(out)
+    t_ref_b = time_fn(lambda: torch.autograd.grad(out, (q, k, v), g, retain_graph=True), iters=iters)
+    flops = 4.0 * B * Hq * T * T * d / 2
+    res = dict(shape=f"B{B} T{T} Hq{Hq} Hkv{Hkv} d{d} causal", fwd_ms=round(t_fwd, 4), bwd_ms=round(t_bwd, 4),
+               sdpa_fwd_ms=round(t_ref_f, 4), sdpa_bwd_ms=round(t_ref_b, 4),
+               fwd_tflops=round(flops / t_fwd / 1e9, 1), bwd_tflops=round(2.5 * flops / t_bwd / 1e9, 1),
+               sdpa_fwd_tflops=round(flops / t_ref_f / 1e9, 1), sdpa_bwd_tflops=round(2.5 * flops / t_ref_b / 1e9, 1))
+    return [res]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "all"])
+    ap.add_argument("what", choices=["gemm", "attn", "attn_fwd_once", "attn_bwd_once", "all"])
     ap.add_argument("--json", action="store_true")
     args = ap.parse_args()
     out = {}
+    if args.what == "attn_fwd_once":  # small fixed case for profiler captures
+        import math
+
+        from tinytron_b200.ops import _ext
+
+        C = _ext.load()
+        B, T, Hq, Hkv, d = 1, 4096, 16, 4, 128
+        qkv = torch.randn(B * T, (Hq + 2 * Hkv) * d, device="cuda").bfloat16()
+        o = torch.empty(B * T, Hq * d, device="cuda", dtype=torch.bfloat16)
+        lse = torch.empty(B, Hq, T, device="cuda")
+        for _ in range(2):
+            C.attn_fwd(qkv, qkv, qkv, 0, Hq * d, (Hq + Hkv) * d, B, T, T, Hq, Hkv, d, o, lse, 1 / math.sqrt(d), True, 0)
+        torch.cuda.synchronize()
+        print("ok")
+        return
+    if args.what == "attn_bwd_once":  # small fixed case for profiler captures: 1 fwd + 2 bwd launches
+        import math
+
+        from tinytron_b200.ops import _ext
+
+        C = _ext.load()
+        B, T, Hq, Hkv, d = 1, 4096, 16, 4, 128
+        W = (Hq + 2 * Hkv) * d
+        qkv = torch.randn(B * T, W, device="cuda").bfloat16()
+        o = torch.empty(B * T, Hq * d, device="cuda", dtype=torch.bfloat16)
+        lse = torch.empty(B, Hq, T, device="cuda")
+        sc = 1 / math.sqrt(d)
+        C.attn_fwd(qkv, qkv, qkv, 0, Hq * d, (Hq + Hkv) * d, B, T, T, Hq, Hkv, d, o, lse, sc, True, 0)
+        do = torch.randn_like(o)
+        dqkv = torch.empty_like(qkv)
+        dq_acc = torch.empty(B * T, Hq * d, device="cuda")
+        delta = torch.empty(B, Hq, T, device="cuda")
+        for _ in range(2):
+            C.attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d, dqkv, 0, dqkv, Hq * d,
+                       dqkv, (Hq + Hkv) * d, dq_acc, delta, sc, True)
+        torch.cuda.synchronize()
+        print("ok")
+        return
     if args.what in ("gemm", "all"):
         out["gemm"] = bench_gemm()
+    if args.what in ("attn", "all"):
+        out["attn"] = bench_attention()
     if args.json:
         print(json.dumps(out))
     else:

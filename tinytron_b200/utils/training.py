@@ -41,3 +41,7 @@ def set_seed(seed: int, deterministic: bool = False) -> None:
     torch.cuda.manual_seed_all(seed)
     if deterministic:
         torch.use_deterministic_algorithms(True, warn_only=True)
+        # Deterministic mode would also fill every torch.empty() with NaN (a full write of
+        # each allocation, ~2 GB per step here).  No kernel of this framework reads memory it
+        # has not written, so the fill only costs bandwidth.
+        torch.utils.deterministic.fill_uninitialized_memory = False
