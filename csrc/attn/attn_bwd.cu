@@ -22,18 +22,19 @@ namespace tt {
 namespace attn {
 
 constexpr int BLOCK_B = 128;
-constexpr int BWD_THREADS = 192;
+constexpr int BWD_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 two compute warpgroups
 
 struct BwdParams {
   int B, T, Hq, Hkv;
   int q_col0, k_col0, v_col0, do_col0;
-  const float* lse;    // [B, Hq, T] natural log
-  const float* delta;  // [B, Hq, T]  rowsum(dO * O)
-  float* dq_acc;       // [B*T, Hq*D] fp32
-  __nv_bfloat16* dk;   // token-major, kv head g at dk_col0 + g*D
+  const float* lse2_pad;   // [B*Hq, T_pad]  lse * log2(e), +inf past T
+  const float* delta_pad;  // [B*Hq, T_pad]  rowsum(dO * O), 0 past T
+  int T_pad;
+  float* dq_acc;           // [B*T, Hq*D] fp32
+  __nv_bfloat16* dk;       // token-major, kv head g at dk_col0 + g*D
   __nv_bfloat16* dv;
   int ld_dk, ld_dv, dk_col0, dv_col0;
-  float scale;         // softmax scale
+  float scale;             // softmax scale
   float scale_log2;
   int causal;
   int* status;
@@ -47,10 +48,9 @@ struct BwdSmem {
   alignas(1024) uint8_t q[2][TILE];
   alignas(1024) uint8_t dout[2][TILE];
   alignas(1024) uint8_t dst[BLOCK_B * BLOCK_B * 2];  // dS^T [keys][queries], 128B-swizzled
-  float lse2[2][BLOCK_B];
+  float lse2[2][BLOCK_B];                             // staged with Q/dO by the producer
   float delta[2][BLOCK_B];
-  uint64_t kv_full, qdo_full[2], qdo_empty[2], s_full, p_ready, dp_full, ds_ready, ds_free, dq_full, dq_empty, done,
-      stage_bar[2];
+  uint64_t kv_full, qdo_full[2], qdo_empty[2], s_full, p_ready, dp_full, ds_ready, dq_full, dq_empty, done;
   uint32_t tmem_slot;
 };
 // Bytes the layout actually uses (sizeof rounds up to the 1 KB member alignment).
@@ -65,10 +65,13 @@ __device__ __forceinline__ uint32_t sw128(int row, int col, int rows) {
   return static_cast<uint32_t>(chunk * rows * 128 + row * 128 + ((unit ^ (row & 7)) << 4) + ((col & 7) << 1));
 }
 
-// Iteration pipeline (it = (q head in group, q tile)), MMAs issued in this order by one thread:
-//   S^T(0), dP^T(0); per it: dV += P^T(it) dO [P^T from TMEM] ; S^T(it+1) ;
-//   dK += dS^T Q, dQ = dS K [into the dP^T columns] ; dP^T(it+1)
-// so the next scores are computed while the compute warps form dS(it).
+// One CTA per (key tile, kv head, batch); it = (q head in the group, q tile).
+// MMA order (one thread):  S^T(0), dP^T(0); per it:
+//   [p_ready(it)] dV += P^T(it) dO ; [next] S^T(it+1) ;
+//   [ds_ready(it)] dK += dS^T Q ; dQ = dS K (into the dP^T columns) ; [dq_empty(it), next] dP^T(it+1)
+// Compute warpgroups (each owns half of the query columns, then half of the head dim):
+//   P(0); per it: dS(it) -> ds_ready ; P(it+1) -> p_ready ; dQ(it) atomics -> dq_empty
+// so the exponentials of the next tile run while the tensor core computes dK and dQ.
 template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -80,6 +83,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   constexpr uint32_t ID_DQ = idesc_bf16_f32(BLOCK_B, D, true, true);          // dQ
   constexpr uint32_t S_COL = 0, DP_COL = BLOCK_B, DV_COL = 2 * BLOCK_B, DK_COL = 2 * BLOCK_B + D;
   constexpr uint32_t TMEM_COLS = 512;
+  constexpr int QH = BLOCK_B / 2;  // query columns per compute warpgroup
+  constexpr int DH = D / 2;        // head-dim columns per compute warpgroup
   static_assert(DK_COL + D <= TMEM_COLS, "TMEM budget");
 
   extern __shared__ uint8_t smem_raw[];
@@ -110,15 +115,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sm.qdo_full[i], 1);
       mbar_init(&sm.qdo_empty[i], 1);
-      mbar_init(&sm.stage_bar[i], 128);
     }
     mbar_init(&sm.s_full, 1);
-    mbar_init(&sm.p_ready, 128);
+    mbar_init(&sm.p_ready, 256);
     mbar_init(&sm.dp_full, 1);
-    mbar_init(&sm.ds_ready, 128);
-    mbar_init(&sm.ds_free, 1);
+    mbar_init(&sm.ds_ready, 256);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_empty, 128);
+    mbar_init(&sm.dq_empty, 256);
     mbar_init(&sm.done, 1);
     fence_barrier_init();
   }
@@ -133,7 +136,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0 && n_iter > 0) {
-      // ------------------------------------------------ producer (Q/dO double-buffered)
+      // ------------------------------------------------ producer (Q/dO/LSE/Delta double-buffered)
       mbar_arrive_expect_tx(&sm.kv_full, 2 * TILE);
 #pragma unroll
       for (int c = 0; c < D / 64; ++c) {
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const int h = g * group + it / per_head;
         const int qt = qt0 + it % per_head;
         if (!mbar_wait(&sm.qdo_empty[s], ((it >> 1) & 1) ^ 1u, p.status, kTimeoutEmpty)) break;
-        mbar_arrive_expect_tx(&sm.qdo_full[s], 2 * TILE);
+        mbar_arrive_expect_tx(&sm.qdo_full[s], 2 * TILE + 2 * BLOCK_B * 4);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
           tma_load_2d(sm.q[s] + c * BLOCK_B * 128, &tmQ, &sm.qdo_full[s], p.q_col0 + h * D + c * 64,
@@ -153,6 +156,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           tma_load_2d(sm.dout[s] + c * BLOCK_B * 128, &tmDO, &sm.qdo_full[s], p.do_col0 + h * D + c * 64,
                       row0 + qt * BLOCK_B);
         }
+        const size_t vo = (static_cast<size_t>(b) * p.Hq + h) * p.T_pad + static_cast<size_t>(qt) * BLOCK_B;
+        bulk_load_1d(sm.lse2[s], p.lse2_pad + vo, BLOCK_B * 4, &sm.qdo_full[s]);
+        bulk_load_1d(sm.delta[s], p.delta_pad + vo, BLOCK_B * 4, &sm.qdo_full[s]);
       }
       mbar_wait(&sm.kv_full, 0, p.status, kTimeoutOther);
       for (int it = max(0, n_iter - 2); it < n_iter; ++it)
@@ -218,9 +224,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         for (int kk = 0; kk < BLOCK_B / 16; ++kk)
           umma_f16_ss(tmem + DP_COL, sdesc_sw128(ds_b + kk * 2048, BLOCK_B * 128, 1024),
                       sdesc_sw128(k_b + kk * 2048, BLOCK_B * 128, 1024), ID_DQ, kk > 0 ? 1u : 0u);
-        umma_commit(&sm.dq_full);
+        umma_commit(&sm.dq_full);  // also tells the compute warps that dS^T in smem is consumed
         umma_commit(&sm.qdo_empty[it & 1]);
-        umma_commit(&sm.ds_free);
         if (next) {
           if (!mbar_wait(&sm.dq_empty, ph, p.status, kTimeoutAccEmpty)) break;
           tc_fence_after();
@@ -231,125 +236,134 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_wait(&sm.done, 0, p.status, kTimeoutOther);
     }
   } else {
-    // ------------------------------------------------ compute warps 2..5 (one TMEM lane each)
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // key row (S/dP phases), query row (dQ phase)
-    const int t = threadIdx.x - 64;     // 0..127
+    // ------------------------------------------------ compute warps 2..9
+    const int half = (warp - 2) >> 2;   // warpgroup: query columns [half*64, +64), head dims [half*D/2, +D/2)
+    const int quarter = warp & 3;       // TMEM lane quarter this warp may access
+    const int r = quarter * 32 + lane;  // key row (P / dS phases), query row (dQ phase)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     const int key = kt * BLOCK_B + r;
     const float key_scale = (key < p.T) ? 1.0f : 0.0f;  // keys past the end were masked in forward
-    bool ok = n_iter > 0;
+    float pv[QH];
+    // P^T row (this warpgroup's 64 queries) = 2^(S^T * scale_log2 - lse2[q]); causal diagonal:
+    // queries before the key are 0.  Written back into TMEM as bf16 pairs over S^T.
+    auto p_phase = [&](int it) -> bool {
+      const int qt = qt0 + it % per_head;
+      const int buf = it & 1;
+      if (!mbar_wait_warp(&sm.s_full, it & 1, p.status, kTimeoutAccFull)) return false;
+      if (!mbar_wait_warp(&sm.qdo_full[buf], (it >> 1) & 1, p.status, kTimeoutFull)) return false;  // lse2 landed
+      tc_fence_after();
+      uint32_t raw[QH];
+      tmem_ld32(tmem + lane_addr + S_COL + half * QH, *reinterpret_cast<uint32_t(*)[32]>(&raw[0]));
+      tmem_ld32(tmem + lane_addr + S_COL + half * QH + 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[32]));
+      tmem_ld_wait();
+      const float* l2 = sm.lse2[buf] + half * QH;
+#pragma unroll
+      for (int i = 0; i < QH; ++i) pv[i] = ex2_mufu(fmaf(__uint_as_float(raw[i]), p.scale_log2, -l2[i])) * key_scale;
+      if (p.causal && qt == kt) {
+#pragma unroll
+        for (int i = 0; i < QH; ++i) pv[i] = (half * QH + i < r) ? 0.0f : pv[i];
+      }
+#pragma unroll
+      for (int c = 0; c < QH; c += 32) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(pv[c + 2 * i], pv[c + 2 * i + 1]);
+        tmem_st16(tmem + lane_addr + S_COL + ((half * QH + c) >> 1), pk);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.p_ready);
+      return true;
+    };
+    bool ok = n_iter > 0 && p_phase(0);
     for (int it = 0; ok && it < n_iter; ++it) {
       const uint32_t ph = it & 1;
       const int h = g * group + it / per_head;
       const int qt = qt0 + it % per_head;
       const int buf = it & 1;
-      {  // this q tile's LSE (log2 domain) and Delta, staged in shared memory
-        const int q = qt * BLOCK_B + t;
-        const size_t idx = (static_cast<size_t>(b) * p.Hq + h) * p.T + q;
-        sm.lse2[buf][t] = (q < p.T) ? p.lse[idx] * 1.4426950408889634f : INFINITY;
-        sm.delta[buf][t] = (q < p.T) ? p.delta[idx] : 0.0f;
-      }
-      mbar_arrive(&sm.stage_bar[buf]);
-      if (!mbar_wait_warp(&sm.stage_bar[buf], (it >> 1) & 1, p.status, kTimeoutOther)) { ok = false; break; }
-      // ---- P^T row = 2^(S^T*scale_log2 - lse2[q]) ; causal diagonal: queries < key are 0
-      if (!mbar_wait_warp(&sm.s_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
-      tc_fence_after();
-      float pv[BLOCK_B];
-      {
-        uint32_t raw[BLOCK_B];
-        tmem_ld32(tmem + lane_addr + S_COL + 0, *reinterpret_cast<uint32_t(*)[32]>(&raw[0]));
-        tmem_ld32(tmem + lane_addr + S_COL + 32, *reinterpret_cast<uint32_t(*)[32]>(&raw[32]));
-        tmem_ld32(tmem + lane_addr + S_COL + 64, *reinterpret_cast<uint32_t(*)[32]>(&raw[64]));
-        tmem_ld32(tmem + lane_addr + S_COL + 96, *reinterpret_cast<uint32_t(*)[32]>(&raw[96]));
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < BLOCK_B; ++i)
-          pv[i] = ex2_mufu(fmaf(__uint_as_float(raw[i]), p.scale_log2, -sm.lse2[buf][i])) * key_scale;
-      }
-      if (p.causal && qt == kt) {
-#pragma unroll
-        for (int i = 0; i < BLOCK_B; ++i) pv[i] = (i < r) ? 0.0f : pv[i];
-      }
-#pragma unroll
-      for (int c = 0; c < BLOCK_B; c += 32) {
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(pv[c + 2 * i], pv[c + 2 * i + 1]);
-        tmem_st16(tmem + lane_addr + S_COL + (c >> 1), pk);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&sm.p_ready);
-      // ---- dS^T = P^T * (dP^T - delta[q]) * scale  -> shared memory (A of dK, MN-major A of dQ)
+      // ---- dS^T = P^T * (dP^T - delta[q]) * scale -> shared memory (A of dK, MN-major A of dQ).
+      // The previous dQ (dq_full, waited below in the previous iteration) retired the MMAs reading dS^T.
       if (!mbar_wait_warp(&sm.dp_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
-      if (it > 0 && !mbar_wait_warp(&sm.ds_free, ph ^ 1u, p.status, kTimeoutAccEmpty)) { ok = false; break; }
       tc_fence_after();
       {
-        uint32_t bufA[32], bufB[32];
-        tmem_ld32(tmem + lane_addr + DP_COL, bufA);
+        uint32_t d0[32], d1[32];
+        tmem_ld32(tmem + lane_addr + DP_COL + half * QH, d0);
+        tmem_ld32(tmem + lane_addr + DP_COL + half * QH + 32, d1);
         tmem_ld_wait();
+        const float* dl = sm.delta[buf] + half * QH;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t(&cur)[32] = (c & 1) ? bufB : bufA;
-          uint32_t(&nxt)[32] = (c & 1) ? bufA : bufB;
-          if (c < 3) tmem_ld32(tmem + lane_addr + DP_COL + (c + 1) * 32, nxt);
-          float ds[32];
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            ds[i] = pv[c * 32 + i] * (__uint_as_float(cur[i]) - sm.delta[buf][c * 32 + i]) * p.scale;
+        for (int c = 0; c < 2; ++c) {
+          const uint32_t(&cur)[32] = c ? d1 : d0;
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
-            const uint4 w = make_uint4(pack_bf16x2(ds[8 * u], ds[8 * u + 1]), pack_bf16x2(ds[8 * u + 2], ds[8 * u + 3]),
-                                       pack_bf16x2(ds[8 * u + 4], ds[8 * u + 5]),
-                                       pack_bf16x2(ds[8 * u + 6], ds[8 * u + 7]));
-            *reinterpret_cast<uint4*>(sm.dst + sw128(r, c * 32 + 8 * u, BLOCK_B)) = w;
+            float ds[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int j = c * 32 + 8 * u + i;
+              ds[i] = pv[j] * (__uint_as_float(cur[8 * u + i]) - dl[j]) * p.scale;
+            }
+            const uint4 w = make_uint4(pack_bf16x2(ds[0], ds[1]), pack_bf16x2(ds[2], ds[3]),
+                                       pack_bf16x2(ds[4], ds[5]), pack_bf16x2(ds[6], ds[7]));
+            *reinterpret_cast<uint4*>(sm.dst + sw128(r, half * QH + c * 32 + 8 * u, BLOCK_B)) = w;
           }
-          if (c < 3) tmem_ld_wait();
         }
       }
       fence_proxy_async();
       tc_fence_before();
       mbar_arrive(&sm.ds_ready);
-      // ---- dQ partial (lane = query row) -> fp32 vector atomics
+      // ---- next tile's probabilities while dK / dQ run on the tensor core
+      if (it + 1 < n_iter && !p_phase(it + 1)) { ok = false; break; }
+      // ---- dQ partial, this warpgroup's head-dim half -> fp32 vector reductions into dq_acc.
+      // TMEM gives one query row per thread; each 32x32 block is transposed through this warp's
+      // own 4 KB slice of the dS^T buffer (the slice it wrote in the dS phase, free again once
+      // dq_full says the MMAs reading it retired) so that every red.v4 instruction covers four
+      // whole 128-byte rows instead of 32 scattered 16-byte pieces.
       if (!mbar_wait_warp(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
-      const int q = qt * BLOCK_B + r;
-      float* dst = p.dq_acc + static_cast<size_t>(row0 + q) * (p.Hq * D) + static_cast<size_t>(h) * D;
       {
-        uint32_t bufA[32], bufB[32];
-        tmem_ld32(tmem + lane_addr + DP_COL, bufA);
-        tmem_ld_wait();
+        uint8_t* stage = sm.dst + half * (BLOCK_B * 128) + quarter * 32 * 128;
+        const int qbase = qt * BLOCK_B + quarter * 32;  // query of this warp's first row
+        float* gbase = p.dq_acc + static_cast<size_t>(row0) * (p.Hq * D) + static_cast<size_t>(h) * D + half * DH;
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t(&cur)[32] = (c & 1) ? bufB : bufA;
-          uint32_t(&nxt)[32] = (c & 1) ? bufA : bufB;
-          if (c + 1 < D / 32) tmem_ld32(tmem + lane_addr + DP_COL + (c + 1) * 32, nxt);
-          if (q < p.T) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              atomicAdd(reinterpret_cast<float4*>(dst + c * 32) + i,
-                        make_float4(__uint_as_float(cur[4 * i]), __uint_as_float(cur[4 * i + 1]),
-                                    __uint_as_float(cur[4 * i + 2]), __uint_as_float(cur[4 * i + 3])));
+        for (int c = 0; c < DH / 32; ++c) {
+          uint32_t cur[32];
+          tmem_ld32(tmem + lane_addr + DP_COL + half * DH + c * 32, cur);
+          tmem_ld_wait();
+          if (c == DH / 32 - 1) {
+            tc_fence_before();
+            mbar_arrive(&sm.dq_empty);  // all values are in registers: the dP^T columns are free again
           }
-          if (c + 1 < D / 32) tmem_ld_wait();
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_uint4(cur[4 * u], cur[4 * u + 1], cur[4 * u + 2], cur[4 * u + 3]);
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int j = i * 4 + (lane >> 3);  // row within the warp's 32
+            const int u = lane & 7;             // 16-byte unit within the 32 columns
+            const float4 v = *reinterpret_cast<const float4*>(stage + j * 128 + ((u ^ (j & 7)) << 4));
+            if (qbase + j < p.T)
+              atomicAdd(reinterpret_cast<float4*>(gbase + static_cast<size_t>(qbase + j) * (p.Hq * D) + c * 32) + u, v);
+          }
+          __syncwarp();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&sm.dq_empty);
     }
-    // ---- dK, dV (lane = key row) -> bf16
+    // ---- dK, dV (lane = key row), this warpgroup's head-dim half -> bf16
     if (ok && n_iter > 0 && mbar_wait_warp(&sm.done, 0, p.status, kTimeoutAccFull)) {
       tc_fence_after();
       const bool key_ok = key < p.T;
-      __nv_bfloat16* dkrow = p.dk + static_cast<size_t>(row0 + key) * p.ld_dk + p.dk_col0 + static_cast<size_t>(g) * D;
-      __nv_bfloat16* dvrow = p.dv + static_cast<size_t>(row0 + key) * p.ld_dv + p.dv_col0 + static_cast<size_t>(g) * D;
+      __nv_bfloat16* dkrow =
+          p.dk + static_cast<size_t>(row0 + key) * p.ld_dk + p.dk_col0 + static_cast<size_t>(g) * D + half * DH;
+      __nv_bfloat16* dvrow =
+          p.dv + static_cast<size_t>(row0 + key) * p.ld_dv + p.dv_col0 + static_cast<size_t>(g) * D + half * DH;
 #pragma unroll
       for (int which = 0; which < 2; ++which) {
-        const uint32_t col = which == 0 ? DK_COL : DV_COL;
+        const uint32_t col = (which == 0 ? DK_COL : DV_COL) + half * DH;
         __nv_bfloat16* out = which == 0 ? dkrow : dvrow;
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
+        for (int c = 0; c < DH; c += 32) {
           uint32_t rr[32];
           tmem_ld32(tmem + lane_addr + col + c, rr);
           tmem_ld_wait();
@@ -373,15 +387,28 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-// delta[b, h, t] = sum_d dO[t, h*D + d] * O[t, h*D + d]; one warp per (token, head).
+// Per (b, h, t < T_pad): delta = sum_d dO[t, h*D + d] * O[t, h*D + d] and lse2 = lse * log2(e);
+// padded positions t >= T get delta 0 and lse2 +inf (their probabilities become 0).
+// One warp per (token slot, head).
 __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, int ld_o, const __nv_bfloat16* __restrict__ dout,
-                                      int ld_do, float* __restrict__ delta, int B, int T, int Hq, int D) {
+                                      int ld_do, const float* __restrict__ lse, float* __restrict__ lse2_pad,
+                                      float* __restrict__ delta_pad, int B, int T, int T_pad, int Hq, int D) {
   const long long wid = (static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
-  const long long total = static_cast<long long>(B) * T * Hq;
+  const long long total = static_cast<long long>(B) * T_pad * Hq;
   if (wid >= total) return;
   const int h = static_cast<int>(wid % Hq);
-  const long long tok = wid / Hq;
+  const long long slot = wid / Hq;
+  const int b = static_cast<int>(slot / T_pad), t = static_cast<int>(slot % T_pad);
+  const size_t out = (static_cast<size_t>(b) * Hq + h) * T_pad + t;
+  if (t >= T) {
+    if (lane == 0) {
+      delta_pad[out] = 0.0f;
+      lse2_pad[out] = INFINITY;
+    }
+    return;
+  }
+  const long long tok = static_cast<long long>(b) * T + t;
   const __nv_bfloat16* a = o + tok * ld_o + static_cast<long long>(h) * D;
   const __nv_bfloat16* c = dout + tok * ld_do + static_cast<long long>(h) * D;
   float s = 0.0f;
@@ -394,8 +421,8 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, int l
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) {
-    const int b = static_cast<int>(tok / T), t = static_cast<int>(tok % T);
-    delta[(static_cast<size_t>(b) * Hq + h) * T + t] = s;
+    delta_pad[out] = s;
+    lse2_pad[out] = lse[(static_cast<size_t>(b) * Hq + h) * T + t] * 1.4426950408889634f;
   }
 }
 
@@ -419,11 +446,11 @@ CUtensorMap attn_head_map(const torch::Tensor& t);
 // Backward of attn_fwd (causal or full, self-attention T == Tk).
 //   q/k/v/o/dout: token-major bf16 buffers with head column offsets; lse [B,Hq,T] (from fwd).
 //   dq/dk/dv: token-major bf16 outputs (may all be the same packed dqkv buffer).
-//   dq_acc: fp32 scratch [B*T, Hq*D]; delta: fp32 scratch [B*Hq*T].
+//   dq_acc: fp32 scratch [B*T, Hq*D]; scratch: fp32, attn_bwd_scratch_numel(B, Hq, T) elements.
 void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
               int64_t q_col0, int64_t k_col0, int64_t v_col0, torch::Tensor lse, int64_t B, int64_t T, int64_t Hq,
               int64_t Hkv, int64_t D, torch::Tensor dq, int64_t dq_col0, torch::Tensor dk, int64_t dk_col0,
-              torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor delta, double scale,
+              torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor scratch, double scale,
               bool causal) {
   using namespace attn;
   for (auto* tp : {&q, &k, &v, &o, &dout, &dq, &dk, &dv}) check_cuda_bf16(*tp, "attn_bwd operand");
@@ -431,7 +458,10 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   TT_CHECK(Hq % Hkv == 0, "Hq must be a multiple of Hkv");
   TT_CHECK(dq_acc.scalar_type() == torch::kFloat32 && dq_acc.is_contiguous() && dq_acc.numel() >= B * T * Hq * D,
            "dq_acc must be fp32 [B*T, Hq*D]");
-  TT_CHECK(delta.scalar_type() == torch::kFloat32 && delta.numel() >= B * Hq * T, "delta must be fp32 [B,Hq,T]");
+  const int64_t T_pad = (T + BLOCK_B - 1) / BLOCK_B * BLOCK_B;
+  TT_CHECK(scratch.scalar_type() == torch::kFloat32 && scratch.is_contiguous() && scratch.numel() >= 2 * B * Hq * T_pad &&
+               reinterpret_cast<uintptr_t>(scratch.data_ptr()) % 16 == 0,
+           "scratch must be fp32 with attn_bwd_scratch_numel(B, Hq, T) elements");
   TT_CHECK(lse.scalar_type() == torch::kFloat32 && lse.numel() >= B * Hq * T, "lse must be fp32");
   TT_CHECK(q_col0 % 64 == 0 && k_col0 % 64 == 0 && v_col0 % 64 == 0, "column offsets must be 64-aligned");
   TT_CHECK(o.stride(1) == 1 && dout.stride(1) == 1 && dout.is_contiguous() == dout.is_contiguous(), "layouts");
@@ -442,12 +472,15 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   const c10::cuda::CUDAGuard guard(q.device());
   cudaStream_t st = cur_stream();
   const long long tokens = B * T;
+  float* lse2_pad = scratch.data_ptr<float>();
+  float* delta_pad = lse2_pad + B * Hq * T_pad;
   {
-    const long long warps = tokens * Hq;
+    const long long warps = B * T_pad * Hq;
     attn_bwd_delta_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), static_cast<int>(o.stride(0)),
-        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), static_cast<int>(dout.stride(0)),
-        delta.data_ptr<float>(), static_cast<int>(B), static_cast<int>(T), static_cast<int>(Hq), static_cast<int>(D));
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), static_cast<int>(dout.stride(0)), lse.data_ptr<float>(),
+        lse2_pad, delta_pad, static_cast<int>(B), static_cast<int>(T), static_cast<int>(T_pad), static_cast<int>(Hq),
+        static_cast<int>(D));
     TT_CUDA_CHECK(cudaGetLastError());
   }
   TT_CUDA_CHECK(cudaMemsetAsync(dq_acc.data_ptr(), 0, static_cast<size_t>(tokens * Hq * D) * sizeof(float), st));
@@ -460,8 +493,9 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   p.k_col0 = static_cast<int>(k_col0);
   p.v_col0 = static_cast<int>(v_col0);
   p.do_col0 = 0;
-  p.lse = lse.data_ptr<float>();
-  p.delta = delta.data_ptr<float>();
+  p.lse2_pad = lse2_pad;
+  p.delta_pad = delta_pad;
+  p.T_pad = static_cast<int>(T_pad);
   p.dq_acc = dq_acc.data_ptr<float>();
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
@@ -491,6 +525,10 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
       dq_acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()), static_cast<int>(dq.stride(0)),
       static_cast<int>(dq_col0), tokens, width);
   TT_CUDA_CHECK(cudaGetLastError());
+}
+
+int64_t attn_bwd_scratch_numel(int64_t B, int64_t Hq, int64_t T) {
+  return 2 * B * Hq * ((T + attn::BLOCK_B - 1) / attn::BLOCK_B * attn::BLOCK_B);
 }
 
 }  // namespace tt

@@ -287,27 +287,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         return v;
       };
-      if (m_ref == -INFINITY) {  // first visible tile of this row: establish the reference max
-        float mx = -INFINITY;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t buf[32];
-          load_chunk(c, buf);
-          tmem_ld_wait();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, masked(buf[i], c * 32 + i));
-        }
-        if (mx != -INFINITY) m_ref = mx * sl2;
-      }
-      // Exp pass against the current reference max, P written to TMEM chunk by chunk. If
-      // the tile's max exceeds the reference by more than 2^8, the written P (and the
-      // row sum) are rescaled by 2^(m_old - m_new) afterwards (rare), which equals
-      // recomputing with the new reference (exponents are clamped at 2^126 first).
-      float alpha = 1.0f;
-      bool rescale = false;
-      const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
-      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      float sq[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      // Exp pass with a lazily raised reference max: each 32-key chunk's max is taken first,
+      // and the reference moves up only when that max exceeds it by more than 2^8, so every
+      // exponential is at most 2^8 and none can overflow, however far a later key's score
+      // jumps.  Chunks computed under an older reference (and the row sum and O) are rescaled
+      // by 2^(m_old - m_new) afterwards; that factor may underflow to 0, which is then exact
+      // in fp32.  Raising is rare after the first chunk of a row.
+      const float m_start = m_ref;
+      float cref[4], csum[4];
       {
         uint32_t bufA[32], bufB[32];
         load_chunk(0, bufA);
@@ -327,23 +314,32 @@ __global__ void __launch_bounds__(THREADS, 1)
               v[i] = (key >= p.Tk || (p.causal && key > q_lim)) ? -INFINITY : v[i];
             }
           }
-          // independent chains: 4 partial maxima / sums, exponentials issued back to back
-          float e[32];
+          float mq[4] = {v[0], v[1], v[2], v[3]};  // independent chains
 #pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = fminf(fmaf(v[i], sl2, neg_m), 126.0f);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = ((VARIANT & 1) && (i & 1)) ? exp2_poly(e[i]) : ex2_mufu(e[i]);
-#pragma unroll
-          for (int i = 0; i < 32; i += 4) {
+          for (int i = 4; i < 32; i += 4) {
             mq[0] = fmaxf(mq[0], v[i]);
             mq[1] = fmaxf(mq[1], v[i + 1]);
             mq[2] = fmaxf(mq[2], v[i + 2]);
             mq[3] = fmaxf(mq[3], v[i + 3]);
+          }
+          const float mcs = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+          if (mcs > m_ref + RESCALE_THRESHOLD) m_ref = mcs;  // also the first visible chunk (m_ref = -inf)
+          const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
+          float e[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = fmaf(v[i], sl2, neg_m);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) e[i] = ((VARIANT & 1) && (i & 1)) ? exp2_poly(e[i]) : ex2_mufu(e[i]);
+          float sq[4] = {e[0], e[1], e[2], e[3]};
+#pragma unroll
+          for (int i = 4; i < 32; i += 4) {
             sq[0] += e[i];
             sq[1] += e[i + 1];
             sq[2] += e[i + 2];
             sq[3] += e[i + 3];
           }
+          csum[c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
+          cref[c] = m_ref;
           uint32_t pk[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -352,36 +348,33 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (c < 3) tmem_ld_wait();
         }
       }
-      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
-      const float rs0 = sq[0] + sq[1], rs1 = sq[2] + sq[3];
-      float rs = rs0 + rs1;
-      const float mx_s = mx * sl2;
-      float pfix = 1.0f;
-      if (mx_s > m_ref + RESCALE_THRESHOLD) {
-        pfix = ex2_ftz(m_ref - mx_s);
-        alpha = pfix;
-        rescale = j > 0;
-        rs *= pfix;
-        m_ref = mx_s;
+      float rs = 0.0f;
+      float cf[4];
+      bool fix = false;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        cf[c] = (cref[c] == m_ref) ? 1.0f : ex2_ftz(cref[c] - m_ref);
+        fix |= cf[c] != 1.0f;
+        rs = fmaf(csum[c], cf[c], rs);
       }
-      if (__any_sync(0xffffffffu, pfix != 1.0f)) {  // rare, warp-collective fix-up of P
+      if (__any_sync(0xffffffffu, fix)) {  // rare, warp-collective fix-up of P chunks (factor 1 elsewhere)
         tmem_st_wait();
 #pragma unroll
-        for (int c = 0; c < BLOCK / 2; c += 16) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t pv[16];
-          tmem_ld16(s_addr + c, pv);
+          tmem_ld16(s_addr + c * 16, pv);
           tmem_ld_wait();
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float2 f = unpack_bf16x2(pv[i]);
-            pv[i] = pack_bf16x2(f.x * pfix, f.y * pfix);
+            pv[i] = pack_bf16x2(f.x * cf[c], f.y * cf[c]);
           }
-          tmem_st16(s_addr + c, pv);
+          tmem_st16(s_addr + c * 16, pv);
         }
       }
+      const float alpha = (m_start == m_ref) ? 1.0f : ex2_ftz(m_start - m_ref);
       l = l * alpha + rs;
-      if (__any_sync(0xffffffffu, rescale)) {  // warp-collective O rescale (alpha = 1 for unchanged rows)
-        if (!rescale) alpha = 1.0f;
+      if (__any_sync(0xffffffffu, j > 0 && alpha != 1.0f)) {  // warp-collective O rescale (alpha = 1 elsewhere)
 #pragma unroll
         for (int c = 0; c < D; c += 16) {
           uint32_t ov[16];

@@ -45,10 +45,11 @@ void clip_coef(torch::Tensor sumsq_t, torch::Tensor norm_out, torch::Tensor coef
 void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t q_col0, int64_t k_col0, int64_t v_col0,
               int64_t B, int64_t T, int64_t Tk, int64_t Hq, int64_t Hkv, int64_t D, torch::Tensor o,
               c10::optional<torch::Tensor> lse, double scale, bool causal, int64_t causal_offset);
+int64_t attn_bwd_scratch_numel(int64_t B, int64_t Hq, int64_t T);
 void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o, torch::Tensor dout,
               int64_t q_col0, int64_t k_col0, int64_t v_col0, torch::Tensor lse, int64_t B, int64_t T, int64_t Hq,
               int64_t Hkv, int64_t D, torch::Tensor dq, int64_t dq_col0, torch::Tensor dk, int64_t dk_col0,
-              torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor delta, double scale,
+              torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor scratch, double scale,
               bool causal);
 void exp2_poly_op(torch::Tensor x, torch::Tensor y);
 }  // namespace tt
@@ -93,5 +94,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_coef", &tt::clip_coef);
   m.def("exp2_poly", &tt::exp2_poly_op, "2^x via the FMA-pipe polynomial (test hook)");
   m.def("attn_fwd", &tt::attn_fwd, "flash attention forward (tcgen05, GQA-native)");
+  m.def("attn_bwd_scratch_numel", &tt::attn_bwd_scratch_numel, "fp32 scratch elements attn_bwd needs");
   m.def("attn_bwd", &tt::attn_bwd, "flash attention backward (tcgen05, GQA-native, dQ via fp32 atomics)");
 }

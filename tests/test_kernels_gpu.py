@@ -190,7 +190,7 @@ def test_attn_bwd_packed_qkv(B, T, Hq, Hkv, d, causal):
     do = torch.randn(B * T, Hq * d, device="cuda", generator=g).bfloat16()
     dqkv = torch.full((B * T, W), float("nan"), device="cuda", dtype=torch.bfloat16)
     dq_acc = torch.empty(B * T, Hq * d, device="cuda")
-    delta = torch.empty(B, Hq, T, device="cuda")
+    delta = torch.empty(ext().attn_bwd_scratch_numel(B, Hq, T), device="cuda")
     ext().attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d,
                    dqkv, 0, dqkv, Hq * d, dqkv, (Hq + Hkv) * d, dq_acc, delta, scale, causal)
     x = qkv.float().view(B, T, Hq + 2 * Hkv, d).transpose(1, 2).detach().requires_grad_(True)
@@ -203,6 +203,40 @@ def test_attn_bwd_packed_qkv(B, T, Hq, Hkv, d, causal):
                      ("dv", slice((Hq + Hkv) * d, W))]:
         err = rel_err(dqkv[:, sl], ref_grad[:, sl])
         assert err < 3e-2, f"{name} rel err {err}"
+    assert ext().status_read(0) == 0
+
+
+def test_attn_large_score_jump_fwd_bwd():
+    """Rows whose last (diagonal) key scores ~200 nats above all earlier keys: the running
+    max must move without any exponential overflowing or the row sum underflowing."""
+    B, T, Hq, Hkv, d = 1, 1024, 2, 1, 128
+    W = (Hq + 2 * Hkv) * d
+    g = torch.Generator(device="cuda").manual_seed(11)
+    qkv = (torch.randn(B * T, W, device="cuda", generator=g) * 0.3)
+    for t in (5, 300, 771, 1023):  # q_t . k_t / sqrt(d) ~ 200 for both q heads
+        qkv[t, :Hq * d] = 4.0
+        qkv[t, Hq * d:(Hq + Hkv) * d] = 4.0
+    qkv = qkv.bfloat16()
+    o = torch.empty(B * T, Hq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device="cuda")
+    scale = 1 / math.sqrt(d)
+    ext().attn_fwd(qkv, qkv, qkv, 0, Hq * d, (Hq + Hkv) * d, B, T, T, Hq, Hkv, d, o, lse, scale, True, 0)
+    x = qkv.float().view(B, T, Hq + 2 * Hkv, d).transpose(1, 2).detach().requires_grad_(True)
+    q, k, v = x[:, :Hq], x[:, Hq:Hq + Hkv], x[:, Hq + Hkv:]
+    ref, ref_lse = _attn_ref(q, k, v, True)
+    assert torch.isfinite(lse).all()
+    assert (lse - ref_lse).abs().max().item() < 2e-2
+    assert rel_err(o.view(B, T, Hq, d).transpose(1, 2), ref) < 2e-2
+    do = torch.randn(B * T, Hq * d, device="cuda", generator=g).bfloat16()
+    dqkv = torch.full((B * T, W), float("nan"), device="cuda", dtype=torch.bfloat16)
+    dq_acc = torch.empty(B * T, Hq * d, device="cuda")
+    scr = torch.empty(ext().attn_bwd_scratch_numel(B, Hq, T), device="cuda")
+    ext().attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d,
+                   dqkv, 0, dqkv, Hq * d, dqkv, (Hq + Hkv) * d, dq_acc, scr, scale, True)
+    ref.backward(do.float().view(B, T, Hq, d).transpose(1, 2))
+    ref_grad = x.grad.transpose(1, 2).reshape(B * T, W)
+    assert torch.isfinite(dqkv.float()).all()
+    assert rel_err(dqkv, ref_grad) < 3e-2
     assert ext().status_read(0) == 0
 
 

@@ -185,3 +185,35 @@ def test_grouped_backward_gemms():
         assert rel_err(gwd[e * H:(e + 1) * H] - 1, dy[a:b].float().t() @ act[a:b].float()) < 1e-3, e
         assert rel_err(gwg[e * I:(e + 1) * I], dgu[a:b, :I].float().t() @ s["xr"][a:b].float()) < 1e-3, e
     assert ext().status_read(0) == 0
+
+
+def test_moe_module_forward_backward_matches_fp32_with_same_routing():
+    """The MoE block on the device path vs an fp32 CPU restatement that uses the same
+    expert selection (bf16 router logits can order near-ties differently from fp32)."""
+    from tinytron_b200.models import ModelConfig
+    from tinytron_b200.models.modules.mlp import MoE
+    from tinytron_b200 import ops
+
+    cfg = ModelConfig(block_size=256, vocab_size=128, num_layer=1, num_attention_heads=2, num_key_value_heads=1,
+                      hidden_size=256, intermediate_size=512, use_moe=True, num_experts=8, num_experts_per_tok=2,
+                      moe_intermediate_size=384, init_std=0.05, seed=4)
+    m = MoE(cfg, 0, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(3)
+    x = torch.randn(2, 200, 256, device="cuda", generator=g).bfloat16().requires_grad_(True)
+    gy = torch.randn(2, 200, 256, device="cuda", generator=g)
+    y, logits = m(x)
+    (y.float() * gy).sum().backward()
+    _, sel = torch.topk(logits.detach().float().view(-1, 8), 2, dim=-1)
+
+    params = {n: p.detach().float().cpu().requires_grad_(True) for n, p in m.named_parameters()}
+    xf = x.detach().float().cpu().requires_grad_(True)
+    lg = xf.view(-1, 256) @ params["router.weight"].t()
+    w_ref = torch.softmax(torch.gather(lg, 1, sel.cpu()), -1)
+    y_ref = ops.moe_experts(xf.view(-1, 256), sel.cpu(), w_ref, params["experts_gate_weights"],
+                            params["experts_up_weights"], params["experts_down_weights"])
+    (y_ref * gy.view(-1, 256).cpu()).sum().backward()
+    assert rel_err(y.view(-1, 256).cpu(), y_ref) < 2e-2
+    assert rel_err(x.grad.cpu(), xf.grad) < 3e-2
+    for n, p in m.named_parameters():
+        assert rel_err(p.grad.cpu(), params[n].grad) < 3e-2, n
+    assert ext().status_read(0) == 0

@@ -110,14 +110,17 @@ class MoE(nn.Module):
     def route(self, x: torch.Tensor):
         """gate_logits [N, E], top-k weights [N, k] (softmax over the selected logits), ids [N, k]."""
         gate_logits = ops.linear(x, self.router.weight)
-        topv, sel = torch.topk(gate_logits, self.top_k, dim=-1)
-        weights = F.softmax(topv.float(), dim=-1)
-        return gate_logits, weights, sel
+        weights, sel = ops.moe_topk_softmax(gate_logits, self.top_k)
+        return gate_logits, weights, sel.long() if not x.is_cuda else sel
 
     def _apply_local_experts(self, rx: torch.Tensor, rexp: torch.Tensor) -> torch.Tensor:
         """rx [R, H] rows routed here with global expert ids rexp [R] -> expert outputs [R, H]."""
         if rx.shape[0] == 0:
             return rx.reshape(0, self.hidden_size) + self._zero_expert_weight_dependency().to(rx.dtype)
+        if rx.is_cuda:  # grouped tcgen05 GEMMs over device-built expert segments
+            local = (rexp % self.num_local_experts).to(torch.int32).view(-1, 1)
+            return ops.moe_experts(rx, local, None, self.experts_gate_weights, self.experts_up_weights,
+                                   self.experts_down_weights)
         local = rexp % self.num_local_experts
         order = torch.argsort(local, stable=True)
         xs = rx[order]
@@ -157,8 +160,12 @@ class MoE(nn.Module):
         if use_cache and ep > 1:
             return self._forward_sep_local_reduce_inference(flat_x, sel, weights, ep_group, ep_rank, B, T), \
                 gate_logits.view(B, T, -1)
+        if ep == 1 and x.is_cuda:  # routing, layout, grouped GEMMs and the weighted sum all on device
+            y = ops.moe_experts(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
+                                self.experts_down_weights)
+            return y.view(B, T, D), gate_logits.view(B, T, -1)
         rep_x = flat_x.repeat_interleave(self.top_k, dim=0)
-        exp_ids = sel.reshape(-1)
+        exp_ids = sel.reshape(-1).long()
         if ep > 1:
             tgt = exp_ids // self.num_local_experts
             gorder = torch.argsort(tgt, stable=True)

@@ -85,6 +85,34 @@ def rotary_attention(qkv: torch.Tensor, B: int, T: int, Hq: int, Hkv: int, D: in
     return o.transpose(1, 2).reshape(B * T, Hq * D)
 
 
+def moe_topk_softmax(gate_logits: torch.Tensor, k: int):
+    """(weights [N, k] fp32, selected experts [N, k]): the k largest router logits per token,
+    descending, and the softmax over them (reference mlp.py:240-244)."""
+    if gate_logits.is_cuda:
+        return _cuda_fn().RouterTopKFn.apply(gate_logits, k)
+    topv, sel = torch.topk(gate_logits, k, dim=-1)
+    return F.softmax(topv.float(), dim=-1), sel
+
+
+def moe_experts(x: torch.Tensor, sel: torch.Tensor, weights: torch.Tensor | None, w_gate: torch.Tensor,
+                w_up: torch.Tensor, w_down: torch.Tensor) -> torch.Tensor:
+    """y[t] = sum_j weights[t, j] * SwiGLU_{sel[t, j]}(x[t])  (weights None: k == 1, unweighted).
+
+    x [N, H]; expert weights [E, I, H], [E, I, H], [E, H, I]; sel holds local expert ids."""
+    if x.is_cuda:
+        return _cuda_fn().MoEExpertsFn.apply(x, sel, weights, w_gate, w_up, w_down)
+    N, k = sel.shape
+    flat = sel.reshape(-1)
+    rep = x.repeat_interleave(k, dim=0)
+    out = torch.zeros(N * k, x.shape[-1], dtype=torch.float32, device=x.device)
+    for e in torch.unique(flat).tolist():
+        idx = torch.nonzero(flat == e).squeeze(-1)
+        out[idx] = swiglu_mlp(rep[idx], w_gate[e], w_up[e], w_down[e]).float()
+    if weights is not None:
+        out = out * weights.reshape(-1, 1).float()
+    return out.view(N, k, -1).sum(1).to(x.dtype)
+
+
 def embedding(idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     if weight.is_cuda:
         return _cuda_fn().EmbeddingFn.apply(idx, weight)

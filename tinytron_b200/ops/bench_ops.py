@@ -110,7 +110,7 @@ def bench_attention(B=4, T=4096, Hq=16, Hkv=4, d=128, iters=10):
     do = torch.randn_like(o)
     dqkv = torch.empty_like(qkv)
     dq_acc = torch.empty(B * T, Hq * d, device="cuda")
-    delta = torch.empty(B, Hq, T, device="cuda")
+    delta = torch.empty(C.attn_bwd_scratch_numel(B, Hq, T), device="cuda")
     bwd = lambda: C.attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d, dqkv, 0, dqkv,
                              Hq * d, dqkv, (Hq + Hkv) * d, dq_acc, delta, sc, True)
     t_bwd = time_fn(bwd, iters=iters)
@@ -168,7 +168,7 @@ def main():
         do = torch.randn_like(o)
         dqkv = torch.empty_like(qkv)
         dq_acc = torch.empty(B * T, Hq * d, device="cuda")
-        delta = torch.empty(B, Hq, T, device="cuda")
+        delta = torch.empty(C.attn_bwd_scratch_numel(B, Hq, T), device="cuda")
         for _ in range(2):
             C.attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d, dqkv, 0, dqkv, Hq * d,
                        dqkv, (Hq + Hkv) * d, dq_acc, delta, sc, True)

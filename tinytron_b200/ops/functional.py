@@ -134,6 +134,117 @@ class SwiGLUMLPFn(torch.autograd.Function):
         return dx, g_gate, g_up, g_down
 
 
+# ----------------------------------------------------------------------------- MoE
+class RouterTopKFn(torch.autograd.Function):
+    """Router top-k + softmax over the selected logits (one warp per token)."""
+
+    @staticmethod
+    def forward(ctx, logits, k):
+        l2d = logits.reshape(-1, logits.shape[-1]).contiguous()
+        N = l2d.shape[0]
+        w = torch.empty(N, k, device=logits.device, dtype=torch.float32)
+        sel = torch.empty(N, k, device=logits.device, dtype=torch.int32)
+        C().moe_topk_softmax(l2d, k, w, sel)
+        ctx.save_for_backward(w, sel)
+        ctx.shape = logits.shape
+        ctx.dtype = l2d.dtype
+        ctx.mark_non_differentiable(sel)
+        return w.view(*logits.shape[:-1], k), sel.view(*logits.shape[:-1], k)
+
+    @staticmethod
+    def backward(ctx, dw, _dsel):
+        w, sel = ctx.saved_tensors
+        dl = torch.empty(w.shape[0], ctx.shape[-1], device=w.device, dtype=ctx.dtype)
+        C().moe_topk_softmax_bwd(dw.reshape(w.shape).float().contiguous(), w, sel, dl)
+        return dl.view(ctx.shape), None
+
+
+def _expert_grad(param, shape2d):
+    """fp32 gradient target of an expert weight viewed as [E*rows, cols]: its main_grad
+    (accumulated) or a fresh buffer returned to autograd."""
+    mg = main_grad_of(param)
+    if mg is not None:
+        return mg.view(shape2d), True
+    return torch.zeros(shape2d, device=param.device, dtype=torch.float32), False
+
+
+class MoEExpertsFn(torch.autograd.Function):
+    """Routed SwiGLU experts on grouped tcgen05 GEMMs.
+
+    Token rows are laid out by expert in 128-row-aligned segments on the device
+    (``moe_layout``); gate|up run as one grouped GEMM with the SwiGLU epilogue, the
+    down projection as a second one, and the top-k weighted sum in ``moe_combine``.
+    Backward: combine -> (dy_rows, dweights); down dgrad with the SwiGLU backward in its
+    epilogue; gate|up dgrad over the stacked weights; per-expert weight gradients
+    reduce over each expert's token segment straight into the fp32 main grads.
+    """
+
+    @staticmethod
+    def forward(ctx, x, sel, weights, w_gate, w_up, w_down):
+        shape = x.shape
+        x2d = _bf16(x.reshape(-1, shape[-1]))
+        N, H = x2d.shape
+        E, I = w_gate.shape[0], w_gate.shape[1]
+        k = sel.shape[-1]
+        c = C()
+        sel32 = sel.reshape(-1).to(torch.int32).contiguous()
+        P = sel32.numel()
+        cap = c.moe_row_capacity(P, E)
+        dev = x.device
+        grp_off = torch.empty(E + 1, device=dev, dtype=torch.int32)
+        slot = torch.empty(P, device=dev, dtype=torch.int32)
+        row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
+        c.moe_layout(sel32, E, grp_off, slot, row_pair)
+        xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+        c.moe_gather_rows(x2d, row_pair, grp_off, k, xr)
+        w_gu = concat_rows([bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
+        wd = bf16_of(w_down).view(E * H, I)
+        act = torch.empty(cap, I, device=dev, dtype=torch.bfloat16)
+        gu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
+        c.moe_gemm_swiglu(xr, w_gu, act, gu, grp_off, E)
+        yr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+        c.moe_gemm(act, wd, yr, grp_off, E, False, H)
+        w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
+        out = torch.empty(N, H, device=dev, dtype=torch.bfloat16)
+        c.moe_combine(yr, slot, w32, k, out)
+        ctx.save_for_backward(xr, act, gu, yr, grp_off, slot, row_pair, w_gu, wd)
+        ctx.w32 = w32
+        ctx.params = (w_gate, w_up, w_down)
+        ctx.dims = (N, H, E, I, k, cap)
+        ctx.shape = shape
+        ctx.has_w = weights is not None
+        return out.view(shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        xr, act, gu, yr, grp_off, slot, row_pair, w_gu, wd = ctx.saved_tensors
+        w_gate, w_up, w_down = ctx.params
+        N, H, E, I, k, cap = ctx.dims
+        c = C()
+        dev = xr.device
+        d2d = _bf16(dout.reshape(N, H))
+        w32 = ctx.w32 if ctx.has_w else torch.ones(N * k, device=dev, dtype=torch.float32)
+        dyr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+        dw = torch.empty(N * k, device=dev, dtype=torch.float32)
+        c.moe_combine_bwd(d2d, yr, row_pair, w32, grp_off, k, dyr, dw)
+        dgu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
+        c.moe_gemm_dswiglu(dyr, wd, gu, dgu, grp_off, E)
+        g_down, main_d = _expert_grad(w_down, (E * H, I))
+        c.moe_gemm_wgrad(dyr, act, g_down, grp_off, E, True)
+        dxr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+        c.moe_gemm(dgu, w_gu, dxr, grp_off, E, True, I, I, E * I)
+        g_gate, main_g = _expert_grad(w_gate, (E * I, H))
+        g_up, main_u = _expert_grad(w_up, (E * I, H))
+        c.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, grp_off, E, True)
+        c.moe_gemm_wgrad(dgu[:, I:], xr, g_up, grp_off, E, True)
+        dx = torch.empty(N, H, device=dev, dtype=torch.bfloat16)
+        c.moe_combine(dxr, slot, None, k, dx)
+        notify_grad_ready([p for p, m in ((w_gate, main_g), (w_up, main_u), (w_down, main_d)) if m])
+        return (dx.view(ctx.shape), None, dw.view(N, k) if ctx.has_w else None,
+                None if main_g else g_gate.view_as(w_gate), None if main_u else g_up.view_as(w_up),
+                None if main_d else g_down.view_as(w_down))
+
+
 # ----------------------------------------------------------------------------- norms
 def _norm_weight_grad(w, dw_buf_needed: bool):
     mg = main_grad_of(w)
@@ -236,7 +347,7 @@ class RotaryAttentionFn(torch.autograd.Function):
         do = _bf16(do)
         dqkv = torch.empty_like(qkv)
         dq_acc = torch.empty(B * T, Hq * D, device=qkv.device, dtype=torch.float32)
-        delta = torch.empty(B, Hq, T, device=qkv.device, dtype=torch.float32)
+        delta = torch.empty(C().attn_bwd_scratch_numel(B, Hq, T), device=qkv.device, dtype=torch.float32)
         C().attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * D, (Hq + Hkv) * D, lse, B, T, Hq, Hkv, D, dqkv, 0, dqkv, Hq * D,
                      dqkv, (Hq + Hkv) * D, dq_acc, delta, scale, causal)
         cos, sin = rope_tables(D, theta, T + pos_offset, qkv.device)
