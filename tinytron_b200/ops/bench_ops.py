@@ -133,10 +133,23 @@ def bench_attention(B=4, T=4096, Hq=16, Hkv=4, d=128, iters=10):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "attn_fwd_once", "attn_bwd_once", "all"])
+    ap.add_argument("what", choices=["gemm", "attn", "attn_fwd_once", "attn_bwd_once", "gemm_once", "all"])
     ap.add_argument("--json", action="store_true")
     args = ap.parse_args()
     out = {}
+    if args.what == "gemm_once":  # small fixed case for profiler captures: gate|up forward GEMM, 2 launches
+        from tinytron_b200.ops import _ext
+
+        C = _ext.load()
+        M, N, K = 16384, 11008, 2048
+        a = torch.randn(M, K, device="cuda").bfloat16()
+        b = torch.randn(N, K, device="cuda").bfloat16()
+        c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        for _ in range(2):
+            C.gemm(a, b, c, False, False, False, 1.0, None, 0)
+        torch.cuda.synchronize()
+        print("ok")
+        return
     if args.what == "attn_fwd_once":  # small fixed case for profiler captures
         import math
 
