@@ -1,0 +1,396 @@
+// KV-cache decode path for sm_100a: fused RoPE + paged KV append, and split-KV
+// ("flash-decoding") attention that reads K/V straight from the pages through the
+// page table.  Both kernels take the sequence position from a device int32, so a
+// whole decode step can be captured once in a CUDA graph and replayed.
+//
+// Replaces, for the reference's cached inference (tinytron/model/modules/attn.py:
+// 188-224, 314-341, 420 and tinytron/inference/cache.py:34-51): the per-step RoPE
+// recomputation (attn.py:13-63), the KV-cache copy_, the GQA expansion
+// (attn.py:66-83), the boolean cache mask (attn.py:86-95) and SDPA over the
+// concatenated cache.  K/V heads are stored unexpanded; one CTA serves all q heads
+// of a kv head, so every K/V byte is read once per step.
+//
+// Decode attention is bound by K/V bytes (a few MB per layer), so the dot products
+// run on the FMA pipe: a warp takes one key at a time (each lane 4 of the head's
+// 128 dims, one 8-byte load), and P·V runs with threads owning output dims.
+#include "common/ptx.cuh"
+#include "common/host_utils.h"
+
+namespace tt {
+namespace decode {
+
+constexpr int kChunk = 256;   // keys per split CTA
+constexpr int kThreads = 128;
+constexpr int kMaxG = 8;      // q heads per kv head
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- RoPE + append
+// One thread per (token, head, 8-dim group of the first half): rotates dims
+// [8c, 8c+8) together with [D/2 + 8c, D/2 + 8c + 8).  q heads -> q_out; k heads ->
+// k pages (rotated); v heads -> v pages (copied).
+__global__ void rope_append_kernel(const __nv_bfloat16* __restrict__ qkv, int ld, int B, int T, int Hq, int Hkv,
+                                   int D, const int* __restrict__ pos_dev, int pos_host, const float* __restrict__ cos_t,
+                                   const float* __restrict__ sin_t, int max_pos, __nv_bfloat16* __restrict__ q_out,
+                                   __nv_bfloat16* __restrict__ k_pages, __nv_bfloat16* __restrict__ v_pages,
+                                   const int* __restrict__ page_table, int pages_per_seq, int page_size,
+                                   int num_pages, int* status) {
+  const int groups = D / 16;  // 8-dim groups in the first half
+  const int H = Hq + 2 * Hkv;
+  const long long total = static_cast<long long>(B) * T * H * groups;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int c = static_cast<int>(idx % groups);
+  const int h = static_cast<int>((idx / groups) % H);
+  const long long tok = idx / (static_cast<long long>(groups) * H);  // b * T + t
+  const int b = static_cast<int>(tok / T);
+  const int t = static_cast<int>(tok % T);
+  const int pos = (pos_dev != nullptr ? *pos_dev : 0) + pos_host + t;
+  if (pos < 0) {
+    atomicCAS(status, 0, static_cast<int>(kBadIndex));
+    return;
+  }
+  const __nv_bfloat16* src = qkv + tok * ld + static_cast<long long>(h) * D;
+  const int d0 = 8 * c, d1 = D / 2 + 8 * c;
+  const uint4 lo4 = *reinterpret_cast<const uint4*>(src + d0);
+  const uint4 hi4 = *reinterpret_cast<const uint4*>(src + d1);
+  uint4 olo = lo4, ohi = hi4;
+  if (h < Hq + Hkv) {  // rotate q and k
+    if (pos >= max_pos) {
+      atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      return;
+    }
+    const float* cr = cos_t + static_cast<long long>(pos) * (D / 2) + d0;
+    const float* sr = sin_t + static_cast<long long>(pos) * (D / 2) + d0;
+    const uint32_t* a = reinterpret_cast<const uint32_t*>(&lo4);
+    const uint32_t* bb = reinterpret_cast<const uint32_t*>(&hi4);
+    uint32_t* oa = reinterpret_cast<uint32_t*>(&olo);
+    uint32_t* ob = reinterpret_cast<uint32_t*>(&ohi);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 x1 = unpack_bf16x2(a[i]);
+      const float2 x2 = unpack_bf16x2(bb[i]);
+      const float c0 = cr[2 * i], c1 = cr[2 * i + 1], s0 = sr[2 * i], s1 = sr[2 * i + 1];
+      // [x1, x2] -> [x1 cos - x2 sin, x2 cos + x1 sin]  (half-split rotation)
+      oa[i] = pack_bf16x2(x1.x * c0 - x2.x * s0, x1.y * c1 - x2.y * s1);
+      ob[i] = pack_bf16x2(x2.x * c0 + x1.x * s0, x2.y * c1 + x1.y * s1);
+    }
+  }
+  __nv_bfloat16* dst;
+  if (h < Hq) {
+    dst = q_out + tok * static_cast<long long>(Hq) * D + static_cast<long long>(h) * D;
+  } else {
+    const int kvh = (h < Hq + Hkv) ? h - Hq : h - Hq - Hkv;
+    const int pi = pos / page_size;
+    if (pi >= pages_per_seq) {
+      atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      return;
+    }
+    const int page = page_table[static_cast<long long>(b) * pages_per_seq + pi];
+    if (page < 0 || page >= num_pages) {
+      atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      return;
+    }
+    __nv_bfloat16* pages = (h < Hq + Hkv) ? k_pages : v_pages;
+    dst = pages + ((static_cast<long long>(page) * page_size + pos % page_size) * Hkv + kvh) * D;
+  }
+  *reinterpret_cast<uint4*>(dst + d0) = olo;
+  *reinterpret_cast<uint4*>(dst + d1) = ohi;
+}
+
+// ---------------------------------------------------------------- split-KV attention
+struct DecodeParams {
+  const __nv_bfloat16* q;        // [B, Hq, D] (one new token per sequence)
+  const __nv_bfloat16* k_pages;  // [num_pages, page_size, Hkv, D]
+  const __nv_bfloat16* v_pages;
+  const int* page_table;         // [B, pages_per_seq]
+  const int* len_dev;            // optional: keys = *len_dev + len_host
+  int len_host;
+  int B, Hq, Hkv, D;
+  int pages_per_seq, page_size, num_pages;
+  int splits;
+  float scale_log2;              // softmax scale * log2(e)
+  float* o_part;                 // [B, Hq, splits, D] unnormalised
+  float* ml_part;                // [B, Hq, splits, 2] (running max in log2 units, sum)
+  int* status;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeParams p) {
+  constexpr int LPL = D / 32;  // dims per lane in the score pass
+  static_assert(LPL == 2 || LPL == 4, "head_dim 64 or 128");
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int G = p.Hq / p.Hkv;
+  const int L = (p.len_dev != nullptr ? *p.len_dev : 0) + p.len_host;
+  const int j0 = split * kChunk;
+  const int n = max(0, min(kChunk, L - j0));
+  __shared__ float q_s[kMaxG][D];
+  __shared__ float s_s[kMaxG][kChunk];
+  __shared__ float red_s[kThreads / 32][kMaxG];
+  __shared__ float m_s[kMaxG], l_s[kMaxG];
+  __shared__ float o_s[2][kMaxG][D];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    q_s[g][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.Hq + kvh * G + g) * D + d]);
+  }
+  __syncthreads();
+  const long long pt_row = static_cast<long long>(b) * p.pages_per_seq;
+  // ---- scores: one warp per key
+  for (int j = warp; j < n; j += kThreads / 32) {
+    const int key = j0 + j;
+    const int pi = key / p.page_size;
+    const int page = pi < p.pages_per_seq ? p.page_table[pt_row + pi] : -1;
+    float acc[kMaxG];
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
+    if (page >= 0 && page < p.num_pages) {
+      const __nv_bfloat16* kr =
+          p.k_pages + ((static_cast<long long>(page) * p.page_size + key % p.page_size) * p.Hkv + kvh) * D;
+      float kv[LPL];
+      if constexpr (LPL == 4) {
+        const uint2 u = *reinterpret_cast<const uint2*>(kr + lane * 4);
+        const float2 a = unpack_bf16x2(u.x), c = unpack_bf16x2(u.y);
+        kv[0] = a.x; kv[1] = a.y; kv[2] = c.x; kv[3] = c.y;
+      } else {
+        const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(kr + lane * 2));
+        kv[0] = a.x; kv[1] = a.y;
+      }
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g) {
+        if (g < G) {
+#pragma unroll
+          for (int e = 0; e < LPL; ++e) acc[g] += kv[e] * q_s[g][lane * LPL + e];
+        }
+      }
+    } else if (lane == 0) {
+      atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
+    }
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+      if (g < G) {
+        float v = acc[g];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0) s_s[g][j] = v * p.scale_log2;
+      }
+    }
+  }
+  __syncthreads();
+  // ---- chunk max per head
+  for (int g = 0; g < G; ++g) {
+    float m = -INFINITY;
+    for (int j = tid; j < n; j += kThreads) m = fmaxf(m, s_s[g][j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) red_s[warp][g] = m;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float m = -INFINITY;
+    for (int w = 0; w < kThreads / 32; ++w) m = fmaxf(m, red_s[w][tid]);
+    m_s[tid] = m;
+  }
+  __syncthreads();
+  // ---- probabilities (in place) and their sums
+  for (int g = 0; g < G; ++g) {
+    const float m = m_s[g];
+    float l = 0.f;
+    for (int j = tid; j < n; j += kThreads) {
+      const float e = exp2f(s_s[g][j] - m);
+      s_s[g][j] = e;
+      l += e;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) red_s[warp][g] = l;
+  }
+  __syncthreads();
+  if (tid < G) {
+    float l = 0.f;
+    for (int w = 0; w < kThreads / 32; ++w) l += red_s[w][tid];
+    l_s[tid] = l;
+  }
+  // ---- P·V: thread owns dims (2 per thread), the two halves of the block split keys
+  constexpr int DT = D / 2;          // threads per key half (each owns 2 dims)
+  const int half = tid / DT;         // 0 or 1 when D == 128; D == 64 -> 0..3 (keys split 4 ways)
+  constexpr int NH = kThreads / DT;  // key partitions
+  const int d2 = (tid % DT) * 2;
+  float oacc[kMaxG][2];
+#pragma unroll
+  for (int g = 0; g < kMaxG; ++g) oacc[g][0] = oacc[g][1] = 0.f;
+  for (int j = half; j < n; j += NH) {
+    const int key = j0 + j;
+    const int pi = key / p.page_size;
+    const int page = pi < p.pages_per_seq ? p.page_table[pt_row + pi] : -1;
+    if (page < 0 || page >= p.num_pages) continue;
+    const __nv_bfloat16* vr =
+        p.v_pages + ((static_cast<long long>(page) * p.page_size + key % p.page_size) * p.Hkv + kvh) * D;
+    const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr + d2));
+#pragma unroll
+    for (int g = 0; g < kMaxG; ++g) {
+      if (g < G) {
+        const float pr = s_s[g][j];
+        oacc[g][0] += pr * vv.x;
+        oacc[g][1] += pr * vv.y;
+      }
+    }
+  }
+  // reduce the NH key partitions through shared memory (NH is 2 or 4)
+  for (int part = 1; part < NH; ++part) {
+    __syncthreads();
+    if (half == part) {
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g)
+        if (g < G) {
+          o_s[part & 1][g][d2] = oacc[g][0];
+          o_s[part & 1][g][d2 + 1] = oacc[g][1];
+        }
+    }
+    __syncthreads();
+    if (half == 0) {
+#pragma unroll
+      for (int g = 0; g < kMaxG; ++g)
+        if (g < G) {
+          oacc[g][0] += o_s[part & 1][g][d2];
+          oacc[g][1] += o_s[part & 1][g][d2 + 1];
+        }
+    }
+  }
+  __syncthreads();
+  if (half == 0) {
+    for (int g = 0; g < G; ++g) {
+      const long long row = (static_cast<long long>(b) * p.Hq + kvh * G + g) * p.splits + split;
+      p.o_part[row * D + d2] = oacc[g][0];
+      p.o_part[row * D + d2 + 1] = oacc[g][1];
+      if (d2 == 0) {
+        p.ml_part[row * 2] = n > 0 ? m_s[g] : -INFINITY;
+        p.ml_part[row * 2 + 1] = n > 0 ? l_s[g] : 0.f;
+      }
+    }
+  }
+}
+
+// out[b, h, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s
+__global__ void decode_combine_kernel(const float* __restrict__ o_part, const float* __restrict__ ml_part, int splits,
+                                      int D, __nv_bfloat16* __restrict__ out) {
+  const long long row = blockIdx.x;  // b * Hq + h
+  const float* ml = ml_part + row * splits * 2;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * s]);
+  float den = 0.f;
+  for (int s = 0; s < splits; ++s)
+    if (ml[2 * s + 1] > 0.f) den += exp2f(ml[2 * s] - M) * ml[2 * s + 1];
+  const float inv = den > 0.f ? 1.0f / den : 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s)
+      if (ml[2 * s + 1] > 0.f) acc += exp2f(ml[2 * s] - M) * o_part[(row * splits + s) * D + d];
+    out[row * D + d] = __float2bfloat16_rn(acc * inv);
+  }
+}
+
+}  // namespace decode
+
+// qkv [B*T, ld] bf16 (q | k | v heads, D each) -> q_out [B*T, Hq*D] rotated; K/V
+// (k rotated) appended at positions (*pos_dev + pos_host + t) into the pages.
+void decode_rope_append(torch::Tensor qkv, int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                        c10::optional<torch::Tensor> pos_dev, int64_t pos_host, torch::Tensor cos_t,
+                        torch::Tensor sin_t, torch::Tensor q_out, torch::Tensor k_pages, torch::Tensor v_pages,
+                        torch::Tensor page_table) {
+  check_cuda_bf16(qkv, "qkv");
+  check_cuda_bf16(q_out, "q_out");
+  check_cuda_bf16(k_pages, "k_pages");
+  check_cuda_bf16(v_pages, "v_pages");
+  TT_CHECK(D % 16 == 0 && D <= 256, "decode_rope_append: head_dim must be a multiple of 16");
+  TT_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(0) == B * T && qkv.size(1) >= (Hq + 2 * Hkv) * D &&
+               qkv.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(qkv.data_ptr()) % 16 == 0,
+           "decode_rope_append: qkv must be [B*T, >=(Hq+2Hkv)*D], 16-byte aligned rows");
+  TT_CHECK(q_out.is_contiguous() && q_out.numel() == B * T * Hq * D, "decode_rope_append: q_out [B*T, Hq*D]");
+  TT_CHECK(k_pages.dim() == 4 && k_pages.size(2) == Hkv && k_pages.size(3) == D && k_pages.is_contiguous() &&
+               v_pages.sizes() == k_pages.sizes() && v_pages.is_contiguous(),
+           "decode_rope_append: pages must be [num_pages, page_size, Hkv, D]");
+  TT_CHECK(page_table.scalar_type() == torch::kInt32 && page_table.dim() == 2 && page_table.size(0) == B &&
+               page_table.is_contiguous(),
+           "decode_rope_append: page_table int32 [B, pages_per_seq]");
+  TT_CHECK(cos_t.scalar_type() == torch::kFloat32 && cos_t.size(1) == D / 2 && sin_t.sizes() == cos_t.sizes(),
+           "decode_rope_append: cos/sin fp32 [max_pos, D/2]");
+  const int* pd = nullptr;
+  if (pos_dev.has_value()) {
+    TT_CHECK(pos_dev->scalar_type() == torch::kInt32 && pos_dev->is_cuda(), "pos_dev must be a CUDA int32 scalar");
+    pd = pos_dev->data_ptr<int>();
+  }
+  const long long total = B * T * (Hq + 2 * Hkv) * (D / 16);
+  if (total == 0) return;
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  const int threads = 256;
+  decode::rope_append_kernel<<<static_cast<unsigned>((total + threads - 1) / threads), threads, 0, cur_stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), static_cast<int>(qkv.stride(0)), static_cast<int>(B),
+      static_cast<int>(T), static_cast<int>(Hq), static_cast<int>(Hkv), static_cast<int>(D), pd,
+      static_cast<int>(pos_host), cos_t.data_ptr<float>(), sin_t.data_ptr<float>(), static_cast<int>(cos_t.size(0)),
+      reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()), reinterpret_cast<__nv_bfloat16*>(k_pages.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(v_pages.data_ptr()), page_table.data_ptr<int>(),
+      static_cast<int>(page_table.size(1)), static_cast<int>(k_pages.size(1)), static_cast<int>(k_pages.size(0)),
+      device_status_ptr(qkv.get_device()));
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+int64_t decode_num_splits(int64_t max_len) { return (max_len + decode::kChunk - 1) / decode::kChunk; }
+
+// Attention of one new token per sequence over keys [0, L), L = *len_dev + len_host
+// (<= splits * 256).  o_part/ml_part: fp32 scratch [B*Hq*splits*D], [B*Hq*splits*2].
+void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages, torch::Tensor page_table,
+                      c10::optional<torch::Tensor> len_dev, int64_t len_host, int64_t splits, double scale,
+                      torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out) {
+  check_cuda_bf16(q, "q");
+  check_cuda_bf16(out, "out");
+  TT_CHECK(q.dim() == 3 && q.is_contiguous(), "decode_attention: q must be [B, Hq, D]");
+  const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2);
+  TT_CHECK(k_pages.dim() == 4 && k_pages.size(3) == D && v_pages.sizes() == k_pages.sizes() &&
+               k_pages.is_contiguous() && v_pages.is_contiguous(),
+           "decode_attention: pages [num_pages, page_size, Hkv, D]");
+  const int64_t Hkv = k_pages.size(2);
+  TT_CHECK(Hq % Hkv == 0 && Hq / Hkv <= decode::kMaxG, "decode_attention: Hq/Hkv must be an integer <= 8");
+  TT_CHECK(D == 64 || D == 128, "decode_attention: head_dim 64 or 128");
+  TT_CHECK(page_table.scalar_type() == torch::kInt32 && page_table.dim() == 2 && page_table.size(0) == B &&
+               page_table.is_contiguous(),
+           "decode_attention: page_table int32 [B, pages_per_seq]");
+  TT_CHECK(splits >= 1 && splits * decode::kChunk >= 1, "decode_attention: splits >= 1");
+  TT_CHECK(o_part.scalar_type() == torch::kFloat32 && o_part.numel() >= B * Hq * splits * D &&
+               ml_part.scalar_type() == torch::kFloat32 && ml_part.numel() >= B * Hq * splits * 2,
+           "decode_attention: scratch too small");
+  TT_CHECK(out.is_contiguous() && out.numel() == B * Hq * D, "decode_attention: out [B, Hq*D]");
+  decode::DecodeParams p;
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k_pages = reinterpret_cast<const __nv_bfloat16*>(k_pages.data_ptr());
+  p.v_pages = reinterpret_cast<const __nv_bfloat16*>(v_pages.data_ptr());
+  p.page_table = page_table.data_ptr<int>();
+  p.len_dev = nullptr;
+  if (len_dev.has_value()) {
+    TT_CHECK(len_dev->scalar_type() == torch::kInt32 && len_dev->is_cuda(), "len_dev must be a CUDA int32 scalar");
+    p.len_dev = len_dev->data_ptr<int>();
+  }
+  p.len_host = static_cast<int>(len_host);
+  p.B = static_cast<int>(B);
+  p.Hq = static_cast<int>(Hq);
+  p.Hkv = static_cast<int>(Hkv);
+  p.D = static_cast<int>(D);
+  p.pages_per_seq = static_cast<int>(page_table.size(1));
+  p.page_size = static_cast<int>(k_pages.size(1));
+  p.num_pages = static_cast<int>(k_pages.size(0));
+  p.splits = static_cast<int>(splits);
+  p.scale_log2 = static_cast<float>(scale) * decode::kLog2e;
+  p.o_part = o_part.data_ptr<float>();
+  p.ml_part = ml_part.data_ptr<float>();
+  p.status = device_status_ptr(q.get_device());
+  if (B == 0) return;
+  const c10::cuda::CUDAGuard guard(q.device());
+  dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  if (D == 128) decode::decode_split_kernel<128><<<grid, decode::kThreads, 0, cur_stream()>>>(p);
+  else decode::decode_split_kernel<64><<<grid, decode::kThreads, 0, cur_stream()>>>(p);
+  TT_CUDA_CHECK(cudaGetLastError());
+  decode::decode_combine_kernel<<<static_cast<unsigned>(B * Hq), static_cast<unsigned>(D), 0, cur_stream()>>>(
+      p.o_part, p.ml_part, p.splits, p.D, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace tt

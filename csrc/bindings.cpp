@@ -52,6 +52,34 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
               torch::Tensor dv, int64_t dv_col0, torch::Tensor dq_acc, torch::Tensor scratch, double scale,
               bool causal);
 void exp2_poly_op(torch::Tensor x, torch::Tensor y);
+void decode_rope_append(torch::Tensor qkv, int64_t B, int64_t T, int64_t Hq, int64_t Hkv, int64_t D,
+                        c10::optional<torch::Tensor> pos_dev, int64_t pos_host, torch::Tensor cos_t,
+                        torch::Tensor sin_t, torch::Tensor q_out, torch::Tensor k_pages, torch::Tensor v_pages,
+                        torch::Tensor page_table);
+int64_t decode_num_splits(int64_t max_len);
+void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages, torch::Tensor page_table,
+                      c10::optional<torch::Tensor> len_dev, int64_t len_host, int64_t splits, double scale,
+                      torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out);
+namespace comm {
+int64_t comm_create(int64_t device, int64_t bytes);
+torch::Tensor comm_ipc_handle(int64_t gid);
+void comm_open(int64_t gid, int64_t rank, int64_t world, torch::Tensor handles);
+void comm_open_emulated(std::vector<int64_t> gids, bool waits);
+void comm_set_timeout(double seconds);
+torch::Tensor comm_view(int64_t gid, int64_t offset_bytes, std::vector<int64_t> shape, int64_t dtype_code);
+int64_t comm_user_offset();
+int64_t comm_heap_base(int64_t gid);
+void comm_barrier(int64_t gid);
+void comm_all_reduce(int64_t gid, int64_t in_offset, torch::Tensor out, c10::optional<torch::Tensor> residual);
+void comm_reduce_scatter_sumsq(int64_t gid, int64_t grad_offset, int64_t lo, int64_t hi, int64_t split, double scale);
+void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset, c10::optional<torch::Tensor> p16,
+                          torch::Tensor m, torch::Tensor v, int64_t lo, int64_t hi, double lr, double beta1,
+                          double beta2, double eps, double wd, int64_t step, double max_norm,
+                          c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out);
+void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, int64_t lo, int64_t hi);
+int64_t comm_epoch(int64_t gid);
+void comm_destroy(int64_t gid);
+}  // namespace comm
 }  // namespace tt
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -96,4 +124,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_fwd", &tt::attn_fwd, "flash attention forward (tcgen05, GQA-native)");
   m.def("attn_bwd_scratch_numel", &tt::attn_bwd_scratch_numel, "fp32 scratch elements attn_bwd needs");
   m.def("attn_bwd", &tt::attn_bwd, "flash attention backward (tcgen05, GQA-native, dQ via fp32 atomics)");
+  m.def("decode_rope_append", &tt::decode_rope_append, "RoPE on q/k + paged KV-cache append (device position)");
+  m.def("decode_num_splits", &tt::decode_num_splits, "split-KV CTAs per (sequence, kv head) for a max length");
+  m.def("decode_attention", &tt::decode_attention, "split-KV paged decode attention (GQA-native) + combine");
+  // tt_comm: symmetric heap over CUDA IPC + device-initiated collectives (csrc/runtime/comm.cu)
+  m.def("comm_create", &tt::comm::comm_create, "allocate a symmetric heap on a device; returns a group id");
+  m.def("comm_ipc_handle", &tt::comm::comm_ipc_handle, "64-byte CUDA IPC handle of the group's heap");
+  m.def("comm_open", &tt::comm::comm_open, "map every peer's heap (handles uint8 [world, 64])");
+  m.def("comm_open_emulated", &tt::comm::comm_open_emulated, "single-GPU test mode: groups act as ranks",
+        py::arg("gids"), py::arg("waits") = false);
+  m.def("comm_set_timeout", &tt::comm::comm_set_timeout, "bound (seconds) on every device-side wait");
+  m.def("comm_view", &tt::comm::comm_view, "tensor view into the local heap");
+  m.def("comm_user_offset", &tt::comm::comm_user_offset, "first byte of the heap's user region");
+  m.def("comm_heap_base", &tt::comm::comm_heap_base, "device address of the local heap");
+  m.def("comm_barrier", &tt::comm::comm_barrier, "device-side barrier over the group (bounded wait)");
+  m.def("comm_all_reduce", &tt::comm::comm_all_reduce, "one-shot all-reduce of a heap region (+ residual)",
+        py::arg("gid"), py::arg("in_offset"), py::arg("out"), py::arg("residual") = py::none());
+  m.def("comm_reduce_scatter_sumsq", &tt::comm::comm_reduce_scatter_sumsq,
+        "ZeRO-1 fp32 gradient reduce-scatter in place + published sums of squares");
+  m.def("comm_adamw_allgather", &tt::comm::comm_adamw_allgather,
+        "ZeRO-1 clip + AdamW on the owned shard + fp32 all-gather by peer stores");
+  m.def("comm_shadow_refresh", &tt::comm::comm_shadow_refresh, "wait for the all-gather; refresh bf16 shadow");
+  m.def("comm_epoch", &tt::comm::comm_epoch);
+  m.def("comm_destroy", &tt::comm::comm_destroy);
 }

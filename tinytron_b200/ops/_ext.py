@@ -20,11 +20,13 @@ EXT_NAME = "tinytron_b200_C"
 SOURCES = [
     "bindings.cpp",
     "runtime/status.cu",
+    "runtime/comm.cu",
     "gemm/gemm.cu",
     "fused/norm.cu",
     "fused/elementwise.cu",
     "attn/attn_fwd.cu",
     "attn/attn_bwd.cu",
+    "attn/decode.cu",
     "moe/moe.cu",
 ]
 

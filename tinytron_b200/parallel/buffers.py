@@ -22,7 +22,12 @@ EXPERT_SUFFIXES = (".experts_gate_weights", ".experts_up_weights", ".experts_dow
 
 
 class FlatParams:
-    def __init__(self, model: torch.nn.Module, align: int = 64, pad_to_multiple: int = 1, with_bf16: bool = True):
+    def __init__(self, model: torch.nn.Module, align: int = 64, pad_to_multiple: int = 1, with_bf16: bool = True,
+                 heap_factory=None):
+        """``heap_factory(nbytes)`` (optional) returns a :class:`~tinytron_b200.parallel.symm.SymmetricHeap`
+        of at least ``nbytes`` from which the three flat buffers are carved, so peers can
+        reduce-scatter the gradients and all-gather the parameters with NVLink loads and
+        stores (every rank builds the same layout, so offsets match across ranks)."""
         named = []
         seen = set()
         for name, p in model.named_parameters():
@@ -47,9 +52,19 @@ class FlatParams:
         self.offsets = offsets
         device = self.params[0].device
         self.device = device
-        self.data = torch.zeros(total, dtype=torch.float32, device=device)
-        self.grad = torch.zeros(total, dtype=torch.float32, device=device)
-        self.bf16 = torch.zeros(total, dtype=torch.bfloat16, device=device) if with_bf16 else None
+        self.heap = None
+        if heap_factory is not None:
+            from .symm import SymmetricHeap
+
+            specs = [(total, torch.float32), (total, torch.float32)] + ([(total, torch.bfloat16)] if with_bf16 else [])
+            self.heap = heap_factory(SymmetricHeap.bytes_needed(*specs))
+            self.data = self.heap.alloc(total, torch.float32)
+            self.grad = self.heap.alloc(total, torch.float32)
+            self.bf16 = self.heap.alloc(total, torch.bfloat16) if with_bf16 else None
+        else:
+            self.data = torch.zeros(total, dtype=torch.float32, device=device)
+            self.grad = torch.zeros(total, dtype=torch.float32, device=device)
+            self.bf16 = torch.zeros(total, dtype=torch.bfloat16, device=device) if with_bf16 else None
         for (name, p), o in zip(self.named, offsets):
             n = p.numel()
             view = self.data[o:o + n].view_as(p)

@@ -1,0 +1,169 @@
+"""Symmetric device heap over NVLink (Python side of ``csrc/runtime/comm.cu``).
+
+A :class:`SymmetricHeap` is one device buffer per rank of a process group, mapped
+into every other rank through CUDA IPC, so kernels can load from and store to
+peers' memory directly.  Tensors are carved from the heap by a bump allocator;
+ranks that make the same ``alloc`` calls in the same order get the same offsets,
+which is what makes the heap *symmetric* (a peer's copy of a tensor lives at the
+same offset of the peer's heap).
+
+The collectives on the heap replace the reference's NCCL calls on the hot paths:
+
+* :meth:`SymmetricHeap.all_reduce` — one-shot all-reduce of a heap tensor (inference
+  row-parallel outputs; reference ``model/modules/attn.py:364``, ``mlp.py:221``).
+* :meth:`SymmetricHeap.reduce_scatter_sumsq` and :meth:`SymmetricHeap.adamw_allgather`
+  — the ZeRO-1 gradient reduce-scatter (with the clip norm's sums of squares) and
+  the fused clip + AdamW + parameter all-gather (reference: DDP all-reduce in
+  ``training/trainer.py:214-220`` plus the per-tensor broadcasts of
+  ``distributed/zero1/distributed_optimizer.py:106-119``).
+
+Every device-side wait is bounded (``TT_COMM_TIMEOUT_S``, default 60 s); a wait
+that gives up records a status code and the host raises from
+:func:`tinytron_b200.ops.check_status`.
+
+Single-GPU test mode (:meth:`SymmetricHeap.create_emulated`): W heaps on one
+device act as the W ranks of one group; the collectives are launched rank by rank
+with waits disabled, so no kernel ever waits for another.
+"""
+from __future__ import annotations
+
+import socket
+
+import torch
+import torch.distributed as dist
+
+ALIGN = 256
+
+
+def _C():
+    from tinytron_b200.ops import _ext
+
+    return _ext.load()
+
+
+def _dtype_code(dtype: torch.dtype) -> int:
+    # c10::ScalarType enum values (stable public ABI of torch)
+    return {torch.uint8: 0, torch.int32: 3, torch.int64: 4, torch.float16: 5, torch.float32: 6,
+            torch.bfloat16: 15}[dtype]
+
+
+def same_host(group) -> bool:
+    """True when every rank of ``group`` runs on this host (CUDA IPC needs that)."""
+    names = [None] * dist.get_world_size(group)
+    dist.all_gather_object(names, socket.gethostname(), group=group)
+    return len(set(names)) == 1
+
+
+class SymmetricHeap:
+    def __init__(self, gid: int, nbytes: int, rank: int, world: int, device: torch.device):
+        self.gid = gid
+        self.nbytes = nbytes
+        self.rank = rank
+        self.world = world
+        self.device = device
+        self._next = int(_C().comm_user_offset())
+        self._base = int(_C().comm_heap_base(gid))
+        self._closed = False
+
+    # ------------------------------------------------------------------ construction
+    @classmethod
+    def create(cls, nbytes: int, group=None, device=None) -> "SymmetricHeap":
+        """Collective over ``group``: allocate this rank's heap and map every peer's."""
+        C = _C()
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        if world > 8:
+            raise ValueError("SymmetricHeap supports at most 8 ranks (one NVLink domain)")
+        nbytes = int(nbytes) + int(C.comm_user_offset())
+        gid = int(C.comm_create(device.index, nbytes))
+        h = C.comm_ipc_handle(gid)
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(h.tolist()), group=group)
+        table = torch.tensor([list(x) for x in handles], dtype=torch.uint8)
+        C.comm_open(gid, rank, world, table)
+        heap = cls(gid, nbytes, rank, world, device)
+        dist.barrier(group=group)
+        return heap
+
+    @classmethod
+    def create_emulated(cls, nbytes: int, world: int, device=None, waits: bool = False) -> list["SymmetricHeap"]:
+        """W heaps on one device acting as the W ranks of one group (tests)."""
+        C = _C()
+        device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        nbytes = int(nbytes) + int(C.comm_user_offset())
+        gids = [int(C.comm_create(device.index, nbytes)) for _ in range(world)]
+        C.comm_open_emulated(gids, waits)
+        return [cls(g, nbytes, r, world, device) for r, g in enumerate(gids)]
+
+    # ------------------------------------------------------------------ memory
+    def alloc(self, shape, dtype: torch.dtype, zero: bool = True) -> torch.Tensor:
+        shape = tuple(int(s) for s in (shape if isinstance(shape, (tuple, list)) else (shape,)))
+        numel = 1
+        for s in shape:
+            numel *= s
+        nb = numel * torch.empty((), dtype=dtype).element_size()
+        off = self._next
+        if off + nb > self.nbytes:
+            raise MemoryError(f"symmetric heap exhausted ({off + nb} > {self.nbytes} bytes)")
+        self._next = (off + nb + ALIGN - 1) // ALIGN * ALIGN
+        t = _C().comm_view(self.gid, off, list(shape), _dtype_code(dtype))
+        if zero:
+            t.zero_()
+        return t
+
+    def offset_of(self, t: torch.Tensor) -> int:
+        off = t.data_ptr() - self._base
+        if not (0 <= off and off + t.numel() * t.element_size() <= self.nbytes):
+            raise ValueError("tensor does not live in this symmetric heap")
+        return off
+
+    @staticmethod
+    def bytes_needed(*specs) -> int:
+        """Heap bytes for a list of (numel, dtype) allocations."""
+        total = 0
+        for numel, dtype in specs:
+            nb = int(numel) * torch.empty((), dtype=dtype).element_size()
+            total += (nb + ALIGN - 1) // ALIGN * ALIGN
+        return total
+
+    # ------------------------------------------------------------------ collectives
+    def barrier(self) -> None:
+        _C().comm_barrier(self.gid)
+
+    def all_reduce(self, src: torch.Tensor, out: torch.Tensor | None = None,
+                   residual: torch.Tensor | None = None) -> torch.Tensor:
+        """out = sum over ranks of ``src`` (a heap tensor) (+ residual); one-shot, every
+        rank gets the bit-identical sum (same rank order everywhere).  The caller must
+        not overwrite ``src`` before the *next* collective on this heap has started on
+        every rank; alternating two source buffers satisfies that."""
+        out = torch.empty_like(src) if out is None else out
+        _C().comm_all_reduce(self.gid, self.offset_of(src), out, residual)
+        return out
+
+    def reduce_scatter_sumsq(self, grad: torch.Tensor, lo: int, hi: int, split: int, scale: float) -> None:
+        """grad[lo:hi] = scale * sum over ranks of grad[lo:hi] (in place); publishes this
+        rank's sums of squares of the reduced shard (split at ``split``) to every peer."""
+        _C().comm_reduce_scatter_sumsq(self.gid, self.offset_of(grad), int(lo), int(hi), int(split), float(scale))
+
+    def adamw_allgather(self, data: torch.Tensor, grad: torch.Tensor, p16: torch.Tensor | None, m: torch.Tensor,
+                        v: torch.Tensor, lo: int, hi: int, lr: float, betas, eps: float, wd: float, step: int,
+                        max_norm: float, norm_out: torch.Tensor | None = None,
+                        extra_sq: torch.Tensor | None = None) -> None:
+        _C().comm_adamw_allgather(self.gid, self.offset_of(data), self.offset_of(grad), p16, m, v, int(lo), int(hi),
+                                  float(lr), float(betas[0]), float(betas[1]), float(eps), float(wd), int(step),
+                                  float(max_norm), extra_sq, norm_out)
+
+    def shadow_refresh(self, data: torch.Tensor, p16: torch.Tensor, lo: int, hi: int) -> None:
+        _C().comm_shadow_refresh(self.gid, self.offset_of(data), p16, int(lo), int(hi))
+
+    @property
+    def epoch(self) -> int:
+        return int(_C().comm_epoch(self.gid))
+
+    def close(self) -> None:
+        """Free the heap (collective in spirit: peers must be done with it).  Tensors
+        carved from it must not be used afterwards."""
+        if not self._closed:
+            _C().comm_destroy(self.gid)
+            self._closed = True

@@ -15,6 +15,14 @@ Two implementations:
   fused kernel applies clip + AdamW to the owned shard (also writing the bf16
   shadow), and the updated master shard is all-gathered.  AdamW is elementwise,
   so element-wise sharding gives exactly the same update as whole-tensor sharding.
+
+  When the flat buffers live in a symmetric heap (``FlatParams(heap_factory=...)``,
+  one node, no SP expert split) the DP path runs on NVLink peer memory instead of
+  NCCL: one kernel reduce-scatters the fp32 gradients by peer loads and publishes
+  this rank's sums of squares into every peer's pad; a second kernel forms the clip
+  coefficient from the pads, applies AdamW to the owned shard and stores the new
+  fp32 shard straight into every peer's parameter buffer; a third waits for the
+  peers' stores and refreshes the local bf16 shadow of their shards.
 """
 from __future__ import annotations
 
@@ -150,6 +158,13 @@ class FlatZeRO1:
         self._norm = torch.zeros(1, device=dev)
         self._coef = torch.ones(1, device=dev)
         self.master_synced = True
+        heap = getattr(flat, "heap", None)
+        # Native NVLink path: heap spans exactly this DP group and no SP-summed expert
+        # norm term is needed (that one still takes the NCCL path).
+        self.native = (heap is not None and self.dp > 1 and heap.world == self.dp
+                       and (self.sp == 1 or flat.dense_numel == flat.numel) and self.shard % 4 == 0)
+        self._max_norm = 0.0
+        self._normc = torch.zeros(2, device=dev)
 
     # ---------------------------------------------------------------- gradient sync
     @torch.no_grad()
@@ -157,6 +172,10 @@ class FlatZeRO1:
         g = self.flat.grad
         if self.sp > 1 and self.flat.dense_numel > 0:
             dist.all_reduce(g[:self.flat.dense_numel], op=dist.ReduceOp.SUM, group=self.sp_group)
+        if self.native:
+            # dense_numel is a multiple of the flat layout's 64-element alignment
+            self.flat.heap.reduce_scatter_sumsq(g, self.lo, self.hi, self.flat.dense_numel, 1.0 / self.dp)
+            return
         if self.dp > 1:
             if dist.get_backend(self.dp_group) == "nccl":
                 dist.reduce_scatter_tensor(g[self.lo:self.hi], g, op=dist.ReduceOp.AVG, group=self.dp_group)
@@ -168,6 +187,11 @@ class FlatZeRO1:
     # ---------------------------------------------------------------- norm
     @torch.no_grad()
     def grad_norm_and_coef(self, max_norm: float):
+        if self.native:
+            # The norm and clip coefficient are formed inside the update kernel from the
+            # sums of squares every rank published; they land in _normc after step().
+            self._max_norm = float(max_norm)
+            return self._normc[0], None
         g = self.flat.grad[self.lo:self.hi]
         dense_hi = max(self.lo, min(self.hi, self.flat.dense_numel))
         if g.is_cuda:
@@ -199,6 +223,15 @@ class FlatZeRO1:
         b1, b2 = grp["betas"]
         self.step_count += 1
         lo, hi = self.lo, self.hi
+        if self.native:
+            heap = self.flat.heap
+            heap.adamw_allgather(self.flat.data, self.flat.grad, self.flat.bf16, self.exp_avg, self.exp_avg_sq, lo, hi,
+                                 lr, (b1, b2), grp["eps"], grp["weight_decay"], self.step_count, self._max_norm,
+                                 norm_out=self._normc)
+            if self.flat.bf16 is not None:
+                heap.shadow_refresh(self.flat.data, self.flat.bf16, lo, hi)
+            self.flat.mark_shadows_fresh()
+            return
         p = self.flat.data[lo:hi]
         g = self.flat.grad[lo:hi]
         if p.is_cuda:

@@ -142,7 +142,28 @@ class Trainer:
         self.model = model
         self.raw_model = model
         pad = max(1, self.dp_world_size) * 64
-        self.flat = FlatParams(model, pad_to_multiple=pad, with_bf16=self.device.type == "cuda")
+        heap_factory = None
+        if self._use_native_comm(config):
+            from tinytron_b200.parallel.symm import SymmetricHeap
+
+            def heap_factory(nbytes):
+                return SymmetricHeap.create(nbytes, group=self.dp_group, device=self.device)
+        self.flat = FlatParams(model, pad_to_multiple=pad, with_bf16=self.device.type == "cuda",
+                               heap_factory=heap_factory)
+
+    def _use_native_comm(self, config: Config) -> bool:
+        """ZeRO-1 gradient/parameter sync over NVLink peer memory (tt_comm) instead of
+        NCCL: CUDA, DP > 1 inside one node, AdamW with the distributed optimizer.
+        ``TT_NATIVE_COMM=0`` selects the NCCL path."""
+        if self.device.type != "cuda" or self.dp_world_size <= 1 or os.environ.get("TT_NATIVE_COMM", "1") == "0":
+            return False
+        if not (config.parallel.use_distributed_optimizer and config.optim.optimizer == "adam"):
+            return False
+        if self.dp_world_size > 8:
+            return False
+        from tinytron_b200.parallel.symm import same_host
+
+        return same_host(self.dp_group)
 
     def _init_optimizer(self, config: Config):
         o = config.optim
