@@ -60,6 +60,13 @@ int64_t decode_num_splits(int64_t max_len);
 void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages, torch::Tensor page_table,
                       c10::optional<torch::Tensor> len_dev, int64_t len_host, int64_t splits, double scale,
                       torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out);
+void ep_allgather_counts(int64_t gid, torch::Tensor counts, int64_t dst_off);
+void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torch::Tensor dst, int64_t recv_off,
+                int64_t cap, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> y_pairs,
+                c10::optional<torch::Tensor> dw);
+void ep_pull_combine(int64_t gid, int64_t y_off, int64_t cap, torch::Tensor tgt, torch::Tensor dst, int64_t k,
+                     c10::optional<torch::Tensor> w, torch::Tensor out, c10::optional<torch::Tensor> y_save);
+void ep_zero_pad(torch::Tensor buf, torch::Tensor seg_off, torch::Tensor seg_cnt);
 namespace comm {
 int64_t comm_create(int64_t device, int64_t bytes);
 torch::Tensor comm_ipc_handle(int64_t gid);
@@ -127,6 +134,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_rope_append", &tt::decode_rope_append, "RoPE on q/k + paged KV-cache append (device position)");
   m.def("decode_num_splits", &tt::decode_num_splits, "split-KV CTAs per (sequence, kv head) for a max length");
   m.def("decode_attention", &tt::decode_attention, "split-KV paged decode attention (GQA-native) + combine");
+  m.def("ep_allgather_counts", &tt::ep_allgather_counts, "EP: all-gather per-expert counts into the heap");
+  m.def("ep_scatter", &tt::ep_scatter, "EP dispatch: pair rows to their owners' receive buffers (peer stores)",
+        py::arg("gid"), py::arg("x"), py::arg("k"), py::arg("tgt"), py::arg("dst"), py::arg("recv_off"),
+        py::arg("cap"), py::arg("w") = py::none(), py::arg("y_pairs") = py::none(), py::arg("dw") = py::none());
+  m.def("ep_pull_combine", &tt::ep_pull_combine, "EP combine: weighted sum of owners' rows (peer loads)",
+        py::arg("gid"), py::arg("y_off"), py::arg("cap"), py::arg("tgt"), py::arg("dst"), py::arg("k"),
+        py::arg("w"), py::arg("out"), py::arg("y_save") = py::none());
+  m.def("ep_zero_pad", &tt::ep_zero_pad, "zero the padding rows of expert segments");
   // tt_comm: symmetric heap over CUDA IPC + device-initiated collectives (csrc/runtime/comm.cu)
   m.def("comm_create", &tt::comm::comm_create, "allocate a symmetric heap on a device; returns a group id");
   m.def("comm_ipc_handle", &tt::comm::comm_ipc_handle, "64-byte CUDA IPC handle of the group's heap");

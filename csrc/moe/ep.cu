@@ -1,0 +1,298 @@
+// Expert-parallel dispatch and combine over NVLink peer memory (symmetric heap of
+// csrc/runtime/comm.cu).  Replaces the reference's EP all-to-alls
+// (tinytron/distributed/expert_parallel/comm.py:22-164, model/modules/mlp.py:257-293):
+//
+//   * allgather_counts  every rank stores its per-expert send counts [E] into row
+//                       `rank` of every peer's count matrix [world, E] (one small
+//                       kernel, bounded wait); the host then knows every segment size.
+//   * scatter           a warp per (token, slot) pair stores the token's hidden row
+//                       straight into the owning rank's expert-grouped receive buffer
+//                       at a precomputed row (P2P stores; no sort-then-a2a copies).
+//                       The backward variant stores w * dout[token] and also computes
+//                       dw = <dout[token], y_pair> for the router weights.
+//   * pull_combine      a warp per token loads its k expert outputs from the owning
+//                       ranks' output buffers (P2P loads), optionally keeps them (for
+//                       the backward), and writes sum_j w_j * y_j (fp32 accumulate).
+//   * zero_pad          zeroes the padding rows of the 128-row-aligned expert segments
+//                       of the local receive buffer (the grouped GEMMs read them).
+//
+// Every launch records a bad index (row beyond the buffer, rank beyond the group)
+// in the device status word and skips that row instead of faulting.
+#include "runtime/comm_common.cuh"
+
+namespace tt {
+namespace ep {
+
+using comm::PeerTable;
+
+constexpr int kThreads = 256;  // 8 warps per block, one pair / token per warp
+
+__global__ void allgather_kernel(PeerTable t, const int* __restrict__ src, int n, size_t dst_off, uint64_t e,
+                                 int* status, uint64_t timeout_ns) {
+  for (int p = 0; p < t.world; ++p) {
+    int* dst = reinterpret_cast<int*>(t.base[p] + dst_off) + static_cast<long long>(t.rank) * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) dst[i] = src[i];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    comm::signal_peers(t, e);
+    comm::wait_peers(t, e, status, timeout_ns);
+  }
+}
+
+// MODE 0 (forward): row = x[pair / k].  MODE 1 (backward): row = w[pair] * x[pair / k]
+// and dw[pair] = <x[pair / k], y_pair[pair]>.
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) scatter_kernel(PeerTable t, const __nv_bfloat16* __restrict__ x,
+                                                          int num_pairs, int k, int H, const int* __restrict__ tgt,
+                                                          const int* __restrict__ dst, long long cap, size_t recv_off,
+                                                          const float* __restrict__ w,
+                                                          const __nv_bfloat16* __restrict__ y_pairs,
+                                                          float* __restrict__ dw, uint64_t e_done, int* status) {
+  const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_warps = (gridDim.x * kThreads) >> 5;
+  const int nv = H / 8;  // uint4 (8 bf16) per row
+  for (int pr = warp; pr < num_pairs; pr += n_warps) {
+    const int r = tgt[pr];
+    const long long row = dst[pr];
+    if (r < 0 || r >= t.world || row < 0 || row >= cap) {
+      if (lane == 0) atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(x + static_cast<long long>(pr / k) * H);
+    uint4* out = reinterpret_cast<uint4*>(t.base[r] + recv_off + row * H * 2);
+    if constexpr (MODE == 0) {
+      for (int i = lane; i < nv; i += 32) out[i] = src[i];
+    } else {
+      const float wv = w[pr];
+      const uint4* yp = reinterpret_cast<const uint4*>(y_pairs + static_cast<long long>(pr) * H);
+      float dot = 0.f;
+      for (int i = lane; i < nv; i += 32) {
+        const uint4 a = src[i];
+        const uint4 b = yp[i];
+        const uint32_t* av = reinterpret_cast<const uint32_t*>(&a);
+        const uint32_t* bv = reinterpret_cast<const uint32_t*>(&b);
+        uint4 o;
+        uint32_t* ov = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 fa = unpack_bf16x2(av[q]);
+          const float2 fb = unpack_bf16x2(bv[q]);
+          dot += fa.x * fb.x + fa.y * fb.y;
+          ov[q] = pack_bf16x2(wv * fa.x, wv * fa.y);
+        }
+        out[i] = o;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      if (lane == 0) dw[pr] = dot;
+    }
+  }
+  comm::grid_last_block(t, [&]() { comm::signal_peers(t, e_done); });
+}
+
+// out[tok] = sum_j w[tok*k+j] * peer(tgt).y[dst]  (w == nullptr: plain sum); y_save[pair] = row.
+template <int PL>  // uint4 columns per lane: H <= PL * 256
+__global__ void __launch_bounds__(kThreads) pull_combine_kernel(PeerTable t, size_t y_off, int N, int k, int H,
+                                                               const int* __restrict__ tgt,
+                                                               const int* __restrict__ dst, long long cap,
+                                                               const float* __restrict__ w,
+                                                               __nv_bfloat16* __restrict__ out,
+                                                               __nv_bfloat16* __restrict__ y_save, int* status) {
+  const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n_warps = (gridDim.x * kThreads) >> 5;
+  const int nv = H / 8;
+  for (int tok = warp; tok < N; tok += n_warps) {
+    // Each lane accumulates its uint4 columns over the k slots.
+    float acc[PL][8];
+#pragma unroll
+    for (int c = 0; c < PL; ++c)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) acc[c][q] = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int pr = tok * k + j;
+      const int r = tgt[pr];
+      const long long row = dst[pr];
+      if (r < 0 || r >= t.world || row < 0 || row >= cap) {
+        if (lane == 0) atomicCAS(status, 0, static_cast<int>(kBadIndex));
+        continue;
+      }
+      const float wv = w != nullptr ? w[pr] : 1.0f;
+      const uint4* src = reinterpret_cast<const uint4*>(t.base[r] + y_off + row * H * 2);
+      uint4* save = y_save != nullptr ? reinterpret_cast<uint4*>(y_save + static_cast<long long>(pr) * H) : nullptr;
+#pragma unroll
+      for (int c = 0; c < PL; ++c) {
+        const int i = lane + 32 * c;
+        if (i < nv) {
+          const uint4 v = src[i];
+          if (save != nullptr) save[i] = v;
+          const uint32_t* vv = reinterpret_cast<const uint32_t*>(&v);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = unpack_bf16x2(vv[q]);
+            acc[c][2 * q] += wv * f.x;
+            acc[c][2 * q + 1] += wv * f.y;
+          }
+        }
+      }
+    }
+    uint4* o = reinterpret_cast<uint4*>(out + static_cast<long long>(tok) * H);
+#pragma unroll
+    for (int c = 0; c < PL; ++c) {
+      const int i = lane + 32 * c;
+      if (i < nv) {
+        uint4 u;
+        uint32_t* uv = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) uv[q] = pack_bf16x2(acc[c][2 * q], acc[c][2 * q + 1]);
+        o[i] = u;
+      }
+    }
+  }
+}
+
+// Zero rows [seg_off[e] + seg_cnt[e], seg_off[e + 1]) of buf [rows, H] for every e.
+__global__ void zero_pad_kernel(__nv_bfloat16* __restrict__ buf, const int* __restrict__ seg_off,
+                                const int* __restrict__ seg_cnt, int n_seg, int H, long long cap) {
+  const int e = blockIdx.y;
+  if (e >= n_seg) return;
+  const long long r0 = static_cast<long long>(seg_off[e]) + seg_cnt[e];
+  const long long r1 = min(static_cast<long long>(seg_off[e + 1]), cap);
+  const int nv = H / 8;
+  const long long total = (r1 - r0) * nv;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    reinterpret_cast<uint4*>(buf + r0 * H)[i] = make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+}  // namespace ep
+
+namespace {
+void check_pairs(const torch::Tensor& tgt, const torch::Tensor& dst, int64_t P) {
+  TT_CHECK(tgt.scalar_type() == torch::kInt32 && dst.scalar_type() == torch::kInt32 && tgt.numel() == P &&
+               dst.numel() == P && tgt.is_contiguous() && dst.is_contiguous() && tgt.is_cuda() && dst.is_cuda(),
+           "ep: tgt/dst must be contiguous CUDA int32 [pairs]");
+}
+}  // namespace
+
+// counts int32 [E] -> row `rank` of the [world, E] matrix at heap offset dst_off on every rank.
+void ep_allgather_counts(int64_t gid, torch::Tensor counts, int64_t dst_off) {
+  TT_CHECK(counts.scalar_type() == torch::kInt32 && counts.is_cuda() && counts.is_contiguous(),
+           "ep_allgather_counts: counts must be CUDA int32");
+  const comm::PeerTable t = comm::group_table(gid);
+  const int64_t n = counts.numel();
+  TT_CHECK(dst_off % 16 == 0 && dst_off + t.world * n * 4 <= static_cast<int64_t>(comm::group_bytes(gid)),
+           "ep_allgather_counts: destination outside the heap");
+  const c10::cuda::CUDAGuard guard(counts.device());
+  const bool emu = comm::group_emulated(gid);
+  const uint64_t e = emu ? 0ull : comm::group_next_epoch(gid);
+  ep::allgather_kernel<<<1, 256, 0, cur_stream()>>>(t, counts.data_ptr<int>(), static_cast<int>(n),
+                                                    static_cast<size_t>(dst_off), e,
+                                                    device_status_ptr(counts.get_device()), comm::wait_timeout_ns());
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// Store pair rows into the owners' receive buffers (heap offset recv_off, cap rows of H
+// bf16), then wait until every peer finished its own scatter.  Backward mode (w given):
+// rows are w[pair] * x[pair / k] and dw[pair] = <x[pair / k], y_pairs[pair]>.
+void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torch::Tensor dst, int64_t recv_off,
+                int64_t cap, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> y_pairs,
+                c10::optional<torch::Tensor> dw) {
+  check_cuda_bf16(x, "x");
+  TT_CHECK(x.dim() == 2 && x.is_contiguous() && x.size(1) % 8 == 0 && x.size(1) <= 4096,
+           "ep_scatter: x must be contiguous [N, H], H % 8 == 0, H <= 4096");
+  const int64_t N = x.size(0), H = x.size(1), P = N * k;
+  check_pairs(tgt, dst, P);
+  const comm::PeerTable t = comm::group_table(gid);
+  TT_CHECK(recv_off % 256 == 0 && recv_off + cap * H * 2 <= static_cast<int64_t>(comm::group_bytes(gid)),
+           "ep_scatter: receive buffer outside the heap");
+  const bool bwd = w.has_value();
+  if (bwd) {
+    TT_CHECK(y_pairs.has_value() && dw.has_value(), "ep_scatter: backward needs y_pairs and dw");
+    TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == P && w->is_contiguous(), "ep_scatter: w fp32 [P]");
+    check_cuda_bf16(*y_pairs, "y_pairs");
+    TT_CHECK(y_pairs->numel() == P * H && y_pairs->is_contiguous(), "ep_scatter: y_pairs [P, H]");
+    TT_CHECK(dw->scalar_type() == torch::kFloat32 && dw->numel() == P, "ep_scatter: dw fp32 [P]");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int dev = x.get_device();
+  const bool emu = comm::group_emulated(gid);
+  const uint64_t e = emu ? 0ull : comm::group_next_epoch(gid);
+  const int grid = comm::grid_blocks(dev, std::max<int64_t>(1, P * 32), ep::kThreads);
+  int* st = device_status_ptr(dev);
+  const auto* xp = reinterpret_cast<const __nv_bfloat16*>(x.data_ptr());
+  if (!bwd) {
+    ep::scatter_kernel<0><<<grid, ep::kThreads, 0, cur_stream()>>>(
+        t, xp, static_cast<int>(P), static_cast<int>(k), static_cast<int>(H), tgt.data_ptr<int>(),
+        dst.data_ptr<int>(), cap, static_cast<size_t>(recv_off), nullptr, nullptr, nullptr, e, st);
+  } else {
+    ep::scatter_kernel<1><<<grid, ep::kThreads, 0, cur_stream()>>>(
+        t, xp, static_cast<int>(P), static_cast<int>(k), static_cast<int>(H), tgt.data_ptr<int>(),
+        dst.data_ptr<int>(), cap, static_cast<size_t>(recv_off), w->data_ptr<float>(),
+        reinterpret_cast<const __nv_bfloat16*>(y_pairs->data_ptr()), dw->data_ptr<float>(), e, st);
+  }
+  TT_CUDA_CHECK(cudaGetLastError());
+  if (!emu) comm::launch_peer_wait(t, e, st, cur_stream());  // every peer's scatter-done epoch
+}
+
+// out[tok] = sum_j w[tok*k+j] * owner(tgt).buffer[dst]  (heap offset y_off); y_save keeps the rows.
+void ep_pull_combine(int64_t gid, int64_t y_off, int64_t cap, torch::Tensor tgt, torch::Tensor dst, int64_t k,
+                     c10::optional<torch::Tensor> w, torch::Tensor out, c10::optional<torch::Tensor> y_save) {
+  check_cuda_bf16(out, "out");
+  TT_CHECK(out.dim() == 2 && out.is_contiguous() && out.size(1) % 8 == 0 && out.size(1) <= 4096,
+           "ep_pull_combine: out [N, H], H % 8 == 0, H <= 4096");
+  const int64_t N = out.size(0), H = out.size(1), P = N * k;
+  check_pairs(tgt, dst, P);
+  TT_CHECK(y_off % 256 == 0 && y_off + cap * H * 2 <= static_cast<int64_t>(comm::group_bytes(gid)),
+           "ep_pull_combine: source buffer outside the heap");
+  const float* wp = nullptr;
+  if (w.has_value()) {
+    TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == P && w->is_contiguous(),
+             "ep_pull_combine: w fp32 [P]");
+    wp = w->data_ptr<float>();
+  }
+  __nv_bfloat16* sp = nullptr;
+  if (y_save.has_value()) {
+    check_cuda_bf16(*y_save, "y_save");
+    TT_CHECK(y_save->numel() == P * H && y_save->is_contiguous(), "ep_pull_combine: y_save [P, H]");
+    sp = reinterpret_cast<__nv_bfloat16*>(y_save->data_ptr());
+  }
+  const comm::PeerTable t = comm::group_table(gid);
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int dev = out.get_device();
+  const int grid = comm::grid_blocks(dev, std::max<int64_t>(1, N * 32), ep::kThreads);
+  const int pl = static_cast<int>((H / 8 + 31) / 32);
+#define TT_PULL(PLV)                                                                                              \
+  ep::pull_combine_kernel<PLV><<<grid, ep::kThreads, 0, cur_stream()>>>(                                           \
+      t, static_cast<size_t>(y_off), static_cast<int>(N), static_cast<int>(k), static_cast<int>(H),              \
+      tgt.data_ptr<int>(), dst.data_ptr<int>(), cap, wp, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), sp, \
+      device_status_ptr(dev))
+  if (pl <= 2) TT_PULL(2);
+  else if (pl <= 4) TT_PULL(4);
+  else if (pl <= 8) TT_PULL(8);
+  else TT_PULL(16);
+#undef TT_PULL
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+void ep_zero_pad(torch::Tensor buf, torch::Tensor seg_off, torch::Tensor seg_cnt) {
+  check_cuda_bf16(buf, "buf");
+  TT_CHECK(buf.dim() == 2 && buf.is_contiguous() && buf.size(1) % 8 == 0, "ep_zero_pad: buf [rows, H]");
+  TT_CHECK(seg_off.scalar_type() == torch::kInt32 && seg_cnt.scalar_type() == torch::kInt32 &&
+               seg_off.numel() == seg_cnt.numel() + 1,
+           "ep_zero_pad: seg_off int32 [E+1], seg_cnt int32 [E]");
+  const int64_t E = seg_cnt.numel();
+  if (E == 0) return;
+  const c10::cuda::CUDAGuard guard(buf.device());
+  dim3 grid(16, static_cast<unsigned>(E));
+  ep::zero_pad_kernel<<<grid, 256, 0, cur_stream()>>>(reinterpret_cast<__nv_bfloat16*>(buf.data_ptr()),
+                                                      seg_off.data_ptr<int>(), seg_cnt.data_ptr<int>(),
+                                                      static_cast<int>(E), static_cast<int>(buf.size(1)),
+                                                      buf.size(0));
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace tt

@@ -38,6 +38,10 @@ class LayerPagedKVCache:
         self._free = list(range(total - 1, -1, -1))
         self.current_length = 0
         self.seq_lens = [0] * batch_size
+        # Device copy of the common length: the fused decode kernels read positions
+        # from it, so a decode step captured in a CUDA graph stays valid on replay.
+        self.len_dev = torch.zeros(1, dtype=torch.int32, device=device)
+        self._scratch = None  # (splits, o_part, ml_part) for decode attention
 
     def _ensure_pages(self, new_len: int) -> None:
         need = math.ceil(new_len / self.page_size)
@@ -53,6 +57,64 @@ class LayerPagedKVCache:
         if changed:
             self.page_table.copy_(torch.tensor(self._host_table, dtype=torch.int32))
 
+    def reserve(self, length: int) -> None:
+        """Map pages for positions [0, length) of every sequence now (no page is
+        allocated during later appends; required before capturing a decode graph)."""
+        if length > self.max_seq_len:
+            raise ValueError(f"KV cache overflow: requested sequence length {length}, max supported is "
+                             f"{self.max_seq_len}")
+        self._ensure_pages(length)
+
+    # ---------------------------------------------------------------- fused CUDA path
+    def append_rope(self, qkv: torch.Tensor, B: int, T: int, Hq: int, Hkv: int, D: int, theta: float) -> torch.Tensor:
+        """qkv [B*T, (Hq+2Hkv)*D] bf16 -> rotated q [B*T, Hq*D]; K (rotated) and V are
+        written into the pages at positions len + t (len read on the device).  Call
+        :meth:`advance` after the attention that reads them."""
+        from tinytron_b200.ops import _ext
+        from tinytron_b200.ops.rope import rope_tables
+
+        end = self.current_length + T
+        if end > self.max_seq_len:
+            raise ValueError(f"KV cache overflow: requested sequence length {end}, max supported is {self.max_seq_len}")
+        self._ensure_pages(end)
+        cos, sin = rope_tables(D, theta, self.max_seq_len, qkv.device)
+        q = torch.empty(B * T, Hq * D, dtype=torch.bfloat16, device=qkv.device)
+        _ext.load().decode_rope_append(qkv, B, T, Hq, Hkv, D, self.len_dev, 0, cos, sin, q, self.k_pages,
+                                       self.v_pages, self.page_table)
+        return q
+
+    def attend_decode(self, q: torch.Tensor, scale: float) -> torch.Tensor:
+        """One new token per sequence: q [B, Hq, D] (rotated, already appended) ->
+        attention over keys [0, len + 1) -> [B, Hq*D] bf16."""
+        from tinytron_b200.ops import _ext
+
+        C = _ext.load()
+        B, Hq, D = q.shape
+        if self._scratch is None or self._scratch[1].numel() < B * Hq * self._scratch[0] * D:
+            splits = int(C.decode_num_splits(self.max_seq_len))
+            self._scratch = (splits, torch.empty(B * Hq * splits * D, device=q.device),
+                             torch.empty(B * Hq * splits * 2, device=q.device))
+        splits, o_part, ml_part = self._scratch
+        out = torch.empty(B, Hq * D, dtype=torch.bfloat16, device=q.device)
+        C.decode_attention(q, self.k_pages, self.v_pages, self.page_table, self.len_dev, 1, splits, scale, o_part,
+                           ml_part, out)
+        return out
+
+    def advance(self, T: int) -> int:
+        """Commit T appended positions (host length and the device copy)."""
+        prev = self.current_length
+        self.current_length += T
+        self.seq_lens = [self.current_length] * self.batch_size
+        self.len_dev.add_(T)
+        return prev
+
+    def set_length(self, length: int) -> None:
+        """Host and device length := length (e.g. after CUDA-graph replays advanced the
+        device copy only)."""
+        self.current_length = length
+        self.seq_lens = [length] * self.batch_size
+        self.len_dev.fill_(length)
+
     def append(self, k: torch.Tensor, v: torch.Tensor) -> int:
         T = k.size(2)
         end = self.current_length + T
@@ -67,6 +129,7 @@ class LayerPagedKVCache:
         prev = self.current_length
         self.current_length = end
         self.seq_lens = [end] * self.batch_size
+        self.len_dev.fill_(end)
         return prev
 
     def gather_tokens(self, length: int | None = None):
@@ -87,6 +150,7 @@ class LayerPagedKVCache:
         self._host_table = [[-1] * self.pages_per_seq for _ in range(self.batch_size)]
         self._free = list(range(self.k_pages.size(0) - 1, -1, -1))
         self.current_length = 0
+        self.len_dev.zero_()
 
 
 class PagedKVCache:
@@ -122,6 +186,18 @@ class PagedKVCache:
     def contiguous(cls, model_config, batch_size: int, device, dtype, max_seq_len: int | None = None):
         L = max_seq_len or model_config.block_size
         return cls.from_model_config(model_config, batch_size, L, device, dtype, max_seq_len=L)
+
+    def reserve(self, length: int) -> None:
+        for c in self._layer_caches:
+            c.reserve(length)
+
+    def set_length(self, length: int) -> None:
+        for c in self._layer_caches:
+            c.set_length(length)
+
+    @property
+    def current_length(self) -> int:
+        return self._layer_caches[0].current_length if self._layer_caches else 0
 
     def get_layer_cache(self, layer_idx: int) -> LayerPagedKVCache:
         return self._layer_caches[layer_idx]

@@ -7,7 +7,12 @@ Differences that matter for speed:
   * the EOS stop test is evaluated on the device and read back every
     ``eos_check_interval`` steps; the returned sequences are cut at the exact step
     where every sequence had produced EOS, so the output equals the per-step check;
-  * with SEP > 1, SEP rank 0 samples and broadcasts the tokens (as the reference).
+  * with SEP > 1, SEP rank 0 samples and broadcasts the tokens (as the reference);
+  * on CUDA with the paged (or contiguous) cache, pages for the whole generation are
+    mapped up front and one decode step (embedding -> every layer's fused RoPE/append
+    + split-KV attention -> LM head) is captured in a CUDA graph and replayed, so a
+    decode step costs one graph launch instead of hundreds of kernel launches from
+    Python; with SEP > 1 the row-parallel all-reduces run on a symmetric heap.
 """
 from __future__ import annotations
 
@@ -28,7 +33,7 @@ from .sampler import sample_next_token, sample_next_token_with_log_prob
 class InferenceEngine:
     def __init__(self, model_config, checkpoint_path: str | None = None, device: str = "cuda",
                  dtype: torch.dtype = torch.bfloat16, use_paged_kv_cache: bool = True, kv_cache_page_size: int = 128,
-                 eos_check_interval: int = 8):
+                 eos_check_interval: int = 8, use_cuda_graph: bool = True):
         self.device = torch.device(device)
         if self.device.type == "cuda":
             if self.device.index is None:
@@ -43,6 +48,41 @@ class InferenceEngine:
             self.model.load_state_dict(load_model_state_dict_for_inference(checkpoint_path, model_config))
         self.model.eval()
         self.dtype = dtype
+        self.use_cuda_graph = use_cuda_graph and self.device.type == "cuda"
+        self._graph = None
+
+    def _graph_ok(self) -> bool:
+        """A decode step is capturable when no layer synchronises with the host: the MoE
+        head-parallel inference path (SEP > 1) selects tokens with nonzero()."""
+        if not self.use_cuda_graph:
+            return False
+        sep = parallel_state.get_sep_world_size() if dist.is_initialized() else 1
+        return not (self.model_config.use_moe and sep > 1)
+
+    def _enable_heap_all_reduce(self, B: int, T: int) -> None:
+        sep = self._sep()
+        if sep is None or self.device.type != "cuda":
+            return
+        from tinytron_b200.parallel.symm import enable_row_parallel_all_reduce, same_host
+
+        if same_host(sep[0]):
+            enable_row_parallel_all_reduce(sep[0], B * T * self.model_config.hidden_size, self.device)
+
+    def _capture_decode(self, cache, B: int):
+        """Capture one decode step at the cache's current length; returns
+        (graph, static token input [B, 1], static logits [B, 1, V])."""
+        L = cache.current_length
+        static_tok = torch.zeros(B, 1, dtype=torch.long, device=self.device)
+        # one eager warm-up step outside the graph (allocations, lazy tables), then rewind
+        self.model._forward_cached(static_tok, cache, True, L, last_only=True)
+        cache.set_length(L)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            static_logits, _ = self.model._forward_cached(static_tok, cache, True, L, last_only=True)
+        cache.set_length(L)  # capture advanced the host length without running anything
+        torch.cuda.synchronize()
+        return g, static_tok, static_logits
 
     # ------------------------------------------------------------------ SEP-synced sampling
     def _sep(self):
@@ -97,6 +137,10 @@ class InferenceEngine:
         tokens[:, :P] = prompt
         cache = self.new_cache(B, max_seq_len=total)
         cuda = self.device.type == "cuda"
+        if cuda:
+            cache.reserve(total)
+            self._enable_heap_all_reduce(B, P)
+        graph = None
         sync = torch.cuda.synchronize if cuda else (lambda *a: None)
         logp_steps = []
         finished = torch.zeros(B, dtype=torch.bool, device=self.device)
@@ -129,7 +173,18 @@ class InferenceEngine:
                         break
             if i == max_new_tokens - 1:
                 break
-            logits, cache = self.model._forward_cached(nxt.unsqueeze(-1), cache, True, cur - 1, last_only=True)
+            if graph is None and cuda and self._graph_ok() and max_new_tokens - i > 2:
+                graph = self._capture_decode(cache, B)
+            if graph is not None:
+                g, static_tok, static_logits = graph
+                static_tok.copy_(nxt.unsqueeze(-1))
+                g.replay()
+                for c in cache._layer_caches:  # the graph advanced the device lengths
+                    c.current_length += 1
+                    c.seq_lens = [c.current_length] * c.batch_size
+                logits = static_logits
+            else:
+                logits, cache = self.model._forward_cached(nxt.unsqueeze(-1), cache, True, cur - 1, last_only=True)
         sync()
         t2 = time.perf_counter()
         if stop_at is not None:

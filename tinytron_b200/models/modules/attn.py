@@ -157,6 +157,8 @@ class Attention(nn.Module):
         k = qkv[:, :, hq_l:hq_l + hkv_l].transpose(1, 2)
         v = qkv[:, :, hq_l + hkv_l:].transpose(1, 2)
         G = self.num_attention_heads // self.num_key_value_heads
+        if self._fused_cache_ok(x, past_kv, position_offset, q0, k0, hq_l, hkv_l, G, sp):
+            return self._forward_cached_fused(qkv, past_kv, B, T, hq_l, hkv_l, q0, q1, sp, sp_group, use_cache)
         if sp > 1 and not self.inference_shard_qkv:
             true_map = [(q0 + i) // G - k0 for i in range(hq_l)]
             ratio = hq_l // hkv_l if hq_l % hkv_l == 0 else 0
@@ -187,6 +189,58 @@ class Attention(nn.Module):
         else:
             y = ops.linear(y, self.c_proj.weight)
         return y, (new_kv if use_cache else None)
+
+    # ------------------------------------------------------------------ fused CUDA cache path
+    def _fused_cache_ok(self, x, past_kv, position_offset, q0, k0, hq_l, hkv_l, G, sp) -> bool:
+        """Paged cache on CUDA whose q heads map uniformly onto its kv heads (no
+        expansion) and whose length equals the requested position."""
+        if not (x.is_cuda and _is_paged_kv_cache(past_kv) and self.head_dim in (64, 128)):
+            return False
+        if position_offset != past_kv.current_length or hq_l % hkv_l or hq_l // hkv_l > 8:
+            return False
+        if sp > 1 and not self.inference_shard_qkv:
+            ratio = hq_l // hkv_l
+            if any((q0 + i) // G - k0 != i // ratio for i in range(hq_l)):
+                return False
+        return True
+
+    def _forward_cached_fused(self, qkv, past_kv, B, T, hq_l, hkv_l, q0, q1, sp, sp_group, use_cache):
+        """RoPE + paged append in one kernel; decode (T == 1) attends straight from the
+        pages (split-KV kernel); prefill attends over the new tokens with the flash
+        kernel.  Graph-capturable for T == 1 (positions come from the cache's device
+        length)."""
+        from tinytron_b200.ops import _ext
+        from tinytron_b200.ops.functional import attention_fwd_only
+        from tinytron_b200.ops.rope import rope_tables
+
+        hd = self.head_dim
+        qkv2 = qkv.reshape(B * T, (hq_l + 2 * hkv_l) * hd)
+        past_len = past_kv.current_length
+        q = past_kv.append_rope(qkv2, B, T, hq_l, hkv_l, hd, self.rope_theta)
+        if T == 1:
+            y = past_kv.attend_decode(q.view(B, hq_l, hd), 1.0 / math.sqrt(hd)).view(B, 1, hq_l * hd)
+        elif past_len == 0:
+            cos, sin = rope_tables(hd, self.rope_theta, past_kv.max_seq_len, qkv.device)
+            qkv_r = qkv2.contiguous().clone()
+            _ext.load().rope_inplace(qkv_r, cos, sin, T, 0, hq_l + hkv_l, hd, False)
+            o, _ = attention_fwd_only(qkv_r, qkv_r, qkv_r, 0, hq_l * hd, (hq_l + hkv_l) * hd, B, T, T, hq_l, hkv_l,
+                                      hd, True, 0)
+            y = o.view(B, T, hq_l * hd)
+        else:
+            k_all, v_all = past_kv.gather_tokens(past_len + T)  # [B, L, Hkv, D], includes the new tokens
+            L = past_len + T
+            o, _ = attention_fwd_only(q, k_all.reshape(B * L, hkv_l * hd).contiguous(),
+                                      v_all.reshape(B * L, hkv_l * hd).contiguous(), 0, 0, 0, B, T, L, hq_l, hkv_l,
+                                      hd, True, past_len)
+            y = o.view(B, T, hq_l * hd)
+        past_kv.advance(T)
+        if sp > 1:
+            from tinytron_b200.parallel.symm import row_parallel_all_reduce
+
+            y = row_parallel_all_reduce(ops.linear(y, self.c_proj.weight[:, q0 * hd:q1 * hd]), sp_group)
+        else:
+            y = ops.linear(y, self.c_proj.weight)
+        return y, (past_kv if use_cache else None)
 
     def _cached_attention(self, q, k_all, v_all, past_len, hq_l, hkv_l):
         B, _, T, hd = q.shape

@@ -74,6 +74,9 @@ class MoE(nn.Module):
         self.router = nn.Linear(self.hidden_size, self.num_experts, bias=False, device=device)
         _, self.ep_size, ep_rank = _ep_context()
         assert self.num_experts % self.ep_size == 0
+        if torch.device(device).type == "cuda" and self.num_experts % 8:
+            # router logits rows must be 16-byte aligned for the TMA-fed GEMM epilogue
+            raise ValueError(f"num_experts ({self.num_experts}) must be a multiple of 8 on CUDA")
         self.num_local_experts = self.num_experts // self.ep_size
         E, I, H = self.num_local_experts, self.intermediate_size, self.hidden_size
         self.experts_gate_weights = nn.Parameter(torch.empty(E, I, H, device=device))
@@ -149,8 +152,9 @@ class MoE(nn.Module):
             out = self._apply_local_experts(flat_x[tok], sel.reshape(-1)[idx])
             partial = partial.index_put((tok,), (out.float() * weights.reshape(-1)[idx, None]).to(partial.dtype),
                                         accumulate=True)
-        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=ep_group)
-        return partial.reshape(B, T, D)
+        from tinytron_b200.parallel.symm import row_parallel_all_reduce
+
+        return row_parallel_all_reduce(partial, ep_group).reshape(B, T, D)
 
     def forward(self, x: torch.Tensor, use_cache: bool = False):
         B, T, D = x.shape
@@ -163,6 +167,15 @@ class MoE(nn.Module):
         if ep == 1 and x.is_cuda:  # routing, layout, grouped GEMMs and the weighted sum all on device
             y = ops.moe_experts(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
                                 self.experts_down_weights)
+            return y.view(B, T, D), gate_logits.view(B, T, -1)
+        if ep > 1 and x.is_cuda and os.environ.get("TT_NATIVE_COMM", "1") != "0":
+            # dispatch/combine by NVLink peer stores/loads around the grouped GEMMs
+            from tinytron_b200.parallel.ep_comm import ep_moe
+
+            y = ep_moe(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
+                       self.experts_down_weights, ep_group)
+            if self.training:
+                y = y + self._zero_expert_weight_dependency().to(y.dtype)
             return y.view(B, T, D), gate_logits.view(B, T, -1)
         rep_x = flat_x.repeat_interleave(self.top_k, dim=0)
         exp_ids = sel.reshape(-1).long()

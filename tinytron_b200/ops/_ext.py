@@ -28,6 +28,7 @@ SOURCES = [
     "attn/attn_bwd.cu",
     "attn/decode.cu",
     "moe/moe.cu",
+    "moe/ep.cu",
 ]
 
 CUDA_FLAGS = [

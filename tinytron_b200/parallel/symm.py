@@ -167,3 +167,67 @@ class SymmetricHeap:
         if not self._closed:
             _C().comm_destroy(self.gid)
             self._closed = True
+
+
+# ---------------------------------------------------------------------------- row-parallel all-reduce
+class RowParallelAllReduce:
+    """Inference row-parallel all-reduce over a SEP group on a symmetric heap (replaces
+    the reference's ``dist.all_reduce`` of c_proj / MoE partial outputs,
+    ``model/modules/attn.py:364``, ``mlp.py:221``).  Two heap slots alternate, which
+    is what makes one barrier per call enough: a rank rewrites a slot only after
+    every peer has started the next all-reduce, i.e. finished reading that slot."""
+
+    def __init__(self, group, max_numel: int, device=None):
+        self.max_numel = int(max_numel)
+        self.heap = SymmetricHeap.create(SymmetricHeap.bytes_needed((max_numel, torch.bfloat16),
+                                                                    (max_numel, torch.bfloat16)), group, device)
+        self.slots = [self.heap.alloc(max_numel, torch.bfloat16), self.heap.alloc(max_numel, torch.bfloat16)]
+        self.i = 0
+
+    def __call__(self, y: torch.Tensor) -> torch.Tensor | None:
+        n = y.numel()
+        if y.dtype != torch.bfloat16 or n > self.max_numel or not y.is_cuda:
+            return None
+        slot = self.slots[self.i][:n]
+        self.i ^= 1
+        slot.copy_(y.reshape(-1))
+        out = torch.empty_like(y)
+        self.heap.all_reduce(slot, out.view(-1))
+        return out
+
+    def close(self):
+        self.heap.close()
+
+
+_ROW_AR: dict = {}
+
+
+def enable_row_parallel_all_reduce(group, max_numel: int, device=None) -> RowParallelAllReduce:
+    """Collective over ``group``: route :func:`row_parallel_all_reduce` on this group
+    through a symmetric heap of ``max_numel`` bf16 elements per slot."""
+    key = id(group)
+    ar = _ROW_AR.get(key)
+    if ar is None or ar.max_numel < max_numel:
+        if ar is not None:
+            ar.close()
+        ar = RowParallelAllReduce(group, max_numel, device)
+        _ROW_AR[key] = ar
+    return ar
+
+
+def disable_row_parallel_all_reduce(group) -> None:
+    ar = _ROW_AR.pop(id(group), None)
+    if ar is not None:
+        ar.close()
+
+
+def row_parallel_all_reduce(y: torch.Tensor, group) -> torch.Tensor:
+    """SUM over ``group``: the symmetric-heap kernel when enabled for the group (and y
+    fits), else NCCL in place."""
+    ar = _ROW_AR.get(id(group))
+    if ar is not None:
+        out = ar(y)
+        if out is not None:
+            return out
+    dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
