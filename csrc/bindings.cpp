@@ -76,7 +76,7 @@ void comm_set_timeout(double seconds);
 torch::Tensor comm_view(int64_t gid, int64_t offset_bytes, std::vector<int64_t> shape, int64_t dtype_code);
 int64_t comm_user_offset();
 int64_t comm_heap_base(int64_t gid);
-void comm_barrier(int64_t gid);
+void comm_barrier(int64_t gid, bool signal);
 void comm_all_reduce(int64_t gid, int64_t in_offset, torch::Tensor out, c10::optional<torch::Tensor> residual);
 void comm_reduce_scatter_sumsq(int64_t gid, int64_t grad_offset, int64_t lo, int64_t hi, int64_t split, double scale);
 void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset, c10::optional<torch::Tensor> p16,
@@ -152,7 +152,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_view", &tt::comm::comm_view, "tensor view into the local heap");
   m.def("comm_user_offset", &tt::comm::comm_user_offset, "first byte of the heap's user region");
   m.def("comm_heap_base", &tt::comm::comm_heap_base, "device address of the local heap");
-  m.def("comm_barrier", &tt::comm::comm_barrier, "device-side barrier over the group (bounded wait)");
+  m.def("comm_barrier", &tt::comm::comm_barrier, "device-side barrier over the group (bounded wait)",
+        py::arg("gid"), py::arg("signal") = true);
   m.def("comm_all_reduce", &tt::comm::comm_all_reduce, "one-shot all-reduce of a heap region (+ residual)",
         py::arg("gid"), py::arg("in_offset"), py::arg("out"), py::arg("residual") = py::none());
   m.def("comm_reduce_scatter_sumsq", &tt::comm::comm_reduce_scatter_sumsq,

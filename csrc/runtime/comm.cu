@@ -382,12 +382,14 @@ int64_t comm_heap_base(int64_t gid) { return static_cast<int64_t>(reinterpret_ca
 
 static uint64_t next_epoch(Group& g) { return ++g.epoch; }
 
-void comm_barrier(int64_t gid) {
+// signal == false leaves this rank's flag unset (host-side fault injection: the
+// peers' bounded waits then expire and record kTimeoutPeer).
+void comm_barrier(int64_t gid, bool signal) {
   Group& g = get(gid);
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
   if (g.emulated) return;
   const uint64_t e = next_epoch(g);
-  barrier_kernel<<<1, 32, 0, cur_stream()>>>(table(g), e, device_status_ptr(g.device), timeout_ns(), 1);
+  barrier_kernel<<<1, 32, 0, cur_stream()>>>(table(g), e, device_status_ptr(g.device), timeout_ns(), signal ? 1 : 0);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -129,7 +129,12 @@ class SymmetricHeap:
 
     # ------------------------------------------------------------------ collectives
     def barrier(self) -> None:
-        _C().comm_barrier(self.gid)
+        from tinytron_b200.utils.watchdog import fault_active
+
+        # TT_FAULT_INJECT=skip_signal@R: rank R waits without signalling, so its peers'
+        # bounded device waits expire with a status code (host-side injection).
+        signal = not fault_active("skip_signal", dist.get_rank() if dist.is_initialized() else self.rank)
+        _C().comm_barrier(self.gid, signal)
 
     def all_reduce(self, src: torch.Tensor, out: torch.Tensor | None = None,
                    residual: torch.Tensor | None = None) -> torch.Tensor:

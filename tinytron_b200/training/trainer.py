@@ -367,7 +367,32 @@ class Trainer:
         return batch
 
     # ------------------------------------------------------------------ loop
+    def _init_heartbeat(self):
+        """Heartbeat watchdog (``TT_HEARTBEAT_TIMEOUT_S`` > 0 and more than one rank):
+        a silent or failed peer is reported between steps as PeerFailure."""
+        timeout = float(os.environ.get("TT_HEARTBEAT_TIMEOUT_S", "0") or 0)
+        if timeout <= 0 or not dist.is_initialized() or dist.get_world_size() <= 1:
+            return None
+        from tinytron_b200.utils.watchdog import Heartbeat
+
+        return Heartbeat(dist.get_rank(), dist.get_world_size(), interval=min(1.0, timeout / 4), timeout=timeout)
+
     def train(self):
+        self.heartbeat = self._init_heartbeat()
+        try:
+            self._train_loop()
+        except BaseException:
+            if self.heartbeat is not None:
+                self.heartbeat.close(exit_code=1)
+                self.heartbeat = None
+            raise
+        if self.heartbeat is not None:
+            self.heartbeat.close(exit_code=0)
+            self.heartbeat = None
+
+    def _train_loop(self):
+        from tinytron_b200.utils.watchdog import fault_point
+
         self.results = {}
         self._resume_from_checkpoint()
         self._init_profiler(self.config)
@@ -376,6 +401,9 @@ class Trainer:
         cfg = self.config
         max_steps = self.training_info["max_steps"]
         for step in range(self.start_step, max_steps):
+            fault_point("exit", self.rank, step)  # host-side fault injection (tests)
+            if self.heartbeat is not None:
+                self.heartbeat.check()  # before this step launches any kernel or collective
             self.one_step_results = {}
             t0 = time.time()
             last = step == max_steps - 1
@@ -417,6 +445,10 @@ class Trainer:
         self.close()
 
     def close(self):
+        hb = getattr(self, "heartbeat", None)
+        if hb is not None:  # clean exit published before the store may go away
+            hb.close(exit_code=0)
+            self.heartbeat = None
         if self._owns_pg and dist.is_initialized():
             dist.barrier()
             dist.destroy_process_group()
