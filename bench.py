@@ -32,6 +32,25 @@ MODEL_FLAGS = ["--num_layer", "24", "--hidden_size", "2048", "--num_attention_he
 MICRO_BATCH, SEQ, GA = 4, 4096, 4
 METRIC = "train_tokens_per_sec_per_box"
 MODEL_NAME = "dense-1.3B (24L d2048 16q/4kv I5504 V50304)"
+PRESET = "b200-dense-1.3b"
+SEP = 1
+
+# MoE GPT, SEP = #GPUs + ZeRO-1, 16L d2048 16q/4kv, 64 experts x SwiGLU 1408,
+# top-8, aux 0.01, seq 4096, micro-batch 2 sequences per GPU (reference launcher convention
+# --batch_size = 2 x SEP: each rank holds 2 x SEP sequences x 4096/SEP tokens = 8192 tokens).
+MOE_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_heads", "16",
+             "--num_key_value_heads", "4", "--intermediate_size", "5504", "--vocab_size", "50304",
+             "--block_size", "4096", "--init_std", "0.02", "--use_moe", "--num_experts", "64",
+             "--num_experts_per_tok", "8", "--moe_intermediate_size", "1408", "--moe_balance_loss_weight", "0.01"]
+
+
+def _select_config(name: str, n_gpus: int) -> None:
+    global MODEL_FLAGS, MICRO_BATCH, GA, MODEL_NAME, PRESET, SEP
+    if name == "moe":
+        MODEL_FLAGS = MOE_FLAGS
+        MICRO_BATCH, GA, SEP = 2 * n_gpus, 4, n_gpus
+        MODEL_NAME = "moe-16L (d2048 16q/4kv, 64 experts x 1408 top-8, V50304)"
+        PRESET = "b200-moe-16x64"
 
 
 def _free_port() -> int:
@@ -43,11 +62,12 @@ def _free_port() -> int:
 
 
 def _train_argv(n_gpus: int, steps: int, log_dir: str) -> list[str]:
-    return ["--use_mock_data", "--deterministic", "--mock_data_num_samples", str(MICRO_BATCH * GA * n_gpus * (steps + 2)),
-            "--log_dir", log_dir, "--total_batch_size", str(MICRO_BATCH * SEQ * GA * n_gpus),
+    dp = n_gpus // SEP
+    return ["--use_mock_data", "--deterministic", "--mock_data_num_samples", str(MICRO_BATCH * GA * dp * (steps + 2)),
+            "--log_dir", log_dir, "--total_batch_size", str(MICRO_BATCH * SEQ * GA * dp),
             "--batch_size", str(MICRO_BATCH), "--seq_len", str(SEQ), "--max_steps", str(steps + 1),
             "--warmup_steps", "1", "--max_lr", "3e-4", "--min_lr", "3e-5", "--weight_decay", "0.1",
-            "--sep_size", "1", "--use_distributed_optimizer", *MODEL_FLAGS]
+            "--sep_size", str(SEP), "--use_distributed_optimizer", *MODEL_FLAGS]
 
 
 class ClockSampler:
@@ -209,7 +229,12 @@ def run(args, impl: str):
         cfg = build_config(parse_args(argv))
         trainer = Trainer(cfg)
         trainer._init_profiler(cfg)  # sets profiler_record_fn (train() normally does this)
-        # the reference's padded-bmm MoE path is forced only for MoE configs; dense here.
+        if args.config == "moe":
+            # The reference's grouped_mm path needs moe_intermediate_size == hidden_size; with 1408 != 2048
+            # it raises, so its own padded-bmm path is selected (attribute flip, no source edit).
+            for m in trainer.raw_model.modules():
+                if hasattr(m, "grouped_gemm_supported"):
+                    m.grouped_gemm_supported = False
         own_marker = ""
     else:
         sys.path.insert(0, ROOT)
@@ -225,8 +250,9 @@ def run(args, impl: str):
     ga = trainer.training_info["grad_accum_steps"]
     assert ga == GA, ga
 
-    # ---- device-resident inputs (the `value` measurement)
-    dev_batches = [{k: v.cuda() for k, v in b.items()} for b in _make_device_batches(50304, ga, seed=1234 + rank)]
+    # ---- device-resident inputs (the `value` measurement); SEP peers share their samples
+    dp_rank = rank // SEP
+    dev_batches = [{k: v.cuda() for k, v in b.items()} for b in _make_device_batches(50304, ga, seed=1234 + dp_rank)]
     state = {"i": 0}
 
     def next_dev():
@@ -234,7 +260,8 @@ def run(args, impl: str):
         state["i"] += 1
         return b
 
-    host_batches = [{k: v.pin_memory() for k, v in b.items()} for b in _make_device_batches(50304, ga, seed=99 + rank)]
+    host_batches = [{k: v.pin_memory() for k, v in b.items()}
+                    for b in _make_device_batches(50304, ga, seed=99 + dp_rank)]
 
     def next_host():
         b = host_batches[state["i"] % ga]
@@ -268,14 +295,16 @@ def run(args, impl: str):
     trainer._next_train_batch = next_dev
     launches, all_kernels = _count_launches(step_fn, args.warmup + 2 * args.steps, own_marker)
 
-    tokens_per_step = MICRO_BATCH * SEQ * ga * world
+    dp = world // SEP
+    tokens_per_step = MICRO_BATCH * SEQ * ga * dp
     value = tokens_per_step / (ms / args.steps / 1e3)
     e2e_value = tokens_per_step / (e2e_ms / args.steps / 1e3)
     sys.path.insert(0, ROOT)
     from tinytron_b200.models.presets import get_preset
     from tinytron_b200.utils.flops import training_flops_per_microstep
 
-    flops_step = training_flops_per_microstep(get_preset("b200-dense-1.3b"), MICRO_BATCH, SEQ) * ga * world
+    # per rank: MICRO_BATCH sequences x SEQ/SEP tokens, attention over the full SEQ
+    flops_step = training_flops_per_microstep(get_preset(PRESET), MICRO_BATCH, SEQ // SEP, sp=SEP) * ga * world
     achieved = flops_step / (ms / args.steps / 1e3)
     peaks = {}
     try:
@@ -296,8 +325,9 @@ def run(args, impl: str):
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic uniform random tokens (seeded), random-init weights N(0,0.02)",
-        "config": {"model": MODEL_NAME, "global_batch": MICRO_BATCH * GA * world, "seq_len": SEQ,
-                   "micro_batch": MICRO_BATCH, "grad_accum": GA, "parallelism": f"dp{world}" + ("+zero1"),
+        "config": {"model": MODEL_NAME, "global_batch": MICRO_BATCH * GA * dp, "seq_len": SEQ,
+                   "micro_batch": MICRO_BATCH, "grad_accum": GA,
+                   "parallelism": (f"sep{SEP}+dp{dp}" if SEP > 1 else f"dp{world}") + "+zero1",
                    "optimizer": "AdamW (ZeRO-1)", "l2": "inputs larger than L2 (no flush needed)"},
         "mfu": round(achieved / (world * 2.25e15), 4),
         "mfu_of_measured_cublas_peak": round(achieved / (world * measured_peak), 4),
@@ -323,6 +353,80 @@ def run(args, impl: str):
         dist.destroy_process_group()
 
 
+def run_decode(args, impl: str):
+    """KV-cache inference of the config-3 MoE model (random init),
+    batch 32 x 1024-token prompts, greedy decode; device-timed prefill and decode."""
+    import torch
+    import torch.distributed as dist
+
+    rank, local, world = _setup_dist(args.gpus)
+    B, P, NEW = 32, 1024, args.decode_steps
+    flags = {"num_layer": 16, "hidden_size": 2048, "num_attention_heads": 16, "num_key_value_heads": 4,
+             "intermediate_size": 5504, "vocab_size": 50304, "block_size": 4096, "init_std": 0.02, "use_moe": True,
+             "num_experts": 64, "num_experts_per_tok": 8, "moe_intermediate_size": 1408}
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    if impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        from tinytron.distributed import parallel_state
+        from tinytron.inference import InferenceEngine
+        from tinytron.model.config import ModelConfig
+        from tinytron.training.config import ParallelConfig
+    else:
+        sys.path.insert(0, ROOT)
+        from tinytron_b200.inference import InferenceEngine
+        from tinytron_b200.models.config import ModelConfig
+        from tinytron_b200.parallel import parallel_state
+        from tinytron_b200.training.config import ParallelConfig
+    if world > 1:
+        parallel_state.initialize_model_parallel(ParallelConfig(sep_size=world))
+    cfg = ModelConfig(**flags)
+    kw = dict(model_config=cfg, device=f"cuda:{local}", dtype=torch.bfloat16, use_paged_kv_cache=args.page_size > 0,
+              kv_cache_page_size=max(1, args.page_size))
+    eng = InferenceEngine(**kw)
+    if impl == "reference":
+        for m in eng.model.modules():
+            if hasattr(m, "grouped_gemm_supported"):
+                m.grouped_gemm_supported = False
+    g = torch.Generator().manual_seed(0)
+    prompt = torch.randint(0, cfg.vocab_size, (B, P), generator=g)
+    gen_kw = dict(temperature=1.0, top_k=1, return_stats=True)  # greedy
+    eng.generate(prompt, 8, **gen_kw)  # warm-up (allocations, graph capture paths)
+    for _ in range(2):
+        eng.generate(prompt, 8, **gen_kw)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(rank == 0 and not args.no_clocks) as clk:
+        s.record()
+        _, stats = eng.generate(prompt, NEW, **gen_kw)
+        e.record()
+        torch.cuda.synchronize()
+    total_ms = _max_over_ranks(s.elapsed_time(e))
+    dec_ms = _max_over_ranks(stats.get("decode_ms_device", stats["decode_tokens"] / max(
+        stats["decode_tokens_per_sec"], 1e-9) * 1e3))
+    pre_ms = _max_over_ranks(stats.get("prefill_ms_device", stats["prefill_tokens"] / max(
+        stats["prefill_tokens_per_sec"], 1e-9) * 1e3))
+    value = B * NEW / (total_ms / 1e3)
+    out = {"metric": "decode_tokens_per_sec_per_box", "value": round(B * stats["decode_tokens"] / B / (dec_ms / 1e3), 1),
+           "unit": "tokens/s", "n_gpus": world, "steps": NEW, "warmup": 3, "ms_per_step": round(dec_ms / NEW, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic uniform prompts (seeded), random-init weights N(0,0.02)",
+           "config": {"model": "moe-16L (d2048 16q/4kv, 64 experts x 1408 top-8)", "batch": B, "prompt_len": P,
+                      "decode_steps": NEW, "kv_cache": f"paged page={args.page_size}" if args.page_size > 0 else
+                      "contiguous", "parallelism": f"sep{world}" if world > 1 else "1 GPU"},
+           "prefill_tokens_per_sec": round(B * P / (pre_ms / 1e3), 1),
+           "e2e": {"value": round(value, 1), "unit": "generated tokens/s (prefill + decode, device-timed)",
+                   "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8 * B},
+           "clocks": clk.summary(world)}
+    if impl == "reference":
+        out["impl"] = "reference"
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -332,9 +436,17 @@ def main():
     ap.add_argument("--ref-eager", action="store_true",
                     help="reference arm: run eager instead of --use_compile (compile is the faster of the two)")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--config", choices=["dense", "moe", "decode"], default="dense",
+                    help="dense: BASELINE config 2 (headline); moe: config 3 (SEP = #GPUs); decode: config 5")
+    ap.add_argument("--decode-steps", type=int, default=512)
+    ap.add_argument("--page-size", type=int, default=16, help="decode: KV page size (0 = contiguous cache)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config == "decode":
+        run_decode(args, args.impl)
+        return
+    _select_config(args.config, args.gpus)
     run(args, args.impl)
 
 

@@ -146,8 +146,13 @@ class InferenceEngine:
         finished = torch.zeros(B, dtype=torch.bool, device=self.device)
         all_done = []
         sync()
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)] if cuda else None
+        if ev:
+            ev[0].record()
         t0 = time.perf_counter()
         logits, cache = self.model._forward_cached(prompt, cache, True, 0, last_only=True)
+        if ev:
+            ev[1].record()
         sync()
         t1 = time.perf_counter()
         cur = P
@@ -185,6 +190,8 @@ class InferenceEngine:
                 logits = static_logits
             else:
                 logits, cache = self.model._forward_cached(nxt.unsqueeze(-1), cache, True, cur - 1, last_only=True)
+        if ev:
+            ev[2].record()
         sync()
         t2 = time.perf_counter()
         if stop_at is not None:
@@ -200,6 +207,11 @@ class InferenceEngine:
             extras.update({"prefill_tokens_per_sec": B * P / dt_p,
                            "decode_tokens_per_sec": (B * steps / dt_d) if steps else 0.0,
                            "prefill_tokens": float(B * P), "decode_tokens": float(B * steps)})
+            if ev:  # the same phases timed on the device (CUDA events on the generating stream)
+                dp_ms, dd_ms = ev[0].elapsed_time(ev[1]), ev[1].elapsed_time(ev[2])
+                extras.update({"prefill_ms_device": dp_ms, "decode_ms_device": dd_ms,
+                               "prefill_tokens_per_sec_device": B * P / max(dp_ms, 1e-6) * 1e3,
+                               "decode_tokens_per_sec_device": (B * steps / max(dd_ms, 1e-6) * 1e3) if steps else 0.0})
         if return_logprobs:
             lp = torch.stack(logp_steps, 1) if logp_steps else torch.empty(B, 0, device=self.device)
             extras.update({"prompt_len": float(P), "decode_steps": float(steps), "token_log_probs": lp,
