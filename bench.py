@@ -224,8 +224,11 @@ def run(args, impl: str):
                 print(json.dumps({"impl": "reference", "unavailable": f"reference import failed: {exc}"}))
             return
         argv = _train_argv(world, total_steps, log_dir) + ["--debug"]
-        if not args.ref_eager:
-            argv.append("--use_compile")  # measured faster than eager on B200 (68.6K vs 47.3K tok/s, 1 GPU)
+        if not args.ref_eager and args.config == "dense":
+            # measured faster than eager on B200 (68.6K vs 47.3K tok/s, 1 GPU, dense); with MoE the
+            # data-dependent expert shapes exceed dynamo's recompile limit and the step fails, so the
+            # MoE reference runs eager
+            argv.append("--use_compile")
         cfg = build_config(parse_args(argv))
         trainer = Trainer(cfg)
         trainer._init_profiler(cfg)  # sets profiler_record_fn (train() normally does this)
@@ -343,7 +346,7 @@ def run(args, impl: str):
         out["impl"] = "reference"
         out.pop("gpu_launches")
         out["config"]["reference_flags"] = "mock data, deterministic, ZeRO-1, " + (
-            "eager" if args.ref_eager else "--use_compile")
+            "--use_compile" if "--use_compile" in argv else "eager")
     if rank == 0:
         print(json.dumps(out), flush=True)
     if hasattr(trainer, "close"):

@@ -84,6 +84,7 @@ void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset,
                           double beta2, double eps, double wd, int64_t step, double max_norm,
                           c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out);
 void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, int64_t lo, int64_t hi);
+void comm_all_to_all(int64_t gid, int64_t slot_offset, torch::Tensor out);
 int64_t comm_epoch(int64_t gid);
 void comm_destroy(int64_t gid);
 }  // namespace comm
@@ -161,6 +162,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_adamw_allgather", &tt::comm::comm_adamw_allgather,
         "ZeRO-1 clip + AdamW on the owned shard + fp32 all-gather by peer stores");
   m.def("comm_shadow_refresh", &tt::comm::comm_shadow_refresh, "wait for the all-gather; refresh bf16 shadow");
+  m.def("comm_all_to_all", &tt::comm::comm_all_to_all, "equal-split all-to-all of a heap slot by peer loads");
   m.def("comm_epoch", &tt::comm::comm_epoch);
   m.def("comm_destroy", &tt::comm::comm_destroy);
 }

@@ -37,6 +37,8 @@
 //                                       every peer's parameter buffer
 //   * shadow_refresh                    waits for the all-gather, rewrites the bf16
 //                                       shadow of the shards other ranks updated
+//   * all_to_all (equal split)          out[c] = rank c's chunk for this rank, by peer
+//                                       loads (Ulysses head<->sequence exchange)
 #include "runtime/comm_common.cuh"
 
 #include <atomic>
@@ -92,6 +94,24 @@ __global__ void allreduce_kernel(PeerTable t, size_t in_off, T* __restrict__ out
     for (int p = 0; p < t.world; ++p) acc += static_cast<float>(reinterpret_cast<const T*>(t.base[p] + in_off)[i]);
     if (residual != nullptr) acc += static_cast<float>(residual[i]);
     out[i] = static_cast<T>(acc);
+  }
+}
+
+// Equal-split all-to-all by peer loads: out[c] = peer_c.slot[my_rank] for every rank c
+// (chunk = chunk_bytes, a multiple of 16).  Each rank's slot holds its `world` outgoing
+// chunks; the start barrier makes every slot complete before anyone reads.
+__global__ void alltoall_kernel(PeerTable t, size_t slot_off, long long chunk_bytes, char* __restrict__ out,
+                                uint64_t e, int* status, uint64_t timeout_ns) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) signal_peers(t, e);
+  if (!block_wait_peers(t, e, status, timeout_ns)) return;
+  const long long nv = chunk_bytes / 16;
+  const long long total = nv * t.world;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
+    const int c = static_cast<int>(i / nv);
+    const long long v = i - c * nv;
+    const uint4* src = reinterpret_cast<const uint4*>(t.base[c] + slot_off + t.rank * chunk_bytes);
+    reinterpret_cast<uint4*>(out + c * chunk_bytes)[v] = src[v];
   }
 }
 
@@ -428,6 +448,26 @@ void comm_all_reduce(int64_t gid, int64_t in_offset, torch::Tensor out, c10::opt
         t, static_cast<size_t>(in_offset), out.data_ptr<float>(), reinterpret_cast<const float*>(res), n, e, st,
         timeout_ns());
   }
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// out (contiguous, world * chunk_bytes) <- chunk my_rank of every rank's slot at slot_offset.
+void comm_all_to_all(int64_t gid, int64_t slot_offset, torch::Tensor out) {
+  Group& g = get(gid);
+  TT_CHECK(out.is_cuda() && out.is_contiguous(), "comm_all_to_all: out must be contiguous CUDA");
+  const long long bytes = out.numel() * static_cast<long long>(out.element_size());
+  TT_CHECK(bytes % (16LL * g.world) == 0, "comm_all_to_all: chunk size must be a multiple of 16 bytes");
+  TT_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0, "comm_all_to_all: out must be 16-byte aligned");
+  TT_CHECK(slot_offset % 256 == 0 && slot_offset >= static_cast<int64_t>(kUserOff) &&
+               slot_offset + bytes <= static_cast<int64_t>(g.bytes),
+           "comm_all_to_all: slot outside the heap");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
+  const uint64_t e = g.emulated ? 0ull : next_epoch(g);
+  const int threads = 256;
+  const int grid = grid_for(g.device, std::max<long long>(1, bytes / 16), threads);
+  alltoall_kernel<<<grid, threads, 0, cur_stream()>>>(table(g), static_cast<size_t>(slot_offset), bytes / g.world,
+                                                      static_cast<char*>(out.data_ptr()), e,
+                                                      device_status_ptr(g.device), timeout_ns());
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

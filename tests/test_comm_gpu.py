@@ -110,6 +110,25 @@ def test_emulated_zero1_step(W):
         h.close()
 
 
+@pytest.mark.parametrize("W,n", [(2, 8), (4, 1024), (8, 4096)])
+def test_emulated_all_to_all(W, n):
+    from tinytron_b200.parallel.symm import SymmetricHeap
+
+    heaps = SymmetricHeap.create_emulated(W * n * 2 + 4096, W)
+    slots = []
+    for r, h in enumerate(heaps):
+        s = h.alloc((W, n), torch.bfloat16)
+        s.copy_(torch.arange(W * n, device="cuda").view(W, n).bfloat16() + 1000 * r)
+        slots.append(s)
+    outs = [h.all_to_all(s, torch.empty_like(s)) for h, s in zip(heaps, slots)]
+    torch.cuda.synchronize()
+    for me, o in enumerate(outs):
+        for c in range(W):
+            assert torch.equal(o[c], slots[c][me])
+    for h in heaps:
+        h.close()
+
+
 def test_peer_wait_gives_up_with_status():
     """A barrier whose peer never signals returns after the (short) bound with
     kTimeoutPeer in the status word; the context stays usable afterwards."""
@@ -176,6 +195,16 @@ def _two_rank_worker(rank, world, port, out_q):
         pr, _, _ = _ref_adamw(p0, gbar * coef, torch.zeros_like(p0), torch.zeros_like(p0), 1e-2, 0.9, 0.95, 1e-8, 0.1,
                               1)
         z_err = (data - pr).abs().max().item()
+        from tinytron_b200.parallel.symm import HeapAllToAll
+
+        a2a = HeapAllToAll(None)
+        x = torch.randn(world, 3, 64, device="cuda", generator=g).bfloat16()
+        slot = a2a.slot(x.shape, x.dtype)
+        slot.copy_(x)
+        ours_a2a = a2a.exchange(slot)
+        ref_a2a = torch.empty_like(x)
+        dist.all_to_all_single(ref_a2a, x.contiguous())
+        z_err = max(z_err, (ours_a2a.float() - ref_a2a.float()).abs().max().item())
         shadow_ok = bool(torch.equal(p16, data.bfloat16()))
         torch.cuda.synchronize()
         from tinytron_b200.ops import check_status

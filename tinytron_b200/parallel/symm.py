@@ -159,6 +159,11 @@ class SymmetricHeap:
                                   float(lr), float(betas[0]), float(betas[1]), float(eps), float(wd), int(step),
                                   float(max_norm), extra_sq, norm_out)
 
+    def all_to_all(self, slot: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """out[c] = chunk ``rank`` of rank c's ``slot`` (both [world, ...], equal chunks)."""
+        _C().comm_all_to_all(self.gid, self.offset_of(slot), out)
+        return out
+
     def shadow_refresh(self, data: torch.Tensor, p16: torch.Tensor, lo: int, hi: int) -> None:
         _C().comm_shadow_refresh(self.gid, self.offset_of(data), p16, int(lo), int(hi))
 
@@ -236,3 +241,58 @@ def row_parallel_all_reduce(y: torch.Tensor, group) -> torch.Tensor:
             return out
     dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
+
+
+# ---------------------------------------------------------------------------- all-to-all
+class HeapAllToAll:
+    """Equal-split all-to-all over a group on a symmetric heap (Ulysses head<->sequence
+    exchange; reference ``distributed/sequence_parallel/ulysses.py:7-22``).  The caller
+    writes its outgoing chunks into :meth:`slot` (e.g. ``torch.stack(..., out=slot)``)
+    and calls :meth:`exchange`.  Two slots alternate, so one start barrier per call
+    suffices (a slot is rewritten only after every peer started the next exchange)."""
+
+    def __init__(self, group, device=None):
+        self.group = group
+        self.device = device
+        self.heap = None
+        self.cap = 0
+        self.slots = None
+        self.i = 0
+
+    def _ensure(self, nbytes: int):
+        if self.heap is None or nbytes > self.cap:  # collective: same sizes on every rank
+            if self.heap is not None:
+                self.heap.close()
+            cap = max(nbytes, 1 << 20)
+            self.heap = SymmetricHeap.create(2 * ((cap + ALIGN - 1) // ALIGN * ALIGN), self.group, self.device)
+            self.slots = [self.heap.alloc(cap, torch.uint8, zero=False), self.heap.alloc(cap, torch.uint8, zero=False)]
+            self.cap = cap
+
+    def slot(self, shape, dtype) -> torch.Tensor:
+        numel = 1
+        for s in shape:
+            numel *= int(s)
+        nbytes = numel * torch.empty((), dtype=dtype).element_size()
+        self._ensure(nbytes)
+        return self.slots[self.i][:nbytes].view(dtype).view(tuple(shape))
+
+    def exchange(self, slot: torch.Tensor) -> torch.Tensor:
+        out = torch.empty_like(slot)
+        self.heap.all_to_all(slot, out)
+        self.i ^= 1
+        return out
+
+
+_A2A: dict = {}
+
+
+def enable_heap_all_to_all(group, device=None) -> HeapAllToAll:
+    a = _A2A.get(id(group))
+    if a is None:
+        a = HeapAllToAll(group, device)
+        _A2A[id(group)] = a
+    return a
+
+
+def heap_all_to_all_for(group) -> HeapAllToAll | None:
+    return _A2A.get(id(group))

@@ -15,21 +15,31 @@ import torch
 import torch.distributed as dist
 
 
+def _a2a(x: torch.Tensor, group) -> torch.Tensor:
+    """Equal-split all-to-all on dim 0: the symmetric-heap kernel (peer loads) when
+    enabled for the group and the chunks are 16-byte multiples, else NCCL."""
+    from .symm import heap_all_to_all_for
+
+    a = heap_all_to_all_for(group) if x.is_cuda else None
+    if a is not None and (x.numel() * x.element_size()) % (16 * x.shape[0]) == 0:
+        slot = a.slot(x.shape, x.dtype)
+        slot.copy_(x)
+        return a.exchange(slot)
+    x = x.contiguous()
+    out = torch.empty_like(x)
+    dist.all_to_all_single(out, x, group=group)
+    return out
+
+
 class UlyssesAllToAll(torch.autograd.Function):
     @staticmethod
     def forward(ctx, input_tensor, sp_group):
         ctx.sp_group = sp_group
-        x = input_tensor.contiguous()
-        out = torch.empty_like(x)
-        dist.all_to_all_single(out, x, group=sp_group)
-        return out
+        return _a2a(input_tensor, sp_group)
 
     @staticmethod
     def backward(ctx, grad_output):
-        g = grad_output.contiguous()
-        out = torch.empty_like(g)
-        dist.all_to_all_single(out, g, group=ctx.sp_group)
-        return out, None
+        return _a2a(grad_output, ctx.sp_group), None
 
 
 def ulysses_all_to_all(input_tensor: torch.Tensor, sp_group) -> torch.Tensor:

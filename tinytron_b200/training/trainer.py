@@ -150,6 +150,12 @@ class Trainer:
                 return SymmetricHeap.create(nbytes, group=self.dp_group, device=self.device)
         self.flat = FlatParams(model, pad_to_multiple=pad, with_bf16=self.device.type == "cuda",
                                heap_factory=heap_factory)
+        if (self.device.type == "cuda" and self.sp_world_size > 1 and os.environ.get("TT_NATIVE_COMM", "1") != "0"
+                and self.sp_world_size <= 8):
+            from tinytron_b200.parallel.symm import enable_heap_all_to_all, same_host
+
+            if same_host(self.sp_group):  # Ulysses exchanges by NVLink peer loads
+                enable_heap_all_to_all(self.sp_group, self.device)
 
     def _use_native_comm(self, config: Config) -> bool:
         """ZeRO-1 gradient/parameter sync over NVLink peer memory (tt_comm) instead of
