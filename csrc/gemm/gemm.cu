@@ -32,6 +32,9 @@
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
 
+#include <atomic>
+#include <cstdlib>
+
 namespace tt {
 namespace gemm {
 
@@ -146,6 +149,104 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&v)[N
   } else {
 #pragma unroll
     for (int i = 0; i < NV; ++i) v[i] = (i < n_valid) ? __bfloat162float(src[i]) : 0.0f;
+  }
+}
+
+// Epilogue of one 128-row accumulator slice: thread = one TMEM lane = one output row.
+// Drains BN fp32 columns from TMEM (t_row) and applies EPI; nb is the tile's column block.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, int nb, int row, bool row_ok,
+                                             float alpha) {
+  constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 32) {
+      uint32_t r[32];
+      tmem_ld32(t_row + c0, r);
+      tmem_ld_wait();
+      const int col0 = nb * BN + c0;
+      if (row_ok && col0 < p.N) {
+        const int nv = min(32, p.N - col0);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
+        if constexpr (EPI == EPI_BF16) {
+          store_bf16<32>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, v, nv);
+        } else {
+          float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
+          if (nv == 32) {
+            float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              if constexpr (EPI == EPI_F32_ACC) {
+                const float4 c = d4[i];
+                o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
+              }
+              d4[i] = o;
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              if (i < nv) {
+                if constexpr (EPI == EPI_F32_ACC) dst[i] += v[i];
+                else dst[i] = v[i];
+              }
+            }
+          }
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < OUT_BN; c0 += 16) {
+      uint32_t g[16], u[16];
+      tmem_ld16(t_row + c0, g);
+      tmem_ld16(t_row + OUT_BN + c0, u);
+      tmem_ld_wait();
+      const int col0 = nb * OUT_BN + c0;
+      if (row_ok && col0 < p.N) {
+        const int nv = min(16, p.N - col0);
+        float gv[16], uv[16], o[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          gv[i] = __uint_as_float(g[i]);
+          uv[i] = __uint_as_float(u[i]);
+          o[i] = silu_f(gv[i]) * uv[i];
+        }
+        store_bf16<16>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, o, nv);
+        if (p.aux_out != nullptr) {
+          __nv_bfloat16* base = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
+          store_bf16<16>(base + col0, gv, nv);
+          store_bf16<16>(base + p.N + col0, uv, nv);
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_DSWIGLU) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      uint32_t r[16];
+      tmem_ld16(t_row + c0, r);
+      tmem_ld_wait();
+      const int col0 = nb * BN + c0;
+      if (row_ok && col0 < p.N) {
+        const int nv = min(16, p.N - col0);
+        const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
+        float gv[16], uv[16], dg[16], du[16];
+        load_bf16<16>(a + col0, gv, nv);
+        load_bf16<16>(a + p.N + col0, uv, nv);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float d = __uint_as_float(r[i]) * alpha;
+          const float s = 1.0f / (1.0f + __expf(-gv[i]));
+          du[i] = d * gv[i] * s;
+          dg[i] = d * uv[i] * s * (1.0f + gv[i] * (1.0f - s));
+        }
+        __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
+        store_bf16<16>(o + col0, dg, nv);
+        store_bf16<16>(o + p.N + col0, du, nv);
+      }
+    }
   }
 }
 
@@ -325,96 +426,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row = (GROUP == GROUP_K) ? t.grp * p.c_grp_rows + row_local : row_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
 
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_ACC) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c0, r);
-          tmem_ld_wait();
-          const int col0 = nb * BN + c0;
-          if (row_ok && col0 < p.N) {
-            const int nv = min(32, p.N - col0);
-            float v[32];
-#pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-            if constexpr (EPI == EPI_BF16) {
-              store_bf16<32>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, v, nv);
-            } else {
-              float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
-              if (nv == 32) {
-                float4* d4 = reinterpret_cast<float4*>(dst);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  float4 o = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                  if constexpr (EPI == EPI_F32_ACC) {
-                    const float4 c = d4[i];
-                    o.x += c.x; o.y += c.y; o.z += c.z; o.w += c.w;
-                  }
-                  d4[i] = o;
-                }
-              } else {
-#pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                  if (i < nv) {
-                    if constexpr (EPI == EPI_F32_ACC) dst[i] += v[i];
-                    else dst[i] = v[i];
-                  }
-                }
-              }
-            }
-          }
-        }
-      } else if constexpr (EPI == EPI_SWIGLU) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < OUT_BN; c0 += 16) {
-          uint32_t g[16], u[16];
-          tmem_ld16(t_row + c0, g);
-          tmem_ld16(t_row + OUT_BN + c0, u);
-          tmem_ld_wait();
-          const int col0 = nb * OUT_BN + c0;
-          if (row_ok && col0 < p.N) {
-            const int nv = min(16, p.N - col0);
-            float gv[16], uv[16], o[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              gv[i] = __uint_as_float(g[i]);
-              uv[i] = __uint_as_float(u[i]);
-              o[i] = silu_f(gv[i]) * uv[i];
-            }
-            store_bf16<16>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, o, nv);
-            if (p.aux_out != nullptr) {
-              __nv_bfloat16* base = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
-              store_bf16<16>(base + col0, gv, nv);
-              store_bf16<16>(base + p.N + col0, uv, nv);
-            }
-          }
-        }
-      } else if constexpr (EPI == EPI_DSWIGLU) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
-          uint32_t r[16];
-          tmem_ld16(t_row + c0, r);
-          tmem_ld_wait();
-          const int col0 = nb * BN + c0;
-          if (row_ok && col0 < p.N) {
-            const int nv = min(16, p.N - col0);
-            const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
-            float gv[16], uv[16], dg[16], du[16];
-            load_bf16<16>(a + col0, gv, nv);
-            load_bf16<16>(a + p.N + col0, uv, nv);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const float d = __uint_as_float(r[i]) * alpha;
-              const float s = 1.0f / (1.0f + __expf(-gv[i]));
-              du[i] = d * gv[i] * s;
-              dg[i] = d * uv[i] * s * (1.0f + gv[i] * (1.0f - s));
-            }
-            __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
-            store_bf16<16>(o + col0, dg, nv);
-            store_bf16<16>(o + p.N + col0, du, nv);
-          }
-        }
-      }
+      epilogue_row<BN, EPI>(p, t_row, nb, row, row_ok, alpha);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) {
@@ -428,6 +440,198 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// ---------------------------------------------------------------------------- CTA-pair kernel
+// 256 x 256 output tiles computed by a cluster of two CTAs with cta_group::2 MMAs
+// (M = 256, N = 256, K = 16 per instruction).  CTA r of the pair loads A rows
+// [256*mb + 128*r, +128) and B rows [256*nb + 128*r, +128) (SwiGLU: CTA 0 the gate rows,
+// CTA 1 the up rows of column block nb) into its own shared memory with plain TMA loads
+// that both signal the even CTA's `full` barrier; the even CTA's single MMA thread issues
+// the pair MMAs, and tcgen05.commit multicasts stage-free and accumulator-ready to both
+// CTAs.  Each CTA's TMEM holds its 128 rows x 256 columns (two buffers); its four
+// epilogue warps drain them with the same epilogues as the single-CTA kernel and release
+// the buffer on the even CTA's barrier.  Per CTA and k-block the pair moves 32 KB of
+// operands for 512 MMA cycles (the single-CTA 128 x 256 tile moves 48 KB), so the
+// operand traffic per flop drops by a third.
+constexpr int BN2 = 256;
+constexpr int STAGES2 = 6;
+constexpr uint32_t PAIR_A_BYTES = BM * BK * 2;
+constexpr uint32_t PAIR_B_BYTES = 128 * BK * 2;
+
+template <bool A_MN, bool B_MN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
+  constexpr uint32_t TMEM_COLS = 2 * BN2;
+  constexpr uint32_t IDESC = idesc_bf16_f32(256, BN2, A_MN, B_MN);
+  constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
+  static_assert(EPI != EPI_SWIGLU || !B_MN, "SwiGLU epilogue needs K-major B");
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_ptr(smem_raw, 1024);
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * PAIR_A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES2 * PAIR_B_BYTES);
+  uint64_t* empty = full + STAGES2;
+  uint64_t* acc_full = empty + STAGES2;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* done_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done_bar + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t crank = cluster_ctarank();
+  const bool leader = crank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int n_pairs = static_cast<int>(gridDim.x >> 1);
+  const int M = p.M;
+  const int num_m = (M + 255) / 256;
+  const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
+  const int num_tiles = num_m * num_n;
+  const int num_k = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp, 4 warps x 2 CTAs
+    }
+    mbar_init(done_bar, 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers initialised and TMEM allocated in both CTAs
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer (both CTAs)
+      const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the even CTA's full[0]
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        const int a_row0 = mb * 256 + static_cast<int>(crank) * 128;
+        const int b_row0 = (EPI == EPI_SWIGLU) ? (crank ? p.b_row_offset2 : 0) + nb * 128
+                                               : nb * BN2 + static_cast<int>(crank) * 128;
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (PAIR_A_BYTES + PAIR_B_BYTES));
+          const uint32_t bar = full0 + static_cast<uint32_t>(stage) * 8u;
+          uint8_t* a_dst = sA + stage * PAIR_A_BYTES;
+          uint8_t* b_dst = sB + stage * PAIR_B_BYTES;
+          const int kc = kb * BK;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, kc, a_row0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) tma_load_2d_pair(a_dst + c * (BK * 128), &tmA, bar, a_row0 + c * 64, kc);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, kc, b_row0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < 2; ++c) tma_load_2d_pair(b_dst + c * (BK * 128), &tmB, bar, b_row0 + c * 64, kc);
+          }
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ------------------------------------------------ MMA issuer (even CTA only)
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+        if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, p.status, kTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
+        for (int kb = 0; kb < num_k; ++kb) {
+          if (!mbar_wait_cluster(&full[stage], phase, p.status, kTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * PAIR_A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * PAIR_B_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            const uint64_t ad = A_MN ? sdesc_sw128(a_base + j * 2048, BK * 128, 1024)
+                                     : sdesc_sw128(a_base + j * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sdesc_sw128(b_base + j * 2048, BK * 128, 1024)
+                                     : sdesc_sw128(b_base + j * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
+          }
+          umma_commit_pair_mc(&empty[stage], 0x3);  // stage free in both CTAs
+          if (++stage == STAGES2) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair_mc(&acc_full[acc], 0x3);  // accumulator ready in both CTAs
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1u;
+        }
+      }
+      umma_commit_pair(done_bar);
+      mbar_wait(done_bar, 0, p.status, kTimeoutOther);
+    }
+  } else {
+    // ------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    float alpha = p.alpha;
+    if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
+    const uint32_t acc_empty0_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait_cluster_warp(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
+      tc_fence_after();
+      const int row = mb * 256 + static_cast<int>(crank) * 128 + q * 32 + lane;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN2);
+      epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (leader) mbar_arrive(&acc_empty[acc]);
+        else mbar_arrive_remote(acc_empty0_leader + static_cast<uint32_t>(acc) * 8u);
+      }
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1u;
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // every MMA retired and every TMEM read done, in both CTAs
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc_pair(tmem_base, TMEM_COLS);
 }
 
 // ---------------------------------------------------------------------------- host
@@ -461,6 +665,66 @@ void launch_bn(int bn, const Params& p, const CUtensorMap& ta, const CUtensorMap
     else
       launch_cfg<128, 6, A_MN, B_MN, EPI, GROUP>(p, ta, tb, device, st);
   }
+}
+
+template <bool A_MN, bool B_MN, int EPI>
+void launch_pair(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
+  constexpr size_t smem = static_cast<size_t>(STAGES2) * (PAIR_A_BYTES + PAIR_B_BYTES) + 1024 + 256;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
+  const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN);
+  const long pairs = std::max(1L, std::min(tiles, static_cast<long>(num_sms(device) / 2)));
+  kern<<<static_cast<unsigned>(2 * pairs), NUM_THREADS, smem, st>>>(ta, tb, p);
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int EPI>
+static void dispatch_pair(bool a_mn, bool b_mn, const Params& p, const CUtensorMap& ta, const CUtensorMap& tb,
+                          int device, cudaStream_t st) {
+  if (!a_mn && !b_mn)
+    launch_pair<false, false, EPI>(p, ta, tb, device, st);
+  else if (!a_mn && b_mn)
+    launch_pair<false, true, EPI>(p, ta, tb, device, st);
+  else if (a_mn && b_mn)
+    launch_pair<true, true, EPI>(p, ta, tb, device, st);
+  else
+    launch_pair<true, false, EPI>(p, ta, tb, device, st);
+}
+
+// CTA-pair kernel mode: 0 = never, 1 = when estimated faster (default), 2 = always (M >= 256).
+// Initialised from TT_GEMM_PAIR; gemm_set_pair_mode changes it at run time (tests).
+static std::atomic<int> g_pair_mode{-1};
+static int pair_mode() {
+  int v = g_pair_mode.load();
+  if (v < 0) {
+    const char* e = std::getenv("TT_GEMM_PAIR");
+    v = (e == nullptr || e[0] == '\0') ? 1 : std::atoi(e);
+    g_pair_mode.store(v);
+  }
+  return v;
+}
+
+// Estimated efficiency of the pair kernel (256 x 256 tiles on SMs/2 clusters) vs the best
+// single-CTA tile (which also pays ~15 % more operand traffic per flop).
+static bool use_pair(int M, int N, int out_bn_pair, int device) {
+  const int mode = pair_mode();
+  if (mode == 0 || M < 256) return false;
+  if (mode >= 2) return true;
+  const int sms = num_sms(device);
+  auto util = [](long tiles, long slots) {
+    const long waves = (tiles + slots - 1) / slots;
+    return static_cast<double>(tiles) / static_cast<double>(waves * slots);
+  };
+  const long t2 = static_cast<long>((M + 255) / 256) * ((N + out_bn_pair - 1) / out_bn_pair);
+  const double e2 = util(t2, sms / 2) * static_cast<double>(N) / (((N + out_bn_pair - 1) / out_bn_pair) * out_bn_pair);
+  double e1 = 0.0;
+  for (int bn : {128, 256}) {
+    const long t1 = static_cast<long>((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+    const double e = util(t1, sms) * static_cast<double>(N) / (((N + bn - 1) / bn) * bn) * (bn == 256 ? 0.85 : 0.78);
+    e1 = std::max(e1, e);
+  }
+  return e2 >= e1;
 }
 
 // Pick the N tile: prefer 256 unless 128 gives clearly fewer idle SM-slots.
@@ -549,11 +813,23 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
     if (!accumulate) c.zero_();
     return;
   }
+  cudaStream_t st = cur_stream();
+  if (bn == 1 || (bn == 0 && use_pair(M, N, BN2, device))) {  // bn == 1: the CTA-pair kernel
+    const CUtensorMap ta = operand_map(a, a_mn, BM);
+    const CUtensorMap tb = operand_map(b, b_mn, 128);
+    Params p = base_params(M, N, K, c, alpha, alpha_t, device);
+    if (out_bf16)
+      dispatch_pair<EPI_BF16>(a_mn, b_mn, p, ta, tb, device, st);
+    else if (accumulate)
+      dispatch_pair<EPI_F32_ACC>(a_mn, b_mn, p, ta, tb, device, st);
+    else
+      dispatch_pair<EPI_F32>(a_mn, b_mn, p, ta, tb, device, st);
+    return;
+  }
   const int use_bn = (bn == 128 || bn == 256) ? static_cast<int>(bn) : choose_bn(M, N, device);
   const CUtensorMap ta = operand_map(a, a_mn, BM);
   const CUtensorMap tb = operand_map(b, b_mn, use_bn);
   Params p = base_params(M, N, K, c, alpha, alpha_t, device);
-  cudaStream_t st = cur_stream();
   if (out_bf16)
     dispatch<EPI_BF16>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
   else if (accumulate)
@@ -561,6 +837,9 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
   else
     dispatch<EPI_F32>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
 }
+
+void gemm_set_pair_mode(int64_t mode) { gemm::g_pair_mode.store(static_cast<int>(mode)); }
+int64_t gemm_pair_mode() { return gemm::pair_mode(); }
 
 // out[M, I] = silu(x Wg^T) * (x Wu^T) with w_gu = [Wg; Wu] ([2I, K], K-major).
 // If gu_out is given, also stores the pre-activations g|u ([M, 2I]) for backward.
@@ -590,6 +869,10 @@ void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10:
     p.ld_aux_out = static_cast<int>(gu_out->stride(0));
   }
   TT_CHECK(I % 8 == 0, "swiglu: intermediate size must be a multiple of 8");
+  if (use_pair(M, I, BN2 / 2, device)) {
+    launch_pair<false, false, EPI_SWIGLU>(p, ta, tb, device, cur_stream());
+    return;
+  }
   launch_bn<false, false, EPI_SWIGLU>(256, p, ta, tb, device, cur_stream());
 }
 
@@ -610,7 +893,8 @@ void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, t
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(dy.device());
   const int device = dy.get_device();
-  const int bn = choose_bn(M, I, device);
+  const bool pair = use_pair(M, I, BN2, device);
+  const int bn = pair ? 128 : choose_bn(M, I, device);
   const CUtensorMap ta = operand_map(dy, false, BM);
   const CUtensorMap tb = operand_map(w_down, true, bn);
   Params p = base_params(M, I, D, dgu, alpha, c10::nullopt, device);
@@ -619,6 +903,10 @@ void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, t
   p.ld_aux = static_cast<int>(gu.stride(0));
   p.aux_out = reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr());
   p.ld_aux_out = static_cast<int>(dgu.stride(0));
+  if (pair) {
+    launch_pair<false, true, EPI_DSWIGLU>(p, ta, tb, device, cur_stream());
+    return;
+  }
   launch_bn<false, true, EPI_DSWIGLU>(bn, p, ta, tb, device, cur_stream());
 }
 

@@ -31,7 +31,7 @@ SHAPES = [(128, 256, 64), (256, 512, 128), (296, 200, 136), (1024, 3072, 2048), 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True), (True, False)])
-@pytest.mark.parametrize("bn", [0, 128])
+@pytest.mark.parametrize("bn", [0, 128, 1])  # 1: the CTA-pair (cta_group::2) kernel
 def test_gemm_bf16_out(M, N, K, a_mn, b_mn, bn):
     A, B, a, b = _operands(M, N, K, a_mn, b_mn)
     c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
@@ -43,21 +43,30 @@ def test_gemm_bf16_out(M, N, K, a_mn, b_mn, bn):
 
 @pytest.mark.parametrize("M,N,K", [(256, 512, 384), (1000, 264, 520)])
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (True, True)])
-def test_gemm_fp32_accumulate_alpha(M, N, K, a_mn, b_mn):
+@pytest.mark.parametrize("bn", [0, 1])
+def test_gemm_fp32_accumulate_alpha(M, N, K, a_mn, b_mn, bn):
     A, B, a, b = _operands(M, N, K, a_mn, b_mn, seed=1)
     c0 = torch.randn(M, N, device="cuda")
     c = c0.clone()
     alpha_t = torch.tensor([0.5], device="cuda")
-    ext().gemm(a, b, c, a_mn, b_mn, True, 2.0, alpha_t, 0)
+    ext().gemm(a, b, c, a_mn, b_mn, True, 2.0, alpha_t, bn)
     ref = c0 + (A.float() @ B.float().t())
     _check(c, ref, 1e-5)
     c2 = torch.empty(M, N, device="cuda")
-    ext().gemm(a, b, c2, a_mn, b_mn, False, 0.25, None, 0)
+    ext().gemm(a, b, c2, a_mn, b_mn, False, 0.25, None, bn)
     _check(c2, 0.25 * (A.float() @ B.float().t()), 1e-5)
 
 
+@pytest.fixture(params=[0, 2], ids=["single_cta", "cta_pair"])
+def pair_mode(request):
+    prev = ext().gemm_pair_mode()
+    ext().gemm_set_pair_mode(request.param)
+    yield request.param
+    ext().gemm_set_pair_mode(prev)
+
+
 @pytest.mark.parametrize("M,I,K", [(256, 256, 128), (300, 5504 // 8, 256), (1024, 1408, 2048)])
-def test_gemm_swiglu(M, I, K):
+def test_gemm_swiglu(M, I, K, pair_mode):
     g = torch.Generator(device="cuda").manual_seed(2)
     x = torch.randn(M, K, device="cuda", generator=g).bfloat16()
     w = (torch.randn(2 * I, K, device="cuda", generator=g) * 0.05).bfloat16()
@@ -72,7 +81,7 @@ def test_gemm_swiglu(M, I, K):
 
 
 @pytest.mark.parametrize("M,D,I", [(256, 256, 256), (300, 128, 704), (1024, 2048, 1408)])
-def test_gemm_dswiglu(M, D, I):
+def test_gemm_dswiglu(M, D, I, pair_mode):
     g = torch.Generator(device="cuda").manual_seed(3)
     dy = torch.randn(M, D, device="cuda", generator=g).bfloat16()
     wd = (torch.randn(D, I, device="cuda", generator=g) * 0.05).bfloat16()
