@@ -18,6 +18,7 @@ import torch.distributed as dist
 import torch.nn as nn
 
 from tinytron_b200 import ops
+from tinytron_b200.utils.profile import nvtx_range
 from tinytron_b200.parallel import parallel_state
 
 from .config import ModelConfig
@@ -96,16 +97,18 @@ class GPT(nn.Module):
         pending = None
         total_aux = 0.0
         valid = (targets != self.loss_fn.ignore_index) if targets is not None else None
-        for blk in self.blocks:
-            x, h = ops.add_rmsnorm(x, pending, blk.ln_1.weight, self.eps)
-            a = blk.attn.forward_train(h, position_offset)
-            x, h = ops.add_rmsnorm(x, a, blk.ln_2.weight, self.eps)
-            if self.use_moe:
-                pending, gate_logits = blk.mlp(h)
-                if self.expert_loss_fn is not None and targets is not None:
-                    total_aux = total_aux + self.expert_loss_fn(gate_logits, valid_mask=valid)
-            else:
-                pending = blk.mlp(h)
+        for li, blk in enumerate(self.blocks):
+            with nvtx_range(f"layer{li}.attn"):
+                x, h = ops.add_rmsnorm(x, pending, blk.ln_1.weight, self.eps)
+                a = blk.attn.forward_train(h, position_offset)
+            with nvtx_range(f"layer{li}.mlp"):
+                x, h = ops.add_rmsnorm(x, a, blk.ln_2.weight, self.eps)
+                if self.use_moe:
+                    pending, gate_logits = blk.mlp(h)
+                    if self.expert_loss_fn is not None and targets is not None:
+                        total_aux = total_aux + self.expert_loss_fn(gate_logits, valid_mask=valid)
+                else:
+                    pending = blk.mlp(h)
         x, h = ops.add_rmsnorm(x, pending, self.lnf.weight, self.eps)
         if targets is None:
             if torch.is_grad_enabled():  # differentiable logits (e.g. RL policy log-probs)

@@ -33,6 +33,7 @@ from tinytron_b200.parallel import parallel_state
 from tinytron_b200.parallel.buffers import FlatParams
 from tinytron_b200.parallel.zero1 import DistributedOptimizer, FlatZeRO1
 from tinytron_b200.utils import compute_mfu, get_model_params, get_training_info, set_seed
+from tinytron_b200.utils.profile import nvtx_range
 
 from .config import Config
 from .data import MockDataset, build_lm_collate_fn
@@ -331,7 +332,8 @@ class Trainer:
             ll, v = self._one_training_micro_step(config, micro, batch)
             loss_accum += ll
             valid_accum += v
-        norm, coef = self._sync_and_clip(config.train.grad_clip_value)
+        with nvtx_range("grad_sync_clip"):
+            norm, coef = self._sync_and_clip(config.train.grad_clip_value)
         lr = self._lr_scheduler(step, self.training_info["max_steps"], config.optim.warmup_steps,
                                 config.optim.max_lr, config.optim.min_lr)
         if self.use_flat_optimizer:
@@ -413,10 +415,21 @@ class Trainer:
             self.one_step_results = {}
             t0 = time.time()
             last = step == max_steps - 1
-            with self.profiler_record_fn("training_step"):
+            dev_timing = self.device.type == "cuda" and os.environ.get("TT_DEVICE_TIMING", "0") == "1"
+            if dev_timing:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+            with self.profiler_record_fn("training_step"), nvtx_range(f"step{step}"):
                 self._one_training_step(cfg, step)
+            if dev_timing:
+                ev1.record()
             if self.device.type == "cuda":
                 torch.cuda.synchronize()
+            if dev_timing:  # device time of the step, max over ranks (same collective on every rank)
+                dev_ms = torch.tensor([ev0.elapsed_time(ev1)], device=self.device)
+                if dist.is_initialized() and dist.get_world_size() > 1:
+                    dist.all_reduce(dev_ms, op=dist.ReduceOp.MAX)
+                self.one_step_results["device_ms"] = float(dev_ms.item())
             if self.profiler:
                 self.profiler.step()
             if not cfg.train.debug and cfg.train.do_val and (step % cfg.train.val_every_steps == 0 or last):
@@ -441,8 +454,9 @@ class Trainer:
                 loss = self.one_step_results["loss"].item()
                 gn = float(self.one_step_results["grad_norm"])
                 print(f"step {step:5d}/{max_steps} | loss: {loss:.6f} | lr {self.one_step_results['lr']:.4e} | "
-                      f"grad norm: {gn:.4f} | dt: {dt * 1000:.2f}ms | tok/sec: {tps:.2f} | MFU: {mfu * 100:.2f}%",
-                      flush=True)
+                      f"grad norm: {gn:.4f} | dt: {dt * 1000:.2f}ms | tok/sec: {tps:.2f} | MFU: {mfu * 100:.2f}%"
+                      + (f" | device: {self.one_step_results['device_ms']:.2f}ms"
+                         if "device_ms" in self.one_step_results else ""), flush=True)
                 with open(self.log_file, "a") as f:
                     f.write(f"{step} train {loss:.6f}\n")
             self.results[step] = self.one_step_results

@@ -61,3 +61,41 @@ def compute_mfu(model, batch_size, seq_len, time, ga=1, dtype="bf16"):
     achieved = flops / time if time > 0 else 0.0
     peak = get_gpu_peak_flops(dtype=dtype, per_device=True)
     return (achieved / peak if peak else 0), achieved, peak
+
+
+# ---------------------------------------------------------------------------- NVTX
+_NVTX = None
+
+
+def nvtx_enabled() -> bool:
+    global _NVTX
+    if _NVTX is None:
+        import os
+
+        _NVTX = os.environ.get("TT_NVTX", "0") == "1"
+    return _NVTX
+
+
+class nvtx_range:
+    """NVTX range around a block (``TT_NVTX=1``; a no-op otherwise), so Nsight/CUPTI timelines
+    show model-level regions (layers, attention, MLP/MoE, ZeRO-1 sync) around the kernels."""
+
+    __slots__ = ("name", "on")
+
+    def __init__(self, name: str):
+        self.name = name
+        self.on = nvtx_enabled()
+
+    def __enter__(self):
+        if self.on:
+            import torch
+
+            torch.cuda.nvtx.range_push(self.name)
+        return self
+
+    def __exit__(self, *exc):
+        if self.on:
+            import torch
+
+            torch.cuda.nvtx.range_pop()
+        return False

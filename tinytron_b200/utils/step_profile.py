@@ -22,6 +22,7 @@ def main():
     ap.add_argument("--grad-accum", type=int, default=4)
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--moe", action="store_true", help="MoE model of BASELINE config 3 (64 experts x 1408, top-8)")
     args = ap.parse_args()
     import torch
 
@@ -36,6 +37,8 @@ def main():
             "--warmup_steps", "1", "--num_layer", str(args.layers), "--hidden_size", "2048",
             "--num_attention_heads", "16", "--num_key_value_heads", "4", "--intermediate_size", "5504",
             "--vocab_size", "50304", "--block_size", str(T), "--init_std", "0.02"]
+    if args.moe:
+        argv += ["--use_moe", "--num_experts", "64", "--num_experts_per_tok", "8", "--moe_intermediate_size", "1408"]
     tr = Trainer(build_config(parse_args(argv)))
     g = torch.Generator().manual_seed(0)
     batches = []
@@ -61,7 +64,7 @@ def main():
     for ev in prof.events():
         if ev.device_type == torch.autograd.DeviceType.CUDA:
             name = ev.name
-            key = name.split("(")[0][:110]
+            key = name.replace("(anonymous namespace)::", "").split("(")[0][:110]
             tot[key] += ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total
             cnt[key] += 1
     total = sum(tot.values())
