@@ -426,6 +426,52 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* __restrict__ o, int l
   }
 }
 
+// Same outputs, one warp per token covering all heads (Hq * D a multiple of 256, D = 64 or
+// 128): lane l reads 16-byte chunks l + 32 j of O and dO, the D/8 lanes of a head reduce by
+// shuffles.  32-bit index math; each warp streams 2 x Hq x D x 2 bytes.
+__global__ void attn_bwd_delta_rows_kernel(const __nv_bfloat16* __restrict__ o, int ld_o,
+                                           const __nv_bfloat16* __restrict__ dout, int ld_do,
+                                           const float* __restrict__ lse, float* __restrict__ lse2_pad,
+                                           float* __restrict__ delta_pad, int B, int T, int T_pad, int Hq, int D) {
+  const int warp = static_cast<int>((static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (warp >= B * T_pad) return;
+  const int b = warp / T_pad, t = warp - (warp / T_pad) * T_pad;
+  if (t >= T) {  // padded slots
+    for (int h = lane; h < Hq; h += 32) {
+      const int out = (b * Hq + h) * T_pad + t;
+      delta_pad[out] = 0.0f;
+      lse2_pad[out] = INFINITY;
+    }
+    return;
+  }
+  const int tok = b * T + t;
+  const uint4* a = reinterpret_cast<const uint4*>(o + static_cast<long long>(tok) * ld_o);
+  const uint4* c = reinterpret_cast<const uint4*>(dout + static_cast<long long>(tok) * ld_do);
+  const int lanes_per_head = D / 8;  // 16 or 8
+  const int n_iter = Hq * D / 256;
+  for (int j = 0; j < n_iter; ++j) {
+    const int chunk = lane + 32 * j;
+    const uint4 x = a[chunk];
+    const uint4 y = c[chunk];
+    const uint32_t* xv = reinterpret_cast<const uint32_t*>(&x);
+    const uint32_t* yv = reinterpret_cast<const uint32_t*>(&y);
+    float s = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 xf = unpack_bf16x2(xv[q]), yf = unpack_bf16x2(yv[q]);
+      s += xf.x * yf.x + xf.y * yf.y;
+    }
+    for (int off = lanes_per_head / 2; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if ((lane & (lanes_per_head - 1)) == 0) {
+      const int h = chunk / lanes_per_head;
+      const int out = (b * Hq + h) * T_pad + t;
+      delta_pad[out] = s;
+      lse2_pad[out] = lse[(b * Hq + h) * T + t] * 1.4426950408889634f;
+    }
+  }
+}
+
 // dq (bf16, token-major, head h at col0 + h*D) = dq_acc (fp32 [tokens, Hq*D])
 __global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int ld_dq,
                                            int col0, long long tokens, int width) {
@@ -474,7 +520,18 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   const long long tokens = B * T;
   float* lse2_pad = scratch.data_ptr<float>();
   float* delta_pad = lse2_pad + B * Hq * T_pad;
-  {
+  const bool rows_ok = (D == 64 || D == 128) && (Hq * D) % 256 == 0 && o.stride(0) % 8 == 0 &&
+                       dout.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(o.data_ptr()) % 16 == 0 &&
+                       reinterpret_cast<uintptr_t>(dout.data_ptr()) % 16 == 0 && B * T_pad * Hq < (1LL << 31);
+  if (rows_ok) {
+    const long long warps = B * T_pad;
+    attn_bwd_delta_rows_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), static_cast<int>(o.stride(0)),
+        reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), static_cast<int>(dout.stride(0)), lse.data_ptr<float>(),
+        lse2_pad, delta_pad, static_cast<int>(B), static_cast<int>(T), static_cast<int>(T_pad), static_cast<int>(Hq),
+        static_cast<int>(D));
+    TT_CUDA_CHECK(cudaGetLastError());
+  } else {
     const long long warps = B * T_pad * Hq;
     attn_bwd_delta_kernel<<<static_cast<unsigned>((warps * 32 + 255) / 256), 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(o.data_ptr()), static_cast<int>(o.stride(0)),

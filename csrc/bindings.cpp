@@ -59,6 +59,8 @@ void decode_rope_append(torch::Tensor qkv, int64_t B, int64_t T, int64_t Hq, int
                         torch::Tensor sin_t, torch::Tensor q_out, torch::Tensor k_pages, torch::Tensor v_pages,
                         torch::Tensor page_table);
 int64_t decode_num_splits(int64_t max_len);
+void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, double top_p, int64_t seed,
+                   int64_t offset, torch::Tensor tokens, c10::optional<torch::Tensor> logprob);
 void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages, torch::Tensor page_table,
                       c10::optional<torch::Tensor> len_dev, int64_t len_host, int64_t splits, double scale,
                       torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out);
@@ -137,6 +139,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_bwd_scratch_numel", &tt::attn_bwd_scratch_numel, "fp32 scratch elements attn_bwd needs");
   m.def("attn_bwd", &tt::attn_bwd, "flash attention backward (tcgen05, GQA-native, dQ via fp32 atomics)");
   m.def("decode_rope_append", &tt::decode_rope_append, "RoPE on q/k + paged KV-cache append (device position)");
+  m.def("sample_tokens", &tt::sample_tokens, "temperature/top-k/top-p sampling in one kernel (Philox draw)",
+        py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"), py::arg("seed"),
+        py::arg("offset"), py::arg("tokens"), py::arg("logprob") = py::none());
   m.def("decode_num_splits", &tt::decode_num_splits, "split-KV CTAs per (sequence, kv head) for a max length");
   m.def("decode_attention", &tt::decode_attention, "split-KV paged decode attention (GQA-native) + combine");
   m.def("ep_allgather_counts", &tt::ep_allgather_counts, "EP: all-gather per-expert counts into the heap");

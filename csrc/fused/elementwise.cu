@@ -150,15 +150,32 @@ __global__ void embedding_fwd_kernel(const int64_t* __restrict__ idx, const floa
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) dst[i] = src[i];
 }
 
-__global__ void embedding_bwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ g,
-                                     float* __restrict__ gtable, int D) {
-  const int row = blockIdx.x;
-  const int64_t t = idx[row];
-  float* dst = gtable + static_cast<size_t>(t) * D;
-  const float4* src = reinterpret_cast<const float4*>(g + static_cast<size_t>(row) * D);
+// Embedding backward: token ids sorted (stable) beforehand; the block at the first
+// position of each run of equal ids sums that run's gradient rows in position order and
+// adds the sum into the table row once (no atomics, fixed summation order).
+__global__ void embedding_bwd_sorted_kernel(const int64_t* __restrict__ sorted_idx, const int64_t* __restrict__ order,
+                                            int N, const float* __restrict__ g, float* __restrict__ gtable, int D,
+                                            long long V, int* status) {
+  const int pos = blockIdx.x;
+  const int64_t t = sorted_idx[pos];
+  if (pos > 0 && sorted_idx[pos - 1] == t) return;  // not the first of its run
+  if (t < 0 || t >= V) {
+    if (threadIdx.x == 0) atomicCAS(status, 0, static_cast<int>(kBadIndex));
+    return;
+  }
+  int end = pos + 1;
+  while (end < N && sorted_idx[end] == t) ++end;
+  float4* dst = reinterpret_cast<float4*>(gtable + static_cast<size_t>(t) * D);
   for (int i = threadIdx.x; i < D / 4; i += blockDim.x) {
-    const float4 v = src[i];
-    atomicAdd(reinterpret_cast<float4*>(dst) + i, v);
+    float4 acc = dst[i];
+    for (int j = pos; j < end; ++j) {
+      const float4 v = reinterpret_cast<const float4*>(g + static_cast<size_t>(order[j]) * D)[i];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    dst[i] = acc;
   }
 }
 
@@ -343,8 +360,15 @@ void embedding_bwd(torch::Tensor idx, torch::Tensor g, torch::Tensor gtable) {
            "embedding_bwd dtypes/shapes");
   if (idx.numel() == 0) return;
   const c10::cuda::CUDAGuard guard(g.device());
-  embedding_bwd_kernel<<<static_cast<unsigned>(idx.numel()), 256, 0, cur_stream()>>>(
-      idx.data_ptr<int64_t>(), g.data_ptr<float>(), gtable.data_ptr<float>(), static_cast<int>(D));
+  // Stable sort of the token ids (device radix sort), then one pass over the runs:
+  // deterministic, unlike per-token atomic adds.
+  auto flat = idx.reshape({-1}).contiguous();
+  auto sr = flat.sort(/*stable=*/true, /*dim=*/0, /*descending=*/false);
+  auto sorted = std::get<0>(sr);
+  auto order = std::get<1>(sr);
+  embedding_bwd_sorted_kernel<<<static_cast<unsigned>(flat.numel()), 256, 0, cur_stream()>>>(
+      sorted.data_ptr<int64_t>(), order.data_ptr<int64_t>(), static_cast<int>(flat.numel()), g.data_ptr<float>(),
+      gtable.data_ptr<float>(), static_cast<int>(D), gtable.size(0), device_status_ptr(g.get_device()));
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

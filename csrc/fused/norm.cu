@@ -131,14 +131,34 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const f
   if (active && dw_part != nullptr) store8_f32(dw_part + static_cast<size_t>(blockIdx.x) * D + c, dw);
 }
 
-// dw[d] (+)= sum_g part[g, d]   (fixed summation order -> deterministic)
-__global__ void reduce_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int G, int D,
-                                   int accumulate) {
-  const int d = blockIdx.x * blockDim.x + threadIdx.x;
-  if (d >= D) return;
-  float s = 0.0f;
-  for (int g = 0; g < G; ++g) s += part[static_cast<size_t>(g) * D + d];
-  out[d] = accumulate ? out[d] + s : s;
+// dw[d] (+)= sum_g part[g, d]   (fixed summation order -> deterministic).
+// Block = 32 columns x 8 row lanes (256 threads): row lane r sums rows g = r (mod 8) with
+// four independent accumulators, then the 8 lane sums are added in lane order.
+constexpr int RR_COLS = 32;
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                                          int G, int D, int accumulate) {
+  __shared__ float red[8][RR_COLS + 1];
+  const int cx = threadIdx.x & 31, ry = threadIdx.x >> 5;
+  const int d = blockIdx.x * RR_COLS + cx;
+  float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+  if (d < D) {
+    int g = ry;
+    for (; g + 24 < G; g += 32) {
+      s0 += part[static_cast<size_t>(g) * D + d];
+      s1 += part[static_cast<size_t>(g + 8) * D + d];
+      s2 += part[static_cast<size_t>(g + 16) * D + d];
+      s3 += part[static_cast<size_t>(g + 24) * D + d];
+    }
+    for (; g < G; g += 8) s0 += part[static_cast<size_t>(g) * D + d];
+  }
+  red[ry][cx] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  if (ry == 0 && d < D) {
+    float s = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) s += red[r][cx];
+    out[d] = accumulate ? out[d] + s : s;
+  }
 }
 
 int norm_threads(int D) { return ((D / EPT + 31) / 32) * 32; }
@@ -202,7 +222,7 @@ void rmsnorm_bwd(torch::Tensor gh, torch::Tensor x, torch::Tensor rstd, torch::T
       reinterpret_cast<const __nv_bfloat16*>(gh.data_ptr()), x.data_ptr<float>(), rstd.data_ptr<float>(),
       w.data_ptr<float>(), gr, gxp, gdp, scratch.data_ptr<float>(), static_cast<int>(M), static_cast<int>(D));
   TT_CUDA_CHECK(cudaGetLastError());
-  reduce_rows_kernel<<<static_cast<unsigned>((D + 255) / 256), 256, 0, st>>>(
+  reduce_rows_kernel<<<static_cast<unsigned>((D + RR_COLS - 1) / RR_COLS), 256, 0, st>>>(
       scratch.data_ptr<float>(), dw.data_ptr<float>(), G, static_cast<int>(D), accumulate_dw ? 1 : 0);
   TT_CUDA_CHECK(cudaGetLastError());
 }
@@ -257,7 +277,7 @@ extern "C" __attribute__((visibility("default"))) int tt_rmsnorm_bwd_noalloc(
   rmsnorm_bwd_kernel<<<static_cast<unsigned>(G), norm_threads(D), 0, stream>>>(gh, x, rstd, w, g_res, gx, g_delta,
                                                                             scratch, M, D);
   if (cudaGetLastError() != cudaSuccess) return 4;
-  reduce_rows_kernel<<<static_cast<unsigned>((D + 255) / 256), 256, 0, stream>>>(scratch, dw, static_cast<int>(G), D,
+  reduce_rows_kernel<<<static_cast<unsigned>((D + RR_COLS - 1) / RR_COLS), 256, 0, stream>>>(scratch, dw, static_cast<int>(G), D,
                                                                                 accumulate_dw ? 1 : 0);
   if (cudaGetLastError() != cudaSuccess) return 4;
   return 0;

@@ -64,6 +64,12 @@ struct Params {
   int b_split_kb;              // GROUP_M, MN-major B: k-blocks >= this come from rows b_off2 + ...
   int b_off2;
   int c_grp_rows;              // GROUP_K: per-group row offset of C
+  // CTA-pair kernel, fp32-accumulate epilogue only: the reduction is split into split_k
+  // ranges whose epilogues add into C one after another (split s waits until the 8
+  // epilogue warps of split s-1 counted themselves in splitk_flags[tile]), so the sum
+  // order is fixed and results are deterministic.
+  int split_k;
+  int* splitk_flags;
 };
 
 struct TileInfo {
@@ -116,6 +122,12 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, int num_m, int num_n, 
 }
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+__device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 
 // Store n (<= 32) fp32 values as bf16 starting at dst; vectorised when a full aligned run.
 template <int NV>
@@ -223,28 +235,61 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
       }
     }
   } else if constexpr (EPI == EPI_DSWIGLU) {
+    // The saved pre-activations g|u are loaded 64 columns at a time (16 independent
+    // 16-byte loads in flight per thread) before the TMEM reads of those columns, so the
+    // per-row load latency is paid BN/64 times per tile instead of BN/16 times.
+    constexpr int QC = 64;
+    const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
+    __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 16) {
-      uint32_t r[16];
-      tmem_ld16(t_row + c0, r);
-      tmem_ld_wait();
-      const int col0 = nb * BN + c0;
-      if (row_ok && col0 < p.N) {
-        const int nv = min(16, p.N - col0);
-        const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
-        float gv[16], uv[16], dg[16], du[16];
-        load_bf16<16>(a + col0, gv, nv);
-        load_bf16<16>(a + p.N + col0, uv, nv);
+    for (int q0 = 0; q0 < BN; q0 += QC) {
+      const int colq = nb * BN + q0;
+      const bool full = row_ok && colq + QC <= p.N;
+      uint4 gq[QC / 8], uq[QC / 8];
+      if (full) {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float d = __uint_as_float(r[i]) * alpha;
-          const float s = 1.0f / (1.0f + __expf(-gv[i]));
-          du[i] = d * gv[i] * s;
-          dg[i] = d * uv[i] * s * (1.0f + gv[i] * (1.0f - s));
+        for (int i = 0; i < QC / 8; ++i) {
+          gq[i] = __ldg(reinterpret_cast<const uint4*>(a + colq) + i);
+          uq[i] = __ldg(reinterpret_cast<const uint4*>(a + p.N + colq) + i);
         }
-        __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
-        store_bf16<16>(o + col0, dg, nv);
-        store_bf16<16>(o + p.N + col0, du, nv);
+      }
+#pragma unroll
+      for (int c = 0; c < QC; c += 16) {
+        uint32_t r[16];
+        tmem_ld16(t_row + q0 + c, r);
+        tmem_ld_wait();
+        const int col0 = colq + c;
+        if (row_ok && col0 < p.N) {
+          const int nv = min(16, p.N - col0);
+          float gv[16], uv[16], dg[16], du[16];
+          if (full) {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const uint32_t* gw = reinterpret_cast<const uint32_t*>(&gq[c / 8 + h]);
+              const uint32_t* uw = reinterpret_cast<const uint32_t*>(&uq[c / 8 + h]);
+#pragma unroll
+              for (int w = 0; w < 4; ++w) {
+                const float2 gf = unpack_bf16x2(gw[w]), uf = unpack_bf16x2(uw[w]);
+                gv[8 * h + 2 * w] = gf.x;
+                gv[8 * h + 2 * w + 1] = gf.y;
+                uv[8 * h + 2 * w] = uf.x;
+                uv[8 * h + 2 * w + 1] = uf.y;
+              }
+            }
+          } else {
+            load_bf16<16>(a + col0, gv, nv);
+            load_bf16<16>(a + p.N + col0, uv, nv);
+          }
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float d = __uint_as_float(r[i]) * alpha;
+            const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+            du[i] = d * gv[i] * sg;
+            dg[i] = d * uv[i] * sg * (1.0f + gv[i] * (1.0f - sg));
+          }
+          store_bf16<16>(o + col0, dg, nv);
+          store_bf16<16>(o + p.N + col0, du, nv);
+        }
       }
     }
   }
@@ -489,6 +534,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
   const int num_tiles = num_m * num_n;
   const int num_k = (p.K + BK - 1) / BK;
+  const int S = (EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1;
+  const int num_units = num_tiles * S;
+  const int kb_per = (num_k + S - 1) / S;
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -520,13 +568,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+      for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
+        const int tile = unit / S, split = unit - (unit / S) * S;
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
         const int a_row0 = mb * 256 + static_cast<int>(crank) * 128;
         const int b_row0 = (EPI == EPI_SWIGLU) ? (crank ? p.b_row_offset2 : 0) + nb * 128
                                                : nb * BN2 + static_cast<int>(crank) * 128;
-        for (int kb = 0; kb < num_k; ++kb) {
+        const int kb_end = min(num_k, (split + 1) * kb_per);
+        for (int kb = split * kb_per; kb < kb_end; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
             ok = false;
             break;
@@ -563,11 +613,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < num_tiles; tile += n_pairs) {
+      for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
+        const int split = unit - (unit / S) * S;
+        const int kb0 = split * kb_per, kb_end = min(num_k, (split + 1) * kb_per);
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, p.status, kTimeoutAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
-        for (int kb = 0; kb < num_k; ++kb) {
+        for (int kb = kb0; kb < kb_end; ++kb) {
           if (!mbar_wait_cluster(&full[stage], phase, p.status, kTimeoutFull)) {
             ok = false;
             break;
@@ -581,7 +633,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
                                      : sdesc_sw128(a_base + j * 32, 16, 1024);
             const uint64_t bd = B_MN ? sdesc_sw128(b_base + j * 2048, BK * 128, 1024)
                                      : sdesc_sw128(b_base + j * 32, 16, 1024);
-            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb > 0 || j > 0) ? 1u : 0u);
+            umma_f16_ss_pair(d_tmem, ad, bd, IDESC, (kb > kb0 || j > 0) ? 1u : 0u);
           }
           umma_commit_pair_mc(&empty[stage], 0x3);  // stage free in both CTAs
           if (++stage == STAGES2) {
@@ -607,14 +659,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     const uint32_t acc_empty0_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = pair; tile < num_tiles; tile += n_pairs) {
+    bool ok = true;
+    for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
+      const int tile = unit / S, split = unit - (unit / S) * S;
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
       if (!mbar_wait_cluster_warp(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
       tc_fence_after();
+      if (S > 1 && split > 0) {  // previous split's partial must be in C first (bounded wait)
+        bool ready = true;
+        if (lane == 0) {
+          const uint64_t t0 = globaltimer();
+          while (ld_acquire_gpu_s32(p.splitk_flags + tile) < 8 * split) {
+            if (globaltimer() - t0 > TT_WAIT_TIMEOUT_NS || *reinterpret_cast<volatile int*>(p.status) != 0) {
+              atomicCAS(p.status, 0, static_cast<int>(kTimeoutOther));
+              ready = false;
+              break;
+            }
+            __nanosleep(128);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
+        __threadfence();
+      }
       const int row = mb * 256 + static_cast<int>(crank) * 128 + q * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN2);
-      epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha);
+      if (ok) epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha);
+      if (S > 1) {  // count this warp's rows as added
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.splitk_flags + tile, 1);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -673,7 +748,8 @@ void launch_pair(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
   TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
-  const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN);
+  const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN) *
+                     ((EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1);
   const long pairs = std::max(1L, std::min(tiles, static_cast<long>(num_sms(device) / 2)));
   kern<<<static_cast<unsigned>(2 * pairs), NUM_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
@@ -703,6 +779,27 @@ static int pair_mode() {
     g_pair_mode.store(v);
   }
   return v;
+}
+
+// Split count for the fp32-accumulate pair kernel.  Each extra split re-reads and rewrites
+// the whole fp32 output and serialises one more epilogue per tile, so split only when the
+// 256x256 tiles leave most of the last wave idle (utilisation < 0.8), and take the
+// smallest split count that reaches 0.85 with >= 32 k-blocks per split.
+static int choose_split_k(int M, int N, int K, int device) {
+  if (pair_mode() == 0 || M < 256) return 1;
+  const long slots = num_sms(device) / 2;
+  const long tiles = static_cast<long>((M + 255) / 256) * ((N + BN2 - 1) / BN2);
+  auto util = [&](int s) {
+    const long u = tiles * s;
+    return static_cast<double>(u) / static_cast<double>(((u + slots - 1) / slots) * slots);
+  };
+  if (util(1) >= 0.8) return 1;
+  const int num_k = (K + BK - 1) / BK;
+  for (int s = 2; s <= 4; ++s) {
+    if (num_k / s < 32) break;
+    if (util(s) >= 0.85) return s;
+  }
+  return 1;
 }
 
 // Estimated efficiency of the pair kernel (256 x 256 tiles on SMs/2 clusters) vs the best
@@ -814,10 +911,20 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
     return;
   }
   cudaStream_t st = cur_stream();
-  if (bn == 1 || (bn == 0 && use_pair(M, N, BN2, device))) {  // bn == 1: the CTA-pair kernel
+  // Deterministic split-K (fp32 accumulate only): when the pair tiles fill few waves and
+  // the reduction is long, e.g. the q|k|v weight gradient (96 tiles, K = 16384).
+  const int splits = (accumulate && bn != 128 && bn != 256) ? choose_split_k(M, N, K, device) : 1;
+  if (bn == 1 || splits > 1 || (bn == 0 && use_pair(M, N, BN2, device))) {  // bn == 1: the CTA-pair kernel
     const CUtensorMap ta = operand_map(a, a_mn, BM);
     const CUtensorMap tb = operand_map(b, b_mn, 128);
     Params p = base_params(M, N, K, c, alpha, alpha_t, device);
+    torch::Tensor flags;
+    if (splits > 1) {
+      const int64_t tiles = static_cast<int64_t>((M + 255) / 256) * ((N + BN2 - 1) / BN2);
+      flags = torch::zeros({tiles}, torch::TensorOptions().dtype(torch::kInt32).device(a.device()));
+      p.split_k = splits;
+      p.splitk_flags = flags.data_ptr<int>();
+    }
     if (out_bf16)
       dispatch_pair<EPI_BF16>(a_mn, b_mn, p, ta, tb, device, st);
     else if (accumulate)
@@ -890,6 +997,8 @@ void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, t
   const int I = static_cast<int>(w_down.size(1));
   TT_CHECK(gu.size(0) == M && gu.size(1) == 2 * I && dgu.size(0) == M && dgu.size(1) == 2 * I, "dswiglu: bad shapes");
   TT_CHECK(I % 64 == 0, "dswiglu: intermediate size must be a multiple of 64");
+  TT_CHECK(gu.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(gu.data_ptr()) % 16 == 0 && gu.stride(1) == 1,
+           "dswiglu: gu rows must be 16-byte aligned");
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(dy.device());
   const int device = dy.get_device();
@@ -1001,6 +1110,8 @@ void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g
   TT_CHECK(w_down.size(0) == n_groups * D && D % BK == 0, "moe_dswiglu: w_down must be [E*D, I], D % 64 == 0");
   TT_CHECK(gu.size(0) == M && gu.size(1) == 2 * I && dgu.size(0) == M && dgu.size(1) == 2 * I && I % 64 == 0,
            "moe_dswiglu: bad shapes");
+  TT_CHECK(gu.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(gu.data_ptr()) % 16 == 0 && gu.stride(1) == 1,
+           "moe_dswiglu: gu rows must be 16-byte aligned");
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(dy.device());
   const int device = dy.get_device();

@@ -24,6 +24,7 @@ SOURCES = [
     "gemm/gemm.cu",
     "fused/norm.cu",
     "fused/elementwise.cu",
+    "fused/sample.cu",
     "attn/attn_fwd.cu",
     "attn/attn_bwd.cu",
     "attn/decode.cu",
