@@ -170,7 +170,44 @@ template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, int nb, int row, bool row_ok,
                                              float alpha) {
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
-  if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_F32_ACC) {
+  if constexpr (EPI == EPI_F32_ACC) {
+    // C (fp32) is read 64 columns at a time (16 independent 16-byte loads in flight per
+    // thread) before the TMEM reads of those columns: the read-modify-write latency is
+    // paid BN/64 times per tile, which matters for short-K tiles (MoE weight gradients).
+    constexpr int QC = 64;
+    float* crow = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc;
+#pragma unroll 1
+    for (int q0 = 0; q0 < BN; q0 += QC) {
+      const int colq = nb * BN + q0;
+      const bool full = row_ok && colq + QC <= p.N;
+      float4 cq[QC / 4];
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < QC / 4; ++i) cq[i] = reinterpret_cast<const float4*>(crow + colq)[i];
+      }
+#pragma unroll
+      for (int c = 0; c < QC; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + q0 + c, r);
+        tmem_ld_wait();
+        const int col0 = colq + c;
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 o = cq[c / 4 + i];
+            reinterpret_cast<float4*>(crow + col0)[i] =
+                make_float4(o.x + __uint_as_float(r[4 * i]) * alpha, o.y + __uint_as_float(r[4 * i + 1]) * alpha,
+                            o.z + __uint_as_float(r[4 * i + 2]) * alpha, o.w + __uint_as_float(r[4 * i + 3]) * alpha);
+          }
+        } else if (row_ok && col0 < p.N) {
+          const int nv = min(32, p.N - col0);
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (i < nv) crow[col0 + i] += __uint_as_float(r[i]) * alpha;
+        }
+      }
+    }
+  } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       uint32_t r[32];
@@ -1144,7 +1181,8 @@ void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch:
   const int K = static_cast<int>(a.size(0));
   TT_CHECK(b.size(0) == K, "moe_wgrad: token rows differ");
   TT_CHECK(c.scalar_type() == torch::kFloat32 && c.size(0) == n_groups * M && c.size(1) == N && c.stride(1) == 1 &&
-               c.stride(0) % 4 == 0, "moe_wgrad: C must be fp32 [E*M, N]");
+               c.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
+           "moe_wgrad: C must be fp32 [E*M, N] with 16-byte aligned rows");
   const c10::cuda::CUDAGuard guard(a.device());
   const int device = a.get_device();
   if (!accumulate) c.zero_();  // empty experts' tiles are skipped
