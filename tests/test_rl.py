@@ -55,3 +55,25 @@ def test_group_advantages_and_grpo_kl():
     lp = torch.tensor([[-1.0, -1.0]])
     out = grpo_loss(lp, lp, torch.tensor([1.0]), torch.ones(1, 2), reference_log_probs=lp - 0.5, kl_coef=0.1)
     assert out.metrics["kl"].item() > 0
+
+
+def test_sampler_filter_matches_reference():
+    import pytest as _pytest
+    import ref_oracle
+
+    if not ref_oracle.available():
+        _pytest.skip("reference not installed under baseline/_ref")
+    from tinytron_b200.inference.sampler import filter_logits, sample_next_token_with_log_prob
+
+    with ref_oracle.cpu_reference():
+        from tinytron.inference.sampler import filter_logits as ref_filter
+        from tinytron.inference.sampler import sample_next_token_with_log_prob as ref_sample_lp
+    g = torch.Generator().manual_seed(0)
+    logits = torch.randn(6, 300, generator=g) * 3
+    for t, k, p in [(1.0, None, None), (0.7, 20, None), (1.3, None, 0.8), (0.9, 50, 0.6), (1.0, 1, None)]:
+        assert torch.equal(filter_logits(logits, t, k, p), ref_filter(logits, t, k, p)), (t, k, p)
+        torch.manual_seed(5)
+        ours = sample_next_token_with_log_prob(logits, t, k, p)
+        torch.manual_seed(5)
+        ref = ref_sample_lp(logits, t, k, p)
+        assert torch.equal(ours[0], ref[0]) and torch.allclose(ours[1], ref[1]), (t, k, p)
