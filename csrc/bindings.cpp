@@ -9,15 +9,16 @@ int64_t gemm_pair_mode();
 void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10::optional<torch::Tensor> gu_out);
 void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu, double alpha);
 void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2);
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair);
 void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, torch::Tensor gu_out,
-                        torch::Tensor grp_off, int64_t n_groups);
+                        torch::Tensor grp_off, int64_t n_groups, bool pair);
 void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
-                         torch::Tensor grp_off, int64_t n_groups);
+                         torch::Tensor grp_off, int64_t n_groups, bool pair);
 void moe_topk_softmax_op(torch::Tensor logits, int64_t k, torch::Tensor w, torch::Tensor sel);
 void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor sel, torch::Tensor dlogits);
-int64_t moe_row_capacity(int64_t P, int64_t E);
-void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair);
+int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align);
+void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair,
+                   int64_t align);
 void moe_gather_rows_op(torch::Tensor x, torch::Tensor row_pair, torch::Tensor grp_off, int64_t k, torch::Tensor out);
 void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k,
                     torch::Tensor out);
@@ -103,17 +104,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair_mode", &tt::gemm_pair_mode);
   m.def("moe_gemm", &tt::moe_gemm_op, "grouped GEMM over expert row segments (bf16 out)", py::arg("a"),
         py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("b_mn"), py::arg("b_grp_rows"),
-        py::arg("b_split_k") = 0, py::arg("b_off2") = 0);
+        py::arg("b_split_k") = 0, py::arg("b_off2") = 0, py::arg("pair") = false);
   m.def("moe_gemm_swiglu", &tt::moe_gemm_swiglu_op, "grouped gate|up GEMM with SwiGLU epilogue", py::arg("x"),
-        py::arg("w_gu"), py::arg("out"), py::arg("gu_out"), py::arg("grp_off"), py::arg("n_groups"));
+        py::arg("w_gu"), py::arg("out"), py::arg("gu_out"), py::arg("grp_off"), py::arg("n_groups"),
+        py::arg("pair") = false);
   m.def("moe_gemm_dswiglu", &tt::moe_gemm_dswiglu_op, "grouped down-proj dgrad with SwiGLU backward epilogue",
-        py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("dgu"), py::arg("grp_off"), py::arg("n_groups"));
+        py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("dgu"), py::arg("grp_off"), py::arg("n_groups"),
+        py::arg("pair") = false);
   m.def("moe_gemm_wgrad", &tt::moe_gemm_wgrad_op, "per-expert weight gradient over token segments (fp32)",
         py::arg("a"), py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("accumulate"));
   m.def("moe_topk_softmax", &tt::moe_topk_softmax_op, "router top-k + softmax over the selected logits");
   m.def("moe_topk_softmax_bwd", &tt::moe_topk_softmax_bwd_op, "backward of moe_topk_softmax");
-  m.def("moe_row_capacity", &tt::moe_row_capacity, "padded expert-row capacity for P pairs and E experts");
-  m.def("moe_layout", &tt::moe_layout_op, "expert segments (128-row aligned, stable) for the grouped GEMMs");
+  m.def("moe_row_capacity", &tt::moe_row_capacity, "padded expert-row capacity for P pairs and E experts",
+        py::arg("P"), py::arg("E"), py::arg("align") = 128);
+  m.def("moe_layout", &tt::moe_layout_op, "expert segments (128- or 256-row aligned, stable) for the grouped GEMMs",
+        py::arg("sel"), py::arg("E"), py::arg("grp_off"), py::arg("slot"), py::arg("row_pair"), py::arg("align") = 128);
   m.def("moe_gather_rows", &tt::moe_gather_rows_op, "x_rows[r] = x[token of row r], zero pad rows");
   m.def("moe_combine", &tt::moe_combine_op, "out[t] = sum_j w[t,j] y_rows[slot[t,j]]", py::arg("y_rows"),
         py::arg("slot"), py::arg("w"), py::arg("k"), py::arg("out"));

@@ -541,7 +541,26 @@ constexpr int STAGES2 = 6;
 constexpr uint32_t PAIR_A_BYTES = BM * BK * 2;
 constexpr uint32_t PAIR_B_BYTES = 128 * BK * 2;
 
-template <bool A_MN, bool B_MN, int EPI>
+// Grouped mode (GROUP_M, MoE experts): the token rows are laid out in expert segments
+// that start on multiples of 256 (so a pair tile never straddles two experts); the tile's
+// expert selects B's rows (K-major) or K offset (MN-major) as in the single-CTA kernel.
+template <int GROUP>
+__device__ __forceinline__ int pair_tile_group(const Params& p, int mb) {
+  if constexpr (GROUP != GROUP_M) {
+    return 0;
+  } else {
+    const int row = mb * 256;
+    int lo = 0, hi = p.n_groups - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (__ldg(p.grp_off + mid) <= row) lo = mid;
+      else hi = mid - 1;
+    }
+    return lo;
+  }
+}
+
+template <bool A_MN, bool B_MN, int EPI, int GROUP = GROUP_NONE>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   constexpr uint32_t TMEM_COLS = 2 * BN2;
@@ -562,11 +581,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  static_assert(GROUP != GROUP_K, "the pair kernel has no grouped-K mode");
   const uint32_t crank = cluster_ctarank();
   const bool leader = crank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1);
   const int n_pairs = static_cast<int>(gridDim.x >> 1);
-  const int M = p.M;
+  // GROUP_M: the row count is the padded token total, known only on the device.
+  const int M = (GROUP == GROUP_M) ? __ldg(p.grp_off + p.n_groups) : p.M;
   const int num_m = (M + 255) / 256;
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
   const int num_tiles = num_m * num_n;
@@ -609,9 +630,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         const int tile = unit / S, split = unit - (unit / S) * S;
         int mb, nb;
         tile_coords(tile, num_m, num_n, mb, nb);
+        const int grp_rows = (GROUP == GROUP_M) ? pair_tile_group<GROUP>(p, mb) * p.b_grp_rows : 0;
         const int a_row0 = mb * 256 + static_cast<int>(crank) * 128;
-        const int b_row0 = (EPI == EPI_SWIGLU) ? (crank ? p.b_row_offset2 : 0) + nb * 128
-                                               : nb * BN2 + static_cast<int>(crank) * 128;
+        // K-major B: first B row of this CTA's half; MN-major B: first N column of it.
+        const int b_row0 = (EPI == EPI_SWIGLU) ? (crank ? p.b_row_offset2 : 0) + grp_rows + nb * 128
+                           : (B_MN ? nb * BN2 + static_cast<int>(crank) * 128
+                                   : grp_rows + nb * BN2 + static_cast<int>(crank) * 128);
         const int kb_end = min(num_k, (split + 1) * kb_per);
         for (int kb = split * kb_per; kb < kb_end; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
@@ -632,8 +656,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
           if constexpr (!B_MN) {
             tma_load_2d_pair(b_dst, &tmB, bar, kc, b_row0);
           } else {
+            int kb_b = kc;
+            if constexpr (GROUP == GROUP_M)
+              kb_b = (kb < p.b_split_kb) ? grp_rows + kb * BK : p.b_off2 + grp_rows + (kb - p.b_split_kb) * BK;
 #pragma unroll
-            for (int c = 0; c < 2; ++c) tma_load_2d_pair(b_dst + c * (BK * 128), &tmB, bar, b_row0 + c * 64, kc);
+            for (int c = 0; c < 2; ++c) tma_load_2d_pair(b_dst + c * (BK * 128), &tmB, bar, b_row0 + c * 64, kb_b);
           }
           if (++stage == STAGES2) {
             stage = 0;
@@ -779,10 +806,10 @@ void launch_bn(int bn, const Params& p, const CUtensorMap& ta, const CUtensorMap
   }
 }
 
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, int GROUP = GROUP_NONE>
 void launch_pair(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, int device, cudaStream_t st) {
   constexpr size_t smem = static_cast<size_t>(STAGES2) * (PAIR_A_BYTES + PAIR_B_BYTES) + 1024 + 256;
-  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI>;
+  auto kern = gemm_pair_kernel<A_MN, B_MN, EPI, GROUP>;
   TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
   const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN) *
@@ -1070,8 +1097,10 @@ static void check_grp(const torch::Tensor& grp_off, int64_t n_groups, const torc
 //   b K-major: [n_groups * b_grp_rows, K], expert e's rows start at e * b_grp_rows.
 //   b MN-major: [rows, N] indexed by k; k-blocks < b_split_k/64 at e*b_grp_rows + k, the rest at
 //   b_off2 + e*b_grp_rows + (k - b_split_k) (gate|up weights stored as two stacked tensors).
+// pair: the caller laid the segments out on 256-row boundaries, so the CTA-pair kernel
+// may run the GEMM (TT_GEMM_PAIR=0 still forces the single-CTA kernel).
 void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2) {
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair) {
   using namespace gemm;
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
@@ -1086,7 +1115,8 @@ void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tenso
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(a.device());
   const int device = a.get_device();
-  const int bn = choose_bn(M, N, device);
+  const bool use2 = pair && pair_mode() != 0 && M >= 256;
+  const int bn = use2 ? 128 : choose_bn(M, N, device);
   const CUtensorMap ta = operand_map(a, false, BM);
   const CUtensorMap tb = operand_map(b, b_mn, bn);
   Params p = base_params(M, N, K, c, 1.0, c10::nullopt, device);
@@ -1095,6 +1125,11 @@ void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tenso
   p.b_grp_rows = static_cast<int>(b_grp_rows);
   p.b_split_kb = b_split_k > 0 ? static_cast<int>(b_split_k / BK) : (1 << 30);
   p.b_off2 = static_cast<int>(b_off2);
+  if (use2) {
+    if (b_mn) launch_pair<false, true, EPI_BF16, GROUP_M>(p, ta, tb, device, cur_stream());
+    else launch_pair<false, false, EPI_BF16, GROUP_M>(p, ta, tb, device, cur_stream());
+    return;
+  }
   if (b_mn)
     launch_bn<false, true, EPI_BF16, GROUP_M>(bn, p, ta, tb, device, cur_stream());
   else
@@ -1103,7 +1138,7 @@ void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tenso
 
 // act[cap, I] = silu(x_e Wg_e^T) * (x_e Wu_e^T) per expert; w_gu = [Wg (n_groups*I rows); Wu (same)].
 void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, torch::Tensor gu_out,
-                        torch::Tensor grp_off, int64_t n_groups) {
+                        torch::Tensor grp_off, int64_t n_groups, bool pair) {
   using namespace gemm;
   check_cuda_bf16(x, "x");
   check_cuda_bf16(w_gu, "w_gu");
@@ -1129,12 +1164,16 @@ void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, 
   p.grp_off = grp_off.data_ptr<int>();
   p.n_groups = static_cast<int>(n_groups);
   p.b_grp_rows = I;
+  if (pair && pair_mode() != 0 && M >= 256) {
+    launch_pair<false, false, EPI_SWIGLU, GROUP_M>(p, ta, tb, device, cur_stream());
+    return;
+  }
   launch_bn<false, false, EPI_SWIGLU, GROUP_M>(256, p, ta, tb, device, cur_stream());
 }
 
 // d(g|u)[cap, 2I] from dy_rows[cap, D], w_down [n_groups*D, I] and the saved g|u.
 void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
-                         torch::Tensor grp_off, int64_t n_groups) {
+                         torch::Tensor grp_off, int64_t n_groups, bool pair) {
   using namespace gemm;
   check_cuda_bf16(dy, "dy");
   check_cuda_bf16(w_down, "w_down");
@@ -1152,7 +1191,8 @@ void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(dy.device());
   const int device = dy.get_device();
-  const int bn = choose_bn(M, I, device);
+  const bool use2 = pair && pair_mode() != 0 && M >= 256;
+  const int bn = use2 ? 128 : choose_bn(M, I, device);
   const CUtensorMap ta = operand_map(dy, false, BM);
   const CUtensorMap tb = operand_map(w_down, true, bn);
   Params p = base_params(M, I, D, dgu, 1.0, c10::nullopt, device);
@@ -1165,6 +1205,10 @@ void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g
   p.n_groups = static_cast<int>(n_groups);
   p.b_grp_rows = D;
   p.b_split_kb = 1 << 30;
+  if (use2) {
+    launch_pair<false, true, EPI_DSWIGLU, GROUP_M>(p, ta, tb, device, cur_stream());
+    return;
+  }
   launch_bn<false, true, EPI_DSWIGLU, GROUP_M>(bn, p, ta, tb, device, cur_stream());
 }
 

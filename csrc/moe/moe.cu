@@ -5,7 +5,7 @@
 //   topk_softmax     : per token, the k largest router logits (descending) and the
 //                      softmax over them, one warp per token.
 //   layout           : expert segments of the grouped GEMMs.  Each expert's rows
-//                      start on a multiple of 128 (pad rows are zero), (token, j)
+//                      start on a multiple of 128 or 256 (pad rows are zero), (token, j)
 //                      pairs keep token order inside an expert (stable, so results
 //                      do not depend on atomics).  Writes grp_off[E+1], the padded
 //                      row of every pair (slot) and the pair of every row (row_pair).
@@ -120,7 +120,7 @@ __global__ void topk_softmax_bwd_kernel(const float* __restrict__ dw, const floa
 // Grid: one block per expert (1024 threads).  Every block builds the full histogram
 // (cheap: the pair list is a few hundred KB and stays in L2), so all offsets are known
 // without a second launch; block e then places its own pairs in token order.
-__global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ sel, int P, int E,
+__global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ sel, int P, int E, int align,
                                                      int* __restrict__ grp_off, int* __restrict__ slot,
                                                      int* __restrict__ row_pair, int* __restrict__ status) {
   __shared__ int hist[kMaxExperts];
@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ se
     int acc = 0;
     for (int i = 0; i < E; ++i) {
       off[i] = acc;
-      acc += (hist[i] + kRowAlign - 1) / kRowAlign * kRowAlign;
+      acc += (hist[i] + align - 1) / align * align;
     }
     off[E] = acc;
     running = 0;
@@ -312,21 +312,24 @@ void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor se
   TT_CUDA_CHECK(cudaGetLastError());
 }
 
-// Capacity of the padded row space for P pairs over E experts.
-int64_t moe_row_capacity(int64_t P, int64_t E) {
-  return (P + E * (moe::kRowAlign - 1) + moe::kRowAlign - 1) / moe::kRowAlign * moe::kRowAlign;
+// Capacity of the padded row space for P pairs over E experts, segments aligned to
+// `align` rows (128, or 256 for the CTA-pair grouped GEMM whose tiles span 256 rows).
+int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align) {
+  TT_CHECK(align == 128 || align == 256, "moe: segment alignment must be 128 or 256");
+  return (P + E * (align - 1) + align - 1) / align * align;
 }
 
-void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair) {
+void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair,
+                   int64_t align) {
   TT_CHECK(sel.is_cuda() && sel.scalar_type() == torch::kInt32 && sel.is_contiguous(), "layout: sel int32");
   const int P = static_cast<int>(sel.numel());
   TT_CHECK(E >= 1 && E <= moe::kMaxExperts, "layout: 1 <= E <= 256");
   TT_CHECK(grp_off.scalar_type() == torch::kInt32 && grp_off.numel() == E + 1 && slot.numel() == P &&
                slot.scalar_type() == torch::kInt32 && row_pair.scalar_type() == torch::kInt32 &&
-               row_pair.numel() >= moe_row_capacity(P, E), "layout: bad outputs");
+               row_pair.numel() >= moe_row_capacity(P, E, align), "layout: bad outputs");
   const c10::cuda::CUDAGuard guard(sel.device());
   moe::layout_kernel<<<static_cast<unsigned>(E), 1024, 0, cur_stream()>>>(
-      sel.data_ptr<int>(), P, static_cast<int>(E), grp_off.data_ptr<int>(), slot.data_ptr<int>(),
+      sel.data_ptr<int>(), P, static_cast<int>(E), static_cast<int>(align), grp_off.data_ptr<int>(), slot.data_ptr<int>(),
       row_pair.data_ptr<int>(), device_status_ptr(sel.get_device()));
   TT_CUDA_CHECK(cudaGetLastError());
 }

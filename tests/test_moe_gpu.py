@@ -26,14 +26,14 @@ def _route(N, E, k, seed=0, skew=0.0):
     return logits, w, sel
 
 
-def _layout(sel, E):
+def _layout(sel, E, align=128):
     C = ext()
     P = sel.numel()
-    cap = C.moe_row_capacity(P, E)
+    cap = C.moe_row_capacity(P, E, align)
     grp_off = torch.empty(E + 1, device="cuda", dtype=torch.int32)
     slot = torch.empty(P, device="cuda", dtype=torch.int32)
     row_pair = torch.empty(cap, device="cuda", dtype=torch.int32)
-    C.moe_layout(sel.reshape(-1), E, grp_off, slot, row_pair)
+    C.moe_layout(sel.reshape(-1), E, grp_off, slot, row_pair, align)
     return cap, grp_off, slot, row_pair
 
 
@@ -104,10 +104,10 @@ def test_gather_combine_and_backward():
     assert not torch.isnan(dy[:total].float()).any()
 
 
-def _expert_setup(N=1500, E=8, k=2, H=256, I=384, seed=0):
+def _expert_setup(N=1500, E=8, k=2, H=256, I=384, seed=0, align=128):
     g = torch.Generator(device="cuda").manual_seed(seed)
     _, w, sel = _route(N, E, k, seed=seed, skew=1.5)
-    cap, grp_off, slot, row_pair = _layout(sel, E)
+    cap, grp_off, slot, row_pair = _layout(sel, E, align)
     x = (torch.randn(N, H, device="cuda", generator=g)).bfloat16()
     wg = (torch.randn(E, I, H, device="cuda", generator=g) * 0.05).bfloat16()
     wu = (torch.randn(E, I, H, device="cuda", generator=g) * 0.05).bfloat16()
@@ -123,16 +123,21 @@ def _segments(s):
     return [(e, off[e], off[e + 1]) for e in range(s["E"])]
 
 
-def test_grouped_swiglu_down_forward():
+# (segment alignment, CTA-pair kernel): 256-aligned segments run on the pair kernel
+LAYOUTS = [(128, False), (256, True)]
+
+
+@pytest.mark.parametrize("align,pair", LAYOUTS)
+def test_grouped_swiglu_down_forward(align, pair):
     C = ext()
-    s = _expert_setup()
+    s = _expert_setup(align=align)
     cap, E, H, I = s["cap"], s["E"], s["H"], s["I"]
     w_gu = torch.cat([s["wg"].reshape(E * I, H), s["wu"].reshape(E * I, H)], 0)
     act = torch.empty(cap, I, device="cuda", dtype=torch.bfloat16)
     gu = torch.empty(cap, 2 * I, device="cuda", dtype=torch.bfloat16)
-    C.moe_gemm_swiglu(s["xr"], w_gu, act, gu, s["grp_off"], E)
+    C.moe_gemm_swiglu(s["xr"], w_gu, act, gu, s["grp_off"], E, pair)
     y = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
-    C.moe_gemm(act, s["wd"].reshape(E * H, I), y, s["grp_off"], E, False, H)
+    C.moe_gemm(act, s["wd"].reshape(E * H, I), y, s["grp_off"], E, False, H, 0, 0, pair)
     for e, a, b in _segments(s):
         if b == a:
             continue
@@ -145,9 +150,10 @@ def test_grouped_swiglu_down_forward():
         assert rel_err(y[a:b], act[a:b].float() @ s["wd"][e].float().t()) < 1e-2, e
 
 
-def test_grouped_backward_gemms():
+@pytest.mark.parametrize("align,pair", LAYOUTS)
+def test_grouped_backward_gemms(align, pair):
     C = ext()
-    s = _expert_setup(seed=1)
+    s = _expert_setup(seed=1, align=align)
     cap, E, H, I = s["cap"], s["E"], s["H"], s["I"]
     gen = torch.Generator(device="cuda").manual_seed(7)
     gu = (torch.randn(cap, 2 * I, device="cuda", generator=gen)).bfloat16()
@@ -159,11 +165,11 @@ def test_grouped_backward_gemms():
     act[:total][pad] = 0
     # down dgrad fused with the SwiGLU backward
     dgu = torch.empty(cap, 2 * I, device="cuda", dtype=torch.bfloat16)
-    C.moe_gemm_dswiglu(dy, s["wd"].reshape(E * H, I), gu, dgu, s["grp_off"], E)
+    C.moe_gemm_dswiglu(dy, s["wd"].reshape(E * H, I), gu, dgu, s["grp_off"], E, pair)
     # gate|up dgrad (B = stacked gate / up weights, MN-major, split at I)
     w_gu = torch.cat([s["wg"].reshape(E * I, H), s["wu"].reshape(E * I, H)], 0)
     dx = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
-    C.moe_gemm(dgu, w_gu, dx, s["grp_off"], E, True, I, I, E * I)
+    C.moe_gemm(dgu, w_gu, dx, s["grp_off"], E, True, I, I, E * I, pair)
     # weight grads, accumulated into fp32
     gwd = torch.ones(E * H, I, device="cuda")
     C.moe_gemm_wgrad(dy, act, gwd, s["grp_off"], E, True)

@@ -38,7 +38,7 @@ from tinytron_b200.ops.weights import bf16_of, concat_rows, main_grad_of, notify
 
 from .symm import SymmetricHeap
 
-ALIGN_ROWS = 128
+ALIGN_ROWS = 256  # expert segments on 256-row boundaries: the grouped GEMMs may use the CTA-pair kernel
 
 
 def _C():
@@ -167,8 +167,8 @@ def experts_forward(bufs: EPBuffers, plan: Plan, xr: torch.Tensor, w_gu: torch.T
     gu = torch.empty(plan.total, 2 * I, device=dev, dtype=torch.bfloat16)
     yr = bufs.buf_b[:plan.total]
     if plan.total > 0:
-        C.moe_gemm_swiglu(xr, w_gu, act, gu, plan.grp_off, plan.E_local)
-        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H)
+        C.moe_gemm_swiglu(xr, w_gu, act, gu, plan.grp_off, plan.E_local, True)
+        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H, 0, 0, True)
     return act, gu
 
 
@@ -201,9 +201,9 @@ def experts_backward(bufs: EPBuffers, plan: Plan, dyr, xr, act, gu, w_gu, wd, I,
     C = _C()
     E_l = plan.E_local
     dgu = torch.empty(plan.total, 2 * I, device=dyr.device, dtype=torch.bfloat16)
-    C.moe_gemm_dswiglu(dyr, wd, gu, dgu, plan.grp_off, E_l)
+    C.moe_gemm_dswiglu(dyr, wd, gu, dgu, plan.grp_off, E_l, True)
     C.moe_gemm_wgrad(dyr, act, g_down, plan.grp_off, E_l, True)
-    C.moe_gemm(dgu, w_gu, bufs.buf_b[:plan.total], plan.grp_off, E_l, True, I, I, E_l * I)
+    C.moe_gemm(dgu, w_gu, bufs.buf_b[:plan.total], plan.grp_off, E_l, True, I, I, E_l * I, True)
     C.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, plan.grp_off, E_l, True)
     C.moe_gemm_wgrad(dgu[:, I:], xr, g_up, plan.grp_off, E_l, True)
 
