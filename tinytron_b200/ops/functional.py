@@ -168,9 +168,11 @@ def _expert_grad(param, shape2d):
     return torch.zeros(shape2d, device=param.device, dtype=torch.float32), False
 
 
-# Expert segments start on 256-row boundaries, so the CTA-pair kernel (256-row tiles)
-# can run the grouped GEMMs; the padding costs at most 255 rows per expert.
-MOE_ALIGN = 256
+# Expert segments start on 256-row boundaries when experts average at least 256 rows
+# (training), so the CTA-pair kernel (256-row tiles) can run the grouped GEMMs; with few
+# rows per expert (decode) 128-row segments halve the padding and the single-CTA kernel runs.
+def moe_align(pairs: int, experts: int) -> int:
+    return 256 if pairs >= 256 * experts else 128
 
 
 class MoEExpertsFn(torch.autograd.Function):
@@ -194,21 +196,23 @@ class MoEExpertsFn(torch.autograd.Function):
         c = C()
         sel32 = sel.reshape(-1).to(torch.int32).contiguous()
         P = sel32.numel()
-        cap = c.moe_row_capacity(P, E, MOE_ALIGN)
+        align = moe_align(P, E)
+        pair = align == 256
+        cap = c.moe_row_capacity(P, E, align)
         dev = x.device
         grp_off = torch.empty(E + 1, device=dev, dtype=torch.int32)
         slot = torch.empty(P, device=dev, dtype=torch.int32)
         row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
-        c.moe_layout(sel32, E, grp_off, slot, row_pair, MOE_ALIGN)
+        c.moe_layout(sel32, E, grp_off, slot, row_pair, align)
         xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
         c.moe_gather_rows(x2d, row_pair, grp_off, k, xr)
         w_gu = concat_rows([bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
         wd = bf16_of(w_down).view(E * H, I)
         act = torch.empty(cap, I, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
-        c.moe_gemm_swiglu(xr, w_gu, act, gu, grp_off, E, True)
+        c.moe_gemm_swiglu(xr, w_gu, act, gu, grp_off, E, pair)
         yr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
-        c.moe_gemm(act, wd, yr, grp_off, E, False, H, 0, 0, True)
+        c.moe_gemm(act, wd, yr, grp_off, E, False, H, 0, 0, pair)
         w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
         out = torch.empty(N, H, device=dev, dtype=torch.bfloat16)
         c.moe_combine(yr, slot, w32, k, out)
@@ -216,6 +220,7 @@ class MoEExpertsFn(torch.autograd.Function):
         ctx.w32 = w32
         ctx.params = (w_gate, w_up, w_down)
         ctx.dims = (N, H, E, I, k, cap)
+        ctx.pair = pair
         ctx.shape = shape
         ctx.has_w = weights is not None
         return out.view(shape)
@@ -233,11 +238,11 @@ class MoEExpertsFn(torch.autograd.Function):
         dw = torch.empty(N * k, device=dev, dtype=torch.float32)
         c.moe_combine_bwd(d2d, yr, row_pair, w32, grp_off, k, dyr, dw)
         dgu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
-        c.moe_gemm_dswiglu(dyr, wd, gu, dgu, grp_off, E, True)
+        c.moe_gemm_dswiglu(dyr, wd, gu, dgu, grp_off, E, ctx.pair)
         g_down, main_d = _expert_grad(w_down, (E * H, I))
         c.moe_gemm_wgrad(dyr, act, g_down, grp_off, E, True)
         dxr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
-        c.moe_gemm(dgu, w_gu, dxr, grp_off, E, True, I, I, E * I, True)
+        c.moe_gemm(dgu, w_gu, dxr, grp_off, E, True, I, I, E * I, ctx.pair)
         g_gate, main_g = _expert_grad(w_gate, (E * I, H))
         g_up, main_u = _expert_grad(w_up, (E * I, H))
         c.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, grp_off, E, True)

@@ -10,7 +10,7 @@ Here, per MoE layer and micro-step:
 1. routing metadata on the device (per-expert counts, each pair's rank within its
    expert); one small kernel all-gathers the [E] count vectors into a [world, E]
    matrix in every rank's heap; the host reads that matrix (the only host sync,
-   64 x world ints) and computes every rank's 128-row-aligned expert segments, so
+   64 x world ints) and computes every rank's 128- or 256-row-aligned expert segments, so
    each (token, slot) pair knows its destination row in the owner's buffer;
 2. ``ep_scatter``: a warp per pair stores the token row straight into the owner's
    expert-grouped receive buffer (no send-side sort copy, no all-to-all);
@@ -38,7 +38,7 @@ from tinytron_b200.ops.weights import bf16_of, concat_rows, main_grad_of, notify
 
 from .symm import SymmetricHeap
 
-ALIGN_ROWS = 256  # expert segments on 256-row boundaries: the grouped GEMMs may use the CTA-pair kernel
+ALIGN_ROWS = 256  # largest segment alignment (capacity bound); see plan_finish
 
 
 def _C():
@@ -107,7 +107,7 @@ def get_ep_buffers(group, E: int, H: int, tokens: int, k: int, device=None) -> E
 class Plan:
     """Where every (token, slot) pair of this rank goes, and this rank's receive layout."""
 
-    __slots__ = ("tgt", "dst", "grp_off", "seg_cnt", "total", "k", "N", "E_local")
+    __slots__ = ("tgt", "dst", "grp_off", "seg_cnt", "total", "k", "N", "E_local", "pair")
 
 
 def plan_routes(bufs: EPBuffers, sel: torch.Tensor) -> torch.Tensor:
@@ -127,7 +127,9 @@ def plan_finish(bufs: EPBuffers, sel: torch.Tensor, counts: torch.Tensor, M: np.
     if M is None:
         M = bufs.counts.cpu().numpy().astype(np.int64)  # host sync: world x E ints
     n = M.sum(0).reshape(world, E_l)  # rows each owner receives per local expert
-    seg = (n + ALIGN_ROWS - 1) // ALIGN_ROWS * ALIGN_ROWS
+    # 256-row segments (CTA-pair grouped GEMMs) when experts average >= 256 rows, else 128
+    align = 256 if int(M.sum()) >= 256 * E else 128
+    seg = (n + align - 1) // align * align
     seg_off = np.cumsum(seg, axis=1) - seg  # [world, E_l] segment starts in each owner's buffer
     src_before = np.cumsum(M, axis=0) - M  # [world(src), E] rows of earlier sources
     base = seg_off.reshape(E) + src_before[rank]  # [E] first row of this rank's pairs per expert
@@ -147,6 +149,7 @@ def plan_finish(bufs: EPBuffers, sel: torch.Tensor, counts: torch.Tensor, M: np.
     p.grp_off = torch.tensor(list(seg_off[rank]) + [total], dtype=torch.int32, device=dev)
     p.seg_cnt = torch.tensor(n[rank], dtype=torch.int32, device=dev)
     p.total, p.k, p.N, p.E_local = total, k, N, E_l
+    p.pair = align == 256
     return p
 
 
@@ -167,8 +170,8 @@ def experts_forward(bufs: EPBuffers, plan: Plan, xr: torch.Tensor, w_gu: torch.T
     gu = torch.empty(plan.total, 2 * I, device=dev, dtype=torch.bfloat16)
     yr = bufs.buf_b[:plan.total]
     if plan.total > 0:
-        C.moe_gemm_swiglu(xr, w_gu, act, gu, plan.grp_off, plan.E_local, True)
-        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H, 0, 0, True)
+        C.moe_gemm_swiglu(xr, w_gu, act, gu, plan.grp_off, plan.E_local, plan.pair)
+        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H, 0, 0, plan.pair)
     return act, gu
 
 
@@ -201,9 +204,9 @@ def experts_backward(bufs: EPBuffers, plan: Plan, dyr, xr, act, gu, w_gu, wd, I,
     C = _C()
     E_l = plan.E_local
     dgu = torch.empty(plan.total, 2 * I, device=dyr.device, dtype=torch.bfloat16)
-    C.moe_gemm_dswiglu(dyr, wd, gu, dgu, plan.grp_off, E_l, True)
+    C.moe_gemm_dswiglu(dyr, wd, gu, dgu, plan.grp_off, E_l, plan.pair)
     C.moe_gemm_wgrad(dyr, act, g_down, plan.grp_off, E_l, True)
-    C.moe_gemm(dgu, w_gu, bufs.buf_b[:plan.total], plan.grp_off, E_l, True, I, I, E_l * I, True)
+    C.moe_gemm(dgu, w_gu, bufs.buf_b[:plan.total], plan.grp_off, E_l, True, I, I, E_l * I, plan.pair)
     C.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, plan.grp_off, E_l, True)
     C.moe_gemm_wgrad(dgu[:, I:], xr, g_up, plan.grp_off, E_l, True)
 
