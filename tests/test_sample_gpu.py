@@ -45,10 +45,15 @@ def test_sampling_distribution_matches_filtered_softmax(temperature, top_k, top_
     assert kept[tok].all(), "sampled a token the reference filter removes"
     # the log-prob returned for each draw is the reference's
     assert (lp - ref_lp[tok]).abs().max().item() < 1e-3
-    # empirical frequencies vs the filtered distribution (total variation)
+    # empirical frequencies vs the filtered distribution (total variation), against the
+    # sampling noise of an equally sized torch.multinomial draw from the same distribution
+    probs = ref_lp.exp()
     freq = torch.bincount(tok, minlength=V).float() / B
-    tv = 0.5 * (freq - ref_lp.exp()).abs().sum().item()
-    assert tv < 0.03, tv
+    tv = 0.5 * (freq - probs).abs().sum().item()
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    noise = torch.bincount(torch.multinomial(probs, B, replacement=True, generator=gen), minlength=V).float() / B
+    tv_noise = 0.5 * (noise - probs).abs().sum().item()
+    assert tv < 1.5 * tv_noise + 0.01, (tv, tv_noise)
 
 
 def test_seed_reproducible_and_rows_independent():
