@@ -114,10 +114,19 @@ struct DecodeParams {
   int* status;
 };
 
+// One CTA per (split of 256 keys, kv head, sequence).
+//   scores: a thread per key (2 keys per thread): the key's row is read with 16-byte
+//           loads (all independent, so a warp has 32 rows in flight) and dotted with the
+//           G query heads held in shared memory (broadcast reads; no shuffles);
+//   softmax: chunk max and sum per head (block reductions);
+//   P.V:    each warp takes every 4th key; a lane owns D/32 dims, so a warp reads whole V
+//           rows; 8 keys per step keep 8 loads in flight per lane; the 4 warp partials
+//           are summed in warp order.  Key rows come from a per-chunk table in shared
+//           memory filled during the score pass (one page-table lookup per key).
 template <int D>
 __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeParams p) {
-  constexpr int LPL = D / 32;  // dims per lane in the score pass
-  static_assert(LPL == 2 || LPL == 4, "head_dim 64 or 128");
+  static_assert(D == 64 || D == 128, "head_dim 64 or 128");
+  constexpr int NV = D / 8;                // uint4 per K row
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int G = p.Hq / p.Hkv;
   const int L = (p.len_dev != nullptr ? *p.len_dev : 0) + p.len_host;
@@ -127,53 +136,53 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodePara
   __shared__ float s_s[kMaxG][kChunk];
   __shared__ float red_s[kThreads / 32][kMaxG];
   __shared__ float m_s[kMaxG], l_s[kMaxG];
-  __shared__ float o_s[2][kMaxG][D];
+  __shared__ float o_s[kThreads / 32][kMaxG][D];
+  __shared__ long long rows_s[kChunk];  // page-pool row of each key of the chunk (-1: unmapped)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
     q_s[g][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.Hq + kvh * G + g) * D + d]);
   }
-  __syncthreads();
   const long long pt_row = static_cast<long long>(b) * p.pages_per_seq;
-  // ---- scores: one warp per key
-  for (int j = warp; j < n; j += kThreads / 32) {
+  // row index of key j (chunk-relative) in the page pool, or -1 when unmapped
+  auto key_row = [&](int j) -> long long {
     const int key = j0 + j;
     const int pi = key / p.page_size;
     const int page = pi < p.pages_per_seq ? p.page_table[pt_row + pi] : -1;
+    if (page < 0 || page >= p.num_pages) return -1;
+    return static_cast<long long>(page) * p.page_size + key % p.page_size;
+  };
+  __syncthreads();
+  // ---- scores: a thread per key
+  for (int j = tid; j < n; j += kThreads) {
+    const long long row = key_row(j);
+    rows_s[j] = row;
     float acc[kMaxG];
 #pragma unroll
     for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
-    if (page >= 0 && page < p.num_pages) {
-      const __nv_bfloat16* kr =
-          p.k_pages + ((static_cast<long long>(page) * p.page_size + key % p.page_size) * p.Hkv + kvh) * D;
-      float kv[LPL];
-      if constexpr (LPL == 4) {
-        const uint2 u = *reinterpret_cast<const uint2*>(kr + lane * 4);
-        const float2 a = unpack_bf16x2(u.x), c = unpack_bf16x2(u.y);
-        kv[0] = a.x; kv[1] = a.y; kv[2] = c.x; kv[3] = c.y;
-      } else {
-        const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(kr + lane * 2));
-        kv[0] = a.x; kv[1] = a.y;
-      }
+    if (row >= 0) {
+      const uint4* kr = reinterpret_cast<const uint4*>(p.k_pages + (row * p.Hkv + kvh) * D);
+      uint4 kv[NV];
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g) {
-        if (g < G) {
+      for (int c = 0; c < NV; ++c) kv[c] = kr[c];
 #pragma unroll
-          for (int e = 0; e < LPL; ++e) acc[g] += kv[e] * q_s[g][lane * LPL + e];
+      for (int c = 0; c < NV; ++c) {
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(&kv[c]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(w[e]);
+#pragma unroll
+          for (int g = 0; g < kMaxG; ++g) {
+            if (g < G) acc[g] += f.x * q_s[g][8 * c + 2 * e] + f.y * q_s[g][8 * c + 2 * e + 1];
+          }
         }
       }
-    } else if (lane == 0) {
+    } else {
       atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
     }
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-      if (g < G) {
-        float v = acc[g];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (lane == 0) s_s[g][j] = v * p.scale_log2;
-      }
-    }
+    for (int g = 0; g < kMaxG; ++g)
+      if (g < G) s_s[g][j] = acc[g] * p.scale_log2;
   }
   __syncthreads();
   // ---- chunk max per head
@@ -210,62 +219,69 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodePara
     for (int w = 0; w < kThreads / 32; ++w) l += red_s[w][tid];
     l_s[tid] = l;
   }
-  // ---- P·V: thread owns dims (2 per thread), the two halves of the block split keys
-  constexpr int DT = D / 2;          // threads per key half (each owns 2 dims)
-  const int half = tid / DT;         // 0 or 1 when D == 128; D == 64 -> 0..3 (keys split 4 ways)
-  constexpr int NH = kThreads / DT;  // key partitions
-  const int d2 = (tid % DT) * 2;
-  float oacc[kMaxG][2];
+  // ---- P.V: warp w takes keys w, w+4, ...; lane owns D/32 consecutive dims (one 8- or
+  // 4-byte load per key, a warp reads whole V rows); 8 keys per step, all loads in flight.
+  constexpr int DPL = D / 32;
+  float oacc[kMaxG][DPL];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g) oacc[g][0] = oacc[g][1] = 0.f;
-  for (int j = half; j < n; j += NH) {
-    const int key = j0 + j;
-    const int pi = key / p.page_size;
-    const int page = pi < p.pages_per_seq ? p.page_table[pt_row + pi] : -1;
-    if (page < 0 || page >= p.num_pages) continue;
-    const __nv_bfloat16* vr =
-        p.v_pages + ((static_cast<long long>(page) * p.page_size + key % p.page_size) * p.Hkv + kvh) * D;
-    const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr + d2));
+  for (int g = 0; g < kMaxG; ++g)
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) {
-      if (g < G) {
-        const float pr = s_s[g][j];
-        oacc[g][0] += pr * vv.x;
-        oacc[g][1] += pr * vv.y;
+    for (int e = 0; e < DPL; ++e) oacc[g][e] = 0.f;
+  constexpr int NW = kThreads / 32;
+  for (int jb = warp; jb < n; jb += 8 * NW) {
+    float vv[8][DPL];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = jb + u * NW;
+      const long long row = j < n ? rows_s[j] : -1;
+      if (row >= 0) {
+        const __nv_bfloat16* vr = p.v_pages + (row * p.Hkv + kvh) * D + lane * DPL;
+        if constexpr (DPL == 4) {
+          const uint2 w = *reinterpret_cast<const uint2*>(vr);
+          const float2 a = unpack_bf16x2(w.x), c = unpack_bf16x2(w.y);
+          vv[u][0] = a.x; vv[u][1] = a.y; vv[u][2] = c.x; vv[u][3] = c.y;
+        } else {
+          const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr));
+          vv[u][0] = a.x; vv[u][1] = a.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < DPL; ++e) vv[u][e] = 0.f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = jb + u * NW;
+      if (j < n) {
+#pragma unroll
+        for (int g = 0; g < kMaxG; ++g) {
+          if (g < G) {
+            const float pr = s_s[g][j];
+#pragma unroll
+            for (int e = 0; e < DPL; ++e) oacc[g][e] += pr * vv[u][e];
+          }
+        }
       }
     }
   }
-  // reduce the NH key partitions through shared memory (NH is 2 or 4)
-  for (int part = 1; part < NH; ++part) {
-    __syncthreads();
-    if (half == part) {
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g)
-        if (g < G) {
-          o_s[part & 1][g][d2] = oacc[g][0];
-          o_s[part & 1][g][d2 + 1] = oacc[g][1];
-        }
-    }
-    __syncthreads();
-    if (half == 0) {
+  for (int g = 0; g < kMaxG; ++g)
+    if (g < G) {
 #pragma unroll
-      for (int g = 0; g < kMaxG; ++g)
-        if (g < G) {
-          oacc[g][0] += o_s[part & 1][g][d2];
-          oacc[g][1] += o_s[part & 1][g][d2 + 1];
-        }
+      for (int e = 0; e < DPL; ++e) o_s[warp][g][lane * DPL + e] = oacc[g][e];
     }
-  }
   __syncthreads();
-  if (half == 0) {
-    for (int g = 0; g < G; ++g) {
-      const long long row = (static_cast<long long>(b) * p.Hq + kvh * G + g) * p.splits + split;
-      p.o_part[row * D + d2] = oacc[g][0];
-      p.o_part[row * D + d2 + 1] = oacc[g][1];
-      if (d2 == 0) {
-        p.ml_part[row * 2] = n > 0 ? m_s[g] : -INFINITY;
-        p.ml_part[row * 2 + 1] = n > 0 ? l_s[g] : 0.f;
-      }
+  // sum the NW partitions in warp order: thread handles (g, d) pairs
+  for (int i = tid; i < G * D; i += kThreads) {
+    const int g = i / D, d = i % D;
+    float o = 0.f;
+#pragma unroll
+    for (int w = 0; w < NW; ++w) o += o_s[w][g][d];
+    const long long rowo = (static_cast<long long>(b) * p.Hq + kvh * G + g) * p.splits + split;
+    p.o_part[rowo * D + d] = o;
+    if (d == 0) {
+      p.ml_part[rowo * 2] = n > 0 ? m_s[g] : -INFINITY;
+      p.ml_part[rowo * 2 + 1] = n > 0 ? l_s[g] : 0.f;
     }
   }
 }

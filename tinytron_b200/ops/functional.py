@@ -15,7 +15,7 @@ import torch
 
 from . import _ext
 from .rope import rope_tables
-from .weights import adjacent_views, bf16_of, concat_rows, main_grad_of, notify_grad_ready
+from .weights import adjacent_views, bf16_of, concat_rows, concat_rows_cached, main_grad_of, notify_grad_ready
 
 
 def C():
@@ -78,7 +78,8 @@ class LinearFn(torch.autograd.Function):
     def forward(ctx, x, *weights):
         shape = x.shape
         x2d = _bf16(x.reshape(-1, shape[-1]))
-        w16 = concat_rows([bf16_of(w) for w in weights])
+        w16 = concat_rows_cached(weights[0], "_tt_cat", [bf16_of(w) for w in weights]) if len(weights) > 1 \
+            else bf16_of(weights[0])
         y = gemm_nt(x2d, w16)
         ctx.save_for_backward(x2d, w16)
         ctx.weights = weights
@@ -109,7 +110,7 @@ class SwiGLUMLPFn(torch.autograd.Function):
         shape = x.shape
         x2d = _bf16(x.reshape(-1, shape[-1]))
         M = x2d.shape[0]
-        w_gu = concat_rows([bf16_of(w_gate), bf16_of(w_up)])
+        w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate), bf16_of(w_up)])
         wd = bf16_of(w_down)
         I = w_gate.shape[0]
         act = torch.empty(M, I, device=x.device, dtype=torch.bfloat16)
@@ -206,7 +207,7 @@ class MoEExpertsFn(torch.autograd.Function):
         c.moe_layout(sel32, E, grp_off, slot, row_pair, align)
         xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
         c.moe_gather_rows(x2d, row_pair, grp_off, k, xr)
-        w_gu = concat_rows([bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
+        w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
         wd = bf16_of(w_down).view(E * H, I)
         act = torch.empty(cap, I, device=dev, dtype=torch.bfloat16)
         gu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)

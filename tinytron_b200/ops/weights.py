@@ -81,3 +81,19 @@ def notify_grad_ready(params) -> None:
         cb = p.__dict__.get("_tt_grad_ready")
         if cb is not None:
             cb(p)
+
+
+def concat_rows_cached(owner: torch.Tensor, key: str, tensors: list[torch.Tensor]) -> torch.Tensor:
+    """:func:`concat_rows`, but when a copy is needed (the tensors are not adjacent, e.g.
+    separate bf16 shadows outside a flat buffer) the copy is kept on ``owner`` and reused
+    while every source tensor keeps its storage and version (weights at inference)."""
+    if adjacent_views(tensors):
+        return concat_rows(tensors)
+    d = owner.__dict__
+    stamp = tuple((t.data_ptr(), t._version) for t in tensors)
+    hit = d.get(key)
+    if hit is not None and hit[0] == stamp:
+        return hit[1]
+    out = torch.cat(tensors, 0)
+    d[key] = (stamp, out)
+    return out

@@ -34,7 +34,7 @@ import numpy as np
 import torch
 import torch.distributed as dist
 
-from tinytron_b200.ops.weights import bf16_of, concat_rows, main_grad_of, notify_grad_ready
+from tinytron_b200.ops.weights import bf16_of, concat_rows_cached, main_grad_of, notify_grad_ready
 
 from .symm import SymmetricHeap
 
@@ -231,7 +231,7 @@ class EPMoEFn(torch.autograd.Function):
         counts = plan_routes(bufs, sel)
         plan = plan_finish(bufs, sel, counts)
         xr = dispatch(bufs, plan, x2d)
-        w_gu = concat_rows([bf16_of(w_gate).view(E_l * I, H), bf16_of(w_up).view(E_l * I, H)])
+        w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate).view(E_l * I, H), bf16_of(w_up).view(E_l * I, H)])
         wd = bf16_of(w_down).view(E_l * H, I)
         act, gu = experts_forward(bufs, plan, xr, w_gu, wd, I)
         w32 = weights.reshape(-1).float().contiguous()
