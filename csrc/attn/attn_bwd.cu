@@ -97,9 +97,13 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + BLOCK_B - 1) / BLOCK_B;
-  const int kt = static_cast<int>(blockIdx.x);  // low kt = most work; launched first
-  const int g = blockIdx.y;
-  const int b = blockIdx.z;
+  // 1-D grid ordered key tile slowest, (kv head, batch) fastest: the block scheduler hands
+  // out blocks in index order, so every low-kt (longest, causal) tile of every head starts in
+  // the first wave and the short tiles fill the tail (longest-first list scheduling).
+  const int n_gb = p.Hkv * p.B;
+  const int kt = static_cast<int>(blockIdx.x) / n_gb;
+  const int g = static_cast<int>(blockIdx.x) % p.Hkv;
+  const int b = (static_cast<int>(blockIdx.x) % n_gb) / p.Hkv;
   const int group = p.Hq / p.Hkv;
   const int qt0 = p.causal ? kt : 0;
   const int per_head = n_qt - qt0;
@@ -565,7 +569,7 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   p.causal = causal ? 1 : 0;
   p.status = device_status_ptr(q.get_device());
   const CUtensorMap tq = attn_head_map(q), tk = attn_head_map(k), tv = attn_head_map(v), tdo = attn_head_map(dout);
-  dim3 grid(static_cast<unsigned>((T + BLOCK_B - 1) / BLOCK_B), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  const dim3 grid(static_cast<unsigned>((T + BLOCK_B - 1) / BLOCK_B * Hkv * B));
   if (D == 128) {
     const size_t smem = std::min<size_t>(bwd_smem_bytes<128>() + 1024, size_t(232448));
     TT_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -109,9 +109,13 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int n_qt = (p.T + BLOCK - 1) / BLOCK;
   const int n_pairs = (n_qt + 1) / 2;
-  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x);  // heaviest tiles first
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  // 1-D grid ordered tile pair slowest, (head, batch) fastest, heaviest pairs first: the block
+  // scheduler hands out blocks in index order, so the long causal tiles of every head run in
+  // the first wave and the short ones fill the tail (longest-first list scheduling).
+  const int n_hb = p.Hq * p.B;
+  const int pair = n_pairs - 1 - static_cast<int>(blockIdx.x) / n_hb;
+  const int h = static_cast<int>(blockIdx.x) % p.Hq;
+  const int b = (static_cast<int>(blockIdx.x) % n_hb) / p.Hq;
   const int g = h / (p.Hq / p.Hkv);
   const int k_row0 = b * p.Tk;
   int n_x[2];
@@ -477,7 +481,7 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t q_col0,
     p.skip_math = skip;
   }
   const CUtensorMap tq = head_map(q), tk = head_map(k), tv = head_map(v);
-  dim3 grid(static_cast<unsigned>(((T + BLOCK - 1) / BLOCK + 1) / 2), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
+  const dim3 grid(static_cast<unsigned>(((T + BLOCK - 1) / BLOCK + 1) / 2 * Hq * B));
   static const int variant = [] { const char* e = std::getenv("TT_ATTN_VARIANT"); return e ? std::atoi(e) : kDefaultVariant; }();
   auto launch = [&](auto kern, size_t smem) {
     TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

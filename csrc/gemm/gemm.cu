@@ -65,7 +65,7 @@ struct Params {
   int b_off2;
   int c_grp_rows;              // GROUP_K: per-group row offset of C
   // CTA-pair kernel, fp32-accumulate epilogue only: the reduction is split into split_k
-  // ranges whose epilogues add into C one after another (split s waits until the 8
+  // ranges whose epilogues add into C one after another (split s waits until the 16
   // epilogue warps of split s-1 counted themselves in splitk_flags[tile]), so the sum
   // order is fixed and results are deterministic.
   int split_k;
@@ -167,9 +167,12 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&v)[N
 // Epilogue of one 128-row accumulator slice: thread = one TMEM lane = one output row.
 // Drains BN fp32 columns from TMEM (t_row) and applies EPI; nb is the tile's column block.
 template <int BN, int EPI>
+// [c_lo, c_hi): the slice of output columns of the tile this thread handles (the CTA-pair
+// kernel splits a row between two epilogue warpgroups); defaults cover the whole tile.
 __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, int nb, int row, bool row_ok,
-                                             float alpha) {
+                                             float alpha, int c_lo = 0, int c_hi = 1 << 30) {
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
+  c_hi = min(c_hi, OUT_BN);
   if constexpr (EPI == EPI_F32_ACC) {
     // C (fp32) is read 64 columns at a time (16 independent 16-byte loads in flight per
     // thread) before the TMEM reads of those columns: the read-modify-write latency is
@@ -177,7 +180,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
     constexpr int QC = 64;
     float* crow = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc;
 #pragma unroll 1
-    for (int q0 = 0; q0 < BN; q0 += QC) {
+    for (int q0 = c_lo; q0 < c_hi; q0 += QC) {
       const int colq = nb * BN + q0;
       const bool full = row_ok && colq + QC <= p.N;
       float4 cq[QC / 4];
@@ -209,7 +212,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
     }
   } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
+    for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
       uint32_t r[32];
       tmem_ld32(t_row + c0, r);
       tmem_ld_wait();
@@ -248,7 +251,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
     }
   } else if constexpr (EPI == EPI_SWIGLU) {
 #pragma unroll 1
-    for (int c0 = 0; c0 < OUT_BN; c0 += 16) {
+    for (int c0 = c_lo; c0 < c_hi; c0 += 16) {
       uint32_t g[16], u[16];
       tmem_ld16(t_row + c0, g);
       tmem_ld16(t_row + OUT_BN + c0, u);
@@ -279,7 +282,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
     const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
     __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
 #pragma unroll 1
-    for (int q0 = 0; q0 < BN; q0 += QC) {
+    for (int q0 = c_lo; q0 < c_hi; q0 += QC) {
       const int colq = nb * BN + q0;
       const bool full = row_ok && colq + QC <= p.N;
       uint4 gq[QC / 8], uq[QC / 8];
@@ -538,6 +541,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 // operand traffic per flop drops by a third.
 constexpr int BN2 = 256;
 constexpr int STAGES2 = 6;
+constexpr int PAIR_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 epilogue (two warpgroups)
 constexpr uint32_t PAIR_A_BYTES = BM * BK * 2;
 constexpr uint32_t PAIR_B_BYTES = 128 * BK * 2;
 
@@ -561,7 +565,7 @@ __device__ __forceinline__ int pair_tile_group(const Params& p, int mb) {
 }
 
 template <bool A_MN, bool B_MN, int EPI, int GROUP = GROUP_NONE>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, const Params p) {
   constexpr uint32_t TMEM_COLS = 2 * BN2;
   constexpr uint32_t IDESC = idesc_bf16_f32(256, BN2, A_MN, B_MN);
@@ -605,7 +609,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);  // one arrival per epilogue warp, 4 warps x 2 CTAs
+      mbar_init(&acc_empty[b], 16);  // one arrival per epilogue warp, 8 warps x 2 CTAs
     }
     mbar_init(done_bar, 1);
     fence_barrier_init();
@@ -716,8 +720,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       mbar_wait(done_bar, 0, p.status, kTimeoutOther);
     }
   } else {
-    // ------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    // ------------------------------------------------ epilogue (warps 2..9, both CTAs)
+    // Warp w reads TMEM lanes 32*(w%4)..+31; warps 2..5 take the tile's first half of the
+    // output columns and warps 6..9 the second, so two warps drain each row.
     const int q = warp & 3;
+    const int col_half = (warp - 2) >> 2;
+    constexpr int OUT_BN_T = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
     float alpha = p.alpha;
     if (p.alpha_ptr != nullptr) alpha *= *p.alpha_ptr;
     const uint32_t acc_empty0_leader = mapa_shared(smem_u32(&acc_empty[0]), 0);
@@ -734,7 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
         bool ready = true;
         if (lane == 0) {
           const uint64_t t0 = globaltimer();
-          while (ld_acquire_gpu_s32(p.splitk_flags + tile) < 8 * split) {
+          while (ld_acquire_gpu_s32(p.splitk_flags + tile) < 16 * split) {
             if (globaltimer() - t0 > TT_WAIT_TIMEOUT_NS || *reinterpret_cast<volatile int*>(p.status) != 0) {
               atomicCAS(p.status, 0, static_cast<int>(kTimeoutOther));
               ready = false;
@@ -748,7 +756,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
       }
       const int row = mb * 256 + static_cast<int>(crank) * 128 + q * 32 + lane;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN2);
-      if (ok) epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha);
+      if (ok)
+        epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha, col_half * (OUT_BN_T / 2),
+                               (col_half + 1) * (OUT_BN_T / 2));
       if (S > 1) {  // count this warp's rows as added
         __threadfence();
         __syncwarp();
@@ -815,7 +825,7 @@ void launch_pair(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN) *
                      ((EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1);
   const long pairs = std::max(1L, std::min(tiles, static_cast<long>(num_sms(device) / 2)));
-  kern<<<static_cast<unsigned>(2 * pairs), NUM_THREADS, smem, st>>>(ta, tb, p);
+  kern<<<static_cast<unsigned>(2 * pairs), PAIR_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

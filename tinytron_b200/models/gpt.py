@@ -126,6 +126,23 @@ class GPT(nn.Module):
         x = ops.embedding(idx, self.wte.weight)
         paged = past_key_values if hasattr(past_key_values, "get_layer_cache") else None
         new_past = paged if paged is not None else ([] if use_cache else None)
+        if x.is_cuda:  # residual adds fused into the following RMSNorm, as in training
+            pending = None
+            for i, blk in enumerate(self.blocks):
+                layer_past = paged.get_layer_cache(i) if paged is not None else (
+                    past_key_values[i] if past_key_values is not None else None)
+                x, h = ops.add_rmsnorm(x, pending, blk.ln_1.weight, self.eps)
+                a, new_kv = blk.attn(h, past_kv=layer_past, use_cache=use_cache, position_offset=position_offset)
+                x, h = ops.add_rmsnorm(x, a, blk.ln_2.weight, self.eps)
+                out = blk.mlp(h, use_cache=use_cache)
+                pending = out[0] if self.use_moe else out
+                if use_cache and paged is None:
+                    new_past.append(new_kv)
+            if last_only:
+                x, pending = x[:, -1:].contiguous(), pending[:, -1:].contiguous()
+            _, h = ops.add_rmsnorm(x, pending, self.lnf.weight, self.eps)
+            logits = ops.lm_logits(h, self.lm_head.weight)
+            return (logits, new_past) if use_cache else logits
         for i, blk in enumerate(self.blocks):
             if paged is not None:
                 layer_past = paged.get_layer_cache(i)
