@@ -15,6 +15,7 @@
 // dQp is added into an fp32 accumulator with vector atomics; a final kernel
 // converts it to bf16.  Inputs/outputs are token-major (packed qkv layout).
 #include "common/host_utils.h"
+#include <cstdlib>
 #include "common/ptx.cuh"
 #include "common/fast_exp2.cuh"
 
@@ -38,6 +39,8 @@ struct BwdParams {
   float scale_log2;
   int causal;
   int* status;
+  int diag;  // diagnostics only (TT_ATTN_BWD_DIAG, wrong results): 1 skips the dQ reductions,
+             // 2 skips the exponentials (P = scores), 4 skips the dQ TMEM read-out entirely
 };
 
 template <int D>
@@ -263,6 +266,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const float* l2 = sm.lse2[buf] + half * QH;
 #pragma unroll
       for (int i = 0; i < QH; ++i) pv[i] = ex2_mufu(fmaf(__uint_as_float(raw[i]), p.scale_log2, -l2[i])) * key_scale;
+      if (p.diag & 2) {
+#pragma unroll
+        for (int i = 0; i < QH; ++i) pv[i] = __uint_as_float(raw[i]) * key_scale;
+      }
       if (p.causal && qt == kt) {
 #pragma unroll
         for (int i = 0; i < QH; ++i) pv[i] = (half * QH + i < r) ? 0.0f : pv[i];
@@ -324,7 +331,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       // whole 128-byte rows instead of 32 scattered 16-byte pieces.
       if (!mbar_wait_warp(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
       tc_fence_after();
-      {
+      if (p.diag & 4) {
+        tc_fence_before();
+        mbar_arrive(&sm.dq_empty);
+      } else {
         uint8_t* stage = sm.dst + half * (BLOCK_B * 128) + quarter * 32 * 128;
         const int qbase = qt * BLOCK_B + quarter * 32;  // query of this warp's first row
         float* gbase = p.dq_acc + static_cast<size_t>(row0) * (p.Hq * D) + static_cast<size_t>(h) * D + half * DH;
@@ -347,7 +357,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             const int j = i * 4 + (lane >> 3);  // row within the warp's 32
             const int u = lane & 7;             // 16-byte unit within the 32 columns
             const float4 v = *reinterpret_cast<const float4*>(stage + j * 128 + ((u ^ (j & 7)) << 4));
-            if (qbase + j < p.T)
+            if (qbase + j < p.T && !(p.diag & 1))
               atomicAdd(reinterpret_cast<float4*>(gbase + static_cast<size_t>(qbase + j) * (p.Hq * D) + c * 32) + u, v);
           }
           __syncwarp();
@@ -568,6 +578,10 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.causal = causal ? 1 : 0;
   p.status = device_status_ptr(q.get_device());
+  {
+    static const int diag = [] { const char* e = std::getenv("TT_ATTN_BWD_DIAG"); return e ? std::atoi(e) : 0; }();
+    p.diag = diag;
+  }
   const CUtensorMap tq = attn_head_map(q), tk = attn_head_map(k), tv = attn_head_map(v), tdo = attn_head_map(dout);
   const dim3 grid(static_cast<unsigned>((T + BLOCK_B - 1) / BLOCK_B * Hkv * B));
   if (D == 128) {

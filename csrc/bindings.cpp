@@ -9,7 +9,8 @@ int64_t gemm_pair_mode();
 void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10::optional<torch::Tensor> gu_out);
 void gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu, double alpha);
 void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair);
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair,
+                 c10::optional<torch::Tensor> row_ptr);
 void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, torch::Tensor gu_out,
                         torch::Tensor grp_off, int64_t n_groups, bool pair);
 void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
@@ -68,7 +69,10 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
 void ep_allgather_counts(int64_t gid, torch::Tensor counts, int64_t dst_off);
 void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torch::Tensor dst, int64_t recv_off,
                 int64_t cap, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> y_pairs,
-                c10::optional<torch::Tensor> dw);
+                c10::optional<torch::Tensor> dw, int64_t ret_off, int64_t back_off);
+void ep_local_combine(int64_t gid, int64_t y_off, int64_t k, c10::optional<torch::Tensor> w, torch::Tensor out,
+                      c10::optional<torch::Tensor> y_save);
+void ep_resolve_rows(int64_t gid, int64_t ret_off, int64_t rows, int64_t H, torch::Tensor row_ptr);
 void ep_pull_combine(int64_t gid, int64_t y_off, int64_t cap, torch::Tensor tgt, torch::Tensor dst, int64_t k,
                      c10::optional<torch::Tensor> w, torch::Tensor out, c10::optional<torch::Tensor> y_save);
 void ep_zero_pad(torch::Tensor buf, torch::Tensor seg_off, torch::Tensor seg_cnt);
@@ -104,7 +108,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_pair_mode", &tt::gemm_pair_mode);
   m.def("moe_gemm", &tt::moe_gemm_op, "grouped GEMM over expert row segments (bf16 out)", py::arg("a"),
         py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("b_mn"), py::arg("b_grp_rows"),
-        py::arg("b_split_k") = 0, py::arg("b_off2") = 0, py::arg("pair") = false);
+        py::arg("b_split_k") = 0, py::arg("b_off2") = 0, py::arg("pair") = false, py::arg("row_ptr") = py::none());
   m.def("moe_gemm_swiglu", &tt::moe_gemm_swiglu_op, "grouped gate|up GEMM with SwiGLU epilogue", py::arg("x"),
         py::arg("w_gu"), py::arg("out"), py::arg("gu_out"), py::arg("grp_off"), py::arg("n_groups"),
         py::arg("pair") = false);
@@ -152,7 +156,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_allgather_counts", &tt::ep_allgather_counts, "EP: all-gather per-expert counts into the heap");
   m.def("ep_scatter", &tt::ep_scatter, "EP dispatch: pair rows to their owners' receive buffers (peer stores)",
         py::arg("gid"), py::arg("x"), py::arg("k"), py::arg("tgt"), py::arg("dst"), py::arg("recv_off"),
-        py::arg("cap"), py::arg("w") = py::none(), py::arg("y_pairs") = py::none(), py::arg("dw") = py::none());
+        py::arg("cap"), py::arg("w") = py::none(), py::arg("y_pairs") = py::none(), py::arg("dw") = py::none(),
+        py::arg("ret_off") = -1, py::arg("back_off") = 0);
+  m.def("ep_local_combine", &tt::ep_local_combine,
+        "EP combine after a pushed exchange: weighted sum of this rank's own return buffer", py::arg("gid"),
+        py::arg("y_off"), py::arg("k"), py::arg("w"), py::arg("out"), py::arg("y_save") = py::none());
+  m.def("ep_resolve_rows", &tt::ep_resolve_rows,
+        "EP: recorded return slots of received rows -> peer addresses for the GEMM epilogue", py::arg("gid"),
+        py::arg("ret_off"), py::arg("rows"), py::arg("H"), py::arg("row_ptr"));
   m.def("ep_pull_combine", &tt::ep_pull_combine, "EP combine: weighted sum of owners' rows (peer loads)",
         py::arg("gid"), py::arg("y_off"), py::arg("cap"), py::arg("tgt"), py::arg("dst"), py::arg("k"),
         py::arg("w"), py::arg("out"), py::arg("y_save") = py::none());

@@ -70,6 +70,11 @@ struct Params {
   // order is fixed and results are deterministic.
   int split_k;
   int* splitk_flags;
+  // bf16 epilogue only: when set, output row r goes to the address row_ptr[r] (0: row
+  // dropped) instead of C + r * ldc.  The expert-parallel combine uses it to store each
+  // expert output row straight into the memory of the rank that owns the token (a peer
+  // address over NVLink), so the transfer overlaps the GEMM tile by tile.
+  const long long* row_ptr;
 };
 
 struct TileInfo {
@@ -211,6 +216,16 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
       }
     }
   } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
+    __nv_bfloat16* brow = nullptr;
+    if constexpr (EPI == EPI_BF16) {
+      if (p.row_ptr != nullptr) {
+        const long long a = row_ok ? p.row_ptr[row] : 0ll;
+        brow = reinterpret_cast<__nv_bfloat16*>(a);
+        row_ok = row_ok && a != 0ll;
+      } else {
+        brow = reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc;
+      }
+    }
 #pragma unroll 1
     for (int c0 = c_lo; c0 < c_hi; c0 += 32) {
       uint32_t r[32];
@@ -223,7 +238,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
         if constexpr (EPI == EPI_BF16) {
-          store_bf16<32>(reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<size_t>(row) * p.ldc + col0, v, nv);
+          store_bf16<32>(brow + col0, v, nv);
         } else {
           float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
           if (nv == 32) {
@@ -1110,7 +1125,8 @@ static void check_grp(const torch::Tensor& grp_off, int64_t n_groups, const torc
 // pair: the caller laid the segments out on 256-row boundaries, so the CTA-pair kernel
 // may run the GEMM (TT_GEMM_PAIR=0 still forces the single-CTA kernel).
 void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair) {
+                 bool b_mn, int64_t b_grp_rows, int64_t b_split_k, int64_t b_off2, bool pair,
+                 c10::optional<torch::Tensor> row_ptr) {
   using namespace gemm;
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
@@ -1120,6 +1136,11 @@ void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tenso
   const int K = static_cast<int>(a.size(1));
   const int N = static_cast<int>(c.size(1));
   TT_CHECK(c.size(0) == M && c.stride(1) == 1 && c.stride(0) % 8 == 0, "moe_gemm: bad output");
+  if (row_ptr.has_value()) {
+    TT_CHECK(row_ptr->is_cuda() && row_ptr->scalar_type() == torch::kInt64 && row_ptr->numel() >= M &&
+                 row_ptr->is_contiguous(),
+             "moe_gemm: row_ptr must be a contiguous CUDA int64 tensor with one address per output row");
+  }
   TT_CHECK(b_mn ? b.size(1) == N : b.size(1) == K, "moe_gemm: B shape");
   TT_CHECK(b_split_k % BK == 0 && b_grp_rows % (b_mn ? BK : 1) == 0, "moe_gemm: group offsets must be 64-aligned");
   if (M == 0) return;
@@ -1135,6 +1156,7 @@ void moe_gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tenso
   p.b_grp_rows = static_cast<int>(b_grp_rows);
   p.b_split_kb = b_split_k > 0 ? static_cast<int>(b_split_k / BK) : (1 << 30);
   p.b_off2 = static_cast<int>(b_off2);
+  p.row_ptr = row_ptr.has_value() ? reinterpret_cast<const long long*>(row_ptr->data_ptr<int64_t>()) : nullptr;
   if (use2) {
     if (b_mn) launch_pair<false, true, EPI_BF16, GROUP_M>(p, ta, tb, device, cur_stream());
     else launch_pair<false, false, EPI_BF16, GROUP_M>(p, ta, tb, device, cur_stream());

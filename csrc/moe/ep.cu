@@ -15,6 +15,13 @@
 //                       the backward), and writes sum_j w_j * y_j (fp32 accumulate).
 //   * zero_pad          zeroes the padding rows of the 128-row-aligned expert segments
 //                       of the local receive buffer (the grouped GEMMs read them).
+//   * fused combine     (push instead of pull) the forward scatter also stores, per
+//                       received row, where its expert output must go: the sender's rank
+//                       and the byte offset of slot `pair` in the sender's return buffer.
+//                       resolve_rows turns those into addresses in this process (peer
+//                       pointers) for the down-projection GEMM, whose epilogue then stores
+//                       every output row straight into the sender's memory; after one
+//                       barrier the sender sums its k rows locally (local_combine).
 //
 // Every launch records a bad index (row beyond the buffer, rank beyond the group)
 // in the device status word and skips that row instead of faulting.
@@ -48,7 +55,8 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(PeerTable t, const __
                                                           const int* __restrict__ dst, long long cap, size_t recv_off,
                                                           const float* __restrict__ w,
                                                           const __nv_bfloat16* __restrict__ y_pairs,
-                                                          float* __restrict__ dw, uint64_t e_done, int* status) {
+                                                          float* __restrict__ dw, uint64_t e_done, int* status,
+                                                          long long ret_off, long long back_off) {
   const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int n_warps = (gridDim.x * kThreads) >> 5;
@@ -64,6 +72,11 @@ __global__ void __launch_bounds__(kThreads) scatter_kernel(PeerTable t, const __
     uint4* out = reinterpret_cast<uint4*>(t.base[r] + recv_off + row * H * 2);
     if constexpr (MODE == 0) {
       for (int i = lane; i < nv; i += 32) out[i] = src[i];
+      if (ret_off >= 0 && lane == 0) {  // return address: (sender rank, offset of slot pr) + 1
+        const unsigned long long v =
+            ((static_cast<unsigned long long>(t.rank) << 48) | static_cast<unsigned long long>(back_off + pr * H * 2ll)) + 1ull;
+        reinterpret_cast<unsigned long long*>(t.base[r] + ret_off)[row] = v;
+      }
     } else {
       const float wv = w[pr];
       const uint4* yp = reinterpret_cast<const uint4*>(y_pairs + static_cast<long long>(pr) * H);
@@ -99,7 +112,8 @@ __global__ void __launch_bounds__(kThreads) pull_combine_kernel(PeerTable t, siz
                                                                const int* __restrict__ dst, long long cap,
                                                                const float* __restrict__ w,
                                                                __nv_bfloat16* __restrict__ out,
-                                                               __nv_bfloat16* __restrict__ y_save, int* status) {
+                                                               __nv_bfloat16* __restrict__ y_save, int* status,
+                                                               int local) {
   const int warp = (blockIdx.x * kThreads + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   const int n_warps = (gridDim.x * kThreads) >> 5;
@@ -113,8 +127,8 @@ __global__ void __launch_bounds__(kThreads) pull_combine_kernel(PeerTable t, siz
       for (int q = 0; q < 8; ++q) acc[c][q] = 0.f;
     for (int j = 0; j < k; ++j) {
       const int pr = tok * k + j;
-      const int r = tgt[pr];
-      const long long row = dst[pr];
+      const int r = local ? t.rank : tgt[pr];        // local: rows were pushed into slot `pr` here
+      const long long row = local ? pr : dst[pr];
       if (r < 0 || r >= t.world || row < 0 || row >= cap) {
         if (lane == 0) atomicCAS(status, 0, static_cast<int>(kBadIndex));
         continue;
@@ -150,6 +164,28 @@ __global__ void __launch_bounds__(kThreads) pull_combine_kernel(PeerTable t, siz
         o[i] = u;
       }
     }
+  }
+}
+
+// row_ptr[r] = address (in this process) of the return slot recorded for received row r,
+// 0 for rows nobody sent (segment padding); the record is cleared for the next exchange.
+__global__ void resolve_rows_kernel(PeerTable t, long long ret_off, int rows, int H, long long heap_bytes,
+                                    long long* __restrict__ row_ptr, int* status) {
+  unsigned long long* ret = reinterpret_cast<unsigned long long*>(t.base[t.rank] + ret_off);
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < rows; r += gridDim.x * blockDim.x) {
+    const unsigned long long v = ret[r];
+    long long a = 0;
+    if (v != 0ull) {
+      const int src = static_cast<int>((v - 1ull) >> 48);
+      const long long off = static_cast<long long>((v - 1ull) & ((1ull << 48) - 1ull));
+      if (src < t.world && off >= 0 && off + 2ll * H <= heap_bytes) {
+        a = reinterpret_cast<long long>(t.base[src] + off);
+      } else {
+        atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      }
+      ret[r] = 0ull;
+    }
+    row_ptr[r] = a;
   }
 }
 
@@ -198,9 +234,11 @@ void ep_allgather_counts(int64_t gid, torch::Tensor counts, int64_t dst_off) {
 // Store pair rows into the owners' receive buffers (heap offset recv_off, cap rows of H
 // bf16), then wait until every peer finished its own scatter.  Backward mode (w given):
 // rows are w[pair] * x[pair / k] and dw[pair] = <x[pair / k], y_pairs[pair]>.
+// Forward mode with ret_off >= 0 also records, for every row, its return address
+// (this rank, heap offset back_off + pair * H * 2) in the owner's int64 array at ret_off.
 void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torch::Tensor dst, int64_t recv_off,
                 int64_t cap, c10::optional<torch::Tensor> w, c10::optional<torch::Tensor> y_pairs,
-                c10::optional<torch::Tensor> dw) {
+                c10::optional<torch::Tensor> dw, int64_t ret_off, int64_t back_off) {
   check_cuda_bf16(x, "x");
   TT_CHECK(x.dim() == 2 && x.is_contiguous() && x.size(1) % 8 == 0 && x.size(1) <= 4096,
            "ep_scatter: x must be contiguous [N, H], H % 8 == 0, H <= 4096");
@@ -210,6 +248,13 @@ void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torc
   TT_CHECK(recv_off % 256 == 0 && recv_off + cap * H * 2 <= static_cast<int64_t>(comm::group_bytes(gid)),
            "ep_scatter: receive buffer outside the heap");
   const bool bwd = w.has_value();
+  if (ret_off >= 0) {
+    TT_CHECK(!bwd, "ep_scatter: return addresses are recorded in forward mode only");
+    TT_CHECK(ret_off % 8 == 0 && ret_off + cap * 8 <= static_cast<int64_t>(comm::group_bytes(gid)) &&
+                 back_off % 16 == 0 && back_off >= 0 && back_off + P * H * 2 <= static_cast<int64_t>(comm::group_bytes(gid)),
+             "ep_scatter: return-address array or return buffer outside the heap");
+    TT_CHECK(back_off + P * H * 2 < (1ll << 48), "ep_scatter: heap offsets must fit in 48 bits");
+  }
   if (bwd) {
     TT_CHECK(y_pairs.has_value() && dw.has_value(), "ep_scatter: backward needs y_pairs and dw");
     TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == P && w->is_contiguous(), "ep_scatter: w fp32 [P]");
@@ -227,12 +272,12 @@ void ep_scatter(int64_t gid, torch::Tensor x, int64_t k, torch::Tensor tgt, torc
   if (!bwd) {
     ep::scatter_kernel<0><<<grid, ep::kThreads, 0, cur_stream()>>>(
         t, xp, static_cast<int>(P), static_cast<int>(k), static_cast<int>(H), tgt.data_ptr<int>(),
-        dst.data_ptr<int>(), cap, static_cast<size_t>(recv_off), nullptr, nullptr, nullptr, e, st);
+        dst.data_ptr<int>(), cap, static_cast<size_t>(recv_off), nullptr, nullptr, nullptr, e, st, ret_off, back_off);
   } else {
     ep::scatter_kernel<1><<<grid, ep::kThreads, 0, cur_stream()>>>(
         t, xp, static_cast<int>(P), static_cast<int>(k), static_cast<int>(H), tgt.data_ptr<int>(),
         dst.data_ptr<int>(), cap, static_cast<size_t>(recv_off), w->data_ptr<float>(),
-        reinterpret_cast<const __nv_bfloat16*>(y_pairs->data_ptr()), dw->data_ptr<float>(), e, st);
+        reinterpret_cast<const __nv_bfloat16*>(y_pairs->data_ptr()), dw->data_ptr<float>(), e, st, -1ll, 0ll);
   }
   TT_CUDA_CHECK(cudaGetLastError());
   if (!emu) comm::launch_peer_wait(t, e, st, cur_stream());  // every peer's scatter-done epoch
@@ -269,12 +314,70 @@ void ep_pull_combine(int64_t gid, int64_t y_off, int64_t cap, torch::Tensor tgt,
   ep::pull_combine_kernel<PLV><<<grid, ep::kThreads, 0, cur_stream()>>>(                                           \
       t, static_cast<size_t>(y_off), static_cast<int>(N), static_cast<int>(k), static_cast<int>(H),              \
       tgt.data_ptr<int>(), dst.data_ptr<int>(), cap, wp, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), sp, \
-      device_status_ptr(dev))
+      device_status_ptr(dev), 0)
   if (pl <= 2) TT_PULL(2);
   else if (pl <= 4) TT_PULL(4);
   else if (pl <= 8) TT_PULL(8);
   else TT_PULL(16);
 #undef TT_PULL
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// out[tok] = sum_j w[tok*k+j] * buffer[tok*k+j] over this rank's own return buffer (heap
+// offset y_off, filled by the owners' down-projection epilogues); y_save keeps the rows.
+void ep_local_combine(int64_t gid, int64_t y_off, int64_t k, c10::optional<torch::Tensor> w, torch::Tensor out,
+                      c10::optional<torch::Tensor> y_save) {
+  check_cuda_bf16(out, "out");
+  TT_CHECK(out.dim() == 2 && out.is_contiguous() && out.size(1) % 8 == 0 && out.size(1) <= 4096,
+           "ep_local_combine: out [N, H], H % 8 == 0, H <= 4096");
+  const int64_t N = out.size(0), H = out.size(1), P = N * k;
+  TT_CHECK(y_off % 256 == 0 && y_off + P * H * 2 <= static_cast<int64_t>(comm::group_bytes(gid)),
+           "ep_local_combine: return buffer outside the heap");
+  const float* wp = nullptr;
+  if (w.has_value()) {
+    TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == P && w->is_contiguous(),
+             "ep_local_combine: w fp32 [P]");
+    wp = w->data_ptr<float>();
+  }
+  __nv_bfloat16* sp = nullptr;
+  if (y_save.has_value()) {
+    check_cuda_bf16(*y_save, "y_save");
+    TT_CHECK(y_save->numel() == P * H && y_save->is_contiguous(), "ep_local_combine: y_save [P, H]");
+    sp = reinterpret_cast<__nv_bfloat16*>(y_save->data_ptr());
+  }
+  const comm::PeerTable t = comm::group_table(gid);
+  const c10::cuda::CUDAGuard guard(out.device());
+  const int dev = out.get_device();
+  const int grid = comm::grid_blocks(dev, std::max<int64_t>(1, N * 32), ep::kThreads);
+  const int pl = static_cast<int>((H / 8 + 31) / 32);
+#define TT_LOCAL(PLV)                                                                                          \
+  ep::pull_combine_kernel<PLV><<<grid, ep::kThreads, 0, cur_stream()>>>(                                        \
+      t, static_cast<size_t>(y_off), static_cast<int>(N), static_cast<int>(k), static_cast<int>(H), nullptr, \
+      nullptr, P, wp, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), sp, device_status_ptr(dev), 1)
+  if (pl <= 2) TT_LOCAL(2);
+  else if (pl <= 4) TT_LOCAL(4);
+  else if (pl <= 8) TT_LOCAL(8);
+  else TT_LOCAL(16);
+#undef TT_LOCAL
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// row_ptr[r] (int64, r < rows) = peer address of the return slot recorded for received row
+// r by the forward scatter (heap offset ret_off), 0 for padding rows; clears the records.
+void ep_resolve_rows(int64_t gid, int64_t ret_off, int64_t rows, int64_t H, torch::Tensor row_ptr) {
+  TT_CHECK(row_ptr.is_cuda() && row_ptr.scalar_type() == torch::kInt64 && row_ptr.is_contiguous() &&
+               row_ptr.numel() >= rows,
+           "ep_resolve_rows: row_ptr must be a contiguous CUDA int64 tensor of >= rows entries");
+  const int64_t bytes = static_cast<int64_t>(comm::group_bytes(gid));
+  TT_CHECK(ret_off % 8 == 0 && ret_off + rows * 8 <= bytes, "ep_resolve_rows: record array outside the heap");
+  if (rows == 0) return;
+  const comm::PeerTable t = comm::group_table(gid);
+  const c10::cuda::CUDAGuard guard(row_ptr.device());
+  const int dev = row_ptr.get_device();
+  const int grid = static_cast<int>(std::min<int64_t>((rows + 255) / 256, 1024));
+  ep::resolve_rows_kernel<<<grid, 256, 0, cur_stream()>>>(t, ret_off, static_cast<int>(rows), static_cast<int>(H),
+                                                          bytes, reinterpret_cast<long long*>(row_ptr.data_ptr<int64_t>()),
+                                                          device_status_ptr(dev));
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -21,8 +21,9 @@ def _rel(a, b):
     return ((a.float() - b.float()).abs().max() / (b.float().abs().max() + 1e-6)).item()
 
 
+@pytest.mark.parametrize("push", [False, True], ids=["pull", "push"])
 @pytest.mark.parametrize("W,E,k", [(2, 8, 2), (4, 8, 3), (4, 16, 8)])
-def test_emulated_ep_forward_backward(W, E, k):
+def test_emulated_ep_forward_backward(W, E, k, push):
     from tinytron_b200 import ops
     from tinytron_b200.ops.weights import bf16_of, concat_rows
     from tinytron_b200.parallel import ep_comm as epc
@@ -58,7 +59,7 @@ def test_emulated_ep_forward_backward(W, E, k):
     M = bufs[0].counts.cpu().numpy()
     for r in range(W):
         assert np.array_equal(bufs[r].counts.cpu().numpy(), M)
-    xrs = [epc.dispatch(bufs[r], plans[r], xs[r]) for r in range(W)]
+    xrs = [epc.dispatch(bufs[r], plans[r], xs[r], push) for r in range(W)]
     xrs = [x.clone() for x in xrs]  # receive buffers are reused by the backward
     loc = []
     for r in range(W):
@@ -66,11 +67,11 @@ def test_emulated_ep_forward_backward(W, E, k):
         w_gu = concat_rows([bf16_of(Wg[sl].contiguous()).view(E_l * I, H),
                             bf16_of(Wu[sl].contiguous()).view(E_l * I, H)])
         wd = bf16_of(Wd[sl].contiguous()).view(E_l * H, I)
-        act, gu = epc.experts_forward(bufs[r], plans[r], xrs[r], w_gu, wd, I)
+        act, gu = epc.experts_forward(bufs[r], plans[r], xrs[r], w_gu, wd, I, push)
         loc.append((w_gu, wd, act, gu))
     outs, rows = [], []
     for r in range(W):
-        o, rw = epc.combine(bufs[r], plans[r], ws[r].reshape(-1).contiguous(), keep_rows=True)
+        o, rw = epc.combine(bufs[r], plans[r], ws[r].reshape(-1).contiguous(), keep_rows=True, push=push)
         outs.append(o)
         rows.append(rw)
     torch.cuda.synchronize()

@@ -15,9 +15,15 @@ Here, per MoE layer and micro-step:
 2. ``ep_scatter``: a warp per pair stores the token row straight into the owner's
    expert-grouped receive buffer (no send-side sort copy, no all-to-all);
 3. the owner runs its local experts on the grouped tcgen05 GEMMs (gate|up with the
-   SwiGLU epilogue, down) writing outputs into a second heap buffer;
-4. a barrier, then ``ep_pull_combine``: a warp per token loads its k outputs from the
-   owners (peer loads) and writes the routing-weighted sum.
+   SwiGLU epilogue, then down).  By default (``TT_EP_PUSH_COMBINE=1``) the combine
+   all-to-all is fused into the down projection: the scatter of step 2 also recorded,
+   per received row, the sender's rank and the slot of that (token, slot) pair in the
+   sender's return buffer; ``ep_resolve_rows`` turns the records into peer addresses
+   and the GEMM's epilogue stores each output row straight into the sender's memory,
+   so the NVLink transfer overlaps the GEMM tile by tile;
+4. a barrier, then the routing-weighted sum of each token's k rows: from the local
+   return buffer (``ep_local_combine``, push mode) or, with ``TT_EP_PUSH_COMBINE=0``,
+   loaded from the owners' output buffers (``ep_pull_combine``, peer loads).
 
 The backward mirrors it: ``ep_scatter`` in backward mode sends w * dout rows (and
 computes d(weights) on the way), the owner runs the expert backward into its output
@@ -29,6 +35,8 @@ receive buffer for layer l+1 only after that peer passed layer l's output barrie
 only after every source scattered l+1, i.e. finished pulling l.
 """
 from __future__ import annotations
+
+import os
 
 import numpy as np
 import torch
@@ -47,9 +55,16 @@ def _C():
     return _ext.load()
 
 
+def push_combine_enabled() -> bool:
+    """Combine fused into the down-projection epilogue (peer stores); off: pull-combine."""
+    return os.environ.get("TT_EP_PUSH_COMBINE", "1") != "0"
+
+
 class EPBuffers:
-    """Per-EP-group symmetric heap: a [world, E] count matrix and two [cap, H] bf16 row
-    buffers (A: receive rows / incoming gradients, B: expert outputs / input gradients)."""
+    """Per-EP-group symmetric heap: a [world, E] count matrix, two [cap, H] bf16 row
+    buffers (A: receive rows / incoming gradients, B: expert outputs -- in push mode the
+    return rows of this rank's own pairs -- / input gradients) and a [cap] int64 array of
+    return-address records (push mode)."""
 
     def __init__(self, heap: SymmetricHeap, E: int, H: int, cap: int):
         self.heap = heap
@@ -58,14 +73,16 @@ class EPBuffers:
         self.counts = heap.alloc((self.world, E), torch.int32)
         self.buf_a = heap.alloc((cap, H), torch.bfloat16, zero=False)
         self.buf_b = heap.alloc((cap, H), torch.bfloat16, zero=False)
+        self.ret = heap.alloc(cap, torch.int64)  # zero = no record
         self.off_counts = heap.offset_of(self.counts)
         self.off_a = heap.offset_of(self.buf_a)
         self.off_b = heap.offset_of(self.buf_b)
+        self.off_ret = heap.offset_of(self.ret)
 
     @staticmethod
     def nbytes(world: int, E: int, H: int, cap: int) -> int:
         return SymmetricHeap.bytes_needed((world * E, torch.int32), (cap * H, torch.bfloat16),
-                                          (cap * H, torch.bfloat16))
+                                          (cap * H, torch.bfloat16), (cap, torch.int64))
 
     @classmethod
     def create(cls, group, E: int, H: int, cap: int, device=None) -> "EPBuffers":
@@ -153,36 +170,52 @@ def plan_finish(bufs: EPBuffers, sel: torch.Tensor, counts: torch.Tensor, M: np.
     return p
 
 
-def dispatch(bufs: EPBuffers, plan: Plan, x2d: torch.Tensor) -> torch.Tensor:
-    """Phase 2 (collective): rows to owners; returns this rank's grouped receive rows."""
+def dispatch(bufs: EPBuffers, plan: Plan, x2d: torch.Tensor, push: bool = False) -> torch.Tensor:
+    """Phase 2 (collective): rows to owners; returns this rank's grouped receive rows.
+    ``push``: also record each row's return slot (this rank, pair index) at the owner."""
     C = _C()
-    C.ep_scatter(bufs.heap.gid, x2d, plan.k, plan.tgt, plan.dst, bufs.off_a, bufs.cap, None, None, None)
+    if push:
+        C.ep_scatter(bufs.heap.gid, x2d, plan.k, plan.tgt, plan.dst, bufs.off_a, bufs.cap, None, None, None,
+                     bufs.off_ret, bufs.off_b)
+    else:
+        C.ep_scatter(bufs.heap.gid, x2d, plan.k, plan.tgt, plan.dst, bufs.off_a, bufs.cap, None, None, None)
     xr = bufs.buf_a[:plan.total]
     C.ep_zero_pad(xr, plan.grp_off, plan.seg_cnt)
     return xr
 
 
-def experts_forward(bufs: EPBuffers, plan: Plan, xr: torch.Tensor, w_gu: torch.Tensor, wd: torch.Tensor, I: int):
-    """Phase 3 (local): grouped SwiGLU experts; outputs land in buffer B."""
+def experts_forward(bufs: EPBuffers, plan: Plan, xr: torch.Tensor, w_gu: torch.Tensor, wd: torch.Tensor, I: int,
+                    push: bool = False):
+    """Phase 3 (local): grouped SwiGLU experts; outputs land in buffer B (pull mode) or,
+    ``push``, in the senders' return buffers straight from the down-projection epilogue."""
     C = _C()
     dev = xr.device
     act = torch.empty(plan.total, I, device=dev, dtype=torch.bfloat16)
     gu = torch.empty(plan.total, 2 * I, device=dev, dtype=torch.bfloat16)
     yr = bufs.buf_b[:plan.total]
+    row_ptr = None
+    if push:
+        row_ptr = torch.empty(max(plan.total, 1), device=dev, dtype=torch.int64)
+        C.ep_resolve_rows(bufs.heap.gid, bufs.off_ret, plan.total, bufs.H, row_ptr)
     if plan.total > 0:
         C.moe_gemm_swiglu(xr, w_gu, act, gu, plan.grp_off, plan.E_local, plan.pair)
-        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H, 0, 0, plan.pair)
+        # push mode: `yr` only gives the output shape; rows go to row_ptr[r]
+        C.moe_gemm(act, wd, yr, plan.grp_off, plan.E_local, False, bufs.H, 0, 0, plan.pair, row_ptr)
     return act, gu
 
 
-def combine(bufs: EPBuffers, plan: Plan, w32: torch.Tensor | None, keep_rows: bool):
-    """Phase 4 (collective): barrier, then the weighted sum of the k owners' rows."""
+def combine(bufs: EPBuffers, plan: Plan, w32: torch.Tensor | None, keep_rows: bool, push: bool = False):
+    """Phase 4 (collective): barrier, then the weighted sum of each token's k rows (read
+    from the owners, or from this rank's return buffer after a pushed exchange)."""
     C = _C()
     bufs.heap.barrier()
     dev = plan.tgt.device
     out = torch.empty(plan.N, bufs.H, device=dev, dtype=torch.bfloat16)
     rows = torch.empty(plan.N * plan.k, bufs.H, device=dev, dtype=torch.bfloat16) if keep_rows else None
-    C.ep_pull_combine(bufs.heap.gid, bufs.off_b, bufs.cap, plan.tgt, plan.dst, plan.k, w32, out, rows)
+    if push:
+        C.ep_local_combine(bufs.heap.gid, bufs.off_b, plan.k, w32, out, rows)
+    else:
+        C.ep_pull_combine(bufs.heap.gid, bufs.off_b, bufs.cap, plan.tgt, plan.dst, plan.k, w32, out, rows)
     return out, rows
 
 
@@ -230,12 +263,13 @@ class EPMoEFn(torch.autograd.Function):
         E_l, I, H = w_gate.shape[0], w_gate.shape[1], w_gate.shape[2]
         counts = plan_routes(bufs, sel)
         plan = plan_finish(bufs, sel, counts)
-        xr = dispatch(bufs, plan, x2d)
+        push = push_combine_enabled()
+        xr = dispatch(bufs, plan, x2d, push)
         w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate).view(E_l * I, H), bf16_of(w_up).view(E_l * I, H)])
         wd = bf16_of(w_down).view(E_l * H, I)
-        act, gu = experts_forward(bufs, plan, xr, w_gu, wd, I)
+        act, gu = experts_forward(bufs, plan, xr, w_gu, wd, I, push)
         w32 = weights.reshape(-1).float().contiguous()
-        out, rows = combine(bufs, plan, w32, keep_rows=True)
+        out, rows = combine(bufs, plan, w32, keep_rows=True, push=push)
         ctx.save_for_backward(xr.clone(), act, gu, rows, w32, w_gu, wd)
         ctx.plan, ctx.bufs, ctx.dims = plan, bufs, (E_l, I, H)
         ctx.params = (w_gate, w_up, w_down)
