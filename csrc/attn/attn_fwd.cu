@@ -36,7 +36,7 @@ namespace attn {
 constexpr int BLOCK = 128;
 constexpr int THREADS = 384;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
-constexpr int kDefaultVariant = 0;
+constexpr int kDefaultVariant = 12;  // packed f32x2 softmax, 2 of every 8 exponentials on the FMA pipe
 
 struct FwdParams {
   int B, T, Tk, Hq, Hkv;
@@ -79,7 +79,8 @@ __device__ __forceinline__ int kv_tiles_for(const FwdParams& p, int qt) {
 }
 
 // VARIANT selects the softmax arithmetic mix: bit 0 = half of the exponentials on the FMA
-// pipe (exp2_poly), bit 1 = bf16 packing with integer ops instead of the conversion unit.
+// pipe (exp2_poly), bit 1 = bf16 packing with integer ops instead of the conversion unit,
+// bit 2 = packed f32x2 math with bits 3-4 exponentials per 8 on the FMA pipe (0, 2, 3, 4).
 __device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
   // round-to-nearest (ties away from zero) of non-negative finite values, then keep the
   // high halves: (hi16(hi) << 16) | hi16(lo)
@@ -318,31 +319,79 @@ __global__ void __launch_bounds__(THREADS, 1)
               v[i] = (key >= p.Tk || (p.causal && key > q_lim)) ? -INFINITY : v[i];
             }
           }
-          float mq[4] = {v[0], v[1], v[2], v[3]};  // independent chains
-#pragma unroll
-          for (int i = 4; i < 32; i += 4) {
-            mq[0] = fmaxf(mq[0], v[i]);
-            mq[1] = fmaxf(mq[1], v[i + 1]);
-            mq[2] = fmaxf(mq[2], v[i + 2]);
-            mq[3] = fmaxf(mq[3], v[i + 3]);
-          }
-          const float mcs = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
-          if (mcs > m_ref + RESCALE_THRESHOLD) m_ref = mcs;  // also the first visible chunk (m_ref = -inf)
-          const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
           float e[32];
+          if constexpr ((VARIANT & 4) != 0) {
+            // Packed path: three-input max, f32x2 FMA for the scale, f32x2 adds for the row
+            // sum, and POLY_PAIRS exponentials out of every 8 on the FMA pipe (exp2_poly2),
+            // the rest on MUFU; halves the FMA/ADD issue slots so the MUFU and issue budgets
+            // both stay under the tensor core's time per tile.
+            constexpr int POLY = (VARIANT >> 3) & 3;  // 0: none, 1: 2 of 8, 2: 3 of 8, 3: 4 of 8
+            float mq[4];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = fmaf(v[i], sl2, neg_m);
+            for (int q = 0; q < 4; ++q) {
+              float m = fmax3(v[q], v[q + 4], v[q + 8]);
+              m = fmax3(m, v[q + 12], v[q + 16]);
+              m = fmax3(m, v[q + 20], v[q + 24]);
+              mq[q] = fmaxf(m, v[q + 28]);
+            }
+            const float mcs = fmax3(mq[0], mq[1], fmaxf(mq[2], mq[3])) * sl2;
+            if (mcs > m_ref + RESCALE_THRESHOLD) m_ref = mcs;  // also the first visible chunk (m_ref = -inf)
+            const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
+            const unsigned long long s2 = f2_pack(sl2, sl2), nm2 = f2_pack(neg_m, neg_m);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) e[i] = ((VARIANT & 1) && (i & 1)) ? exp2_poly(e[i]) : ex2_mufu(e[i]);
-          float sq[4] = {e[0], e[1], e[2], e[3]};
+            for (int i = 0; i < 32; i += 2) {
+              const unsigned long long r2 = f2_fma(f2_pack(v[i], v[i + 1]), s2, nm2);
+              f2_unpack(r2, e[i], e[i + 1]);
+            }
 #pragma unroll
-          for (int i = 4; i < 32; i += 4) {
-            sq[0] += e[i];
-            sq[1] += e[i + 1];
-            sq[2] += e[i + 2];
-            sq[3] += e[i + 3];
+            for (int i = 0; i < 32; i += 2) {
+              const int w = i & 7;  // position of the pair within its group of 8
+              const bool poly_pair = (POLY >= 1 && w == 6) || (POLY == 3 && w == 4);
+              if (poly_pair) {
+                exp2_poly2(e[i], e[i + 1]);
+              } else if (POLY == 2 && w == 4) {
+                e[i] = ex2_mufu(e[i]);
+                e[i + 1] = exp2_poly(e[i + 1]);
+              } else {
+                e[i] = ex2_mufu(e[i]);
+                e[i + 1] = ex2_mufu(e[i + 1]);
+              }
+            }
+            unsigned long long sa = f2_pack(e[0], e[1]), sb = f2_pack(e[2], e[3]);
+#pragma unroll
+            for (int i = 4; i < 32; i += 4) {
+              sa = f2_add(sa, f2_pack(e[i], e[i + 1]));
+              sb = f2_add(sb, f2_pack(e[i + 2], e[i + 3]));
+            }
+            float a0, a1;
+            f2_unpack(f2_add(sa, sb), a0, a1);
+            csum[c] = a0 + a1;
+          } else {
+            float mq[4] = {v[0], v[1], v[2], v[3]};  // independent chains
+#pragma unroll
+            for (int i = 4; i < 32; i += 4) {
+              mq[0] = fmaxf(mq[0], v[i]);
+              mq[1] = fmaxf(mq[1], v[i + 1]);
+              mq[2] = fmaxf(mq[2], v[i + 2]);
+              mq[3] = fmaxf(mq[3], v[i + 3]);
+            }
+            const float mcs = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
+            if (mcs > m_ref + RESCALE_THRESHOLD) m_ref = mcs;  // also the first visible chunk (m_ref = -inf)
+            const float neg_m = (m_ref == -INFINITY) ? 0.0f : -m_ref;
+#pragma unroll
+            for (int i = 0; i < 32; ++i) e[i] = fmaf(v[i], sl2, neg_m);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) e[i] = ((VARIANT & 1) && (i & 1)) ? exp2_poly(e[i]) : ex2_mufu(e[i]);
+            float sq[4] = {e[0], e[1], e[2], e[3]};
+#pragma unroll
+            for (int i = 4; i < 32; i += 4) {
+              sq[0] += e[i];
+              sq[1] += e[i + 1];
+              sq[2] += e[i + 2];
+              sq[3] += e[i + 3];
+            }
+            csum[c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
           }
-          csum[c] = (sq[0] + sq[1]) + (sq[2] + sq[3]);
           cref[c] = m_ref;
           uint32_t pk[16];
 #pragma unroll
@@ -491,9 +540,12 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t q_col0,
     const size_t smem = sizeof(FwdSmem<128>) + 1024;
     switch (variant) {
       case 1: launch(attn_fwd_kernel<128, 1>, smem); break;
-      case 2: launch(attn_fwd_kernel<128, 2>, smem); break;
-      case 3: launch(attn_fwd_kernel<128, 3>, smem); break;
-      default: launch(attn_fwd_kernel<128, 0>, smem); break;
+      case 4: launch(attn_fwd_kernel<128, 4>, smem); break;
+      case 12: launch(attn_fwd_kernel<128, 12>, smem); break;
+      case 20: launch(attn_fwd_kernel<128, 20>, smem); break;
+      case 28: launch(attn_fwd_kernel<128, 28>, smem); break;
+      case 0: launch(attn_fwd_kernel<128, 0>, smem); break;
+      default: launch(attn_fwd_kernel<128, kDefaultVariant>, smem); break;
     }
   } else {
     launch(attn_fwd_kernel<64, 0>, sizeof(FwdSmem<64>) + 1024);

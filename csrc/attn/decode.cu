@@ -11,15 +11,15 @@
 // of a kv head, so every K/V byte is read once per step.
 //
 // Decode attention is bound by K/V bytes (a few MB per layer), so the dot products
-// run on the FMA pipe: a warp takes one key at a time (each lane 4 of the head's
-// 128 dims, one 8-byte load), and P·V runs with threads owning output dims.
+// run on the FMA pipe: two threads per key for the scores, and P·V with lanes owning
+// output dims; small 64-key splits keep enough independent loads in flight.
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
 
 namespace tt {
 namespace decode {
 
-constexpr int kChunk = 256;   // keys per split CTA
+constexpr int kChunk = 64;    // keys per split CTA
 constexpr int kThreads = 128;
 constexpr int kMaxG = 8;      // q heads per kv head
 constexpr float kLog2e = 1.4426950408889634f;
@@ -114,125 +114,143 @@ struct DecodeParams {
   int* status;
 };
 
-// One CTA per (split of 256 keys, kv head, sequence).
-//   scores: a thread per key (2 keys per thread): the key's row is read with 16-byte
-//           loads (all independent, so a warp has 32 rows in flight) and dotted with the
-//           G query heads held in shared memory (broadcast reads; no shuffles);
+// One CTA per (split of 64 keys, kv head, sequence); G (q heads per kv head) is a template
+// parameter so no register or instruction is spent on absent heads.  Every phase has at
+// most one dependent round trip to memory, so a CTA's life is a few memory latencies and
+// the many small CTAs (4x more than 256-key splits) keep HBM busy:
+//   scores: two threads per key, each dotting alternate 16-byte pieces of the key's row
+//           (all of the chunk's K loads in flight at once) with the G query heads held in
+//           shared memory (16-byte broadcast reads), then one shuffle;
 //   softmax: chunk max and sum per head (block reductions);
 //   P.V:    each warp takes every 4th key; a lane owns D/32 dims, so a warp reads whole V
-//           rows; 8 keys per step keep 8 loads in flight per lane; the 4 warp partials
-//           are summed in warp order.  Key rows come from a per-chunk table in shared
-//           memory filled during the score pass (one page-table lookup per key).
-template <int D>
-__global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodeParams p) {
+//           rows; 16 keys per warp = the whole chunk in one step, all loads in flight; the
+//           4 warp partials are summed in warp order.  Key rows come from a per-chunk table
+//           in shared memory filled during the score pass (one page-table lookup per key).
+template <int D, int G>
+__global__ void __launch_bounds__(kThreads, 4) decode_split_kernel(const DecodeParams p) {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-  constexpr int NV = D / 8;                // uint4 per K row
+  static_assert(kChunk * 2 == kThreads, "two threads per key");
+  constexpr int NV = D / 8;  // uint4 per K row
+  constexpr int NW = kThreads / 32;
+  constexpr int KPW = kChunk / NW;  // keys per warp in P.V
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
-  const int G = p.Hq / p.Hkv;
   const int L = (p.len_dev != nullptr ? *p.len_dev : 0) + p.len_host;
   const int j0 = split * kChunk;
   const int n = max(0, min(kChunk, L - j0));
-  __shared__ float q_s[kMaxG][D];
-  __shared__ float s_s[kMaxG][kChunk];
-  __shared__ float red_s[kThreads / 32][kMaxG];
-  __shared__ float m_s[kMaxG], l_s[kMaxG];
-  __shared__ float o_s[kThreads / 32][kMaxG][D];
+  __shared__ __align__(16) float q_s[G][D];
+  __shared__ float s_s[G][kChunk];
+  __shared__ float red_s[NW][G];
+  __shared__ float m_s[G], l_s[G];
+  __shared__ __align__(16) float o_s[NW][G][D];
   __shared__ long long rows_s[kChunk];  // page-pool row of each key of the chunk (-1: unmapped)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (n == 0) {  // split past the current length (uniform per CTA): an empty partial
+    if (tid < G) {
+      const long long rowo = (static_cast<long long>(b) * p.Hq + kvh * G + tid) * p.splits + split;
+      p.ml_part[rowo * 2] = -INFINITY;
+      p.ml_part[rowo * 2 + 1] = 0.f;
+    }
+    return;
+  }
   for (int i = tid; i < G * D; i += kThreads) {
     const int g = i / D, d = i % D;
     q_s[g][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.Hq + kvh * G + g) * D + d]);
   }
-  const long long pt_row = static_cast<long long>(b) * p.pages_per_seq;
-  // row index of key j (chunk-relative) in the page pool, or -1 when unmapped
-  auto key_row = [&](int j) -> long long {
-    const int key = j0 + j;
-    const int pi = key / p.page_size;
-    const int page = pi < p.pages_per_seq ? p.page_table[pt_row + pi] : -1;
-    if (page < 0 || page >= p.num_pages) return -1;
-    return static_cast<long long>(page) * p.page_size + key % p.page_size;
-  };
   __syncthreads();
-  // ---- scores: a thread per key
-  for (int j = tid; j < n; j += kThreads) {
-    const long long row = key_row(j);
-    rows_s[j] = row;
-    float acc[kMaxG];
+  // ---- scores: thread pair (2j, 2j+1) takes key j; thread hh dots 16-byte pieces hh, hh+2, ...
+  {
+    const int j = tid >> 1, hh = tid & 1;
+    float acc[G];
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g) acc[g] = 0.f;
-    if (row >= 0) {
-      const uint4* kr = reinterpret_cast<const uint4*>(p.k_pages + (row * p.Hkv + kvh) * D);
-      uint4 kv[NV];
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    if (j < n) {
+      const int key = j0 + j;
+      const int pi = key / p.page_size;
+      const int page = pi < p.pages_per_seq ? p.page_table[static_cast<long long>(b) * p.pages_per_seq + pi] : -1;
+      const long long row =
+          (page < 0 || page >= p.num_pages) ? -1ll : static_cast<long long>(page) * p.page_size + key % p.page_size;
+      if (hh == 0) rows_s[j] = row;
+      if (row >= 0) {
+        const uint4* kr = reinterpret_cast<const uint4*>(p.k_pages + (row * p.Hkv + kvh) * D);
+        uint4 kv[NV / 2];
 #pragma unroll
-      for (int c = 0; c < NV; ++c) kv[c] = kr[c];
+        for (int c = 0; c < NV / 2; ++c) kv[c] = kr[2 * c + hh];
 #pragma unroll
-      for (int c = 0; c < NV; ++c) {
-        const uint32_t* w = reinterpret_cast<const uint32_t*>(&kv[c]);
+        for (int c = 0; c < NV / 2; ++c) {
+          const int d0 = 8 * (2 * c + hh);
+          const uint32_t* w = reinterpret_cast<const uint32_t*>(&kv[c]);
+          float kf[8];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float2 f = unpack_bf16x2(w[e]);
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(w[e]);
+            kf[2 * e] = f.x;
+            kf[2 * e + 1] = f.y;
+          }
 #pragma unroll
-          for (int g = 0; g < kMaxG; ++g) {
-            if (g < G) acc[g] += f.x * q_s[g][8 * c + 2 * e] + f.y * q_s[g][8 * c + 2 * e + 1];
+          for (int g = 0; g < G; ++g) {
+            const float4 qa = *reinterpret_cast<const float4*>(&q_s[g][d0]);
+            const float4 qb = *reinterpret_cast<const float4*>(&q_s[g][d0 + 4]);
+            acc[g] += kf[0] * qa.x + kf[1] * qa.y + kf[2] * qa.z + kf[3] * qa.w + kf[4] * qb.x + kf[5] * qb.y +
+                      kf[6] * qb.z + kf[7] * qb.w;
           }
         }
+      } else if (hh == 0) {
+        atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
       }
-    } else {
-      atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
     }
 #pragma unroll
-    for (int g = 0; g < kMaxG; ++g)
-      if (g < G) s_s[g][j] = acc[g] * p.scale_log2;
+    for (int g = 0; g < G; ++g) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
+    if (j < n && hh == 0) {
+#pragma unroll
+      for (int g = 0; g < G; ++g) s_s[g][j] = acc[g] * p.scale_log2;
+    }
   }
   __syncthreads();
-  // ---- chunk max per head
-  for (int g = 0; g < G; ++g) {
+  // ---- chunk max per head (warp w < G reduces head w over the chunk)
+  if (warp < G) {
     float m = -INFINITY;
-    for (int j = tid; j < n; j += kThreads) m = fmaxf(m, s_s[g][j]);
+    for (int j = lane; j < n; j += 32) m = fmaxf(m, s_s[warp][j]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) red_s[warp][g] = m;
+    if (lane == 0) m_s[warp] = m;
   }
-  __syncthreads();
-  if (tid < G) {
-    float m = -INFINITY;
-    for (int w = 0; w < kThreads / 32; ++w) m = fmaxf(m, red_s[w][tid]);
-    m_s[tid] = m;
+  if constexpr (G > NW) {
+    for (int g = NW + warp; g < G; g += NW) {
+      float m = -INFINITY;
+      for (int j = lane; j < n; j += 32) m = fmaxf(m, s_s[g][j]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (lane == 0) m_s[g] = m;
+    }
   }
   __syncthreads();
   // ---- probabilities (in place) and their sums
-  for (int g = 0; g < G; ++g) {
+  for (int g = warp; g < G; g += NW) {
     const float m = m_s[g];
     float l = 0.f;
-    for (int j = tid; j < n; j += kThreads) {
+    for (int j = lane; j < n; j += 32) {
       const float e = exp2f(s_s[g][j] - m);
       s_s[g][j] = e;
       l += e;
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) red_s[warp][g] = l;
+    if (lane == 0) l_s[g] = l;
   }
   __syncthreads();
-  if (tid < G) {
-    float l = 0.f;
-    for (int w = 0; w < kThreads / 32; ++w) l += red_s[w][tid];
-    l_s[tid] = l;
-  }
   // ---- P.V: warp w takes keys w, w+4, ...; lane owns D/32 consecutive dims (one 8- or
-  // 4-byte load per key, a warp reads whole V rows); 8 keys per step, all loads in flight.
+  // 4-byte load per key, a warp reads whole V rows); the chunk in one step, all loads in flight.
   constexpr int DPL = D / 32;
-  float oacc[kMaxG][DPL];
+  float oacc[G][DPL];
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g)
+  for (int g = 0; g < G; ++g)
 #pragma unroll
     for (int e = 0; e < DPL; ++e) oacc[g][e] = 0.f;
-  constexpr int NW = kThreads / 32;
-  for (int jb = warp; jb < n; jb += 8 * NW) {
-    float vv[8][DPL];
+  {
+    float vv[KPW][DPL];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = jb + u * NW;
+    for (int u = 0; u < KPW; ++u) {
+      const int j = warp + u * NW;
       const long long row = j < n ? rows_s[j] : -1;
       if (row >= 0) {
         const __nv_bfloat16* vr = p.v_pages + (row * p.Hkv + kvh) * D + lane * DPL;
@@ -250,26 +268,23 @@ __global__ void __launch_bounds__(kThreads) decode_split_kernel(const DecodePara
       }
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const int j = jb + u * NW;
+    for (int u = 0; u < KPW; ++u) {
+      const int j = warp + u * NW;
       if (j < n) {
 #pragma unroll
-        for (int g = 0; g < kMaxG; ++g) {
-          if (g < G) {
-            const float pr = s_s[g][j];
+        for (int g = 0; g < G; ++g) {
+          const float pr = s_s[g][j];
 #pragma unroll
-            for (int e = 0; e < DPL; ++e) oacc[g][e] += pr * vv[u][e];
-          }
+          for (int e = 0; e < DPL; ++e) oacc[g][e] += pr * vv[u][e];
         }
       }
     }
   }
 #pragma unroll
-  for (int g = 0; g < kMaxG; ++g)
-    if (g < G) {
+  for (int g = 0; g < G; ++g) {
 #pragma unroll
-      for (int e = 0; e < DPL; ++e) o_s[warp][g][lane * DPL + e] = oacc[g][e];
-    }
+    for (int e = 0; e < DPL; ++e) o_s[warp][g][lane * DPL + e] = oacc[g][e];
+  }
   __syncthreads();
   // sum the NW partitions in warp order: thread handles (g, d) pairs
   for (int i = tid; i < G * D; i += kThreads) {
@@ -366,6 +381,8 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
            "decode_attention: pages [num_pages, page_size, Hkv, D]");
   const int64_t Hkv = k_pages.size(2);
   TT_CHECK(Hq % Hkv == 0 && Hq / Hkv <= decode::kMaxG, "decode_attention: Hq/Hkv must be an integer <= 8");
+  TT_CHECK((Hq / Hkv) == 1 || (Hq / Hkv) == 2 || (Hq / Hkv) == 4 || (Hq / Hkv) == 8,
+           "decode_attention: Hq/Hkv must be 1, 2, 4 or 8");
   TT_CHECK(D == 64 || D == 128, "decode_attention: head_dim 64 or 128");
   TT_CHECK(page_table.scalar_type() == torch::kInt32 && page_table.dim() == 2 && page_table.size(0) == B &&
                page_table.is_contiguous(),
@@ -401,8 +418,26 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(q.device());
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
-  if (D == 128) decode::decode_split_kernel<128><<<grid, decode::kThreads, 0, cur_stream()>>>(p);
-  else decode::decode_split_kernel<64><<<grid, decode::kThreads, 0, cur_stream()>>>(p);
+  const int G = static_cast<int>(Hq / Hkv);
+#define TT_DECODE(DV, GV) decode::decode_split_kernel<DV, GV><<<grid, decode::kThreads, 0, cur_stream()>>>(p)
+  if (D == 128) {
+    switch (G) {
+      case 1: TT_DECODE(128, 1); break;
+      case 2: TT_DECODE(128, 2); break;
+      case 4: TT_DECODE(128, 4); break;
+      case 8: TT_DECODE(128, 8); break;
+      default: TT_CHECK(false, "decode_attention: Hq/Hkv must be 1, 2, 4 or 8");
+    }
+  } else {
+    switch (G) {
+      case 1: TT_DECODE(64, 1); break;
+      case 2: TT_DECODE(64, 2); break;
+      case 4: TT_DECODE(64, 4); break;
+      case 8: TT_DECODE(64, 8); break;
+      default: TT_CHECK(false, "decode_attention: Hq/Hkv must be 1, 2, 4 or 8");
+    }
+  }
+#undef TT_DECODE
   TT_CUDA_CHECK(cudaGetLastError());
   decode::decode_combine_kernel<<<static_cast<unsigned>(B * Hq), static_cast<unsigned>(D), 0, cur_stream()>>>(
       p.o_part, p.ml_part, p.splits, p.D, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));

@@ -26,7 +26,7 @@ void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torc
 void moe_combine_bwd_op(torch::Tensor dout, torch::Tensor y_rows, torch::Tensor row_pair, torch::Tensor w,
                         torch::Tensor grp_off, int64_t k, torch::Tensor dy_rows, torch::Tensor dw);
 void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                       bool accumulate);
+                       bool accumulate, bool pair);
 int64_t status_read(int64_t device);
 void status_clear(int64_t device);
 void add_rmsnorm_fwd(torch::Tensor x, c10::optional<torch::Tensor> delta, torch::Tensor w,
@@ -116,7 +116,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("dy"), py::arg("w_down"), py::arg("gu"), py::arg("dgu"), py::arg("grp_off"), py::arg("n_groups"),
         py::arg("pair") = false);
   m.def("moe_gemm_wgrad", &tt::moe_gemm_wgrad_op, "per-expert weight gradient over token segments (fp32)",
-        py::arg("a"), py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("accumulate"));
+        py::arg("a"), py::arg("b"), py::arg("c"), py::arg("grp_off"), py::arg("n_groups"), py::arg("accumulate"),
+        py::arg("pair") = false);
   m.def("moe_topk_softmax", &tt::moe_topk_softmax_op, "router top-k + softmax over the selected logits");
   m.def("moe_topk_softmax_bwd", &tt::moe_topk_softmax_bwd_op, "backward of moe_topk_softmax");
   m.def("moe_row_capacity", &tt::moe_row_capacity, "padded expert-row capacity for P pairs and E experts",

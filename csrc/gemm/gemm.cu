@@ -600,7 +600,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  static_assert(GROUP != GROUP_K, "the pair kernel has no grouped-K mode");
+  static_assert(GROUP != GROUP_K || (A_MN && B_MN && EPI == EPI_F32_ACC),
+                "grouped-K (MoE weight gradients) reduces over token rows: MN-major operands, fp32 accumulate");
   const uint32_t crank = cluster_ctarank();
   const bool leader = crank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1);
@@ -609,11 +610,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   const int M = (GROUP == GROUP_M) ? __ldg(p.grp_off + p.n_groups) : p.M;
   const int num_m = (M + 255) / 256;
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
-  const int num_tiles = num_m * num_n;
+  // GROUP_K: one tile set per group (expert); the reduction runs over the group's token
+  // segment [grp_off[g], grp_off[g+1]) and the output rows are offset by g * c_grp_rows.
+  const int num_tiles = num_m * num_n * (GROUP == GROUP_K ? p.n_groups : 1);
   const int num_k = (p.K + BK - 1) / BK;
-  const int S = (EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1;
+  const int S = (GROUP != GROUP_K && EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1;
   const int num_units = num_tiles * S;
   const int kb_per = (num_k + S - 1) / S;
+  // (group, m block, n block, first k-block, end k-block) of a work unit; the three roles
+  // derive it identically, so an empty group's tiles are skipped by all of them.
+  auto unit_info = [&](int unit, int& grp, int& mb, int& nb, int& kb_lo, int& kb_hi) {
+    const int tile = unit / S, split = unit - (unit / S) * S;
+    if constexpr (GROUP == GROUP_K) {
+      const int per = num_m * num_n;
+      grp = tile / per;
+      tile_coords(tile - grp * per, num_m, num_n, mb, nb);
+      kb_lo = __ldg(p.grp_off + grp) / BK;
+      kb_hi = __ldg(p.grp_off + grp + 1) / BK;
+    } else {
+      grp = 0;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      kb_lo = split * kb_per;
+      kb_hi = min(num_k, (split + 1) * kb_per);
+    }
+  };
 
   if (threadIdx.x == 0) {
     tma_prefetch_desc(&tmA);
@@ -646,17 +666,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
-        const int tile = unit / S, split = unit - (unit / S) * S;
-        int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
+        int grp, mb, nb, kb_lo, kb_hi;
+        unit_info(unit, grp, mb, nb, kb_lo, kb_hi);
         const int grp_rows = (GROUP == GROUP_M) ? pair_tile_group<GROUP>(p, mb) * p.b_grp_rows : 0;
         const int a_row0 = mb * 256 + static_cast<int>(crank) * 128;
         // K-major B: first B row of this CTA's half; MN-major B: first N column of it.
         const int b_row0 = (EPI == EPI_SWIGLU) ? (crank ? p.b_row_offset2 : 0) + grp_rows + nb * 128
                            : (B_MN ? nb * BN2 + static_cast<int>(crank) * 128
                                    : grp_rows + nb * BN2 + static_cast<int>(crank) * 128);
-        const int kb_end = min(num_k, (split + 1) * kb_per);
-        for (int kb = split * kb_per; kb < kb_end; ++kb) {
+        for (int kb = kb_lo; kb < kb_hi; ++kb) {
           if (!mbar_wait_cluster(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
             ok = false;
             break;
@@ -697,8 +715,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
-        const int split = unit - (unit / S) * S;
-        const int kb0 = split * kb_per, kb_end = min(num_k, (split + 1) * kb_per);
+        int grp, mb, nb, kb0, kb_end;
+        unit_info(unit, grp, mb, nb, kb0, kb_end);
+        if (GROUP == GROUP_K && kb_end <= kb0) continue;  // empty group: no accumulator used
         if (!mbar_wait_cluster(&acc_empty[acc], acc_phase ^ 1u, p.status, kTimeoutAccEmpty)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN2);
@@ -749,8 +768,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
     bool ok = true;
     for (int unit = pair; ok && unit < num_units; unit += n_pairs) {
       const int tile = unit / S, split = unit - (unit / S) * S;
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      int grp, mb, nb, kb_lo, kb_hi;
+      unit_info(unit, grp, mb, nb, kb_lo, kb_hi);
+      if (GROUP == GROUP_K && kb_hi <= kb_lo) continue;  // empty group: nothing was accumulated
       if (!mbar_wait_cluster_warp(&acc_full[acc], acc_phase, p.status, kTimeoutAccFull)) break;
       tc_fence_after();
       if (S > 1 && split > 0) {  // previous split's partial must be in C first (bounded wait)
@@ -769,10 +789,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
         ok = __shfl_sync(0xffffffffu, ready ? 1 : 0, 0) != 0;
         __threadfence();
       }
-      const int row = mb * 256 + static_cast<int>(crank) * 128 + q * 32 + lane;
+      const int row_local = mb * 256 + static_cast<int>(crank) * 128 + q * 32 + lane;
+      const int row = (GROUP == GROUP_K) ? grp * p.c_grp_rows + row_local : row_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN2);
       if (ok)
-        epilogue_row<BN2, EPI>(p, t_row, nb, row, row < M, alpha, col_half * (OUT_BN_T / 2),
+        epilogue_row<BN2, EPI>(p, t_row, nb, row, row_local < M, alpha, col_half * (OUT_BN_T / 2),
                                (col_half + 1) * (OUT_BN_T / 2));
       if (S > 1) {  // count this warp's rows as added
         __threadfence();
@@ -838,7 +859,8 @@ void launch_pair(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, 
   TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
   const long tiles = static_cast<long>((p.M + 255) / 256) * ((p.N + OUT_BN - 1) / OUT_BN) *
-                     ((EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1);
+                     ((GROUP != GROUP_K && EPI == EPI_F32_ACC && p.split_k > 1) ? p.split_k : 1) *
+                     (GROUP == GROUP_K ? p.n_groups : 1);
   const long pairs = std::max(1L, std::min(tiles, static_cast<long>(num_sms(device) / 2)));
   kern<<<static_cast<unsigned>(2 * pairs), PAIR_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
@@ -1246,8 +1268,10 @@ void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor g
 
 // Per-expert weight gradient: C[e*M:(e+1)*M, N] (+)= A_e^T B_e with A [cap, M], B [cap, N]
 // (token rows; the reduction covers expert e's segment only).  C is fp32.
+// pair: CTA-pair kernel (256 x 256 tiles per expert); any segment alignment of 64 rows works,
+// since the reduction runs over whole k-blocks of each expert's token segment.
 void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
-                       bool accumulate) {
+                       bool accumulate, bool pair) {
   using namespace gemm;
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
@@ -1263,13 +1287,18 @@ void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch:
   const int device = a.get_device();
   if (!accumulate) c.zero_();  // empty experts' tiles are skipped
   if (K == 0) return;
-  const int bn = choose_bn(M, N, device);
+  const bool use2 = pair && pair_mode() != 0;
+  const int bn = use2 ? 128 : choose_bn(M, N, device);
   const CUtensorMap ta = operand_map(a, true, BM);
   const CUtensorMap tb = operand_map(b, true, bn);
   Params p = base_params(M, N, K, c, 1.0, c10::nullopt, device);
   p.grp_off = grp_off.data_ptr<int>();
   p.n_groups = static_cast<int>(n_groups);
   p.c_grp_rows = M;
+  if (use2) {
+    launch_pair<true, true, EPI_F32_ACC, GROUP_K>(p, ta, tb, device, cur_stream());
+    return;
+  }
   launch_bn<true, true, EPI_F32_ACC, GROUP_K>(bn, p, ta, tb, device, cur_stream());
 }
 

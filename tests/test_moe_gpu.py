@@ -172,9 +172,9 @@ def test_grouped_backward_gemms(align, pair):
     C.moe_gemm(dgu, w_gu, dx, s["grp_off"], E, True, I, I, E * I, pair)
     # weight grads, accumulated into fp32
     gwd = torch.ones(E * H, I, device="cuda")
-    C.moe_gemm_wgrad(dy, act, gwd, s["grp_off"], E, True)
+    C.moe_gemm_wgrad(dy, act, gwd, s["grp_off"], E, True, pair)
     gwg = torch.empty(E * I, H, device="cuda")
-    C.moe_gemm_wgrad(dgu[:, :I], s["xr"], gwg, s["grp_off"], E, False)
+    C.moe_gemm_wgrad(dgu[:, :I], s["xr"], gwg, s["grp_off"], E, False, pair)
     for e, a, b in _segments(s):
         wd_e = s["wd"][e].float()
         if b == a:

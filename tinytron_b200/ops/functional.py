@@ -241,13 +241,13 @@ class MoEExpertsFn(torch.autograd.Function):
         dgu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
         c.moe_gemm_dswiglu(dyr, wd, gu, dgu, grp_off, E, ctx.pair)
         g_down, main_d = _expert_grad(w_down, (E * H, I))
-        c.moe_gemm_wgrad(dyr, act, g_down, grp_off, E, True)
+        c.moe_gemm_wgrad(dyr, act, g_down, grp_off, E, True, True)
         dxr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
         c.moe_gemm(dgu, w_gu, dxr, grp_off, E, True, I, I, E * I, ctx.pair)
         g_gate, main_g = _expert_grad(w_gate, (E * I, H))
         g_up, main_u = _expert_grad(w_up, (E * I, H))
-        c.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, grp_off, E, True)
-        c.moe_gemm_wgrad(dgu[:, I:], xr, g_up, grp_off, E, True)
+        c.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, grp_off, E, True, True)
+        c.moe_gemm_wgrad(dgu[:, I:], xr, g_up, grp_off, E, True, True)
         dx = torch.empty(N, H, device=dev, dtype=torch.bfloat16)
         c.moe_combine(dxr, slot, None, k, dx)
         notify_grad_ready([p for p, m in ((w_gate, main_g), (w_up, main_u), (w_down, main_d)) if m])

@@ -238,10 +238,10 @@ def experts_backward(bufs: EPBuffers, plan: Plan, dyr, xr, act, gu, w_gu, wd, I,
     E_l = plan.E_local
     dgu = torch.empty(plan.total, 2 * I, device=dyr.device, dtype=torch.bfloat16)
     C.moe_gemm_dswiglu(dyr, wd, gu, dgu, plan.grp_off, E_l, plan.pair)
-    C.moe_gemm_wgrad(dyr, act, g_down, plan.grp_off, E_l, True)
+    C.moe_gemm_wgrad(dyr, act, g_down, plan.grp_off, E_l, True, True)
     C.moe_gemm(dgu, w_gu, bufs.buf_b[:plan.total], plan.grp_off, E_l, True, I, I, E_l * I, plan.pair)
-    C.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, plan.grp_off, E_l, True)
-    C.moe_gemm_wgrad(dgu[:, I:], xr, g_up, plan.grp_off, E_l, True)
+    C.moe_gemm_wgrad(dgu[:, :I], xr, g_gate, plan.grp_off, E_l, True, True)
+    C.moe_gemm_wgrad(dgu[:, I:], xr, g_up, plan.grp_off, E_l, True, True)
 
 
 def _expert_grad(param, shape2d):
