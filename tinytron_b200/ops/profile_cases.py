@@ -19,6 +19,10 @@ Cases:
 * ``decode``  one decode step's attention kernels (RoPE + paged KV append, split-KV
               attention, combine) for batch 32, context 1024, page 16, 16q/4kv heads.
 * ``attn_bwd_b4``  flash-attention backward at the training shape (B4 T4096 Hq16 Hkv4 d128).
+* ``dswiglu`` the down-projection dgrad GEMM with the fused SwiGLU-backward epilogue
+              (M 16384, H 2048, I 5504).
+* ``moe_decode``  one decode step of the 64-expert MoE (32 tokens, top-8): grouped
+              GEMMs that stream every expert's weights.
 """
 from __future__ import annotations
 
@@ -127,7 +131,44 @@ def case_attn_bwd_b4(B: int = 4, T: int = 4096, Hq: int = 16, Hkv: int = 4, d: i
     torch.cuda.synchronize()
 
 
-CASES = {"zero1": case_zero1, "ep": case_ep, "decode": case_decode, "attn_bwd_b4": case_attn_bwd_b4}
+def case_dswiglu(M: int = 16384, H: int = 2048, I: int = 5504):
+    """Down-projection dgrad fused with the SwiGLU backward (dense 1.3B MLP, one micro-batch)."""
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    dy = torch.randn(M, H, device="cuda", generator=g).bfloat16()
+    wd = (torch.randn(H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    gu = torch.randn(M, 2 * I, device="cuda", generator=g).bfloat16()
+    dgu = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    for _ in range(2):
+        C.gemm_dswiglu(dy, wd, gu, dgu, 1.0)
+    torch.cuda.synchronize()
+    check_status()
+
+
+def case_moe_decode(N: int = 32, E: int = 64, k: int = 8, H: int = 2048, I: int = 1408):
+    """One decode step of the MoE experts (32 tokens, top-8 of 64): routing layout, grouped
+    SwiGLU gate|up and down GEMMs (weight-streaming bound), weighted combine."""
+    from tinytron_b200 import ops
+    from tinytron_b200.ops import check_status
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(E, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wu = (torch.randn(E, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wd = (torch.randn(E, H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    with torch.no_grad():
+        for _ in range(3):
+            sel = torch.topk(torch.randn(N, E, device="cuda", generator=g), k, -1).indices.to(torch.int32)
+            w = torch.softmax(torch.randn(N, k, device="cuda", generator=g), -1)
+            ops.moe_experts(x, sel, w, wg, wu, wd)
+    torch.cuda.synchronize()
+    check_status()
+
+
+CASES = {"zero1": case_zero1, "ep": case_ep, "decode": case_decode, "attn_bwd_b4": case_attn_bwd_b4,
+         "dswiglu": case_dswiglu, "moe_decode": case_moe_decode}
 
 
 def main():
