@@ -23,7 +23,12 @@ namespace tt {
 namespace attn {
 
 constexpr int BLOCK_B = 128;
-constexpr int BWD_THREADS = 320;  // warp 0 TMA, warp 1 MMA, warps 2..9 two compute warpgroups
+constexpr int BWD_THREADS = 512;  // warp 0 TMA, warp 1 MMA, warps 4..11 two compute warpgroups,
+                                   // warps 12..15 the dQ read-out warpgroup (warps 2-3 idle)
+// Registers per thread after setmaxnreg (launch: 65536 / 512 = 128 each):
+// 96 (warpgroup 0: TMA + MMA issue) + 2 x 144 (compute) + 128 (dQ) = 512 = 4 x 128.
+constexpr int REG_WG0 = 96, REG_COMPUTE = 144, REG_DQ = 128;
+static_assert(REG_WG0 + 2 * REG_COMPUTE + REG_DQ <= 4 * (65536 / BWD_THREADS), "register split exceeds the launch");
 
 struct BwdParams {
   int B, T, Hq, Hkv;
@@ -39,6 +44,7 @@ struct BwdParams {
   float scale_log2;
   int causal;
   int* status;
+  int dq_tma;  // 1: dQ partials reduced into dq_acc by TMA (T a multiple of 128), 0: red.v4 per thread
   int diag;  // diagnostics only (TT_ATTN_BWD_DIAG, wrong results): 1 skips the dQ reductions,
              // 2 skips the exponentials (P = scores), 4 skips the dQ TMEM read-out entirely
 };
@@ -54,6 +60,7 @@ struct BwdSmem {
   float lse2[2][BLOCK_B];                             // staged with Q/dO by the producer
   float delta[2][BLOCK_B];
   uint64_t kv_full, qdo_full[2], qdo_empty[2], s_full, p_ready, dp_full, ds_ready, dq_full, dq_empty, done;
+  uint64_t stage_free;  // the dQ warpgroup finished staging through the dS^T buffer
   uint32_t tmem_slot;
 };
 // Bytes the layout actually uses (sizeof rounds up to the 1 KB member alignment).
@@ -73,13 +80,17 @@ __device__ __forceinline__ uint32_t sw128(int row, int col, int rows) {
 //   [p_ready(it)] dV += P^T(it) dO ; [next] S^T(it+1) ;
 //   [ds_ready(it)] dK += dS^T Q ; dQ = dS K (into the dP^T columns) ; [dq_empty(it), next] dP^T(it+1)
 // Compute warpgroups (each owns half of the query columns, then half of the head dim):
-//   P(0); per it: dS(it) -> ds_ready ; P(it+1) -> p_ready ; dQ(it) atomics -> dq_empty
-// so the exponentials of the next tile run while the tensor core computes dK and dQ.
+//   P(0); per it: [stage_free(it-1)] dS(it) -> ds_ready ; P(it+1) -> p_ready
+// dQ warpgroup (all head dims of its 32 query rows per warp):
+//   per it: [dq_full(it)] dQ read out of TMEM -> dq_empty ; staged transpose + fp32 vector
+//   reductions into dq_acc -> stage_free
+// so the exponentials of the next tile and the dQ read-out run side by side while the
+// tensor core computes dK, dQ and the next dP^T.
 template <int D>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
-                    const BwdParams p) {
+                    const __grid_constant__ CUtensorMap tmDQ, const BwdParams p) {
   constexpr uint32_t TILE = BwdSmem<D>::TILE;
   constexpr uint32_t ID_SQ = idesc_bf16_f32(BLOCK_B, BLOCK_B, false, false);  // S^T, dP^T
   constexpr uint32_t ID_KV = idesc_bf16_f32(BLOCK_B, D, false, true);         // dV (A from TMEM), dK
@@ -128,7 +139,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     mbar_init(&sm.dp_full, 1);
     mbar_init(&sm.ds_ready, 256);
     mbar_init(&sm.dq_full, 1);
-    mbar_init(&sm.dq_empty, 256);
+    mbar_init(&sm.dq_empty, 128);
+    mbar_init(&sm.stage_free, 128);
     mbar_init(&sm.done, 1);
     fence_barrier_init();
   }
@@ -140,7 +152,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_slot;
-
+  // Register reallocation inside each role's branch, so the compiler allocates each role
+  // for its own limit (every warp of a warpgroup executes its warpgroup's instruction).
+  if (warp < 4) {
+  setmaxnreg_dec<REG_WG0>();
   if (warp == 0) {
     if (lane == 0 && n_iter > 0) {
       // ------------------------------------------------ producer (Q/dO/LSE/Delta double-buffered)
@@ -242,9 +257,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       umma_commit(&sm.done);
       mbar_wait(&sm.done, 0, p.status, kTimeoutOther);
     }
-  } else {
-    // ------------------------------------------------ compute warps 2..9
-    const int half = (warp - 2) >> 2;   // warpgroup: query columns [half*64, +64), head dims [half*D/2, +D/2)
+  }  // warps 2-3: idle
+  } else if (warp < 12) {
+    setmaxnreg_inc<REG_COMPUTE>();
+    // ------------------------------------------------ compute warps 4..11
+    const int half = (warp - 4) >> 2;   // warpgroup: query columns [half*64, +64), head dims [half*D/2, +D/2)
     const int quarter = warp & 3;       // TMEM lane quarter this warp may access
     const int r = quarter * 32 + lane;  // key row (P / dS phases), query row (dQ phase)
     const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
@@ -289,12 +306,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     bool ok = n_iter > 0 && p_phase(0);
     for (int it = 0; ok && it < n_iter; ++it) {
       const uint32_t ph = it & 1;
-      const int h = g * group + it / per_head;
-      const int qt = qt0 + it % per_head;
       const int buf = it & 1;
       // ---- dS^T = P^T * (dP^T - delta[q]) * scale -> shared memory (A of dK, MN-major A of dQ).
-      // The previous dQ (dq_full, waited below in the previous iteration) retired the MMAs reading dS^T.
+      // dp_full(it) follows dK/dQ(it-1), the MMAs that read the previous dS^T.
       if (!mbar_wait_warp(&sm.dp_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
+      // the dQ warpgroup's staging of the previous iteration must be out of the dS^T buffer
+      if (it > 0 && !mbar_wait_warp(&sm.stage_free, (it - 1) & 1, p.status, kTimeoutOther)) { ok = false; break; }
       tc_fence_after();
       {
         uint32_t d0[32], d1[32];
@@ -324,45 +341,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       mbar_arrive(&sm.ds_ready);
       // ---- next tile's probabilities while dK / dQ run on the tensor core
       if (it + 1 < n_iter && !p_phase(it + 1)) { ok = false; break; }
-      // ---- dQ partial, this warpgroup's head-dim half -> fp32 vector reductions into dq_acc.
-      // TMEM gives one query row per thread; each 32x32 block is transposed through this warp's
-      // own 4 KB slice of the dS^T buffer (the slice it wrote in the dS phase, free again once
-      // dq_full says the MMAs reading it retired) so that every red.v4 instruction covers four
-      // whole 128-byte rows instead of 32 scattered 16-byte pieces.
-      if (!mbar_wait_warp(&sm.dq_full, ph, p.status, kTimeoutAccFull)) { ok = false; break; }
-      tc_fence_after();
-      if (p.diag & 4) {
-        tc_fence_before();
-        mbar_arrive(&sm.dq_empty);
-      } else {
-        uint8_t* stage = sm.dst + half * (BLOCK_B * 128) + quarter * 32 * 128;
-        const int qbase = qt * BLOCK_B + quarter * 32;  // query of this warp's first row
-        float* gbase = p.dq_acc + static_cast<size_t>(row0) * (p.Hq * D) + static_cast<size_t>(h) * D + half * DH;
-#pragma unroll
-        for (int c = 0; c < DH / 32; ++c) {
-          uint32_t cur[32];
-          tmem_ld32(tmem + lane_addr + DP_COL + half * DH + c * 32, cur);
-          tmem_ld_wait();
-          if (c == DH / 32 - 1) {
-            tc_fence_before();
-            mbar_arrive(&sm.dq_empty);  // all values are in registers: the dP^T columns are free again
-          }
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
-                make_uint4(cur[4 * u], cur[4 * u + 1], cur[4 * u + 2], cur[4 * u + 3]);
-          __syncwarp();
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const int j = i * 4 + (lane >> 3);  // row within the warp's 32
-            const int u = lane & 7;             // 16-byte unit within the 32 columns
-            const float4 v = *reinterpret_cast<const float4*>(stage + j * 128 + ((u ^ (j & 7)) << 4));
-            if (qbase + j < p.T && !(p.diag & 1))
-              atomicAdd(reinterpret_cast<float4*>(gbase + static_cast<size_t>(qbase + j) * (p.Hq * D) + c * 32) + u, v);
-          }
-          __syncwarp();
-        }
-      }
     }
     // ---- dK, dV (lane = key row), this warpgroup's head-dim half -> bf16
     if (ok && n_iter > 0 && mbar_wait_warp(&sm.done, 0, p.status, kTimeoutAccFull)) {
@@ -392,6 +370,86 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           }
         }
       }
+    }
+  } else {
+    setmaxnreg_dec<REG_DQ>();
+    // ------------------------------------------------ dQ warpgroup (warps 12..15)
+    // Per iteration: dQ(it) (128 queries x D, in the dP^T columns) is read out of TMEM,
+    // the columns released (dq_empty) as soon as every value is in registers, then each
+    // 32x32 block is transposed through this warp's 4 KB slice of the dS^T buffer so every
+    // red.v4 instruction covers four whole 128-byte rows of dq_acc instead of 32 scattered
+    // 16-byte pieces; stage_free then lets the compute warps write the next dS^T.
+    const int quarter = warp & 3;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    // Staging: two 4 KB slices of the dS^T buffer per warp (1 KB aligned, laid out with the
+    // 128-byte swizzle the TMA reduction reads), alternating per 32-column block.
+    uint8_t* stage0 = sm.dst + quarter * 2 * 4096;
+    for (int it = 0; it < n_iter; ++it) {
+      const int h = g * group + it / per_head;
+      const int qt = qt0 + it % per_head;
+      if (!mbar_wait_warp(&sm.dq_full, it & 1, p.status, kTimeoutAccFull)) break;
+      tc_fence_after();
+      if (p.diag & 4) {  // diagnostics: skip the read-out
+        tc_fence_before();
+        mbar_arrive(&sm.dq_empty);
+        mbar_arrive(&sm.stage_free);
+        continue;
+      }
+      const int qbase = qt * BLOCK_B + quarter * 32;  // query of this warp's first row
+      float* gbase = p.dq_acc + static_cast<size_t>(row0) * (p.Hq * D) + static_cast<size_t>(h) * D;
+#pragma unroll
+      for (int c2 = 0; c2 < D / 64; ++c2) {
+        uint32_t cur[2][32];
+        tmem_ld32(tmem + lane_addr + DP_COL + c2 * 64, cur[0]);
+        tmem_ld32(tmem + lane_addr + DP_COL + c2 * 64 + 32, cur[1]);
+        tmem_ld_wait();
+        if (c2 == D / 64 - 1) {
+          tc_fence_before();
+          mbar_arrive(&sm.dq_empty);  // all values are in registers: the dP^T columns are free again
+        }
+#pragma unroll
+        for (int hb = 0; hb < 2; ++hb) {
+          const int blk = c2 * 2 + hb;  // 32-column block of the head dim
+          uint8_t* stage = stage0 + (blk & 1) * 4096;
+          if (p.dq_tma && blk >= 2) {  // the reduction issued two blocks ago has read this slice
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(stage + lane * 128 + ((u ^ (lane & 7)) << 4)) =
+                make_uint4(cur[hb][4 * u], cur[hb][4 * u + 1], cur[hb][4 * u + 2], cur[hb][4 * u + 3]);
+          if (p.dq_tma) {
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0 && !(p.diag & 1)) {
+              tma_reduce_add_2d(&tmDQ, stage, h * D + blk * 32, row0 + qbase);
+              bulk_commit_group();
+            }
+          } else {
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const int j = i * 4 + (lane >> 3);  // row within the warp's 32
+              const int u = lane & 7;             // 16-byte unit within the 32 columns
+              const float4 v = *reinterpret_cast<const float4*>(stage + j * 128 + ((u ^ (j & 7)) << 4));
+              if (qbase + j < p.T && !(p.diag & 1))
+                atomicAdd(reinterpret_cast<float4*>(gbase + static_cast<size_t>(qbase + j) * (p.Hq * D) + blk * 32) + u,
+                          v);
+            }
+            __syncwarp();
+          }
+        }
+      }
+      if (p.dq_tma) {  // the staging slices are read before the compute warps may overwrite them
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+      }
+      mbar_arrive(&sm.stage_free);
+    }
+    if (p.dq_tma) {  // every reduction performed before the block exits
+      if (lane == 0) bulk_wait_group<0>();
+      __syncwarp();
     }
   }
 
@@ -583,15 +641,23 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
     p.diag = diag;
   }
   const CUtensorMap tq = attn_head_map(q), tk = attn_head_map(k), tv = attn_head_map(v), tdo = attn_head_map(dout);
+  // TT_ATTN_DQ_TMA=1: dQ partials are added by TMA tile reductions of 32 queries x 32 dims
+  // (only when no tile can reach past the end of a sequence: T a multiple of 128).  Off by
+  // default: measured slower than the per-thread red.v4 path (1.029 vs 1.005 ms backward at
+  // B4 T4096 Hq16 Hkv4 d128).
+  static const bool dq_tma_env = [] { const char* e = std::getenv("TT_ATTN_DQ_TMA"); return e && std::atoi(e) != 0; }();
+  p.dq_tma = (dq_tma_env && T % BLOCK_B == 0) ? 1 : 0;
+  const CUtensorMap tdq = make_tmap_2d_f32(dq_acc.data_ptr(), static_cast<uint64_t>(Hq * D),
+                                           static_cast<uint64_t>(B * T), static_cast<uint64_t>(Hq * D * 4), 32, 32);
   const dim3 grid(static_cast<unsigned>((T + BLOCK_B - 1) / BLOCK_B * Hkv * B));
   if (D == 128) {
     const size_t smem = std::min<size_t>(bwd_smem_bytes<128>() + 1024, size_t(232448));
     TT_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attn_bwd_kernel<128><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, p);
+    attn_bwd_kernel<128><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, tdq, p);
   } else {
     const size_t smem = std::min<size_t>(bwd_smem_bytes<64>() + 1024, size_t(232448));
     TT_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attn_bwd_kernel<64><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, p);
+    attn_bwd_kernel<64><<<grid, BWD_THREADS, smem, st>>>(tq, tk, tv, tdo, tdq, p);
   }
   TT_CUDA_CHECK(cudaGetLastError());
   const int width = static_cast<int>(Hq * D);

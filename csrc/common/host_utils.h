@@ -64,6 +64,25 @@ inline CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t 
   return m;
 }
 
+// 2-D fp32 tensor map over a row-major matrix [outer, inner] (row stride in bytes),
+// box {box_inner, box_outer}; used as the destination of TMA reductions.
+inline CUtensorMap make_tmap_2d_f32(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
+                                    uint32_t box_inner, uint32_t box_outer,
+                                    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  TT_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "TMA base address must be 16-byte aligned");
+  TT_CHECK(row_stride_bytes % 16 == 0, "TMA row stride must be a multiple of 16 bytes");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_tiled_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box,
+                                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TT_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (code " + std::to_string((int)r) + ")");
+  return m;
+}
+
 inline int num_sms(int device) {
   static int cached[64] = {0};
   if (device < 64 && cached[device]) return cached[device];

@@ -290,24 +290,27 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
       }
     }
   } else if constexpr (EPI == EPI_DSWIGLU) {
-    // The saved pre-activations g|u are loaded 64 columns at a time (16 independent
-    // 16-byte loads in flight per thread) before the TMEM reads of those columns, so the
-    // per-row load latency is paid BN/64 times per tile instead of BN/16 times.
-    constexpr int QC = 64;
+    // The saved pre-activations g|u are read 32 columns at a time (8 independent 16-byte
+    // loads per thread), double-buffered: the loads of the next 32 columns are issued
+    // before the current ones are processed, so the load latency is paid once per row
+    // segment instead of once per block.
+    constexpr int QC = 32;
     const __nv_bfloat16* a = p.aux + static_cast<size_t>(row) * p.ld_aux;
     __nv_bfloat16* o = p.aux_out + static_cast<size_t>(row) * p.ld_aux_out;
-#pragma unroll 1
-    for (int q0 = c_lo; q0 < c_hi; q0 += QC) {
+    uint4 gA[QC / 8], uA[QC / 8], gB[QC / 8], uB[QC / 8];
+    auto fetch = [&](int q0, uint4(&gq)[QC / 8], uint4(&uq)[QC / 8]) {
       const int colq = nb * BN + q0;
-      const bool full = row_ok && colq + QC <= p.N;
-      uint4 gq[QC / 8], uq[QC / 8];
-      if (full) {
+      if (row_ok && colq + QC <= p.N) {
 #pragma unroll
         for (int i = 0; i < QC / 8; ++i) {
           gq[i] = __ldg(reinterpret_cast<const uint4*>(a + colq) + i);
           uq[i] = __ldg(reinterpret_cast<const uint4*>(a + p.N + colq) + i);
         }
       }
+    };
+    auto process = [&](int q0, const uint4(&gq)[QC / 8], const uint4(&uq)[QC / 8]) {
+      const int colq = nb * BN + q0;
+      const bool full = row_ok && colq + QC <= p.N;
 #pragma unroll
       for (int c = 0; c < QC; c += 16) {
         uint32_t r[16];
@@ -346,6 +349,15 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
           store_bf16<16>(o + p.N + col0, du, nv);
         }
       }
+    };
+    // (c_hi - c_lo) is a multiple of 2 * QC for every caller (128 or 256 columns).
+    fetch(c_lo, gA, uA);
+#pragma unroll 1
+    for (int q0 = c_lo; q0 < c_hi; q0 += 2 * QC) {
+      fetch(q0 + QC, gB, uB);
+      process(q0, gA, uA);
+      if (q0 + 2 * QC < c_hi) fetch(q0 + 2 * QC, gA, uA);
+      process(q0 + QC, gB, uB);
     }
   }
 }
