@@ -110,3 +110,19 @@ def test_gemm_splitk_accumulate_deterministic(M, N, K):
     _check(c1, ref, 1e-5)
     assert torch.equal(c1, c2)
     assert ext().status_read(0) == 0
+
+
+@pytest.mark.parametrize("M,N,K", [(32, 3072, 2048), (32, 2048, 2048), (1, 64, 2048), (64, 2048, 5504), (17, 304, 1000)])
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True)])
+def test_gemm_small_m(M, N, K, a_mn, b_mn):
+    """Decode-sized M (one 128-row tile, mostly padding): bf16 output, alpha applied,
+    result identical across calls."""
+    A, B, a, b = _operands(M, N, K, a_mn, b_mn, seed=5)
+    c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    alpha_t = torch.tensor([0.5], device="cuda")
+    ext().gemm(a, b, c, a_mn, b_mn, False, 2.0, alpha_t, 0)
+    _check(c, A.float() @ B.float().t(), 1e-2)
+    c2 = torch.empty_like(c)
+    ext().gemm(a, b, c2, a_mn, b_mn, False, 2.0, alpha_t, 0)
+    assert torch.equal(c, c2)
+    assert ext().status_read(0) == 0
