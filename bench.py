@@ -282,7 +282,14 @@ def run(args, impl: str):
         trainer._one_training_step(trainer.config, step)
         losses.append(float(trainer.one_step_results["loss"].item()))  # device -> host read of the result
 
-    trainer._next_train_batch = next_dev
+    # With SEP > 1 the reference's _prepare_local_batch (tinytron/training/trainer.py:339-350)
+    # slices each rank's sequence chunk out of the batch and relies on its `.to(cuda)` copy to
+    # make the chunk contiguous (its loss calls `.view` on the targets), i.e. its stock input
+    # is a host batch from the DataLoader; device-resident batches would stay non-contiguous
+    # and fail.  So for SEP > 1 the timed reference step is fed pinned host batches (this
+    # framework's arm keeps device-resident batches).
+    feed = next_host if (SEP > 1 and impl == "reference") else next_dev
+    trainer._next_train_batch = feed
     for w in range(args.warmup):
         step_fn(w)
     torch.cuda.synchronize()
@@ -295,7 +302,7 @@ def run(args, impl: str):
     h2d = ga * MICRO_BATCH * SEQ * 8 * 2  # int64 input_ids + labels per rank per step
     d2h = 4
 
-    trainer._next_train_batch = next_dev
+    trainer._next_train_batch = feed
     launches, all_kernels = _count_launches(step_fn, args.warmup + 2 * args.steps, own_marker)
 
     dp = world // SEP
@@ -331,7 +338,9 @@ def run(args, impl: str):
         "config": {"model": MODEL_NAME, "global_batch": MICRO_BATCH * GA * dp, "seq_len": SEQ,
                    "micro_batch": MICRO_BATCH, "grad_accum": GA,
                    "parallelism": (f"sep{SEP}+dp{dp}" if SEP > 1 else f"dp{world}") + "+zero1",
-                   "optimizer": "AdamW (ZeRO-1)", "l2": "inputs larger than L2 (no flush needed)"},
+                   "optimizer": "AdamW (ZeRO-1)", "l2": "inputs larger than L2 (no flush needed)",
+                   "inputs": ("pinned host batches (the reference slices SEP chunks on the host)"
+                              if feed is next_host else "device-resident batches")},
         "mfu": round(achieved / (world * 2.25e15), 4),
         "mfu_of_measured_cublas_peak": round(achieved / (world * measured_peak), 4),
         "model_tflops_per_gpu": round(achieved / world / 1e12, 1),
