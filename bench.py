@@ -354,7 +354,7 @@ def run(args, impl: str):
     if impl == "reference":
         out["impl"] = "reference"
         out.pop("gpu_launches")
-        out["config"]["reference_flags"] = "mock data, deterministic, ZeRO-1, " + (
+        out["reference_flags"] = "mock data, deterministic, ZeRO-1, " + (
             "--use_compile" if "--use_compile" in argv else "eager")
     if rank == 0:
         print(json.dumps(out), flush=True)

@@ -45,9 +45,18 @@ struct BwdParams {
   int causal;
   int* status;
   int dq_tma;  // 1: dQ partials reduced into dq_acc by TMA (T a multiple of 128), 0: red.v4 per thread
-  int diag;  // diagnostics only (TT_ATTN_BWD_DIAG, wrong results): 1 skips the dQ reductions,
-             // 2 skips the exponentials (P = scores), 4 skips the dQ TMEM read-out entirely
+  int diag;  // diagnostics only, compiled in with -DTT_ATTN_DIAGNOSTICS (TT_ATTN_BWD_DIAG, wrong
+             // results): 1 skips the dQ reductions, 2 skips the exponentials (P = scores), 4 skips the
+             // dQ TMEM read-out entirely.  Without the macro every test below folds to false.
 };
+
+// Diagnostic bit test: constant false unless the build defines TT_ATTN_DIAGNOSTICS, so the
+// production kernel carries no branch that could produce wrong gradients.
+#ifdef TT_ATTN_DIAGNOSTICS
+#define TT_BWD_DIAG(p, bit) (((p).diag & (bit)) != 0)
+#else
+#define TT_BWD_DIAG(p, bit) false
+#endif
 
 template <int D>
 struct BwdSmem {
@@ -283,7 +292,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const float* l2 = sm.lse2[buf] + half * QH;
 #pragma unroll
       for (int i = 0; i < QH; ++i) pv[i] = ex2_mufu(fmaf(__uint_as_float(raw[i]), p.scale_log2, -l2[i])) * key_scale;
-      if (p.diag & 2) {
+      if (TT_BWD_DIAG(p, 2)) {
 #pragma unroll
         for (int i = 0; i < QH; ++i) pv[i] = __uint_as_float(raw[i]) * key_scale;
       }
@@ -389,7 +398,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       const int qt = qt0 + it % per_head;
       if (!mbar_wait_warp(&sm.dq_full, it & 1, p.status, kTimeoutAccFull)) break;
       tc_fence_after();
-      if (p.diag & 4) {  // diagnostics: skip the read-out
+      if (TT_BWD_DIAG(p, 4)) {  // diagnostics: skip the read-out
         tc_fence_before();
         mbar_arrive(&sm.dq_empty);
         mbar_arrive(&sm.stage_free);
@@ -422,7 +431,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           if (p.dq_tma) {
             fence_proxy_async();
             __syncwarp();
-            if (lane == 0 && !(p.diag & 1)) {
+            if (lane == 0 && !TT_BWD_DIAG(p, 1)) {
               tma_reduce_add_2d(&tmDQ, stage, h * D + blk * 32, row0 + qbase);
               bulk_commit_group();
             }
@@ -433,7 +442,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
               const int j = i * 4 + (lane >> 3);  // row within the warp's 32
               const int u = lane & 7;             // 16-byte unit within the 32 columns
               const float4 v = *reinterpret_cast<const float4*>(stage + j * 128 + ((u ^ (j & 7)) << 4));
-              if (qbase + j < p.T && !(p.diag & 1))
+              if (qbase + j < p.T && !TT_BWD_DIAG(p, 1))
                 atomicAdd(reinterpret_cast<float4*>(gbase + static_cast<size_t>(qbase + j) * (p.Hq * D) + blk * 32) + u,
                           v);
             }
@@ -636,10 +645,14 @@ void attn_bwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor o
   p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   p.causal = causal ? 1 : 0;
   p.status = device_status_ptr(q.get_device());
+#ifdef TT_ATTN_DIAGNOSTICS
   {
     static const int diag = [] { const char* e = std::getenv("TT_ATTN_BWD_DIAG"); return e ? std::atoi(e) : 0; }();
     p.diag = diag;
   }
+#else
+  p.diag = 0;
+#endif
   const CUtensorMap tq = attn_head_map(q), tk = attn_head_map(k), tv = attn_head_map(v), tdo = attn_head_map(dout);
   // TT_ATTN_DQ_TMA=1: dQ partials are added by TMA tile reductions of 32 queries x 32 dims
   // (only when no tile can reach past the end of a sequence: T a multiple of 128).  Off by

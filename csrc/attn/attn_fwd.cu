@@ -50,7 +50,8 @@ struct FwdParams {
   int* status;
   int handoff;    // 1: the two softmax warpgroups take turns per tile (TT_ATTN_HANDOFF=1; off by default,
                   //    measured slower: 0.53 vs 0.43 ms at B4 T4096 Hq16 Hkv4 d128 causal)
-  int skip_math;  // diagnostics (TT_ATTN_SKIP_MATH=1): publish an all-zero P, to time the pipeline alone
+  int skip_math;  // diagnostics (-DTT_ATTN_DIAGNOSTICS and TT_ATTN_SKIP_MATH=1): publish an all-zero P,
+                  // to time the pipeline alone; always 0 in a production build
 };
 
 template <int D>
@@ -265,7 +266,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       tc_fence_after();
+#ifdef TT_ATTN_DIAGNOSTICS
       if (p.skip_math) {  // pipeline-only timing: publish an all-zero P
+#else
+      if (false) {
+#endif
         uint32_t z[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) z[i] = 0u;
@@ -525,9 +530,13 @@ void attn_fwd(torch::Tensor q, torch::Tensor k, torch::Tensor v, int64_t q_col0,
   p.status = device_status_ptr(q.get_device());
   {
     static const int handoff = [] { const char* e = std::getenv("TT_ATTN_HANDOFF"); return e ? std::atoi(e) : 0; }();
-    static const int skip = [] { const char* e = std::getenv("TT_ATTN_SKIP_MATH"); return e ? std::atoi(e) : 0; }();
     p.handoff = handoff;
+#ifdef TT_ATTN_DIAGNOSTICS
+    static const int skip = [] { const char* e = std::getenv("TT_ATTN_SKIP_MATH"); return e ? std::atoi(e) : 0; }();
     p.skip_math = skip;
+#else
+    p.skip_math = 0;
+#endif
   }
   const CUtensorMap tq = head_map(q), tk = head_map(k), tv = head_map(v);
   const dim3 grid(static_cast<unsigned>(((T + BLOCK - 1) / BLOCK + 1) / 2 * Hq * B));

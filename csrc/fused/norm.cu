@@ -265,6 +265,10 @@ extern "C" __attribute__((visibility("default"))) int tt_rmsnorm_bwd_noalloc(
     const __nv_bfloat16* gh, const float* x, const float* rstd, const float* w, const float* g_res, float* gx,
     __nv_bfloat16* g_delta, float* dw, int M, int D, int accumulate_dw, cudaStream_t stream) {
   using namespace tt;
+  // An error left pending on this thread by earlier, unrelated work would otherwise be
+  // picked up (and cleared) by the launch checks below and reported as this call's launch
+  // failure; report it as such instead and launch nothing.
+  if (cudaPeekAtLastError() != cudaSuccess) return 5;
   if (gh == nullptr || x == nullptr || rstd == nullptr || w == nullptr || dw == nullptr || M < 0 || D <= 0 ||
       D % EPT != 0 || D / EPT > 1024)
     return 1;

@@ -17,6 +17,8 @@
 //  * The first call on a device looks up the scratch array's device address for
 //    that device (cudaGetSymbolAddress with the device current); make that first
 //    call before any CUDA stream capture.
+//  * The scratch address is taken for the CURRENT device, so `stream` must belong to
+//    the current device (a stream of another device makes the launches fail: code 4).
 //  * All calls share the one scratch array and it keeps the last call's partial
 //    sums. Every partial a call reads is written by the same call first, so no
 //    clearing is needed, but calls whose executions overlap on the GPU (different
@@ -39,7 +41,9 @@ extern "C" {
 // gx:      [M, D] fp32 output (may be NULL), g_delta: [M, D] bf16 output (may be NULL)
 // dw:      [D]    fp32 weight gradient; accumulated into when accumulate_dw != 0
 // Returns 0 on success, 1 for invalid arguments, 2 if ceil(M/16)*D exceeds the
-// scratch limit, 3 if the scratch address lookup failed, 4 if a launch failed.
+// scratch limit, 3 if the scratch address lookup failed, 4 if a launch failed, and
+// 5 if a CUDA error was already pending on the calling thread when the call began
+// (nothing is launched then, and the pending error is left for its owner to read).
 int tt_rmsnorm_bwd_noalloc(const __nv_bfloat16* gh, const float* x, const float* rstd, const float* w,
                            const float* g_res, float* gx, __nv_bfloat16* g_delta, float* dw, int M, int D,
                            int accumulate_dw, cudaStream_t stream);

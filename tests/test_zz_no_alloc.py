@@ -78,3 +78,33 @@ def test_noalloc_rejects_oversized_problem():
     rc = fn(_ptr(t), _ptr(t), _ptr(t), _ptr(t), None, None, None, _ptr(t), M, D, 0,
             ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == 2
+
+
+def test_noalloc_overwrite_mode_and_optional_outputs():
+    """accumulate_dw=0 overwrites dw; g_res and gx may be NULL (only g_delta and dw written)."""
+    from tinytron_b200.ops import _ext
+
+    C = _ext.load()
+    fn = _symbol()
+    M, D = 777, 1024
+    x, rstd, w, gh, _ = _case(M, D, 7)
+    ref_gd = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    ref_dw = torch.zeros(D, device="cuda")
+    C.rmsnorm_bwd(gh, x, rstd, w, None, None, ref_gd, ref_dw, False, torch.empty(C.rmsnorm_bwd_scratch_numel(M, D),
+                                                                                   device="cuda"))
+    gd = torch.full((M, D), float("nan"), device="cuda", dtype=torch.bfloat16)
+    dw = torch.full((D,), 123.0, device="cuda")  # overwritten, not added to
+    rc = fn(_ptr(gh), _ptr(x), _ptr(rstd), _ptr(w), None, None, _ptr(gd), _ptr(dw), M, D, 0,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    torch.cuda.synchronize()
+    assert rc == 0
+    assert _rel(gd, ref_gd) < 1e-2
+    assert _rel(dw, ref_dw) < 1e-5
+
+
+def test_noalloc_rejects_bad_hidden_size():
+    fn = _symbol()
+    t = torch.empty(64, device="cuda")
+    rc = fn(_ptr(t), _ptr(t), _ptr(t), _ptr(t), None, None, None, _ptr(t), 4, 12, 0,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == 1  # D must be a multiple of 8

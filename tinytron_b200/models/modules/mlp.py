@@ -168,7 +168,7 @@ class MoE(nn.Module):
             y = ops.moe_experts(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
                                 self.experts_down_weights)
             return y.view(B, T, D), gate_logits.view(B, T, -1)
-        if ep > 1 and x.is_cuda and os.environ.get("TT_NATIVE_COMM", "1") != "0":
+        if ep > 1 and x.is_cuda and parallel_state.native_comm_enabled():
             # dispatch/combine by NVLink peer stores/loads around the grouped GEMMs
             from tinytron_b200.parallel.ep_comm import ep_moe
 

@@ -1,5 +1,9 @@
 """Kernel microbenchmarks: ``python -m tinytron_b200.ops.bench_ops <what> [--json]``.
 
+``gemm`` and ``attn`` sweep the training shapes against cuBLAS / torch SDPA; the fixed
+kernel cases (``zero1``, ``ep``, ``decode``, ``attn_bwd_b4``, ``dswiglu``, ``moe_decode``)
+time one workload each (``--iters``/``--warmup``).
+
 Each measurement is CUDA-event timed on the launching stream, after warm-up,
 with L2 flushed (a 256 MiB buffer write) before every timed launch.  Results are
 reported against the measured peaks in MEASURED_PEAKS.json when present.
@@ -8,6 +12,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 from pathlib import Path
 
@@ -131,12 +136,185 @@ def bench_attention(B=4, T=4096, Hq=16, Hkv=4, d=128, iters=10):
     return [res]
 
 
+# ----------------------------------------------------------------------------- fixed kernel cases
+# Each builder sets up one workload and returns (run, close): ``run()`` launches the kernels
+# of one iteration, ``close()`` checks the device status word and releases buffers.  Inputs
+# exceed the 126 MB L2 where the kernel streams memory and every case holds at most a few
+# GB, so ``--iters 2 --warmup 1`` also serves as a short case for a profiler capture.
+
+
+def _case_zero1(n: int = 64 * 1024 * 1024, W: int = 2):
+    from tinytron_b200.ops import check_status
+    from tinytron_b200.parallel.symm import SymmetricHeap
+
+    n = (n + 64 * W - 1) // (64 * W) * (64 * W)
+    shard = n // W
+    heaps = SymmetricHeap.create_emulated(SymmetricHeap.bytes_needed((n, torch.float32), (n, torch.float32),
+                                                                     (n, torch.bfloat16)), W)
+    bufs = []
+    for h in heaps:
+        data, grad, p16 = h.alloc(n, torch.float32), h.alloc(n, torch.float32), h.alloc(n, torch.bfloat16)
+        data.normal_()
+        grad.normal_()
+        bufs.append(dict(data=data, grad=grad, p16=p16, m=torch.zeros(shard, device="cuda"),
+                         v=torch.zeros(shard, device="cuda"), norm=torch.zeros(2, device="cuda")))
+    state = {"step": 0}
+
+    def run():
+        state["step"] += 1
+        for r, (h, b) in enumerate(zip(heaps, bufs)):
+            h.reduce_scatter_sumsq(b["grad"], r * shard, (r + 1) * shard, n, 1.0 / W)
+        for r, (h, b) in enumerate(zip(heaps, bufs)):
+            h.adamw_allgather(b["data"], b["grad"], b["p16"], b["m"], b["v"], r * shard, (r + 1) * shard, 1e-4,
+                              (0.9, 0.95), 1e-8, 0.1, state["step"], 1.0, norm_out=b["norm"])
+        for r, (h, b) in enumerate(zip(heaps, bufs)):
+            h.shadow_refresh(b["data"], b["p16"], r * shard, (r + 1) * shard)
+
+    def close():
+        check_status()
+        for h in heaps:
+            h.close()
+
+    return run, close
+
+
+def _case_ep(N: int = 4096, W: int = 2, E: int = 64, k: int = 8, H: int = 2048, I: int = 1408):
+    from tinytron_b200.ops import check_status
+    from tinytron_b200.ops.weights import concat_rows
+    from tinytron_b200.parallel import ep_comm as epc
+
+    E_l = E // W
+    g = torch.Generator(device="cuda").manual_seed(0)
+    xs = [torch.randn(N, H, device="cuda", generator=g).bfloat16() for _ in range(W)]
+    sels = [torch.topk(torch.randn(N, E, device="cuda", generator=g), k, -1).indices.to(torch.int32)
+            for _ in range(W)]
+    ws = [torch.softmax(torch.randn(N, k, device="cuda", generator=g), -1).reshape(-1).contiguous()
+          for _ in range(W)]
+    w_gu = [concat_rows([(torch.randn(E_l * I, H, device="cuda", generator=g) * 0.02).bfloat16(),
+                         (torch.randn(E_l * I, H, device="cuda", generator=g) * 0.02).bfloat16()]) for _ in range(W)]
+    wd = [(torch.randn(E_l * H, I, device="cuda", generator=g) * 0.02).bfloat16() for _ in range(W)]
+    bufs = epc.EPBuffers.create_emulated(W, E, H, epc.capacity(W, N, k, E_l))
+
+    def run():
+        counts = [epc.plan_routes(bufs[r], sels[r]) for r in range(W)]
+        plans = [epc.plan_finish(bufs[r], sels[r], counts[r]) for r in range(W)]
+        xrs = [epc.dispatch(bufs[r], plans[r], xs[r], True) for r in range(W)]
+        for r in range(W):
+            epc.experts_forward(bufs[r], plans[r], xrs[r], w_gu[r], wd[r], I, True)
+        for r in range(W):
+            epc.combine(bufs[r], plans[r], ws[r], keep_rows=True, push=True)
+
+    def close():
+        check_status()
+        for b in bufs:
+            b.close()
+
+    return run, close
+
+
+def _case_decode(B: int = 32, ctx: int = 1024, Hq: int = 16, Hkv: int = 4, D: int = 128, page: int = 16):
+    from tinytron_b200.inference.cache import LayerPagedKVCache
+    from tinytron_b200.ops import check_status
+
+    cache = LayerPagedKVCache(B, Hkv, D, ctx + 16, page, "cuda", torch.bfloat16)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    W = (Hq + 2 * Hkv) * D
+    prompt = torch.randn(B * ctx, W, device="cuda", generator=g).bfloat16()
+    cache.append_rope(prompt, B, ctx, Hq, Hkv, D, 10000.0)
+    cache.advance(ctx)
+    cache.reserve(ctx + 16)
+    qkv = torch.randn(B, W, device="cuda", generator=g).bfloat16()
+
+    def run():  # one decode step's attention; the cache length is not advanced, so every
+        # iteration appends at (and attends over) the same position
+        q = cache.append_rope(qkv, B, 1, Hq, Hkv, D, 10000.0)
+        cache.attend_decode(q.view(B, Hq, D), 1.0 / math.sqrt(D))
+
+    return run, check_status
+
+
+def _case_attn_bwd_b4(B: int = 4, T: int = 4096, Hq: int = 16, Hkv: int = 4, d: int = 128):
+    from tinytron_b200.ops import _ext
+
+    C = _ext.load()
+    W = (Hq + 2 * Hkv) * d
+    qkv = torch.randn(B * T, W, device="cuda").bfloat16()
+    o = torch.empty(B * T, Hq * d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(B, Hq, T, device="cuda")
+    sc = 1 / math.sqrt(d)
+    C.attn_fwd(qkv, qkv, qkv, 0, Hq * d, (Hq + Hkv) * d, B, T, T, Hq, Hkv, d, o, lse, sc, True, 0)
+    do = torch.randn_like(o)
+    dqkv = torch.empty_like(qkv)
+    dq_acc = torch.empty(B * T, Hq * d, device="cuda")
+    delta = torch.empty(C.attn_bwd_scratch_numel(B, Hq, T), device="cuda")
+
+    def run():
+        C.attn_bwd(qkv, qkv, qkv, o, do, 0, Hq * d, (Hq + Hkv) * d, lse, B, T, Hq, Hkv, d, dqkv, 0, dqkv, Hq * d,
+                   dqkv, (Hq + Hkv) * d, dq_acc, delta, sc, True)
+
+    return run, (lambda: None)
+
+
+def _case_dswiglu(M: int = 16384, H: int = 2048, I: int = 5504):
+    """Down-projection dgrad fused with the SwiGLU backward (dense 1.3B MLP, one micro-batch)."""
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    dy = torch.randn(M, H, device="cuda", generator=g).bfloat16()
+    wd = (torch.randn(H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    gu = torch.randn(M, 2 * I, device="cuda", generator=g).bfloat16()
+    dgu = torch.empty(M, 2 * I, device="cuda", dtype=torch.bfloat16)
+    return (lambda: C.gemm_dswiglu(dy, wd, gu, dgu, 1.0)), check_status
+
+
+def _case_moe_decode(N: int = 32, E: int = 64, k: int = 8, H: int = 2048, I: int = 1408):
+    """One decode step of the MoE experts (32 tokens, top-8 of 64): routing layout, grouped
+    SwiGLU gate|up and down GEMMs (weight-streaming bound), weighted combine."""
+    from tinytron_b200 import ops
+    from tinytron_b200.ops import check_status
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(E, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wu = (torch.randn(E, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wd = (torch.randn(E, H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    sel = torch.topk(torch.randn(N, E, device="cuda", generator=g), k, -1).indices.to(torch.int32)
+    w = torch.softmax(torch.randn(N, k, device="cuda", generator=g), -1)
+
+    def run():
+        with torch.no_grad():
+            ops.moe_experts(x, sel, w, wg, wu, wd)
+
+    return run, check_status
+
+
+KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
+                "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode}
+
+
+def bench_case(name: str, iters: int, warmup: int) -> list[dict]:
+    """Median device ms of one iteration of a fixed kernel case (L2 flushed before each)."""
+    run, close = KERNEL_CASES[name]()
+    try:
+        ms = time_fn(run, iters=iters, warmup=warmup)
+    finally:
+        torch.cuda.synchronize()
+        close()
+    return [dict(case=name, ms=round(ms, 4), iters=iters)]
+
+
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["gemm", "attn", "attn_fwd_once", "attn_bwd_once", "gemm_once", "all"])
+    ap.add_argument("what", choices=["gemm", "attn", "attn_fwd_once", "attn_bwd_once", "gemm_once", "all",
+                                     *sorted(KERNEL_CASES)])
     ap.add_argument("--json", action="store_true")
+    ap.add_argument("--iters", type=int, default=20, help="fixed kernel cases: timed iterations")
+    ap.add_argument("--warmup", type=int, default=3, help="fixed kernel cases: untimed iterations")
     args = ap.parse_args()
     out = {}
+    if args.what in KERNEL_CASES:
+        out[args.what] = bench_case(args.what, args.iters, args.warmup)
     if args.what == "gemm_once":  # small fixed case for profiler captures: gate|up forward GEMM, 2 launches
         from tinytron_b200.ops import _ext
 

@@ -22,6 +22,9 @@ _DP_SP_GROUP = None
 _SEP_SIZE = None
 _DP_SIZE = None
 _DP_SP_SIZE = None
+# Collective implementation for the training/inference hot paths: "native" runs them as
+# peer loads/stores on symmetric heaps (one node), "nccl" keeps every collective on NCCL.
+_COMM_IMPL = "native"
 _SEP_RANKS: list[int] | None = None
 _DP_RANKS: list[int] | None = None
 
@@ -210,3 +213,19 @@ def print_model_parallel_topology(master_process: bool, tag: str = "Parallel Top
         p(f"rank {row[0]:>3}: sep_gid={row[1]} sep={row[2]}/{row[3]} dp_gid={row[4]} dp={row[5]}/{row[6]} "
           f"sep_members={row[7:7 + S]} dp_members={row[7 + S:7 + S + D]}")
     p("=" * (len(tag) + 8))
+
+
+def set_comm_impl(impl: str) -> None:
+    """Select the collective implementation (``--comm_impl``): "native" or "nccl"."""
+    global _COMM_IMPL
+    if impl not in ("native", "nccl"):
+        raise ValueError(f"Unsupported comm_impl: {impl}")
+    _COMM_IMPL = impl
+
+
+def native_comm_enabled() -> bool:
+    """True when the symmetric-heap collectives are selected.  ``TT_NATIVE_COMM=0`` in the
+    environment forces NCCL for callers that do not go through the trainer's flags."""
+    import os
+
+    return _COMM_IMPL == "native" and os.environ.get("TT_NATIVE_COMM", "1") != "0"

@@ -1,6 +1,6 @@
 """Training CLI (reference: tinytron/training/arguments.py:8-120): same flag names,
-groups and defaults, plus a few B200 extensions (``--grad_bucket_mb``,
-``--comm_impl``, ``--rms_norm_eps``, ``--rope_theta``, ``--model_preset``)."""
+groups and defaults, plus a few B200 extensions (``--comm_impl``, ``--rms_norm_eps``,
+``--rope_theta``, ``--model_preset``)."""
 from __future__ import annotations
 
 import argparse
@@ -96,8 +96,9 @@ def _parallel(p):
     g.add_argument("--ddp_find_unused_parameters", action="store_true")
     g.add_argument("--ddp_gradient_as_bucket_view", action=argparse.BooleanOptionalAction, default=True)
     g.add_argument("--use_distributed_optimizer", action=argparse.BooleanOptionalAction, default=True)
-    g.add_argument("--grad_bucket_mb", type=int, default=64)
-    g.add_argument("--comm_impl", type=str, default="nccl", choices=["nccl", "p2p"])
+    g.add_argument("--comm_impl", type=str, default="native", choices=["native", "nccl"],
+                   help="native: ZeRO-1, EP and Ulysses collectives as NVLink peer loads/stores on symmetric "
+                        "heaps (one node); nccl: every collective on NCCL")
     return p
 
 

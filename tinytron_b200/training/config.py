@@ -86,10 +86,9 @@ class ParallelConfig:
     ddp_find_unused_parameters: bool = False
     ddp_gradient_as_bucket_view: bool = True
     use_distributed_optimizer: bool = True
-    # ext: gradient bucket size (MB of fp32 grads) for the overlapped reduce-scatter.
-    grad_bucket_mb: int = 64
-    # ext: collective implementation for gradient/param sync ("nccl" or "p2p" peer-memory kernels).
-    comm_impl: str = "nccl"
+    # ext: collective implementation of the hot paths: "native" (peer loads/stores on symmetric
+    # heaps inside one node) or "nccl".
+    comm_impl: str = "native"
 
 
 @dataclass(frozen=True)
@@ -145,7 +144,7 @@ def build_config(args: argparse.Namespace) -> Config:
         ddp_find_unused_parameters=args.ddp_find_unused_parameters,
         ddp_gradient_as_bucket_view=args.ddp_gradient_as_bucket_view,
         use_distributed_optimizer=args.use_distributed_optimizer,
-        grad_bucket_mb=getattr(args, "grad_bucket_mb", 64), comm_impl=getattr(args, "comm_impl", "nccl"),
+        comm_impl=getattr(args, "comm_impl", "native"),
     )
     model_cfg = build_model_config(args, seed=args.seed)
     cfg = Config(logging=logging_cfg, seed=seed_cfg, data=data_cfg, train=train_cfg, optim=optim_cfg,
@@ -179,5 +178,5 @@ def validate_static(cfg: Config) -> None:
         raise ValueError("num_experts_per_tok must be positive when use_moe is enabled.")
     if m.moe_balance_loss_weight < 0:
         raise ValueError("moe_balance_loss_weight must be non-negative.")
-    if cfg.parallel.comm_impl not in ("nccl", "p2p"):
+    if cfg.parallel.comm_impl not in ("native", "nccl"):
         raise ValueError(f"Unsupported comm_impl: {cfg.parallel.comm_impl}")

@@ -86,6 +86,7 @@ class Trainer:
             self._owns_pg = True
         set_seed(config.seed.seed + self.rank, deterministic=config.seed.deterministic)
         self.master_process = self.rank == 0
+        parallel_state.set_comm_impl(config.parallel.comm_impl)
         if dist.is_initialized():
             parallel_state.initialize_model_parallel(config.parallel)
             parallel_state.print_model_parallel_topology(self.master_process and config.logging.print_config,
@@ -151,7 +152,7 @@ class Trainer:
                 return SymmetricHeap.create(nbytes, group=self.dp_group, device=self.device)
         self.flat = FlatParams(model, pad_to_multiple=pad, with_bf16=self.device.type == "cuda",
                                heap_factory=heap_factory)
-        if (self.device.type == "cuda" and self.sp_world_size > 1 and os.environ.get("TT_NATIVE_COMM", "1") != "0"
+        if (self.device.type == "cuda" and self.sp_world_size > 1 and parallel_state.native_comm_enabled()
                 and self.sp_world_size <= 8):
             from tinytron_b200.parallel.symm import enable_heap_all_to_all, same_host
 
@@ -161,8 +162,8 @@ class Trainer:
     def _use_native_comm(self, config: Config) -> bool:
         """ZeRO-1 gradient/parameter sync over NVLink peer memory (tt_comm) instead of
         NCCL: CUDA, DP > 1 inside one node, AdamW with the distributed optimizer.
-        ``TT_NATIVE_COMM=0`` selects the NCCL path."""
-        if self.device.type != "cuda" or self.dp_world_size <= 1 or os.environ.get("TT_NATIVE_COMM", "1") == "0":
+        ``--comm_impl nccl`` (or ``TT_NATIVE_COMM=0``) selects the NCCL path."""
+        if self.device.type != "cuda" or self.dp_world_size <= 1 or not parallel_state.native_comm_enabled():
             return False
         if not (config.parallel.use_distributed_optimizer and config.optim.optimizer == "adam"):
             return False
