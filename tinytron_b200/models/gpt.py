@@ -93,6 +93,31 @@ class GPT(nn.Module):
         assert T <= self.config.block_size, f"Cannot forward sequence of length {T}, block size is only {self.config.block_size}"
         if use_cache or past_key_values is not None:
             return self._forward_cached(idx, past_key_values, use_cache, position_offset)
+        h, total_aux = self._trunk(idx, targets, position_offset)
+        if targets is None:
+            if torch.is_grad_enabled():  # differentiable logits (e.g. RL policy log-probs)
+                return ops.linear(h, self.lm_head.weight)
+            return ops.lm_logits(h, self.lm_head.weight)
+        valid = targets != self.loss_fn.ignore_index
+        loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index)
+        loss, logging_loss = self.loss_fn.reduce(loss_sum, valid.sum())
+        logits = None
+        if return_logits:
+            with torch.no_grad():
+                logits = ops.lm_logits(h.detach(), self.lm_head.weight)
+        return logits, loss + total_aux, logging_loss
+
+    def token_log_probs(self, idx, targets, position_offset: int = 0):
+        """log p(targets[b, t] | idx[b, :t+1]) as fp32 ``[B, T]``, differentiable, without
+        materialising logits beyond the fused LM-head + cross-entropy kernel's bf16 buffer
+        (which its backward reuses in place).  Targets equal to the ignore index (-100)
+        get log-prob 0 and no gradient.  Used by the RL trainers for the actor's log-probs."""
+        h, _ = self._trunk(idx, None, position_offset)
+        return ops.lm_head_token_logprobs(h, self.lm_head.weight, targets, self.loss_fn.ignore_index).view(
+            targets.shape)
+
+    def _trunk(self, idx, targets, position_offset: int = 0):
+        """Embedding -> blocks -> final norm; returns (normalised hidden states, MoE aux loss)."""
         x = ops.embedding(idx, self.wte.weight)
         pending = None
         total_aux = 0.0
@@ -110,17 +135,7 @@ class GPT(nn.Module):
                 else:
                     pending = blk.mlp(h)
         x, h = ops.add_rmsnorm(x, pending, self.lnf.weight, self.eps)
-        if targets is None:
-            if torch.is_grad_enabled():  # differentiable logits (e.g. RL policy log-probs)
-                return ops.linear(h, self.lm_head.weight)
-            return ops.lm_logits(h, self.lm_head.weight)
-        loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index)
-        loss, logging_loss = self.loss_fn.reduce(loss_sum, valid.sum())
-        logits = None
-        if return_logits:
-            with torch.no_grad():
-                logits = ops.lm_logits(h.detach(), self.lm_head.weight)
-        return logits, loss + total_aux, logging_loss
+        return h, total_aux
 
     def _forward_cached(self, idx, past_key_values, use_cache, position_offset, last_only: bool = False):
         x = ops.embedding(idx, self.wte.weight)

@@ -130,6 +130,16 @@ def lm_head_ce_sum(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
     return (per * valid).sum()
 
 
+def lm_head_token_logprobs(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
+                           ignore_index: int = -100) -> torch.Tensor:
+    """Per-token log p(target) (fp32 [N]) of logits = h @ weight^T; ignored targets give 0.
+    On CUDA the fused LM-head + CE kernel computes it and its buffer carries the backward."""
+    if h.is_cuda:
+        return _cuda_fn().LMHeadTokenLogProbFn.apply(h, weight, targets, ignore_index)
+    logits = F.linear(h.reshape(-1, h.shape[-1]), weight).float()
+    return -F.cross_entropy(logits, targets.reshape(-1), ignore_index=ignore_index, reduction="none")
+
+
 def lm_logits(h: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     if h.is_cuda:
         return _cuda_fn().lm_logits(h, weight)

@@ -433,6 +433,38 @@ class LMHeadCrossEntropyFn(torch.autograd.Function):
         return dh, gw, None, None
 
 
+class LMHeadTokenLogProbFn(torch.autograd.Function):
+    """Per-token log-probabilities -CE(h @ W^T, targets) (fp32 [N]).
+
+    Same kernels as :class:`LMHeadCrossEntropyFn`; the upstream gradient is per row
+    instead of one scalar, so backward scales row r of the in-place (softmax - onehot)
+    buffer by -g[r] before the two GEMMs.  Backward reuses that buffer in place, so it
+    can run once per forward."""
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, ignore_index):
+        h2d = _bf16(h.reshape(-1, h.shape[-1]))
+        w16 = bf16_of(weight)
+        logits = gemm_nt(h2d, w16)
+        nll = torch.empty(h2d.shape[0], device=h.device, dtype=torch.float32)
+        C().cross_entropy_fwd(logits, targets.reshape(-1).contiguous(), nll, None, ignore_index, True)
+        ctx.save_for_backward(h2d, logits, w16)
+        ctx.weight = weight
+        ctx.h_shape = h.shape
+        ctx.h_dtype = h.dtype
+        return nll.neg_()
+
+    @staticmethod
+    def backward(ctx, g):
+        h2d, grad_logits, w16 = ctx.saved_tensors
+        grad_logits.mul_(g.detach().neg().reshape(-1, 1))  # d logp / d logits = -(softmax - onehot)
+        dh = gemm_nn(grad_logits, w16).view(ctx.h_shape)
+        if ctx.h_dtype != torch.bfloat16:
+            dh = dh.to(ctx.h_dtype)
+        (gw,) = weight_grads([ctx.weight], grad_logits, h2d)
+        return dh, gw, None, None
+
+
 def lm_logits(h: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     """Forward-only logits (bf16) for inference."""
     h2d = _bf16(h.reshape(-1, h.shape[-1]))
