@@ -51,6 +51,32 @@ def test_same_rank_source_preferred():
     assert [m.src.rank for m in q] == [0, 1] and [m.dst.rank for m in q] == [0, 1]
 
 
+def test_balanced_planner_spreads_replicated_sources():
+    """With balancing, the DP replicas of the expert shards share the sending, every
+    target region is still covered exactly once, and local copies stay preferred."""
+    from tinytron_b200.bridge.planner import group_by_rank_pair
+
+    cfg = moe_cfg()
+    src = build_tinytron_training_layout(cfg, ParallelSpec(2, 4, "training"))
+    dst = build_tinytron_inference_layout(cfg, ParallelSpec(1, 2, "inference"), shard_qkv=True)
+    plain, bal = LayoutPlanner().plan(src, dst), LayoutPlanner(balance_sources=True).plan(src, dst)
+    key = lambda m: (m.param_name, m.dst.rank, m.global_slices)  # noqa: E731
+    assert sorted(map(key, plain)) == sorted(map(key, bal))  # same pieces, possibly other sources
+
+    def busiest(plan):
+        sent = {}
+        for m in plan:
+            if m.src.rank != m.dst.rank:
+                sent[m.src.rank] = sent.get(m.src.rank, 0) + m.numel
+        return max(sent.values())
+
+    assert busiest(bal) < busiest(plain)
+    assert all(m.src.rank == m.dst.rank for m in bal if m.param_name == "blocks.0.attn.q_proj.weight")
+    pairs = group_by_rank_pair(bal)
+    assert sum(len(v) for v in pairs.values()) == len(bal)
+    assert list(pairs) == sorted(pairs)
+
+
 def test_canonical_to_inference_slices_qkv():
     cfg = moe_cfg()
     plan = LayoutPlanner().plan(build_tinytron_canonical_layout(cfg),

@@ -89,3 +89,18 @@ def test_trainer_matches_reference_loop(tmp_path, monkeypatch):
             ref.append(ll.item())
     for a, b in zip(ours, ref):
         assert abs(a - b) < 1e-4 * max(1.0, abs(b)), (ours, ref)
+
+
+def test_lm_collator_pads_to_sep_multiple_and_shifts():
+    from tinytron_b200.training.data import build_lm_collate_fn
+
+    c = build_lm_collate_fn(seq_len=8, sp_world_size=2)
+    out = c([{"input_ids": [1, 2, 3, 4, 5]}, {"input_ids": torch.tensor([7, 8, 9]), "labels": torch.tensor([8, 9, 10])}])
+    assert out["input_ids"].tolist() == [[1, 2, 3, 4], [7, 8, 9, 0]]
+    assert out["labels"].tolist() == [[2, 3, 4, 5], [8, 9, 10, -100]]
+    assert int(out["valid_token_count"]) == 7 and int(out["padded_token_count"]) == 8
+    with pytest.raises(ValueError):
+        build_lm_collate_fn(seq_len=5, sp_world_size=2)([{"input_ids": list(range(10))}])
+    import pickle
+
+    pickle.dumps(c)  # DataLoader workers can receive it

@@ -11,7 +11,7 @@ import torch.distributed as dist
 from tinytron_b200.parallel import parallel_state
 
 from .layout import LayoutIndex, Placement
-from .materializers import BridgeContext, LocalCopyRoute, P2PCopyRoute, RoutedMaterializer
+from .materializers import BridgeContext, LocalCopyRoute, RoutedMaterializer
 from .planner import LayoutPlanner
 from .rules import (EXPERT_SUFFIXES, ParallelSpec, build_tinytron_canonical_layout, build_tinytron_inference_layout,
                     build_tinytron_training_layout)
@@ -117,7 +117,8 @@ def state_dict_to_local_inference(state_dict, model_config):
 def distributed_training_state_dict_to_local_inference(state_dict, model_config, process_group=None,
                                                        use_p2p: bool = True):
     """Live reshard of every rank's training state dict into its inference shard.
-    With ``use_p2p`` each slice moves only between its source and destination ranks."""
+    With ``use_p2p`` slices move only between their source and destination ranks, one
+    packed transfer per rank pair; otherwise every slice is broadcast (reference semantics)."""
     if not (dist.is_available() and dist.is_initialized()):
         return local_training_state_dict_to_local_inference(state_dict, model_config)
     src = build_tinytron_training_layout(model_config, current_tinytron_parallel_spec("training"))
@@ -126,12 +127,18 @@ def distributed_training_state_dict_to_local_inference(state_dict, model_config,
     out: dict[str, torch.Tensor] = {}
     src_store = DistributedStateDictStore(state_dict, process_group=process_group)
     dst_store = DistributedStateDictStore(out, process_group=process_group)
-    plan = LayoutPlanner().plan(src, dst)
     rank = dist.get_rank()
+    ctx = BridgeContext(src_store=src_store, dst_store=dst_store)
+    if use_p2p:  # replicated sources share the sending (every rank plans identically)
+        plan = LayoutPlanner(balance_sources=True).plan(src, dst)  # one packed transfer per (source, destination) rank pair
+        from .materializers import PackedP2PMaterializer
+
+        PackedP2PMaterializer(rank, process_group).materialize(plan, ctx)
+        return out
+    plan = LayoutPlanner().plan(src, dst)
     from .materializers import DistributedCopyRoute
 
-    route = P2PCopyRoute(rank) if use_p2p else DistributedCopyRoute(rank)
-    RoutedMaterializer(routes=[route]).materialize(plan, BridgeContext(src_store=src_store, dst_store=dst_store))
+    RoutedMaterializer(routes=[DistributedCopyRoute(rank)]).materialize(plan, ctx)
     return out
 
 

@@ -1,8 +1,9 @@
-"""Mock dataset, LM collate and batch helpers (reference: tinytron/training/trainer.py:93-192)."""
+"""Mock dataset and the LM collate function (capabilities of the reference's
+tinytron/training/trainer.py:93-192).  ``MockDataset`` reproduces the reference's token
+stream exactly (same seeding rule per sample), so loss curves compare directly."""
 from __future__ import annotations
 
 import torch
-from torch.nn.utils.rnn import pad_sequence
 from torch.utils.data import Dataset
 
 IGNORE_INDEX = -100
@@ -35,40 +36,55 @@ class MockDataset(Dataset):
         return {"input_ids": data[:self.seq_len], "labels": data[1:self.seq_len + 1]}
 
 
-def build_lm_collate_fn(seq_len: int, sp_world_size: int, pad_token_id: int = 0, ignore_index: int = IGNORE_INDEX):
-    """Collate to [B, T]; T is padded up to a multiple of the SP size (labels padded
-    with ignore_index); items without labels are shifted by one."""
+class LMCollator:
+    """Batches variable-length LM samples into ``[B, T]`` ``input_ids`` / ``labels``.
 
-    def _1d(v) -> torch.Tensor:
-        t = v if torch.is_tensor(v) else torch.tensor(v, dtype=torch.long)
-        return t.to(torch.long).view(-1)
+    Each sample is ``{"input_ids", "labels"}`` (already shifted) or ``{"input_ids"}``
+    alone (shifted here: inputs drop the last token, labels the first), and is cut to
+    ``seq_len``.  T is the longest sample rounded up to a multiple of the SEP size, so the
+    batch splits into equal sequence chunks; it may not exceed ``seq_len``.  The output
+    rows are written into two preallocated tensors (inputs padded with ``pad_token_id``,
+    labels with ``ignore_index``) with no per-sample padding pass.  A class rather than
+    a closure so that DataLoader worker processes can pickle it.  Output keys and
+    padding rules follow the reference collate (tinytron/training/trainer.py:145-192)."""
 
-    def collate(batch):
-        xs, ys = [], []
-        for item in batch:
-            if "labels" in item:
-                x, y = _1d(item["input_ids"]), _1d(item["labels"])
-            else:
-                tok = _1d(item["input_ids"])
-                x, y = tok[:-1], tok[1:]
-            n = min(x.numel(), y.numel(), seq_len)
-            xs.append(x[:n])
-            ys.append(y[:n])
-        max_len = max((x.numel() for x in xs), default=0)
-        if max_len == 0:
-            raise ValueError("Encountered an empty language-modeling batch.")
-        target = min(max_len, seq_len)
-        if target % sp_world_size:
-            target += sp_world_size - target % sp_world_size
-        if target > seq_len:
-            raise ValueError(f"Batch max sequence length {max_len} cannot be padded to sep_size={sp_world_size} "
-                             f"within seq_len={seq_len}.")
-        x = pad_sequence([t[:target] for t in xs], batch_first=True, padding_value=pad_token_id)
-        y = pad_sequence([t[:target] for t in ys], batch_first=True, padding_value=ignore_index)
-        if x.size(1) < target:
-            x = torch.nn.functional.pad(x, (0, target - x.size(1)), value=pad_token_id)
-            y = torch.nn.functional.pad(y, (0, target - y.size(1)), value=ignore_index)
-        return {"input_ids": x, "labels": y, "valid_token_count": (y != ignore_index).sum(),
+    def __init__(self, seq_len: int, sp_world_size: int, pad_token_id: int = 0, ignore_index: int = IGNORE_INDEX):
+        self.seq_len = int(seq_len)
+        self.sp = max(1, int(sp_world_size))
+        self.pad_token_id = int(pad_token_id)
+        self.ignore_index = int(ignore_index)
+
+    @staticmethod
+    def _tokens(v) -> torch.Tensor:
+        return (v if torch.is_tensor(v) else torch.as_tensor(v)).reshape(-1).long()
+
+    def _pair(self, item) -> tuple[torch.Tensor, torch.Tensor]:
+        ids = self._tokens(item["input_ids"])
+        if "labels" in item:
+            x, y = ids, self._tokens(item["labels"])
+        else:
+            x, y = ids[:-1], ids[1:]
+        n = min(x.numel(), y.numel(), self.seq_len)
+        return x[:n], y[:n]
+
+    def __call__(self, batch):
+        pairs = [self._pair(item) for item in batch]
+        longest = max((x.numel() for x, _ in pairs), default=0)
+        if longest == 0:
+            raise ValueError("cannot collate a batch whose samples are all empty")
+        width = -(-longest // self.sp) * self.sp  # round up to a multiple of the SEP size
+        if width > self.seq_len:
+            raise ValueError(f"the longest sample ({longest} tokens) rounds up to {width} for sep_size={self.sp}, "
+                             f"more than seq_len={self.seq_len}")
+        x = torch.full((len(pairs), width), self.pad_token_id, dtype=torch.long)
+        y = torch.full((len(pairs), width), self.ignore_index, dtype=torch.long)
+        for row, (a, b) in enumerate(pairs):
+            x[row, :a.numel()] = a
+            y[row, :b.numel()] = b
+        return {"input_ids": x, "labels": y, "valid_token_count": (y != self.ignore_index).sum(),
                 "padded_token_count": torch.tensor(x.numel(), dtype=torch.long)}
 
-    return collate
+
+def build_lm_collate_fn(seq_len: int, sp_world_size: int, pad_token_id: int = 0, ignore_index: int = IGNORE_INDEX):
+    """The trainer's collate function (an :class:`LMCollator`)."""
+    return LMCollator(seq_len, sp_world_size, pad_token_id, ignore_index)
