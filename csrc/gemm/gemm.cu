@@ -42,8 +42,13 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int NUM_THREADS = 192;
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_DSWIGLU = 4 };
-enum Group : int { GROUP_NONE = 0, GROUP_M = 1, GROUP_K = 2 };
+// EPI_AXPBY: bf16 out = alpha * acc + beta * aux (a bf16 [M, N] addend), the fused
+// "a*X + B@X" / "b*A + c*A@A" steps of the Newton-Schulz iteration.
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_DSWIGLU = 4, EPI_AXPBY = 5 };
+// GROUP_SYM: the output is symmetric (C = X X^T, or A A^T with A symmetric); only the
+// 128x128 tiles on or above the diagonal are computed, and each off-diagonal tile is
+// also stored transposed into its mirror position.
+enum Group : int { GROUP_NONE = 0, GROUP_M = 1, GROUP_K = 2, GROUP_SYM = 3 };
 
 struct Params {
   int M, N, K;                 // output rows, output cols, reduction length
@@ -54,6 +59,7 @@ struct Params {
   __nv_bfloat16* aux_out;      // SWIGLU: optional g|u store [M, 2N]; DSWIGLU: d(g|u) [M, 2N]
   int ld_aux_out;
   float alpha;
+  float beta;                  // EPI_AXPBY: weight of the addend `aux`
   const float* alpha_ptr;      // optional device scalar multiplied into alpha
   int b_row_offset2;           // SWIGLU: first row of the "up" half inside B
   int* status;                 // device status word for bounded waits
@@ -103,7 +109,15 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, int num_m, int num_n, 
   t.grp = 0;
   t.kb0 = 0;
   t.nk = num_k;
-  if constexpr (GROUP == GROUP_K) {
+  if constexpr (GROUP == GROUP_SYM) {  // row-major walk over the upper triangle (num_m == num_n)
+    int mb = 0, rem = tile;
+    while (rem >= num_m - mb) {
+      rem -= num_m - mb;
+      ++mb;
+    }
+    t.mb = mb;
+    t.nb = mb + rem;
+  } else if constexpr (GROUP == GROUP_K) {
     const int per = num_m * num_n;
     t.grp = tile / per;
     tile_coords(tile - t.grp * per, num_m, num_n, t.mb, t.nb);
@@ -174,8 +188,11 @@ __device__ __forceinline__ void load_bf16(const __nv_bfloat16* src, float (&v)[N
 template <int BN, int EPI>
 // [c_lo, c_hi): the slice of output columns of the tile this thread handles (the CTA-pair
 // kernel splits a row between two epilogue warpgroups); defaults cover the whole tile.
+// `mirror` (GROUP_SYM, off-diagonal tiles): every stored value (row, col) is also stored
+// at (col, row); lanes hold consecutive rows, so each mirrored column is one 64-byte
+// warp-wide store.
 __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, int nb, int row, bool row_ok,
-                                             float alpha, int c_lo = 0, int c_hi = 1 << 30) {
+                                             float alpha, int c_lo = 0, int c_hi = 1 << 30, bool mirror = false) {
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   c_hi = min(c_hi, OUT_BN);
   if constexpr (EPI == EPI_F32_ACC) {
@@ -215,9 +232,9 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
         }
       }
     }
-  } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
+  } else if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_AXPBY) {
     __nv_bfloat16* brow = nullptr;
-    if constexpr (EPI == EPI_BF16) {
+    if constexpr (EPI == EPI_BF16 || EPI == EPI_AXPBY) {
       if (p.row_ptr != nullptr) {
         const long long a = row_ok ? p.row_ptr[row] : 0ll;
         brow = reinterpret_cast<__nv_bfloat16*>(a);
@@ -237,8 +254,20 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
         float v[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]) * alpha;
-        if constexpr (EPI == EPI_BF16) {
+        if constexpr (EPI == EPI_AXPBY) {
+          float av[32];
+          load_bf16<32>(p.aux + static_cast<size_t>(row) * p.ld_aux + col0, av, nv);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fmaf(p.beta, av[i], v[i]);
+        }
+        if constexpr (EPI == EPI_BF16 || EPI == EPI_AXPBY) {
           store_bf16<32>(brow + col0, v, nv);
+          if (mirror) {
+            __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (i < nv) cb[static_cast<size_t>(col0 + i) * p.ldc + row] = __float2bfloat16_rn(v[i]);
+          }
         } else {
           float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
           if (nv == 32) {
@@ -392,7 +421,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int M = (GROUP == GROUP_M) ? __ldg(p.grp_off + p.n_groups) : p.M;
   const int num_m = (M + BM - 1) / BM;
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
-  const int num_tiles = num_m * num_n * (GROUP == GROUP_K ? p.n_groups : 1);
+  const int num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2
+                                             : num_m * num_n * (GROUP == GROUP_K ? p.n_groups : 1);
   const int num_k = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -538,7 +568,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       const int row = (GROUP == GROUP_K) ? t.grp * p.c_grp_rows + row_local : row_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
 
-      epilogue_row<BN, EPI>(p, t_row, nb, row, row_ok, alpha);
+      epilogue_row<BN, EPI>(p, t_row, nb, row, row_ok, alpha, 0, 1 << 30, GROUP == GROUP_SYM && t.mb != t.nb);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) {
@@ -598,6 +628,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   constexpr uint32_t IDESC = idesc_bf16_f32(256, BN2, A_MN, B_MN);
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
   static_assert(EPI != EPI_SWIGLU || !B_MN, "SwiGLU epilogue needs K-major B");
+  static_assert(GROUP != GROUP_SYM, "symmetric (upper-triangle) tiles run on the single-CTA kernel");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_ptr(smem_raw, 1024);
@@ -845,8 +876,10 @@ void launch_cfg(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, i
   TT_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   // GROUP_M: p.M is the row capacity (an upper bound of the device-side total).
-  const long num_tiles = static_cast<long>((p.M + BM - 1) / BM) * ((p.N + OUT_BN - 1) / OUT_BN) *
-                         (GROUP == GROUP_K ? p.n_groups : 1);
+  const long num_m = (p.M + BM - 1) / BM;
+  const long num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2
+                                              : num_m * ((p.N + OUT_BN - 1) / OUT_BN) *
+                                                    (GROUP == GROUP_K ? p.n_groups : 1);
   const int grid = static_cast<int>(std::max(1L, std::min(num_tiles, static_cast<long>(num_sms(device)))));
   kern<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
@@ -1066,6 +1099,62 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
     dispatch<EPI_F32_ACC>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
   else
     dispatch<EPI_F32>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
+}
+
+// Newton-Schulz building block (Muon): C = alpha * A op(B)^T + beta * addend, bf16 out.
+//   a: [M, K] K-major; b: [N, K] (K-major) or [K, N] (b_mn); addend (optional): bf16 [M, N].
+//   symmetric: the product is known to be symmetric (B == A giving A A^T, or A symmetric
+//   giving A A = A A^T): only the 128x128 tiles on or above the diagonal are computed and
+//   each is mirrored, which halves the work of X X^T and of A^2.  The addend must then be
+//   symmetric as well (it is A itself in b*A + c*A^2).
+void gemm_axpby_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool b_mn, double alpha,
+                   c10::optional<torch::Tensor> addend, double beta, bool symmetric) {
+  using namespace gemm;
+  check_cuda_bf16(a, "a");
+  check_cuda_bf16(b, "b");
+  check_cuda_bf16(c, "c");
+  TT_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_axpby expects 2-D tensors");
+  const int M = static_cast<int>(a.size(0)), K = static_cast<int>(a.size(1));
+  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0));
+  TT_CHECK(K == static_cast<int>(b_mn ? b.size(0) : b.size(1)), "gemm_axpby: reduction dims differ");
+  TT_CHECK(c.size(0) == M && c.size(1) == N && c.stride(1) == 1 && c.stride(0) % 8 == 0 &&
+               reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
+           "gemm_axpby: output must be [M, N] with 16-byte aligned rows");
+  TT_CHECK(!symmetric || (M == N && !b_mn), "gemm_axpby: a symmetric product needs M == N and K-major B");
+  if (M == 0 || N == 0) return;
+  const c10::cuda::CUDAGuard guard(a.device());
+  const int device = a.get_device();
+  Params p = base_params(M, N, K, c, alpha, c10::nullopt, device);
+  p.beta = static_cast<float>(beta);
+  if (addend.has_value()) {
+    check_cuda_bf16(*addend, "addend");
+    TT_CHECK(addend->dim() == 2 && addend->size(0) == M && addend->size(1) == N && addend->stride(1) == 1 &&
+                 addend->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(addend->data_ptr()) % 16 == 0,
+             "gemm_axpby: addend must be bf16 [M, N] with 16-byte aligned rows");
+    p.aux = reinterpret_cast<const __nv_bfloat16*>(addend->data_ptr());
+    p.ld_aux = static_cast<int>(addend->stride(0));
+  }
+  cudaStream_t st = cur_stream();
+  const CUtensorMap ta = operand_map(a, false, BM);
+  if (symmetric) {
+    const CUtensorMap tb = operand_map(b, false, 128);
+    if (addend.has_value())
+      launch_cfg<128, 6, false, false, EPI_AXPBY, GROUP_SYM>(p, ta, tb, device, st);
+    else
+      launch_cfg<128, 6, false, false, EPI_BF16, GROUP_SYM>(p, ta, tb, device, st);
+    return;
+  }
+  TT_CHECK(addend.has_value(), "gemm_axpby: a plain product goes through gemm()");
+  if (use_pair(M, N, BN2, device)) {
+    const CUtensorMap tb = operand_map(b, b_mn, 128);
+    if (b_mn) launch_pair<false, true, EPI_AXPBY>(p, ta, tb, device, st);
+    else launch_pair<false, false, EPI_AXPBY>(p, ta, tb, device, st);
+    return;
+  }
+  const int bn = choose_bn(M, N, device);
+  const CUtensorMap tb = operand_map(b, b_mn, bn);
+  if (b_mn) launch_bn<false, true, EPI_AXPBY>(bn, p, ta, tb, device, st);
+  else launch_bn<false, false, EPI_AXPBY>(bn, p, ta, tb, device, st);
 }
 
 void gemm_set_pair_mode(int64_t mode) { gemm::g_pair_mode.store(static_cast<int>(mode)); }

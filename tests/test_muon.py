@@ -64,3 +64,136 @@ def test_newton_schulz_tcgen05_matches_fp32(shape):
         X = X.mT
     err = ((out.double() - X).norm() / X.norm()).item()
     assert out.shape == G.shape and err < 3e-2, err
+
+
+# ----------------------------------------------------------------------------- fused NS GEMMs
+@pytest.mark.gpu
+@pytest.mark.parametrize("r,n", [(256, 2048), (384, 1024), (2048, 2048), (200, 520)])
+def test_gemm_axpby_symmetric_and_fused_epilogue(r, n):
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(r + n)
+    X = (torch.randn(r, n, device="cuda", generator=g) / n ** 0.5).bfloat16()
+    A = torch.empty(r, r, device="cuda", dtype=torch.bfloat16)
+    C.gemm_axpby(X, X, A, False, 1.0, None, 0.0, True)  # symmetric X X^T
+    Xf = X.float()
+    ref_A = Xf @ Xf.t()
+    B = torch.empty_like(A)
+    C.gemm_axpby(A, A, B, False, 2.0315, A, -4.775, True)  # c A^2 + b A
+    Af = A.float()
+    ref_B = 2.0315 * Af @ Af + -4.775 * Af
+    out = torch.empty_like(X)
+    C.gemm_axpby(B, X, out, True, 1.0, X, 3.4445, False)  # B X + a X
+    ref_out = B.float() @ Xf + 3.4445 * Xf
+    torch.cuda.synchronize()
+    check_status()
+    rel = lambda a, b: ((a.float() - b).norm() / b.norm()).item()  # noqa: E731
+    assert rel(A, ref_A) < 1e-2 and torch.equal(A, A.t())
+    assert rel(B, ref_B) < 1e-2 and torch.equal(B, B.t())
+    assert rel(out, ref_out) < 1e-2
+
+
+# ----------------------------------------------------------------------------- ZeRO-1 Muon
+def _dist_muon_worker(rank, world, out_dir):
+    import os
+
+    import torch.distributed as dist
+
+    from tinytron_b200.models import GPT, ModelConfig
+    from tinytron_b200.optim import Muon
+    from tinytron_b200.optim.muon import DistributedMuon
+    from tinytron_b200.parallel.buffers import FlatParams
+
+    cfg = ModelConfig(block_size=32, vocab_size=64, num_layer=2, num_attention_heads=4, num_key_value_heads=2,
+                      hidden_size=32, intermediate_size=48, init_std=0.02, seed=5)
+
+    def build():
+        m = GPT(cfg, device="cpu")
+        flat = FlatParams(m, with_bf16=False)
+        mat = [p for n, p in m.named_parameters() if p.ndim == 2 and "wte" not in n and "lm_head" not in n]
+        rest = [p for n, p in m.named_parameters() if not any(p is q for q in mat)]
+        opt = Muon([{"params": mat, "use_muon": True, "lr": 0.02, "momentum": 0.95, "weight_decay": 0.1},
+                    {"params": rest, "use_muon": False, "use_adam": True, "lr": 1e-3, "weight_decay": 0.1}])
+        return m, flat, opt
+
+    m, flat, opt = build()
+    dopt = DistributedMuon(opt, flat, dense_group=dist.group.WORLD)
+    owned = sum(len(g["params"]) for g in opt.param_groups)
+    single_m, single_flat, single_opt = build()
+    gen = torch.Generator().manual_seed(0)
+    for step in range(3):
+        grad = torch.randn(flat.numel, generator=gen)
+        for f in (flat, single_flat):
+            f.grad.copy_(grad)
+            f.expose_grads()
+        coef = torch.tensor(0.5)
+        dopt.step(grad_scale=coef)
+        single_opt.step(grad_scale=coef)
+    torch.save({"diff": (flat.data - single_flat.data).abs().max().item(), "owned": owned,
+                "total": sum(len(g["params"]) for g in single_opt.param_groups)},
+               os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_distributed_muon_matches_single_rank(tmp_path):
+    import os
+
+    from test_parallel_cpu import spawn
+
+    spawn(_dist_muon_worker, 2, str(tmp_path))
+    r0, r1 = (torch.load(os.path.join(tmp_path, f"r{i}.pt")) for i in range(2))
+    assert r0["diff"] < 1e-6 and r1["diff"] < 1e-6, (r0, r1)
+    assert 0 < r0["owned"] < r0["total"] and r0["owned"] + r1["owned"] == r0["total"]
+
+
+def test_trainer_with_muon_runs_cpu(tmp_path, monkeypatch):
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR"):
+        monkeypatch.delenv(k, raising=False)
+    from tinytron_b200.training import build_config, parse_args
+    from tinytron_b200.training.trainer import Trainer
+
+    argv = ["--use_mock_data", "--deterministic", "--mock_data_num_samples", "8", "--log_dir", str(tmp_path),
+            "--total_batch_size", str(4 * 32), "--batch_size", "4", "--seq_len", "32", "--max_steps", "6",
+            "--warmup_steps", "1", "--max_lr", "2e-2", "--min_lr", "2e-3", "--optimizer", "muon",
+            "--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--vocab_size", "128", "--block_size", "32", "--backend", "gloo"]
+    tr = Trainer(build_config(parse_args(argv)))
+    tr.train()
+    losses = [tr.results[s]["loss"].item() for s in sorted(tr.results)]
+    assert all(torch.isfinite(torch.tensor(losses))) and losses[-1] < losses[0], losses
+
+
+def _muon_trainer_rank(rank, world, port, tmp, out):
+    import os
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    from tinytron_b200.training import build_config, parse_args
+    from tinytron_b200.training.trainer import Trainer
+
+    argv = ["--use_mock_data", "--deterministic", "--mock_data_num_samples", "8", "--log_dir", tmp,
+            "--total_batch_size", str(4 * 32), "--batch_size", "4", "--seq_len", "32", "--max_steps", "4",
+            "--warmup_steps", "1", "--max_lr", "2e-2", "--min_lr", "2e-3", "--optimizer", "muon", "--sep_size", "2",
+            "--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--vocab_size", "128", "--block_size", "32", "--backend", "gloo"]
+    tr = Trainer(build_config(parse_args(argv)))
+    for s in range(3):
+        tr.train_step(s)
+    torch.save({"data": tr.flat.data.clone(), "loss": float(tr.one_step_results["loss"])},
+               os.path.join(out, f"r{rank}.pt"))
+    tr.close()
+
+
+def test_trainer_with_distributed_muon_sep2_gloo(tmp_path):
+    """SEP=2: each matrix is orthogonalised by one of the two ranks and broadcast; both
+    ranks end with identical dense parameters."""
+    import os
+
+    import torch.multiprocessing as mp
+    from test_rl_trainer import _port
+
+    mp.spawn(_muon_trainer_rank, args=(2, _port(), str(tmp_path / "logs"), str(tmp_path)), nprocs=2, join=True)
+    r0, r1 = (torch.load(os.path.join(tmp_path, f"r{i}.pt")) for i in range(2))
+    assert torch.equal(r0["data"], r1["data"])
+    assert abs(r0["loss"] - r1["loss"]) < 1e-6

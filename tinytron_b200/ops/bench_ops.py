@@ -1,8 +1,9 @@
 """Kernel microbenchmarks: ``python -m tinytron_b200.ops.bench_ops <what> [--json]``.
 
 ``gemm`` and ``attn`` sweep the training shapes against cuBLAS / torch SDPA; the fixed
-kernel cases (``zero1``, ``ep``, ``decode``, ``attn_bwd_b4``, ``dswiglu``, ``moe_decode``)
-time one workload each (``--iters``/``--warmup``).
+kernel cases (``zero1``, ``ep``, ``decode``, ``attn_bwd_b4``, ``dswiglu``, ``moe_decode``,
+``muon`` and its cuBLAS/eager baseline ``muon_torch``) time one workload each
+(``--iters``/``--warmup``).
 
 Each measurement is CUDA-event timed on the launching stream, after warm-up,
 with L2 flushed (a 256 MiB buffer write) before every timed launch.  Results are
@@ -289,8 +290,53 @@ def _case_moe_decode(N: int = 32, E: int = 64, k: int = 8, H: int = 2048, I: int
     return run, check_status
 
 
+def _case_muon(layers: int = 16, H: int = 2048, kv: int = 256, I: int = 5504):
+    """One Muon step over the matrices of the long-context preset (16 layers, d2048,
+    2 kv heads, SwiGLU 5504) on one GPU: momentum, tcgen05 Newton-Schulz (symmetric
+    tiles, fused axpby epilogues, side streams for the k/v matrices), update."""
+    from tinytron_b200.optim import Muon
+
+    shapes = [(H, H), (kv, H), (kv, H), (H, H), (I, H), (I, H), (H, I)] * layers
+    g = torch.Generator(device="cuda").manual_seed(0)
+    params = [torch.nn.Parameter(torch.randn(s, device="cuda", generator=g) * 0.02) for s in shapes]
+    for p in params:
+        p.grad = torch.randn(p.shape, device="cuda", generator=g)
+    opt = Muon([{"params": params, "use_muon": True, "lr": 0.02, "momentum": 0.95, "weight_decay": 0.1}])
+    return (lambda: opt.step()), (lambda: None)
+
+
+def _case_muon_torch(layers: int = 16, H: int = 2048, kv: int = 256, I: int = 5504):
+    """The same Muon step written with torch bf16 matmuls (cuBLAS) and eager elementwise
+    ops, one matrix after another: the library baseline for ``muon``."""
+    a, b, c = 3.4445, -4.7750, 2.0315
+    shapes = [(H, H), (kv, H), (kv, H), (H, H), (I, H), (I, H), (H, I)] * layers
+    g = torch.Generator(device="cuda").manual_seed(0)
+    params = [torch.randn(s, device="cuda", generator=g) * 0.02 for s in shapes]
+    grads = [torch.randn(s, device="cuda", generator=g) for s in shapes]
+    moms = [torch.zeros(s, device="cuda") for s in shapes]
+
+    def run():
+        for p, gr, m in zip(params, grads, moms):
+            m.lerp_(gr, 0.05)
+            u = gr.lerp(m, 0.95)
+            X = u.bfloat16()
+            tall = X.size(0) > X.size(1)
+            if tall:
+                X = X.mT
+            X = X / (X.norm() + 1e-7)
+            for _ in range(5):
+                A = X @ X.mT
+                X = a * X + (b * A + c * A @ A) @ X
+            if tall:
+                X = X.mT
+            p.mul_(1 - 0.02 * 0.1).add_(X.float(), alpha=-0.02 * max(1.0, p.size(0) / p.size(1)) ** 0.5)
+
+    return run, (lambda: None)
+
+
 KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
-                "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode}
+                "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "muon": _case_muon,
+                "muon_torch": _case_muon_torch}
 
 
 def bench_case(name: str, iters: int, warmup: int) -> list[dict]:

@@ -92,7 +92,7 @@ class RLTrainer(Trainer):
         else:
             for g in self.optimizer.param_groups:
                 g["lr"] = lr
-            self.optimizer.step()
+            self.optimizer.step(grad_scale=coef)
             for p in self.flat.params:
                 p.grad = None
             if self.device.type == "cuda":

@@ -201,8 +201,12 @@ class Trainer:
              "betas": (o.adam_beta1, o.adam_beta2), "eps": o.adam_eps, "weight_decay": o.weight_decay},
         ]
         opt = Muon(groups)
-        if config.parallel.use_distributed_optimizer and self.dp_group is not None:
-            self.optimizer = DistributedOptimizer(opt, process_group=self.dp_group)
+        if config.parallel.use_distributed_optimizer and self.dp_sp_world_size > 1:
+            # ZeRO-1 over each tensor's replica group: dense matrices over DP x SEP, expert
+            # matrices over DP; one Newton-Schulz per matrix in the whole job
+            from tinytron_b200.optim.muon import DistributedMuon
+
+            self.optimizer = DistributedMuon(opt, self.flat, dense_group=self.dp_sp_group, expert_group=self.dp_group)
             self.raw_optimizer = self.optimizer.optimizer
         else:
             self.optimizer = opt
@@ -313,7 +317,9 @@ class Trainer:
                 opt.reduce_gradients()
             norm, coef = opt.grad_norm_and_coef(max_norm)
             return norm, coef
-        # Muon path: reference ordering (SP sum, DP average, clip on full grads)
+        # Muon path: SP sum of the dense grads, DP average, then the global norm from two
+        # flat sums of squares (expert part summed over EP); the clip coefficient is
+        # applied by the optimizer to the gradients it uses (on their owners).
         g = self.flat.grad
         if self.sp_world_size > 1:
             dist.all_reduce(g[:self.flat.dense_numel], op=dist.ReduceOp.SUM, group=self.sp_group)
@@ -321,7 +327,27 @@ class Trainer:
             g.div_(self.dp_world_size)
             dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.dp_group)
         self.flat.expose_grads()
-        return self.raw_model.clip_grad_norm(max_norm), None
+        return self._flat_clip_coef(max_norm)
+
+    def _flat_clip_coef(self, max_norm: float):
+        """(global grad norm, clip coefficient) as device scalars, after the gradient sync."""
+        g, split = self.flat.grad, self.flat.dense_numel
+        sq = torch.zeros(2, device=g.device, dtype=torch.float32)
+        if g.is_cuda:
+            from tinytron_b200.ops import _ext
+
+            C = _ext.load()
+            scratch = torch.empty(4096, device=g.device)
+            C.sumsq(g[:split], sq[0:1], scratch, False)
+            C.sumsq(g[split:], sq[1:2], scratch, False)
+        else:
+            sq[0] = g[:split].double().pow(2).sum().float()
+            sq[1] = g[split:].double().pow(2).sum().float()
+        if self.sp_world_size > 1 and split < self.flat.numel:
+            dist.all_reduce(sq[1:2], op=dist.ReduceOp.SUM, group=self.sp_group)
+        norm = sq.sum().sqrt()
+        coef = torch.clamp(max_norm / (norm + 1e-6), max=1.0)
+        return norm, coef
 
     def _one_training_step(self, config: Config, step: int):
         self.model.train()
@@ -342,7 +368,7 @@ class Trainer:
         else:
             for g in self.optimizer.param_groups:
                 g["lr"] = lr
-            self.optimizer.step()
+            self.optimizer.step(grad_scale=coef)
             for p in self.flat.params:
                 p.grad = None
             self.flat.refresh_bf16() if self.device.type == "cuda" else None
