@@ -5,7 +5,7 @@ namespace tt {
 void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool b_mn, bool accumulate, double alpha,
              c10::optional<torch::Tensor> alpha_t, int64_t bn);
 void gemm_axpby_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool b_mn, double alpha,
-                   c10::optional<torch::Tensor> addend, double beta, bool symmetric);
+                   c10::optional<torch::Tensor> addend, double beta, bool symmetric, int64_t batch);
 void gemm_set_pair_mode(int64_t mode);
 int64_t gemm_pair_mode();
 void gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, c10::optional<torch::Tensor> gu_out);
@@ -108,7 +108,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha_t") = py::none(), py::arg("bn") = 0);
   m.def("gemm_axpby", &tt::gemm_axpby_op, "C = alpha * A op(B)^T + beta * addend (bf16); symmetric: upper tiles mirrored",
         py::arg("a"), py::arg("b"), py::arg("c"), py::arg("b_mn") = false, py::arg("alpha") = 1.0,
-        py::arg("addend") = py::none(), py::arg("beta") = 0.0, py::arg("symmetric") = false);
+        py::arg("addend") = py::none(), py::arg("beta") = 0.0, py::arg("symmetric") = false,
+        py::arg("batch") = 1);
   m.def("gemm_set_pair_mode", &tt::gemm_set_pair_mode, "CTA-pair GEMM: 0 never, 1 when faster, 2 always");
   m.def("gemm_pair_mode", &tt::gemm_pair_mode);
   m.def("moe_gemm", &tt::moe_gemm_op, "grouped GEMM over expert row segments (bf16 out)", py::arg("a"),

@@ -47,8 +47,14 @@ constexpr int NUM_THREADS = 192;
 enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_F32_ACC = 2, EPI_SWIGLU = 3, EPI_DSWIGLU = 4, EPI_AXPBY = 5 };
 // GROUP_SYM: the output is symmetric (C = X X^T, or A A^T with A symmetric); only the
 // 128x128 tiles on or above the diagonal are computed, and each off-diagonal tile is
-// also stored transposed into its mirror position.
-enum Group : int { GROUP_NONE = 0, GROUP_M = 1, GROUP_K = 2, GROUP_SYM = 3 };
+// also stored transposed into its mirror position.  GROUP_SYM and GROUP_BATCH run
+// n_groups independent products of one shape stacked along the rows (batch g reads A
+// rows from g * a_grp_rows, B rows / K coordinates from g * b_grp_rows, and writes C and
+// reads the addend at rows g * c_grp_rows): one launch for a whole set of matrices.
+enum Group : int { GROUP_NONE = 0, GROUP_M = 1, GROUP_K = 2, GROUP_SYM = 3, GROUP_BATCH = 4 };
+
+template <int GROUP>
+constexpr bool kBatched = (GROUP == GROUP_SYM || GROUP == GROUP_BATCH);
 
 struct Params {
   int M, N, K;                 // output rows, output cols, reduction length
@@ -69,7 +75,8 @@ struct Params {
   int b_grp_rows;              // GROUP_M: per-group offset of B rows (K-major) or K coordinate (MN-major)
   int b_split_kb;              // GROUP_M, MN-major B: k-blocks >= this come from rows b_off2 + ...
   int b_off2;
-  int c_grp_rows;              // GROUP_K: per-group row offset of C
+  int c_grp_rows;              // GROUP_K, batched modes: per-group row offset of C (and of the addend)
+  int a_grp_rows;              // batched modes: per-group row offset of A
   // CTA-pair kernel, fp32-accumulate epilogue only: the reduction is split into split_k
   // ranges whose epilogues add into C one after another (split s waits until the 16
   // epilogue warps of split s-1 counted themselves in splitk_flags[tile]), so the sum
@@ -110,13 +117,19 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, int num_m, int num_n, 
   t.kb0 = 0;
   t.nk = num_k;
   if constexpr (GROUP == GROUP_SYM) {  // row-major walk over the upper triangle (num_m == num_n)
-    int mb = 0, rem = tile;
+    const int per = num_m * (num_m + 1) / 2;
+    t.grp = tile / per;
+    int mb = 0, rem = tile - t.grp * per;
     while (rem >= num_m - mb) {
       rem -= num_m - mb;
       ++mb;
     }
     t.mb = mb;
     t.nb = mb + rem;
+  } else if constexpr (GROUP == GROUP_BATCH) {
+    const int per = num_m * num_n;
+    t.grp = tile / per;
+    tile_coords(tile - t.grp * per, num_m, num_n, t.mb, t.nb);
   } else if constexpr (GROUP == GROUP_K) {
     const int per = num_m * num_n;
     t.grp = tile / per;
@@ -191,8 +204,10 @@ template <int BN, int EPI>
 // `mirror` (GROUP_SYM, off-diagonal tiles): every stored value (row, col) is also stored
 // at (col, row); lanes hold consecutive rows, so each mirrored column is one 64-byte
 // warp-wide store.
+// (the mirrored store of batch g goes to rows mirror_row0 + col, column mirror_col).
 __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, int nb, int row, bool row_ok,
-                                             float alpha, int c_lo = 0, int c_hi = 1 << 30, bool mirror = false) {
+                                             float alpha, int c_lo = 0, int c_hi = 1 << 30, bool mirror = false,
+                                             int mirror_row0 = 0, int mirror_col = 0) {
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   c_hi = min(c_hi, OUT_BN);
   if constexpr (EPI == EPI_F32_ACC) {
@@ -266,7 +281,8 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
             __nv_bfloat16* cb = reinterpret_cast<__nv_bfloat16*>(p.C);
 #pragma unroll
             for (int i = 0; i < 32; ++i)
-              if (i < nv) cb[static_cast<size_t>(col0 + i) * p.ldc + row] = __float2bfloat16_rn(v[i]);
+              if (i < nv)
+                cb[static_cast<size_t>(mirror_row0 + col0 + i) * p.ldc + mirror_col] = __float2bfloat16_rn(v[i]);
           }
         } else {
           float* dst = reinterpret_cast<float*>(p.C) + static_cast<size_t>(row) * p.ldc + col0;
@@ -421,8 +437,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
   const int M = (GROUP == GROUP_M) ? __ldg(p.grp_off + p.n_groups) : p.M;
   const int num_m = (M + BM - 1) / BM;
   const int num_n = (p.N + OUT_BN - 1) / OUT_BN;
-  const int num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2
-                                             : num_m * num_n * (GROUP == GROUP_K ? p.n_groups : 1);
+  const int num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2 * p.n_groups
+                                             : num_m * num_n * ((GROUP == GROUP_K || GROUP == GROUP_BATCH) ? p.n_groups : 1);
   const int num_k = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -459,7 +475,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
         const TileInfo t = decode_tile<GROUP>(tile, num_m, num_n, num_k, p);
         const int mb = t.mb, nb = t.nb;
-        const int b_rows0 = (GROUP == GROUP_M) ? t.grp * p.b_grp_rows : 0;
+        const int b_rows0 = (GROUP == GROUP_M || kBatched<GROUP>) ? t.grp * p.b_grp_rows : 0;
+        const int a_rows0 = kBatched<GROUP> ? t.grp * p.a_grp_rows : 0;
         for (int kb = 0; kb < t.nk; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, kTimeoutEmpty)) {
             ok = false;
@@ -470,7 +487,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
           uint8_t* b_dst = sB + stage * B_BYTES;
           const int kc = (t.kb0 + kb) * BK;  // k coordinate (token row for GROUP_K)
           if constexpr (!A_MN) {
-            tma_load_2d(a_dst, &tmA, &full[stage], kc, mb * BM);
+            tma_load_2d(a_dst, &tmA, &full[stage], kc, a_rows0 + mb * BM);
           } else {
 #pragma unroll
             for (int c = 0; c < BM / 64; ++c)
@@ -485,6 +502,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
             int kb_b = kc;
             if constexpr (GROUP == GROUP_M)
               kb_b = (kb < p.b_split_kb) ? b_rows0 + kb * BK : p.b_off2 + b_rows0 + (kb - p.b_split_kb) * BK;
+            if constexpr (kBatched<GROUP>) kb_b = b_rows0 + kc;
 #pragma unroll
             for (int c = 0; c < BN / 64; ++c)
               tma_load_2d(b_dst + c * (BK * 128), &tmB, &full[stage], nb * BN + c * 64, kb_b);
@@ -565,10 +583,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
       tc_fence_after();
       const int row_local = t.mb * BM + row_in_tile;
       const bool row_ok = row_local < M;
-      const int row = (GROUP == GROUP_K) ? t.grp * p.c_grp_rows + row_local : row_local;
+      const int row = (GROUP == GROUP_K || kBatched<GROUP>) ? t.grp * p.c_grp_rows + row_local : row_local;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
 
-      epilogue_row<BN, EPI>(p, t_row, nb, row, row_ok, alpha, 0, 1 << 30, GROUP == GROUP_SYM && t.mb != t.nb);
+      epilogue_row<BN, EPI>(p, t_row, nb, row, row_ok, alpha, 0, 1 << 30, GROUP == GROUP_SYM && t.mb != t.nb,
+                            t.grp * p.c_grp_rows, row_local);
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
       if (++acc == 2) {
@@ -628,7 +647,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PAIR_THREADS, 1)
   constexpr uint32_t IDESC = idesc_bf16_f32(256, BN2, A_MN, B_MN);
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN2 / 2 : BN2;
   static_assert(EPI != EPI_SWIGLU || !B_MN, "SwiGLU epilogue needs K-major B");
-  static_assert(GROUP != GROUP_SYM, "symmetric (upper-triangle) tiles run on the single-CTA kernel");
+  static_assert(!kBatched<GROUP>, "batched and symmetric products run on the single-CTA kernel");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_ptr(smem_raw, 1024);
@@ -877,9 +896,9 @@ void launch_cfg(const Params& p, const CUtensorMap& ta, const CUtensorMap& tb, i
   constexpr int OUT_BN = (EPI == EPI_SWIGLU) ? BN / 2 : BN;
   // GROUP_M: p.M is the row capacity (an upper bound of the device-side total).
   const long num_m = (p.M + BM - 1) / BM;
-  const long num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2
+  const long num_tiles = (GROUP == GROUP_SYM) ? num_m * (num_m + 1) / 2 * p.n_groups
                                               : num_m * ((p.N + OUT_BN - 1) / OUT_BN) *
-                                                    (GROUP == GROUP_K ? p.n_groups : 1);
+                                                    ((GROUP == GROUP_K || GROUP == GROUP_BATCH) ? p.n_groups : 1);
   const int grid = static_cast<int>(std::max(1L, std::min(num_tiles, static_cast<long>(num_sms(device)))));
   kern<<<grid, NUM_THREADS, smem, st>>>(ta, tb, p);
   TT_CUDA_CHECK(cudaGetLastError());
@@ -1101,36 +1120,44 @@ void gemm_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool a_mn, bool 
     dispatch<EPI_F32>(a_mn, b_mn, use_bn, p, ta, tb, device, st);
 }
 
-// Newton-Schulz building block (Muon): C = alpha * A op(B)^T + beta * addend, bf16 out.
-//   a: [M, K] K-major; b: [N, K] (K-major) or [K, N] (b_mn); addend (optional): bf16 [M, N].
-//   symmetric: the product is known to be symmetric (B == A giving A A^T, or A symmetric
+// Newton-Schulz building block (Muon): C = alpha * A op(B)^T + beta * addend, bf16 out,
+// for `batch` independent products of one shape stacked along the rows:
+//   a: [batch * M, K] K-major;  b: [batch * N, K] (K-major) or [batch * K, N] (b_mn);
+//   c and addend (optional): bf16 [batch * M, N].
+//   symmetric: each product is known to be symmetric (B == A giving A A^T, or A symmetric
 //   giving A A = A A^T): only the 128x128 tiles on or above the diagonal are computed and
 //   each is mirrored, which halves the work of X X^T and of A^2.  The addend must then be
 //   symmetric as well (it is A itself in b*A + c*A^2).
 void gemm_axpby_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool b_mn, double alpha,
-                   c10::optional<torch::Tensor> addend, double beta, bool symmetric) {
+                   c10::optional<torch::Tensor> addend, double beta, bool symmetric, int64_t batch) {
   using namespace gemm;
   check_cuda_bf16(a, "a");
   check_cuda_bf16(b, "b");
   check_cuda_bf16(c, "c");
   TT_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm_axpby expects 2-D tensors");
-  const int M = static_cast<int>(a.size(0)), K = static_cast<int>(a.size(1));
-  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0));
-  TT_CHECK(K == static_cast<int>(b_mn ? b.size(0) : b.size(1)), "gemm_axpby: reduction dims differ");
-  TT_CHECK(c.size(0) == M && c.size(1) == N && c.stride(1) == 1 && c.stride(0) % 8 == 0 &&
+  TT_CHECK(batch >= 1 && a.size(0) % batch == 0 && b.size(0) % batch == 0 && c.size(0) % batch == 0,
+           "gemm_axpby: row counts must be divisible by the batch");
+  const int M = static_cast<int>(a.size(0) / batch), K = static_cast<int>(a.size(1));
+  const int N = static_cast<int>(b_mn ? b.size(1) : b.size(0) / batch);
+  TT_CHECK(K == static_cast<int>(b_mn ? b.size(0) / batch : b.size(1)), "gemm_axpby: reduction dims differ");
+  TT_CHECK(c.size(0) == batch * M && c.size(1) == N && c.stride(1) == 1 && c.stride(0) % 8 == 0 &&
                reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0,
-           "gemm_axpby: output must be [M, N] with 16-byte aligned rows");
+           "gemm_axpby: output must be [batch * M, N] with 16-byte aligned rows");
   TT_CHECK(!symmetric || (M == N && !b_mn), "gemm_axpby: a symmetric product needs M == N and K-major B");
   if (M == 0 || N == 0) return;
   const c10::cuda::CUDAGuard guard(a.device());
   const int device = a.get_device();
   Params p = base_params(M, N, K, c, alpha, c10::nullopt, device);
   p.beta = static_cast<float>(beta);
+  p.n_groups = static_cast<int>(batch);
+  p.a_grp_rows = M;
+  p.b_grp_rows = b_mn ? K : N;
+  p.c_grp_rows = M;
   if (addend.has_value()) {
     check_cuda_bf16(*addend, "addend");
-    TT_CHECK(addend->dim() == 2 && addend->size(0) == M && addend->size(1) == N && addend->stride(1) == 1 &&
+    TT_CHECK(addend->dim() == 2 && addend->size(0) == batch * M && addend->size(1) == N && addend->stride(1) == 1 &&
                  addend->stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(addend->data_ptr()) % 16 == 0,
-             "gemm_axpby: addend must be bf16 [M, N] with 16-byte aligned rows");
+             "gemm_axpby: addend must be bf16 [batch * M, N] with 16-byte aligned rows");
     p.aux = reinterpret_cast<const __nv_bfloat16*>(addend->data_ptr());
     p.ld_aux = static_cast<int>(addend->stride(0));
   }
@@ -1145,7 +1172,7 @@ void gemm_axpby_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool b_mn,
     return;
   }
   TT_CHECK(addend.has_value(), "gemm_axpby: a plain product goes through gemm()");
-  if (use_pair(M, N, BN2, device)) {
+  if (batch == 1 && use_pair(M, N, BN2, device)) {
     const CUtensorMap tb = operand_map(b, b_mn, 128);
     if (b_mn) launch_pair<false, true, EPI_AXPBY>(p, ta, tb, device, st);
     else launch_pair<false, false, EPI_AXPBY>(p, ta, tb, device, st);
@@ -1153,8 +1180,8 @@ void gemm_axpby_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, bool b_mn,
   }
   const int bn = choose_bn(M, N, device);
   const CUtensorMap tb = operand_map(b, b_mn, bn);
-  if (b_mn) launch_bn<false, true, EPI_AXPBY>(bn, p, ta, tb, device, st);
-  else launch_bn<false, false, EPI_AXPBY>(bn, p, ta, tb, device, st);
+  if (b_mn) launch_bn<false, true, EPI_AXPBY, GROUP_BATCH>(bn, p, ta, tb, device, st);
+  else launch_bn<false, false, EPI_AXPBY, GROUP_BATCH>(bn, p, ta, tb, device, st);
 }
 
 void gemm_set_pair_mode(int64_t mode) { gemm::g_pair_mode.store(static_cast<int>(mode)); }

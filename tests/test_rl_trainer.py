@@ -12,15 +12,14 @@ import torch.multiprocessing as mp
 from tinytron_b200.training import build_config, parse_args
 
 
-def _cfg(tmp_path, steps=2, sep=1, world=1, extra=()):
-    # prompts of 7 tokens + 9 generated tokens -> 15 trained positions per sequence ... use
-    # seq_len 8 and 9 new tokens so that prompt_len + max_new_tokens - 1 = 16 splits over SEP=2
+def _cfg(tmp_path, steps=2, sep=1, world=1, extra=(), hidden=64):
+    # seq_len 8 and 9 new tokens: prompt_len + max_new_tokens - 1 = 16 splits over SEP=2
     argv = ["--use_mock_data", "--deterministic", "--mock_data_num_samples", "16", "--log_dir", str(tmp_path),
             "--total_batch_size", str(2 * 8 * 2 * (world // sep)), "--batch_size", "2", "--seq_len", "8",
             "--max_steps", str(steps + 1), "--warmup_steps", "1", "--max_lr", "1e-3", "--min_lr", "1e-4",
-            "--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
-            "--intermediate_size", "96", "--vocab_size", "128", "--block_size", "64", "--init_std", "0.02",
-            "--backend", "gloo", "--sep_size", str(sep), *extra]
+            "--num_layer", "2", "--hidden_size", str(hidden), "--num_attention_heads", "4",
+            "--num_key_value_heads", "2", "--intermediate_size", "256", "--vocab_size", "128", "--block_size", "64",
+            "--init_std", "0.02", "--backend", "gloo", "--sep_size", str(sep), *extra]
     return build_config(parse_args(argv))
 
 
@@ -132,7 +131,7 @@ def test_grpo_trainer_two_steps_gpu(tmp_path, monkeypatch):
     from tinytron_b200.ops import _ext, check_status
 
     _ext.load()
-    res, moved = _run_grpo(_cfg(tmp_path, extra=["--backend", "nccl"]), steps=2)
+    res, moved = _run_grpo(_cfg(tmp_path, extra=["--backend", "nccl"], hidden=256), steps=2)  # head_dim 64
     check_status()
     for r in res:
         for k in ("loss", "reward", "grad_norm"):

@@ -15,9 +15,11 @@ B200 design:
     3. X' = B X + a X          with the "+ a X" fused into the epilogue.
   Against three plain GEMMs plus two elementwise passes this halves the FLOPs of the
   two r x r products and removes every separate elementwise pass over A and X.
-* Small matrices (fewer than 1024 rows after transposing, e.g. GQA k/v projections)
-  cannot fill 148 SMs with 128x128 tiles; their iterations run on a few side streams
-  so several of them share the GPU.
+* Matrices of one shape are orthogonalised together: their normalised updates are
+  stacked along the rows and every GEMM of an iteration is ONE batched launch over the
+  whole stack (e.g. all 48 [2048 x 5504] MLP matrices of a 16-layer model), which fills
+  the 148 SMs even for small matrices (GQA k/v projections: 2 x 2 tiles each) and
+  replaces thousands of per-matrix launches by a few dozen.
 * ``DistributedMuon`` (ZeRO-1): each matrix is orthogonalised by exactly one rank of
   its replica group — every rank of DP x SEP for the dense parameters (they are
   identical there after the gradient sync), every DP rank for expert parameters —
@@ -34,8 +36,6 @@ import torch
 import torch.distributed as dist
 
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
-_SIDE_STREAM_ROWS = 1024  # matrices with fewer rows (after transposing) share side streams
-_N_SIDE_STREAMS = 4
 
 
 # ----------------------------------------------------------------------------- Newton-Schulz
@@ -44,27 +44,30 @@ def _kernel_ok(X: torch.Tensor) -> bool:
 
 
 class _NSWorkspace:
-    """bf16 buffers of one matrix shape: A, B [r, r] and the ping-pong X [r, n]."""
+    """bf16 buffers for ``batch`` matrices of one shape [r, n] (r <= n), stacked along the
+    rows: A, B [batch * r, r] and the ping-pong X [batch * r, n]."""
 
-    def __init__(self, r: int, n: int, device):
-        self.A = torch.empty(r, r, device=device, dtype=torch.bfloat16)
-        self.B = torch.empty(r, r, device=device, dtype=torch.bfloat16)
-        self.X = [torch.empty(r, n, device=device, dtype=torch.bfloat16) for _ in range(2)]
+    def __init__(self, r: int, n: int, device, batch: int = 1):
+        self.r, self.n, self.batch = r, n, batch
+        self.A = torch.empty(batch * r, r, device=device, dtype=torch.bfloat16)
+        self.B = torch.empty(batch * r, r, device=device, dtype=torch.bfloat16)
+        self.X = [torch.empty(batch * r, n, device=device, dtype=torch.bfloat16) for _ in range(2)]
 
 
 def _ns_tcgen05(X0: torch.Tensor, steps: int, ws: _NSWorkspace) -> torch.Tensor:
-    """``steps`` iterations on the tcgen05 GEMM; X0: bf16 [r, n] (r <= n), already
-    normalised.  Returns a workspace buffer holding the result."""
+    """``steps`` iterations on the tcgen05 GEMM for ``ws.batch`` stacked matrices;
+    X0: bf16 [batch * r, n] (r <= n), each matrix already normalised.  Three launches
+    per iteration for the whole stack.  Returns a workspace buffer holding the result."""
     from tinytron_b200.ops import _ext
 
     C = _ext.load()
     a, b, c = NS_COEFFS
     src = X0
     for i in range(steps):
-        dst = ws.X[i % 2]
-        C.gemm_axpby(src, src, ws.A, False, 1.0, None, 0.0, True)   # A = X X^T
-        C.gemm_axpby(ws.A, ws.A, ws.B, False, c, ws.A, b, True)      # B = c A^2 + b A
-        C.gemm_axpby(ws.B, src, dst, True, 1.0, src, a, False)       # X' = B X + a X
+        dst = ws.X[i % 2] if src is not ws.X[i % 2] else ws.X[(i + 1) % 2]
+        C.gemm_axpby(src, src, ws.A, False, 1.0, None, 0.0, True, ws.batch)   # A = X X^T
+        C.gemm_axpby(ws.A, ws.A, ws.B, False, c, ws.A, b, True, ws.batch)      # B = c A^2 + b A
+        C.gemm_axpby(ws.B, src, dst, True, 1.0, src, a, False, ws.batch)       # X' = B X + a X
         src = dst
     return src
 
@@ -80,7 +83,8 @@ def _ns_torch(X: torch.Tensor, steps: int) -> torch.Tensor:
 def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, workspace: _NSWorkspace | None = None) -> torch.Tensor:
     """Approximately orthogonalise G (the nearest semi-orthogonal matrix U V^T of its SVD,
     up to the iteration's tolerance) in bf16: Frobenius-normalise, iterate on the wide
-    orientation (rows <= cols), transpose back.  Leading dims are batch dims."""
+    orientation (rows <= cols), transpose back.  Leading dims are batch dims.  With a
+    ``workspace`` the result may live in one of its buffers."""
     if G.dim() < 2:
         raise ValueError("Newton-Schulz needs a matrix (or a batch of matrices)")
     tall = G.size(-2) > G.size(-1)
@@ -90,7 +94,7 @@ def zeropower_via_newtonschulz5(G: torch.Tensor, steps: int, workspace: _NSWorks
     X = X / (X.norm(dim=(-2, -1), keepdim=True) + 1e-7)
     if _kernel_ok(X):
         r, n = X.shape
-        ws = workspace if workspace is not None else _NSWorkspace(r, n, X.device)
+        ws = workspace if workspace is not None and workspace.batch == 1 else _NSWorkspace(r, n, X.device)
         X = _ns_tcgen05(X.contiguous(), steps, ws)
     else:
         X = _ns_torch(X, steps)
@@ -154,15 +158,6 @@ class Muon(torch.optim.Optimizer):
             groups.append(g)
         super().__init__(groups, {})
         self._workspaces: dict[tuple, _NSWorkspace] = {}
-        self._streams: list = []
-
-    def _workspace(self, shape, device, lane: int):
-        rows, cols = shape
-        r, n = (cols, rows) if rows > cols else (rows, cols)
-        key = (r, n, str(device), lane)
-        if key not in self._workspaces:
-            self._workspaces[key] = _NSWorkspace(r, n, device)
-        return self._workspaces[key]
 
     @torch.no_grad()
     def step(self, closure=None, grad_scale: torch.Tensor | None = None):
@@ -195,35 +190,53 @@ class Muon(torch.optim.Optimizer):
         p.mul_(1 - group["lr"] * group["weight_decay"])
         p.add_(upd, alpha=-group["lr"])
 
-    def _muon_one(self, p, group, lane: int):
+    def _momentum(self, p):
         st = self.state[p]
         if not st:
             st["momentum_buffer"] = torch.zeros_like(p)
-        ws = self._workspace(tuple(p.view(p.size(0), -1).shape), p.device, lane) if p.is_cuda and p.dim() >= 2 \
-            else None
-        upd = muon_update(p.grad, st["momentum_buffer"], beta=group["momentum"], workspace=ws)
+        return st["momentum_buffer"]
+
+    def _muon_one(self, p, group):
+        upd = muon_update(p.grad, self._momentum(p), beta=group["momentum"])
         p.mul_(1 - group["lr"] * group["weight_decay"])
         p.add_(upd.reshape(p.shape), alpha=-group["lr"])
 
     def _muon_steps(self, matrices):
-        small = [(p, g) for p, g in matrices
-                 if p.is_cuda and p.dim() >= 2 and min(p.size(0), p[0].numel()) < _SIDE_STREAM_ROWS]
-        big = [(p, g) for p, g in matrices if not any(p is q for q, _ in small)]
-        for p, g in big:
-            self._muon_one(p, g, 0)
-        if not small:
-            return
-        main = torch.cuda.current_stream(small[0][0].device)
-        if not self._streams:
-            self._streams = [torch.cuda.Stream(device=small[0][0].device) for _ in range(_N_SIDE_STREAMS)]
-        for s in self._streams:
-            s.wait_stream(main)
-        for i, (p, g) in enumerate(small):
-            lane = i % _N_SIDE_STREAMS
-            with torch.cuda.stream(self._streams[lane]):
-                self._muon_one(p, g, 1 + lane)
-        for s in self._streams:
-            main.wait_stream(s)
+        """Matrices of one shape and group are updated together: multi-tensor momentum
+        and Nesterov ops, one stacked bf16 buffer, three batched GEMM launches per
+        Newton-Schulz iteration for the whole bucket, multi-tensor weight decay + update."""
+        buckets: dict[tuple, list] = {}
+        for p, g in matrices:
+            if p.is_cuda and p.dim() == 2 and p.size(0) % 8 == 0 and p.size(1) % 8 == 0:
+                buckets.setdefault((tuple(p.shape), id(g)), []).append((p, g))
+            else:
+                self._muon_one(p, g)
+        for (shape, _), items in buckets.items():
+            self._muon_bucket(shape, [p for p, _ in items], items[0][1])
+
+    def _muon_bucket(self, shape, params, group):
+        rows, cols = shape
+        tall = rows > cols
+        r, n = (cols, rows) if tall else (rows, cols)
+        nb = len(params)
+        key = (r, n, nb, str(params[0].device))
+        ws = self._workspaces.get(key)
+        if ws is None:
+            ws = self._workspaces[key] = _NSWorkspace(r, n, params[0].device, nb)
+        grads = [p.grad for p in params]
+        moms = [self._momentum(p) for p in params]
+        beta = group["momentum"]
+        torch._foreach_lerp_(moms, grads, 1 - beta)   # momentum EMA
+        torch._foreach_lerp_(grads, moms, beta)       # Nesterov direction (in place, as muon_update)
+        X0 = ws.X[0].view(nb, r, n)
+        for i, g in enumerate(grads):                 # bf16 [r, n] (wide orientation)
+            X0[i].copy_(g.mT if tall else g)
+        norms = X0.view(nb, -1).norm(dim=-1)          # Frobenius norm of each bf16 matrix
+        X0.div_((norms + 1e-7).view(nb, 1, 1))
+        out = _ns_tcgen05(ws.X[0], 5, ws).view(nb, r, n)
+        scale = _scale_for_shape(rows, cols)
+        torch._foreach_mul_(params, 1 - group["lr"] * group["weight_decay"])
+        torch._foreach_add_(params, [o.mT if tall else o for o in out.unbind(0)], alpha=-group["lr"] * scale)
 
 
 # ----------------------------------------------------------------------------- ZeRO-1
