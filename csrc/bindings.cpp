@@ -24,7 +24,7 @@ void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::T
                    int64_t align);
 void moe_gather_rows_op(torch::Tensor x, torch::Tensor row_pair, torch::Tensor grp_off, int64_t k, torch::Tensor out);
 void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k,
-                    torch::Tensor out);
+                    torch::Tensor out, c10::optional<torch::Tensor> row_limit);
 void moe_combine_bwd_op(torch::Tensor dout, torch::Tensor y_rows, torch::Tensor row_pair, torch::Tensor w,
                         torch::Tensor grp_off, int64_t k, torch::Tensor dy_rows, torch::Tensor dw);
 void moe_gemm_wgrad_op(torch::Tensor a, torch::Tensor b, torch::Tensor c, torch::Tensor grp_off, int64_t n_groups,
@@ -97,6 +97,9 @@ void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset,
 void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, int64_t lo, int64_t hi);
 void comm_all_to_all(int64_t gid, int64_t slot_offset, torch::Tensor out);
 int64_t comm_epoch(int64_t gid);
+void comm_replay_publish(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor in);
+void comm_replay_reduce(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor out,
+                        c10::optional<torch::Tensor> residual, int64_t root);
 void comm_destroy(int64_t gid);
 }  // namespace comm
 }  // namespace tt
@@ -131,8 +134,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_layout", &tt::moe_layout_op, "expert segments (128- or 256-row aligned, stable) for the grouped GEMMs",
         py::arg("sel"), py::arg("E"), py::arg("grp_off"), py::arg("slot"), py::arg("row_pair"), py::arg("align") = 128);
   m.def("moe_gather_rows", &tt::moe_gather_rows_op, "x_rows[r] = x[token of row r], zero pad rows");
-  m.def("moe_combine", &tt::moe_combine_op, "out[t] = sum_j w[t,j] y_rows[slot[t,j]]", py::arg("y_rows"),
-        py::arg("slot"), py::arg("w"), py::arg("k"), py::arg("out"));
+  m.def("moe_combine", &tt::moe_combine_op, "out[t] = sum_j w[t,j] y_rows[slot[t,j]] (slots below row_limit)",
+        py::arg("y_rows"), py::arg("slot"), py::arg("w"), py::arg("k"), py::arg("out"),
+        py::arg("row_limit") = py::none());
   m.def("moe_combine_bwd", &tt::moe_combine_bwd_op, "backward of moe_combine (dy_rows, dw)");
   m.def("gemm_swiglu", &tt::gemm_swiglu_op, "silu(x Wg^T) * (x Wu^T) with fused gate|up weight", py::arg("x"),
         py::arg("w_gu"), py::arg("out"), py::arg("gu_out") = py::none());
@@ -189,6 +193,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gid"), py::arg("signal") = true);
   m.def("comm_all_reduce", &tt::comm::comm_all_reduce, "one-shot all-reduce of a heap region (+ residual)",
         py::arg("gid"), py::arg("in_offset"), py::arg("out"), py::arg("residual") = py::none());
+  m.def("comm_replay_publish", &tt::comm::comm_replay_publish,
+        "graph-safe collective, step 1: copy the input into this rank's slot and signal (device epoch)");
+  m.def("comm_replay_reduce", &tt::comm::comm_replay_reduce,
+        "graph-safe collective, step 2: wait, sum the ranks' slots (root >= 0: copy the root's) (+ residual)",
+        py::arg("gid"), py::arg("slot_offset"), py::arg("slot_bytes"), py::arg("out"), py::arg("residual") = py::none(),
+        py::arg("root") = -1);
   m.def("comm_reduce_scatter_sumsq", &tt::comm::comm_reduce_scatter_sumsq,
         "ZeRO-1 fp32 gradient reduce-scatter in place + published sums of squares");
   m.def("comm_adamw_allgather", &tt::comm::comm_adamw_allgather,

@@ -195,20 +195,34 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, int ld_x
 }
 
 // One block per token, 8 bf16 per thread per step.
+// row_limit (optional, device): pairs whose row is at or past *row_limit are skipped (the
+// pairs routed to experts on other ranks in expert-parallel inference, whose rows the
+// grouped GEMMs never computed); a token with no remaining pair gets zeros.
 __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y_rows, const int* __restrict__ slot,
                                const float* __restrict__ w, int k, int H, __nv_bfloat16* __restrict__ out,
-                               int ld_out) {
+                               int ld_out, const int* __restrict__ row_limit) {
   const int t = blockIdx.x;
   __shared__ int s_slot[kMaxExperts];
   __shared__ float s_w[kMaxExperts];
-  for (int j = threadIdx.x; j < k; j += blockDim.x) {
-    s_slot[j] = slot[static_cast<size_t>(t) * k + j];
-    s_w[j] = w ? w[static_cast<size_t>(t) * k + j] : 1.0f;
+  __shared__ int s_k;
+  if (threadIdx.x == 0) {  // compact the pairs this rank computed, keeping their order
+    const int lim = row_limit ? *row_limit : 0x7fffffff;
+    int kk = 0;
+    for (int j = 0; j < k; ++j) {
+      const int sl = slot[static_cast<size_t>(t) * k + j];
+      if (sl < lim) {
+        s_slot[kk] = sl;
+        s_w[kk] = w ? w[static_cast<size_t>(t) * k + j] : 1.0f;
+        ++kk;
+      }
+    }
+    s_k = kk;
   }
   __syncthreads();
+  const int kk = s_k;
   for (int v = threadIdx.x; v < H / 8; v += blockDim.x) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    for (int j = 0; j < k; ++j) {
+    for (int j = 0; j < kk; ++j) {
       const uint4 q = reinterpret_cast<const uint4*>(y_rows + static_cast<size_t>(s_slot[j]) * H)[v];
       const float wj = s_w[j];
       const uint32_t u[4] = {q.x, q.y, q.z, q.w};
@@ -351,7 +365,7 @@ void moe_gather_rows_op(torch::Tensor x, torch::Tensor row_pair, torch::Tensor g
 }
 
 void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k,
-                    torch::Tensor out) {
+                    torch::Tensor out, c10::optional<torch::Tensor> row_limit) {
   check_cuda_bf16(y_rows, "y_rows");
   check_cuda_bf16(out, "out");
   const int H = static_cast<int>(y_rows.size(1));
@@ -359,12 +373,16 @@ void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torc
   TT_CHECK(k >= 1 && k <= moe::kMaxExperts && H % 8 == 0 && y_rows.is_contiguous() && out.size(1) == H &&
                out.stride(1) == 1 && out.stride(0) % 8 == 0 && slot.numel() == N * k, "combine: bad shapes");
   if (w.has_value()) TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == N * k, "combine: w fp32 [N, k]");
+  if (row_limit.has_value())
+    TT_CHECK(row_limit->is_cuda() && row_limit->scalar_type() == torch::kInt32 && row_limit->numel() >= 1,
+             "combine: row_limit int32 device scalar");
   if (N == 0) return;
   const c10::cuda::CUDAGuard guard(out.device());
   moe::combine_kernel<<<static_cast<unsigned>(N), std::min(256, std::max(32, H / 8)), 0, cur_stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(y_rows.data_ptr()), slot.data_ptr<int>(),
       w.has_value() ? w->data_ptr<float>() : nullptr, static_cast<int>(k), H,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), static_cast<int>(out.stride(0)));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), static_cast<int>(out.stride(0)),
+      row_limit.has_value() ? row_limit->data_ptr<int>() : nullptr);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -256,6 +256,72 @@ __global__ void shadow_refresh_kernel(PeerTable t, size_t data_off, __nv_bfloat1
   }
 }
 
+// ------------------------------------------------------------------ replayable all-reduce
+// Graph-capturable all-reduce / broadcast (SEP inference: row-parallel partial sums, and
+// the decode step is one CUDA graph).  Two kernels per call:
+//   publish:  e = dev_epoch + 1; copy `in` into this rank's slot (e & 1); the last block
+//             signals e to every peer.
+//   reduce:   e = dev_epoch + 1; wait for every peer's e; out = sum over ranks (or the
+//             root's slot only) in rank order (+ residual); the last block stores
+//             dev_epoch = e.
+// Slots alternate with the epoch's parity: a rank rewrites slot (e & 1) at call e + 2 only
+// after its reduce of call e + 1 saw every peer's publish of e + 1, which each peer issued
+// after finishing its reduce of call e (stream order), i.e. after reading that slot.
+__device__ __forceinline__ uint64_t dev_epoch_next(const PeerTable& t) {
+  return *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) + 1;
+}
+
+__global__ void replay_publish_kernel(PeerTable t, size_t slot_off, long long slot_bytes, const char* __restrict__ in,
+                                      long long bytes) {
+  const uint64_t e = dev_epoch_next(t);
+  char* dst = t.base[t.rank] + slot_off + static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes);
+  const long long nv = bytes / 16;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(in)[i];
+  grid_last_block(t, [&]() { signal_peers(t, e); });
+}
+
+template <typename T>
+__global__ void replay_reduce_kernel(PeerTable t, size_t slot_off, long long slot_bytes, T* __restrict__ out,
+                                     const T* __restrict__ residual, long long n, int root, int* status,
+                                     uint64_t timeout_ns) {
+  const uint64_t e = dev_epoch_next(t);
+  const size_t off = slot_off + static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes);
+  bool ok = block_wait_peers(t, e, status, timeout_ns);
+  if (ok) {
+    constexpr int V = 16 / sizeof(T);
+    const long long nv = n / V;
+    const int p0 = root >= 0 ? root : 0, p1 = root >= 0 ? root + 1 : t.world;
+    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < nv; i += stride) {
+      float acc[V];
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k] = 0.f;
+      for (int p = p0; p < p1; ++p) {
+        const uint4 q = reinterpret_cast<const uint4*>(t.base[p] + off)[i];
+        const T* qv = reinterpret_cast<const T*>(&q);
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] += static_cast<float>(qv[k]);
+      }
+      if (residual != nullptr) {
+        const uint4 r = reinterpret_cast<const uint4*>(residual)[i];
+        const T* rv = reinterpret_cast<const T*>(&r);
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k] += static_cast<float>(rv[k]);
+      }
+      uint4 o;
+      T* ov = reinterpret_cast<T*>(&o);
+#pragma unroll
+      for (int k = 0; k < V; ++k) ov[k] = static_cast<T>(acc[k]);
+      reinterpret_cast<uint4*>(out)[i] = o;
+    }
+  }
+  // Advance the epoch even after a timeout (the status word is set and the host raises),
+  // so every rank's epoch keeps counting calls.
+  grid_last_block(t, [&]() { *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) = e; });
+}
+
 // ------------------------------------------------------------------ host side
 struct Group {
   int device = -1;
@@ -551,6 +617,61 @@ void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, in
   shadow_refresh_kernel<<<grid, threads, 0, cur_stream()>>>(
       table(g), static_cast<size_t>(data_offset), reinterpret_cast<__nv_bfloat16*>(p16.data_ptr()), lo, hi, n,
       g.emulated ? 0ull : g.epoch, device_status_ptr(g.device), timeout_ns());
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// Replayable (CUDA-graph safe) all-reduce of `in` over the group: out = sum over ranks
+// (root < 0) or out = root's `in` (root >= 0, a broadcast), plus `residual` if given.
+// The two slots of slot_bytes each at slot_offset hold the published inputs.  bf16 or
+// fp32, numel * element size a multiple of 16 bytes.  Emulated groups must be launched
+// rank by rank with every rank's publish before any reduce (replay_publish/reduce below).
+static void check_replay_args(const Group& g, int64_t slot_offset, int64_t slot_bytes, const torch::Tensor& x) {
+  const long long bytes = x.numel() * static_cast<long long>(x.element_size());
+  TT_CHECK(x.is_cuda() && x.is_contiguous() && reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0 && bytes % 16 == 0,
+           "comm_replay: tensors must be contiguous, 16-byte aligned, a multiple of 16 bytes");
+  TT_CHECK(x.scalar_type() == torch::kBFloat16 || x.scalar_type() == torch::kFloat32, "comm_replay: bf16 or fp32");
+  TT_CHECK(bytes <= slot_bytes && slot_offset % 256 == 0 && slot_bytes % 256 == 0 &&
+               slot_offset >= static_cast<int64_t>(kUserOff) &&
+               slot_offset + 2 * slot_bytes <= static_cast<int64_t>(g.bytes),
+           "comm_replay: slots outside the heap or too small");
+}
+
+void comm_replay_publish(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor in) {
+  Group& g = get(gid);
+  check_replay_args(g, slot_offset, slot_bytes, in);
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
+  const long long bytes = in.numel() * static_cast<long long>(in.element_size());
+  const int grid = std::min(grid_for(g.device, std::max<long long>(1, bytes / 16), 256), num_sms(g.device));
+  replay_publish_kernel<<<grid, 256, 0, cur_stream()>>>(table(g), static_cast<size_t>(slot_offset), slot_bytes,
+                                                        static_cast<const char*>(in.data_ptr()), bytes);
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+void comm_replay_reduce(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor out,
+                        c10::optional<torch::Tensor> residual, int64_t root) {
+  Group& g = get(gid);
+  check_replay_args(g, slot_offset, slot_bytes, out);
+  TT_CHECK(root < g.world, "comm_replay: root out of range");
+  const void* res = nullptr;
+  if (residual.has_value()) {
+    TT_CHECK(residual->scalar_type() == out.scalar_type() && residual->numel() == out.numel() &&
+                 residual->is_contiguous() && reinterpret_cast<uintptr_t>(residual->data_ptr()) % 16 == 0,
+             "comm_replay: residual must match out");
+    res = residual->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
+  const long long n = out.numel();
+  const int grid = std::min(grid_for(g.device, std::max<long long>(1, n / 8), 256), num_sms(g.device));
+  const PeerTable t = table(g);
+  int* st = device_status_ptr(g.device);
+  if (out.scalar_type() == torch::kBFloat16)
+    replay_reduce_kernel<__nv_bfloat16><<<grid, 256, 0, cur_stream()>>>(
+        t, static_cast<size_t>(slot_offset), slot_bytes, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+        reinterpret_cast<const __nv_bfloat16*>(res), n, static_cast<int>(root), st, timeout_ns());
+  else
+    replay_reduce_kernel<float><<<grid, 256, 0, cur_stream()>>>(
+        t, static_cast<size_t>(slot_offset), slot_bytes, out.data_ptr<float>(), reinterpret_cast<const float*>(res), n,
+        static_cast<int>(root), st, timeout_ns());
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

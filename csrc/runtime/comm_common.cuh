@@ -16,6 +16,11 @@ constexpr int kPadFloats = 64;
 constexpr size_t kCounterOff = 4096;
 constexpr size_t kPartialOff = 8192;
 constexpr int kMaxBlocks = 512;  // kPartialOff + kMaxBlocks * 4 floats fits below the user region
+// Device-side epoch of the replayable collectives (local use only).  Kernels read it at
+// their start and the last block of a collective's final kernel advances it, so a
+// collective captured in a CUDA graph synchronises correctly on every replay (a host
+// epoch baked into the graph would not).
+constexpr size_t kDevEpochOff = 16384;
 constexpr size_t kUserOff = 65536;
 
 struct PeerTable {

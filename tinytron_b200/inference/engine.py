@@ -7,7 +7,11 @@ Differences that matter for speed:
   * the EOS stop test is evaluated on the device and read back every
     ``eos_check_interval`` steps; the returned sequences are cut at the exact step
     where every sequence had produced EOS, so the output equals the per-step check;
-  * with SEP > 1, SEP rank 0 samples and broadcasts the tokens (as the reference);
+  * with SEP > 1 every rank samples by itself and no token is broadcast: the row-parallel
+    all-reduces sum in the same rank order on every rank, so all ranks hold bit-identical
+    logits, and the sampler's seeds come from a CPU generator whose seed SEP rank 0 sends
+    once per ``generate`` call, so every rank draws the same tokens (the reference lets
+    SEP rank 0 sample and broadcasts every step's tokens);
   * on CUDA with the paged (or contiguous) cache, pages for the whole generation are
     mapped up front and one decode step (embedding -> every layer's fused RoPE/append
     + split-KV attention -> LM head) is captured in a CUDA graph and replayed, so a
@@ -52,12 +56,17 @@ class InferenceEngine:
         self._graph = None
 
     def _graph_ok(self) -> bool:
-        """A decode step is capturable when no layer synchronises with the host: the MoE
-        head-parallel inference path (SEP > 1) selects tokens with nonzero()."""
+        """A decode step is capturable when nothing in it synchronises with the host.  With
+        SEP > 1 that needs the row-parallel all-reduces on the symmetric heap (their epochs
+        live on the device); the MoE local-expert path is device-only."""
         if not self.use_cuda_graph:
             return False
-        sep = parallel_state.get_sep_world_size() if dist.is_initialized() else 1
-        return not (self.model_config.use_moe and sep > 1)
+        sep = self._sep()
+        if sep is None:
+            return True
+        from tinytron_b200.parallel.symm import row_parallel_heap_enabled
+
+        return row_parallel_heap_enabled(sep[0])
 
     def _enable_heap_all_reduce(self, B: int, T: int) -> None:
         sep = self._sep()
@@ -91,29 +100,27 @@ class InferenceEngine:
             return None
         return g, parallel_state.get_sep_rank(), parallel_state.get_sep_global_rank(0)
 
-    def _sample_next_token_synced(self, logits, temperature=1.0, top_k=None, top_p=None):
+    def _sampling_generator(self):
+        """CPU generator for the sampler's seeds.  Without SEP: None (torch's global RNG, as
+        before).  With SEP: one seed drawn by SEP rank 0 and sent once per generate call, so
+        every rank's draws are identical (one small collective per call, none per step)."""
         sep = self._sep()
         if sep is None:
-            return sample_next_token(logits, temperature=temperature, top_k=top_k, top_p=top_p)
+            return None
         g, r, src = sep
-        tok = sample_next_token(logits, temperature, top_k, top_p) if r == 0 else \
-            torch.empty(logits.size(0), dtype=torch.long, device=logits.device)
-        dist.broadcast(tok, src=src, group=g)
-        return tok
+        seed = torch.randint(0, 2 ** 62, (1,), dtype=torch.long)
+        dev = self.device if dist.get_backend(g) == "nccl" else torch.device("cpu")
+        seed = seed.to(dev)
+        dist.broadcast(seed, src=src, group=g)
+        return torch.Generator().manual_seed(int(seed.item()))
 
-    def _sample_next_token_with_log_prob_synced(self, logits, temperature=1.0, top_k=None, top_p=None):
-        sep = self._sep()
-        if sep is None:
-            return sample_next_token_with_log_prob(logits, temperature=temperature, top_k=top_k, top_p=top_p)
-        g, r, src = sep
-        if r == 0:
-            tok, lp = sample_next_token_with_log_prob(logits, temperature, top_k, top_p)
-        else:
-            tok = torch.empty(logits.size(0), dtype=torch.long, device=logits.device)
-            lp = torch.empty(logits.size(0), dtype=torch.float32, device=logits.device)
-        dist.broadcast(tok, src=src, group=g)
-        dist.broadcast(lp, src=src, group=g)
-        return tok, lp
+    def _sample_next_token_synced(self, logits, temperature=1.0, top_k=None, top_p=None, generator=None):
+        return sample_next_token(logits, temperature=temperature, top_k=top_k, top_p=top_p, generator=generator)
+
+    def _sample_next_token_with_log_prob_synced(self, logits, temperature=1.0, top_k=None, top_p=None,
+                                                generator=None):
+        return sample_next_token_with_log_prob(logits, temperature=temperature, top_k=top_k, top_p=top_p,
+                                               generator=generator)
 
     def new_cache(self, batch_size: int, max_seq_len: int | None = None):
         if self.use_paged_kv_cache:
@@ -141,6 +148,7 @@ class InferenceEngine:
             cache.reserve(total)
             self._enable_heap_all_reduce(B, P)
         graph = None
+        gen = self._sampling_generator()
         sync = torch.cuda.synchronize if cuda else (lambda *a: None)
         logp_steps = []
         finished = torch.zeros(B, dtype=torch.bool, device=self.device)
@@ -161,10 +169,10 @@ class InferenceEngine:
         for i in range(max_new_tokens):
             last = logits[:, -1, :]
             if return_logprobs:
-                nxt, lp = self._sample_next_token_with_log_prob_synced(last, temperature, top_k, top_p)
+                nxt, lp = self._sample_next_token_with_log_prob_synced(last, temperature, top_k, top_p, gen)
                 logp_steps.append(lp)
             else:
-                nxt = self._sample_next_token_synced(last, temperature, top_k, top_p)
+                nxt = self._sample_next_token_synced(last, temperature, top_k, top_p, gen)
             tokens[:, cur] = nxt
             cur += 1
             steps += 1

@@ -26,10 +26,11 @@ def filter_logits(logits: torch.Tensor, temperature: float = 1.0, top_k: int | N
     return logits
 
 
-def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_log_prob: bool):
+def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_log_prob: bool, generator=None):
     """One fused kernel (csrc/fused/sample.cu): temperature, top-k / top-p thresholds by
-    radix selection, Philox draw.  The seed comes from torch's CPU generator, so
-    ``set_seed`` makes sampling reproducible and no device sync is needed."""
+    radix selection, Philox draw.  The seed comes from a CPU generator (torch's global one
+    unless ``generator`` is given), so ``set_seed`` makes sampling reproducible, ranks that
+    share a generator state draw identical tokens, and no device sync is needed."""
     from tinytron_b200.ops import _ext
 
     if temperature <= 0:
@@ -40,23 +41,24 @@ def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_lo
     B = x.shape[0]
     tok = torch.empty(B, dtype=torch.long, device=x.device)
     lp = torch.empty(B, dtype=torch.float32, device=x.device) if with_log_prob else None
-    seed = int(torch.randint(0, 2 ** 62, (1,)).item())
+    seed = int(torch.randint(0, 2 ** 62, (1,), generator=generator).item())
     _ext.load().sample_tokens(x, float(temperature), int(top_k or 0), float(top_p or 0.0), seed, 0, tok, lp)
     return tok, lp
 
 
-def sample_next_token(logits, temperature: float = 1.0, top_k=None, top_p=None) -> torch.Tensor:
+def sample_next_token(logits, temperature: float = 1.0, top_k=None, top_p=None, generator=None) -> torch.Tensor:
     if logits.is_cuda and logits.dim() == 2:
-        return _cuda_sample(logits, temperature, top_k, top_p, False)[0]
+        return _cuda_sample(logits, temperature, top_k, top_p, False, generator)[0]
     if top_k == 1 and temperature > 0:  # greedy: identical result without a multinomial draw
         return logits.argmax(dim=-1)
     probs = torch.softmax(filter_logits(logits, temperature, top_k, top_p), dim=-1)
-    return torch.multinomial(probs, num_samples=1).squeeze(-1)
+    return torch.multinomial(probs, num_samples=1, generator=generator).squeeze(-1)
 
 
-def sample_next_token_with_log_prob(logits, temperature: float = 1.0, top_k=None, top_p=None):
+def sample_next_token_with_log_prob(logits, temperature: float = 1.0, top_k=None, top_p=None, generator=None):
     if logits.is_cuda and logits.dim() == 2:
-        return _cuda_sample(logits, temperature, top_k, top_p, True)
+        return _cuda_sample(logits, temperature, top_k, top_p, True, generator)
     lp = torch.log_softmax(filter_logits(logits, temperature, top_k, top_p), dim=-1)
-    tok = lp.argmax(dim=-1) if top_k == 1 else torch.multinomial(lp.exp(), num_samples=1).squeeze(-1)
+    tok = lp.argmax(dim=-1) if top_k == 1 else torch.multinomial(lp.exp(), num_samples=1,
+                                                                  generator=generator).squeeze(-1)
     return tok, lp.gather(-1, tok.unsqueeze(-1)).squeeze(-1)

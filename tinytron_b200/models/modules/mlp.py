@@ -142,7 +142,17 @@ class MoE(nn.Module):
         return out
 
     def _forward_sep_local_reduce_inference(self, flat_x, sel, weights, ep_group, ep_rank, B, T):
+        """Head-parallel (SEP) inference (reference mlp.py:193-222): every rank holds all
+        tokens, computes the pairs routed to its own experts and the partial sums are
+        all-reduced.  On CUDA this is device-only (grouped GEMMs over the local segments,
+        graph-capturable heap all-reduce); the CPU path selects the local pairs eagerly."""
         D = self.hidden_size
+        from tinytron_b200.parallel.symm import row_parallel_all_reduce
+
+        if flat_x.is_cuda:
+            partial = ops.moe_experts_local(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
+                                            self.experts_down_weights, ep_rank * self.num_local_experts)
+            return row_parallel_all_reduce(partial, ep_group).reshape(B, T, D)
         tgt = sel // self.num_local_experts
         mask = tgt == ep_rank
         partial = flat_x.new_zeros((flat_x.size(0), D))
@@ -152,8 +162,6 @@ class MoE(nn.Module):
             out = self._apply_local_experts(flat_x[tok], sel.reshape(-1)[idx])
             partial = partial.index_put((tok,), (out.float() * weights.reshape(-1)[idx, None]).to(partial.dtype),
                                         accumulate=True)
-        from tinytron_b200.parallel.symm import row_parallel_all_reduce
-
         return row_parallel_all_reduce(partial, ep_group).reshape(B, T, D)
 
     def forward(self, x: torch.Tensor, use_cache: bool = False):

@@ -113,6 +113,20 @@ def moe_experts(x: torch.Tensor, sel: torch.Tensor, weights: torch.Tensor | None
     return out.view(N, k, -1).sum(1).to(x.dtype)
 
 
+def moe_experts_local(x: torch.Tensor, sel: torch.Tensor, weights: torch.Tensor, w_gate: torch.Tensor,
+                      w_up: torch.Tensor, w_down: torch.Tensor, e_lo: int) -> torch.Tensor:
+    """Inference with experts sharded over ranks: sum over j of weights[t, j] *
+    SwiGLU_{sel[t, j]}(x[t]) restricted to the experts [e_lo, e_lo + E_local) held here
+    (``sel`` holds global expert ids; the caller all-reduces the partial sums)."""
+    if x.is_cuda:
+        return _cuda_fn().moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo)
+    E = w_gate.shape[0]
+    local = sel - e_lo
+    mine = (local >= 0) & (local < E)
+    y = moe_experts(x, local.clamp(0, E - 1), weights * mine.to(weights.dtype), w_gate, w_up, w_down)
+    return y
+
+
 def embedding(idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     if weight.is_cuda:
         return _cuda_fn().EmbeddingFn.apply(idx, weight)

@@ -176,6 +176,45 @@ def moe_align(pairs: int, experts: int) -> int:
     return 256 if pairs >= 256 * experts else 128
 
 
+@torch.no_grad()
+def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None):
+    """Expert-parallel inference: the weighted partial sum over the experts
+    [e_lo, e_lo + E_local) held by this rank, for every token (zeros where none of a
+    token's experts is here).  Everything stays on the device (no host synchronisation,
+    so a decode step containing it can be captured in a CUDA graph): pairs routed
+    elsewhere go to an extra "remote" segment that the grouped GEMMs never compute, and
+    the combine stops at the local row count read on the device."""
+    x2d = _bf16(x.reshape(-1, x.shape[-1]))
+    N, H = x2d.shape
+    E, I = w_gate.shape[0], w_gate.shape[1]
+    k = sel.shape[-1]
+    c = C()
+    dev = x.device
+    local = sel.reshape(-1).to(torch.int32) - int(e_lo)
+    local = torch.where((local >= 0) & (local < E), local, torch.full_like(local, E)).contiguous()
+    P = local.numel()
+    align = moe_align(P, E + 1)
+    pair = align == 256
+    cap = c.moe_row_capacity(P, E + 1, align)
+    grp_off = torch.empty(E + 2, device=dev, dtype=torch.int32)
+    slot = torch.empty(P, device=dev, dtype=torch.int32)
+    row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
+    c.moe_layout(local, E + 1, grp_off, slot, row_pair, align)
+    g_loc = grp_off[:E + 1]  # local expert segments; g_loc[E] = rows computed on this rank
+    xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+    c.moe_gather_rows(x2d, row_pair, g_loc, k, xr)
+    w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
+    act = torch.empty(cap, I, device=dev, dtype=torch.bfloat16)
+    gu = torch.empty(cap, 2 * I, device=dev, dtype=torch.bfloat16)
+    c.moe_gemm_swiglu(xr, w_gu, act, gu, g_loc, E, pair)
+    yr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+    c.moe_gemm(act, bf16_of(w_down).view(E * H, I), yr, g_loc, E, False, H, 0, 0, pair)
+    out = torch.empty(N, H, device=dev, dtype=torch.bfloat16) if out is None else out
+    w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
+    c.moe_combine(yr, slot, w32, k, out, grp_off[E:E + 1])
+    return out
+
+
 class MoEExpertsFn(torch.autograd.Function):
     """Routed SwiGLU experts on grouped tcgen05 GEMMs.
 

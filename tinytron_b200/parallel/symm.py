@@ -167,6 +167,24 @@ class SymmetricHeap:
     def shadow_refresh(self, data: torch.Tensor, p16: torch.Tensor, lo: int, hi: int) -> None:
         _C().comm_shadow_refresh(self.gid, self.offset_of(data), p16, int(lo), int(hi))
 
+    def replay_slots(self, slot_bytes: int) -> tuple[torch.Tensor, int]:
+        """Two adjacent slots of ``slot_bytes`` (a multiple of 256) for the replayable
+        collectives; returns (buffer, slot_bytes)."""
+        slot_bytes = (int(slot_bytes) + ALIGN - 1) // ALIGN * ALIGN
+        return self.alloc(2 * slot_bytes, torch.uint8), slot_bytes
+
+    def replay_publish(self, slots: torch.Tensor, slot_bytes: int, x: torch.Tensor) -> None:
+        """Step 1 of a graph-safe collective: copy ``x`` into this rank's current slot and
+        signal the peers (the epoch lives on the device, so a CUDA graph may hold this)."""
+        _C().comm_replay_publish(self.gid, self.offset_of(slots), int(slot_bytes), x)
+
+    def replay_reduce(self, slots: torch.Tensor, slot_bytes: int, out: torch.Tensor,
+                      residual: torch.Tensor | None = None, root: int = -1) -> torch.Tensor:
+        """Step 2: wait for every peer's publish, then out = sum over ranks (or the ``root``
+        rank's input) (+ residual); bit-identical on every rank (fixed rank order)."""
+        _C().comm_replay_reduce(self.gid, self.offset_of(slots), int(slot_bytes), out, residual, int(root))
+        return out
+
     @property
     def epoch(self) -> int:
         return int(_C().comm_epoch(self.gid))
@@ -183,26 +201,25 @@ class SymmetricHeap:
 class RowParallelAllReduce:
     """Inference row-parallel all-reduce over a SEP group on a symmetric heap (replaces
     the reference's ``dist.all_reduce`` of c_proj / MoE partial outputs,
-    ``model/modules/attn.py:364``, ``mlp.py:221``).  Two heap slots alternate, which
-    is what makes one barrier per call enough: a rank rewrites a slot only after
-    every peer has started the next all-reduce, i.e. finished reading that slot."""
+    ``model/modules/attn.py:364``, ``mlp.py:221``).  Graph-safe: both of its kernels take
+    their epoch from device memory, so the decode step that contains it can be captured
+    in one CUDA graph and replayed (the two heap slots alternate with the epoch's parity,
+    which is what makes one wait per call enough)."""
 
     def __init__(self, group, max_numel: int, device=None):
         self.max_numel = int(max_numel)
-        self.heap = SymmetricHeap.create(SymmetricHeap.bytes_needed((max_numel, torch.bfloat16),
-                                                                    (max_numel, torch.bfloat16)), group, device)
-        self.slots = [self.heap.alloc(max_numel, torch.bfloat16), self.heap.alloc(max_numel, torch.bfloat16)]
-        self.i = 0
+        nbytes = self.max_numel * 2
+        self.heap = SymmetricHeap.create(2 * ((nbytes + ALIGN - 1) // ALIGN * ALIGN), group, device)
+        self.slots, self.slot_bytes = self.heap.replay_slots(nbytes)
 
     def __call__(self, y: torch.Tensor) -> torch.Tensor | None:
         n = y.numel()
-        if y.dtype != torch.bfloat16 or n > self.max_numel or not y.is_cuda:
+        if y.dtype != torch.bfloat16 or n > self.max_numel or not y.is_cuda or n % 8:
             return None
-        slot = self.slots[self.i][:n]
-        self.i ^= 1
-        slot.copy_(y.reshape(-1))
+        y = y.contiguous()
         out = torch.empty_like(y)
-        self.heap.all_reduce(slot, out.view(-1))
+        self.heap.replay_publish(self.slots, self.slot_bytes, y.view(-1))
+        self.heap.replay_reduce(self.slots, self.slot_bytes, out.view(-1))
         return out
 
     def close(self):
@@ -229,6 +246,10 @@ def disable_row_parallel_all_reduce(group) -> None:
     ar = _ROW_AR.pop(id(group), None)
     if ar is not None:
         ar.close()
+
+
+def row_parallel_heap_enabled(group) -> bool:
+    return id(group) in _ROW_AR
 
 
 def row_parallel_all_reduce(y: torch.Tensor, group) -> torch.Tensor:
