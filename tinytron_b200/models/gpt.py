@@ -93,19 +93,59 @@ class GPT(nn.Module):
         assert T <= self.config.block_size, f"Cannot forward sequence of length {T}, block size is only {self.config.block_size}"
         if use_cache or past_key_values is not None:
             return self._forward_cached(idx, past_key_values, use_cache, position_offset)
-        h, total_aux = self._trunk(idx, targets, position_offset)
+        aux_stats = [] if targets is not None and self.expert_loss_fn is not None else None
+        h, _ = self._trunk(idx, targets, position_offset, aux_stats=aux_stats)
         if targets is None:
             if torch.is_grad_enabled():  # differentiable logits (e.g. RL policy log-probs)
                 return ops.linear(h, self.lm_head.weight)
             return ops.lm_logits(h, self.lm_head.weight)
         valid = targets != self.loss_fn.ignore_index
         loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index)
-        loss, logging_loss = self.loss_fn.reduce(loss_sum, valid.sum())
+        loss, logging_loss, total_aux = self._reduce_step_stats(loss_sum, valid.sum(), aux_stats)
         logits = None
         if return_logits:
             with torch.no_grad():
                 logits = ops.lm_logits(h.detach(), self.lm_head.weight)
         return logits, loss + total_aux, logging_loss
+
+    def _reduce_step_stats(self, loss_sum, valid_count, aux_stats):
+        """Every cross-rank statistic of the forward in ONE packed all-reduce over DP x SP
+        (the reference issues one per quantity and two per MoE layer): the MoE selection
+        counts of every layer, and one slot per rank for the valid-token count, the local
+        loss sum and the routed-token count, from which the SP/EP-group sums follow.
+        Also leaves (SP-group valid tokens, DP x SP valid tokens) in ``last_token_counts``
+        for the trainer's loss weighting."""
+        from tinytron_b200.parallel.scalars import all_reduce_scalars
+
+        group = parallel_state._DP_SP_GROUP
+        world = parallel_state.get_dp_sp_world_size()
+        me = parallel_state.get_dp_sp_rank()
+        sp_ranks = parallel_state.get_sep_ranks() if group is not None else [0]
+        sp_idx = torch.tensor(sp_ranks, device=loss_sum.device)
+        E = self.config.num_experts if aux_stats else 0
+        n_layers = len(aux_stats) if aux_stats else 0
+        with torch.no_grad():
+            vec = torch.zeros(n_layers * E + 3 * world, dtype=torch.float32, device=loss_sum.device)
+            base = n_layers * E
+            vec[base + me] = valid_count.float()
+            vec[base + world + me] = loss_sum.detach().float()
+            for li, (_, f_sum, n_local) in enumerate(aux_stats or []):
+                vec[li * E:(li + 1) * E] = f_sum
+                if li == 0:
+                    vec[base + 2 * world + me] = n_local
+            red = all_reduce_scalars(vec, group)
+            counts, sums, routed = red[base:base + world], red[base + world:base + 2 * world], red[base + 2 * world:]
+            sp_count = counts[sp_idx].sum().clamp(min=1.0)
+            logging_loss = sums[sp_idx].sum() / sp_count
+            self.last_token_counts = (counts[sp_idx].sum(), counts.sum())
+        loss = loss_sum / sp_count
+        total_aux = 0.0
+        if aux_stats:
+            tokens_ep, tokens_all = routed[sp_idx].sum(), routed.sum()
+            for li, (p_sum, _, _) in enumerate(aux_stats):
+                total_aux = total_aux + self.expert_loss_fn.from_global_stats(p_sum, red[li * E:(li + 1) * E],
+                                                                              tokens_ep, tokens_all)
+        return loss, logging_loss, total_aux
 
     def token_log_probs(self, idx, targets, position_offset: int = 0):
         """log p(targets[b, t] | idx[b, :t+1]) as fp32 ``[B, T]``, differentiable, without
@@ -116,8 +156,10 @@ class GPT(nn.Module):
         return ops.lm_head_token_logprobs(h, self.lm_head.weight, targets, self.loss_fn.ignore_index).view(
             targets.shape)
 
-    def _trunk(self, idx, targets, position_offset: int = 0):
-        """Embedding -> blocks -> final norm; returns (normalised hidden states, MoE aux loss)."""
+    def _trunk(self, idx, targets, position_offset: int = 0, aux_stats: list | None = None):
+        """Embedding -> blocks -> final norm; returns (normalised hidden states, MoE aux loss).
+        With ``aux_stats`` (a list) the MoE layers append their local load-balancing
+        statistics there instead of reducing them one layer at a time (aux loss 0 then)."""
         x = ops.embedding(idx, self.wte.weight)
         pending = None
         total_aux = 0.0
@@ -130,7 +172,10 @@ class GPT(nn.Module):
                 x, h = ops.add_rmsnorm(x, a, blk.ln_2.weight, self.eps)
                 if self.use_moe:
                     pending, gate_logits = blk.mlp(h)
-                    if self.expert_loss_fn is not None and targets is not None:
+                    if aux_stats is not None:
+                        aux_stats.append(self.expert_loss_fn.local_stats(
+                            gate_logits, valid_mask=valid, selected_experts=getattr(blk.mlp, "last_selected", None)))
+                    elif self.expert_loss_fn is not None and targets is not None:
                         total_aux = total_aux + self.expert_loss_fn(gate_logits, valid_mask=valid)
                 else:
                     pending = blk.mlp(h)

@@ -59,6 +59,39 @@ class ExpertLoadBalancingLoss(nn.Module):
         self.top_k = top_k
         self.alpha = alpha
 
+    def local_stats(self, gate_logits: torch.Tensor, valid_mask: torch.Tensor | None = None,
+                    selected_experts: torch.Tensor | None = None):
+        """This rank's part of the loss before any collective: (sum over valid tokens of
+        the router softmax [E] (with grad), top-k selection counts [E] (no grad), number
+        of valid tokens (0-dim, no grad)).  ``from_global_stats`` finishes the loss once the
+        counts have been reduced; ``GPT.forward`` reduces every layer's counts together."""
+        E = self.num_experts
+        flat = gate_logits.reshape(-1, E)
+        if valid_mask is not None:
+            keep = valid_mask.reshape(-1).to(torch.float32)
+            p_sum = (F.softmax(flat.float(), dim=-1) * keep[:, None]).sum(0)
+            if selected_experts is None:
+                selected_experts = torch.topk(flat, self.top_k, dim=-1).indices
+            sel = selected_experts.reshape(-1, self.top_k).long()
+            f_sum = torch.zeros(E, dtype=torch.float32, device=flat.device)
+            f_sum.index_add_(0, sel.reshape(-1), keep.repeat_interleave(self.top_k))
+            n_local = keep.sum()
+        else:
+            p_sum = F.softmax(flat.float(), dim=-1).sum(0)
+            if selected_experts is None:
+                selected_experts = torch.topk(flat, self.top_k, dim=-1).indices
+            f_sum = torch.bincount(selected_experts.reshape(-1).long(), minlength=E).float()
+            n_local = torch.tensor(float(flat.size(0)), device=flat.device)
+        return p_sum, f_sum.detach(), n_local.detach()
+
+    def from_global_stats(self, p_sum: torch.Tensor, f_global: torch.Tensor, tokens_ep: torch.Tensor,
+                          tokens_global: torch.Tensor) -> torch.Tensor:
+        """alpha * E * sum_i f_i * P_i with f_i = global selection share (DP x SP) and
+        P_i = mean router probability over the EP group's tokens."""
+        P_i = p_sum / tokens_ep.clamp(min=1.0)
+        f_i = f_global / (tokens_global.clamp(min=1.0) * self.top_k)
+        return self.alpha * self.num_experts * torch.sum(f_i * P_i)
+
     def forward(self, gate_logits: torch.Tensor, valid_mask: torch.Tensor | None = None,
                 selected_experts: torch.Tensor | None = None) -> torch.Tensor:
         E = self.num_experts

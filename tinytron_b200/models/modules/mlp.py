@@ -168,6 +168,7 @@ class MoE(nn.Module):
         B, T, D = x.shape
         ep_group, ep, ep_rank = _ep_context()
         gate_logits, weights, sel = self.route(x.reshape(B * T, D))
+        self.last_selected = sel  # the load-balancing statistics reuse the router's top-k
         flat_x = x.reshape(B * T, D)
         if use_cache and ep > 1:
             return self._forward_sep_local_reduce_inference(flat_x, sel, weights, ep_group, ep_rank, B, T), \

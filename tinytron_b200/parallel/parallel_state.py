@@ -60,6 +60,9 @@ def initialize_model_parallel(config=None, sep_size: int | None = None, timeout=
 
 def destroy_model_parallel() -> None:
     global _SEP_GROUP, _DP_GROUP, _DP_SP_GROUP, _SEP_SIZE, _DP_SIZE, _DP_SP_SIZE, _SEP_RANKS, _DP_RANKS
+    from .scalars import release_scalar_reducers
+
+    release_scalar_reducers()
     _SEP_GROUP = _DP_GROUP = _DP_SP_GROUP = None
     _SEP_SIZE = _DP_SIZE = _DP_SP_SIZE = None
     _SEP_RANKS = _DP_RANKS = None

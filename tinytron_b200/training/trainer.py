@@ -283,12 +283,9 @@ class Trainer:
         with self.profiler_record_fn("forward"):
             with self._autocast_context(config.train.precision):
                 _, loss, logging_loss = self.model(x.reshape(x.shape[0], -1), y.reshape(y.shape[0], -1))
-        tok = valid.to(torch.float32).reshape(1)
-        if self.sp_world_size > 1:
-            dist.all_reduce(tok, op=dist.ReduceOp.SUM, group=self.sp_group)
-        tok_all = tok.clone()
-        if self.dp_world_size > 1:
-            dist.all_reduce(tok_all, op=dist.ReduceOp.SUM, group=self.dp_group)
+        # SP-group and global valid-token counts, reduced inside the model's forward together
+        # with its other statistics (one packed collective per micro-step)
+        tok, tok_all = self.raw_model.last_token_counts
         weight = (tok * self.dp_world_size / tok_all.clamp(min=1.0)).reshape(())
         ga = self.training_info["grad_accum_steps"]
         loss = loss * weight.to(loss.dtype) / ga
@@ -372,11 +369,14 @@ class Trainer:
             for p in self.flat.params:
                 p.grad = None
             self.flat.refresh_bf16() if self.device.type == "cuda" else None
-        if self.dp_world_size > 1:
-            dist.all_reduce(loss_accum, op=dist.ReduceOp.SUM, group=self.dp_group)
-            loss_accum /= self.dp_world_size
         if self.dp_sp_world_size > 1:
-            dist.all_reduce(valid_accum, op=dist.ReduceOp.SUM, group=self.dp_sp_group)
+            # one packed collective for the step's loss (identical across SP ranks, so its
+            # DP x SP sum / (DP x SP) is the DP mean) and the global valid-token count
+            from tinytron_b200.parallel.scalars import all_reduce_scalars
+
+            red = all_reduce_scalars(torch.stack([loss_accum.float(), valid_accum.float()]), self.dp_sp_group)
+            loss_accum = red[0] / self.dp_sp_world_size
+            valid_accum = red[1].round().long()
         self.one_step_results["lr"] = lr
         self.one_step_results["loss"] = loss_accum
         self.one_step_results["grad_norm"] = norm
