@@ -44,13 +44,26 @@ MOE_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_head
              "--num_experts_per_tok", "8", "--moe_intermediate_size", "1408", "--moe_balance_loss_weight", "0.01"]
 
 
+# long-context dense GPT, Muon + ZeRO-1, SEP = #GPUs, 16L d2048 16q/2kv,
+# SwiGLU 5504 (not given by the config; the same value in both arms), seq 32768 = 4096 per rank
+# at SEP 8, micro-batch 1 sequence per GPU (--batch_size = 1 x SEP, the launcher convention).
+LONGCTX_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_heads", "16",
+                 "--num_key_value_heads", "2", "--intermediate_size", "5504", "--vocab_size", "50304",
+                 "--block_size", "32768", "--init_std", "0.02", "--optimizer", "muon"]
+
+
 def _select_config(name: str, n_gpus: int) -> None:
-    global MODEL_FLAGS, MICRO_BATCH, GA, MODEL_NAME, PRESET, SEP
+    global MODEL_FLAGS, MICRO_BATCH, GA, MODEL_NAME, PRESET, SEP, SEQ
     if name == "moe":
         MODEL_FLAGS = MOE_FLAGS
         MICRO_BATCH, GA, SEP = 2 * n_gpus, 4, n_gpus
         MODEL_NAME = "moe-16L (d2048 16q/4kv, 64 experts x 1408 top-8, V50304)"
         PRESET = "b200-moe-16x64"
+    elif name == "longctx":
+        MODEL_FLAGS = LONGCTX_FLAGS
+        MICRO_BATCH, GA, SEP, SEQ = n_gpus, 4, n_gpus, 32768
+        MODEL_NAME = "dense-16L long-context (d2048 16q/2kv I5504 V50304, seq 32768), Muon"
+        PRESET = "b200-longctx"
 
 
 def _free_port() -> int:
@@ -224,7 +237,7 @@ def run(args, impl: str):
                 print(json.dumps({"impl": "reference", "unavailable": f"reference import failed: {exc}"}))
             return
         argv = _train_argv(world, total_steps, log_dir) + ["--debug"]
-        if not args.ref_eager and args.config == "dense":
+        if not args.ref_eager and args.config in ("dense", "longctx"):
             # measured faster than eager on B200 (68.6K vs 47.3K tok/s, 1 GPU, dense); with MoE the
             # data-dependent expert shapes exceed dynamo's recompile limit and the step fails, so the
             # MoE reference runs eager
@@ -338,7 +351,8 @@ def run(args, impl: str):
         "config": {"model": MODEL_NAME, "global_batch": MICRO_BATCH * GA * dp, "seq_len": SEQ,
                    "micro_batch": MICRO_BATCH, "grad_accum": GA,
                    "parallelism": (f"sep{SEP}+dp{dp}" if SEP > 1 else f"dp{world}") + "+zero1",
-                   "optimizer": "AdamW (ZeRO-1)", "l2": "inputs larger than L2 (no flush needed)",
+                   "optimizer": ("Muon (ZeRO-1)" if "muon" in MODEL_FLAGS else "AdamW (ZeRO-1)"),
+                   "l2": "inputs larger than L2 (no flush needed)",
                    "inputs": ("pinned host batches (the reference slices SEP chunks on the host)"
                               if feed is next_host else "device-resident batches")},
         "mfu": round(achieved / (world * 2.25e15), 4),
@@ -448,8 +462,9 @@ def main():
     ap.add_argument("--ref-eager", action="store_true",
                     help="reference arm: run eager instead of --use_compile (compile is the faster of the two)")
     ap.add_argument("--no-clocks", action="store_true")
-    ap.add_argument("--config", choices=["dense", "moe", "decode"], default="dense",
-                    help="dense: BASELINE config 2 (headline); moe: config 3 (SEP = #GPUs); decode: config 5")
+    ap.add_argument("--config", choices=["dense", "moe", "longctx", "decode"], default="dense",
+                    help="dense: BASELINE config 2 (headline); moe: config 3 (SEP = #GPUs); longctx: config 4 "
+                         "(Muon, SEP = #GPUs, seq 32768); decode: config 5")
     ap.add_argument("--decode-steps", type=int, default=512)
     ap.add_argument("--page-size", type=int, default=16, help="decode: KV page size (0 = contiguous cache)")
     args = ap.parse_args()

@@ -97,6 +97,14 @@ void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset,
 void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, int64_t lo, int64_t hi);
 void comm_all_to_all(int64_t gid, int64_t slot_offset, torch::Tensor out);
 int64_t comm_epoch(int64_t gid);
+void ul_pack(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor src, int64_t B, int64_t T,
+             std::vector<int64_t> rows, int64_t W, int64_t s1, int64_t s2, std::vector<int64_t> b0,
+             std::vector<int64_t> b1, std::vector<int64_t> b2);
+void ul_exchange(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor out, int64_t B, int64_t T,
+                 std::vector<int64_t> rows, int64_t dcol_c, int64_t W);
+void ul_exchange_qkv_grad(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor dqkv, int64_t B,
+                          int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t hq_l, int64_t hkv_l,
+                          std::vector<int64_t> kv0);
 void comm_replay_publish(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor in);
 void comm_replay_reduce(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor out,
                         c10::optional<torch::Tensor> residual, int64_t root);
@@ -193,6 +201,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gid"), py::arg("signal") = true);
   m.def("comm_all_reduce", &tt::comm::comm_all_reduce, "one-shot all-reduce of a heap region (+ residual)",
         py::arg("gid"), py::arg("in_offset"), py::arg("out"), py::arg("residual") = py::none());
+  m.def("ul_pack", &tt::comm::ul_pack, "Ulysses: gather this rank's outgoing chunks into its send slot and signal");
+  m.def("ul_exchange", &tt::comm::ul_exchange, "Ulysses: wait, load chunk `me` of every peer into out (remapped)");
+  m.def("ul_exchange_qkv_grad", &tt::comm::ul_exchange_qkv_grad,
+        "Ulysses backward of the q|k|v direction: d(q|k|v) summed over ranks sharing a kv head");
   m.def("comm_replay_publish", &tt::comm::comm_replay_publish,
         "graph-safe collective, step 1: copy the input into this rank's slot and signal (device epoch)");
   m.def("comm_replay_reduce", &tt::comm::comm_replay_reduce,

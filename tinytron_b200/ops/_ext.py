@@ -21,6 +21,7 @@ SOURCES = [
     "bindings.cpp",
     "runtime/status.cu",
     "runtime/comm.cu",
+    "runtime/ulysses.cu",
     "gemm/gemm.cu",
     "fused/norm.cu",
     "fused/elementwise.cu",

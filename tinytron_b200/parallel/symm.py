@@ -304,14 +304,54 @@ class HeapAllToAll:
         return out
 
 
+class UlyssesExchange:
+    """Send slots and the device-epoch protocol of the fused Ulysses kernels
+    (``csrc/runtime/ulysses.cu``) for one SEP group.  The heap grows (collectively: every
+    rank asks for the same sizes in the same order) when a larger exchange is needed."""
+
+    def __init__(self, group, device=None):
+        self.group = group
+        self.device = device
+        self.heap = None
+        self.slots = None
+        self.slot_bytes = 0
+
+    def ensure(self, nbytes: int):
+        if self.heap is None or nbytes > self.slot_bytes:
+            if self.heap is not None:
+                torch.cuda.synchronize()
+                self.heap.close()
+            cap = max(int(nbytes), 1 << 20)
+            cap = (cap + ALIGN - 1) // ALIGN * ALIGN
+            self.heap = SymmetricHeap.create(2 * cap + ALIGN, self.group, self.device)
+            self.slots, self.slot_bytes = self.heap.replay_slots(cap)
+        return self.heap.gid, self.heap.offset_of(self.slots), self.slot_bytes
+
+    def close(self):
+        if self.heap is not None:
+            self.heap.close()
+            self.heap = None
+
+
+_UL: dict = {}
+
+
+def ulysses_exchange_for(group) -> UlyssesExchange | None:
+    return _UL.get(id(group))
+
+
 _A2A: dict = {}
 
 
 def enable_heap_all_to_all(group, device=None) -> HeapAllToAll:
+    """Route the SEP group's all-to-alls through symmetric heaps: the generic equal-split
+    exchange and the fused Ulysses head<->sequence kernels."""
     a = _A2A.get(id(group))
     if a is None:
         a = HeapAllToAll(group, device)
         _A2A[id(group)] = a
+    if id(group) not in _UL:
+        _UL[id(group)] = UlyssesExchange(group, device)
     return a
 
 

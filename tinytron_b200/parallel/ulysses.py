@@ -7,7 +7,10 @@ bucketed; it reduces ``main_grad`` buffers when the model uses flat fp32 grads.
 
 The attention module uses :func:`route_heads_to_ranks` / :func:`gather_heads_from_ranks`
 (head<->sequence transposes with *unexpanded* GQA routing: a kv head is sent only to
-the ranks whose q heads read it, instead of expanding kv to Hq heads first).
+the ranks whose q heads read it, instead of expanding kv to Hq heads first).  On CUDA
+inside one node both run as fused pack / exchange kernels on a symmetric heap
+(``csrc/runtime/ulysses.cu``): the routing and the layout changes happen inside the
+kernels that move the data, so no stacked, permuted or expanded copy is ever made.
 """
 from __future__ import annotations
 
@@ -64,10 +67,99 @@ def native_gqa_routing(sp: int, Hq: int, Hkv: int) -> bool:
     return G % hq_l == 0  # every rank's q heads fall inside one kv group
 
 
+# ----------------------------------------------------------------------------- fused kernels
+def _C():
+    from tinytron_b200.ops import _ext
+
+    return _ext.load()
+
+
+def _kv_starts(sp: int, Hq: int, Hkv: int) -> list[int]:
+    return [kv_heads_for_rank(r, sp, Hq, Hkv)[0] for r in range(sp)]
+
+
+class _FusedHeadsFn(torch.autograd.Function):
+    """q|k|v of this rank's tokens -> this rank's heads over the full sequence, by the
+    fused pack / exchange kernels (the GQA routing and both layout changes are inside
+    the kernels; no intermediate tensors)."""
+
+    @staticmethod
+    def forward(ctx, qkv, ex, B, T, Hq, Hkv, D, sp, hq_l, hkv_l):
+        W = (hq_l + 2 * hkv_l) * D
+        kv0 = _kv_starts(sp, Hq, Hkv)
+        gid, off, sb = ex.ensure(sp * B * T * W * 2)
+        C = _C()
+        C.ul_pack(gid, off, sb, qkv, B, T, [T, 0, 1], W, hq_l * D, (hq_l + hkv_l) * D,
+                  [c * hq_l * D for c in range(sp)], [Hq * D + k * D for k in kv0],
+                  [(Hq + Hkv) * D + k * D for k in kv0])
+        full = torch.empty(B * sp * T, W, device=qkv.device, dtype=torch.bfloat16)
+        C.ul_exchange(gid, off, sb, full, B, T, [sp * T, T, 1], 0, W)
+        ctx.cfg = (ex, B, T, Hq, Hkv, D, sp, hq_l, hkv_l, kv0)
+        return full
+
+    @staticmethod
+    def backward(ctx, g_full):
+        ex, B, T, Hq, Hkv, D, sp, hq_l, hkv_l, kv0 = ctx.cfg
+        W = (hq_l + 2 * hkv_l) * D
+        g_full = g_full.to(torch.bfloat16).contiguous()
+        gid, off, sb = ex.ensure(sp * B * T * W * 2)
+        C = _C()
+        C.ul_pack(gid, off, sb, g_full, B, T, [sp * T, T, 1], W, W, W, [0] * sp, [0] * sp, [0] * sp)
+        dqkv = torch.empty(B * T, (Hq + 2 * Hkv) * D, device=g_full.device, dtype=torch.bfloat16)
+        C.ul_exchange_qkv_grad(gid, off, sb, dqkv, B, T, Hq, Hkv, D, hq_l, hkv_l, kv0)
+        return dqkv, None, None, None, None, None, None, None, None, None
+
+
+class _FusedTokensFn(torch.autograd.Function):
+    """Attention output of this rank's heads over the full sequence -> all heads of this
+    rank's tokens (the c_proj input layout), by the fused pack / exchange kernels."""
+
+    @staticmethod
+    def forward(ctx, o, ex, B, T, Hq, D, sp):
+        hq_l = Hq // sp
+        W = hq_l * D
+        gid, off, sb = ex.ensure(sp * B * T * W * 2)
+        C = _C()
+        C.ul_pack(gid, off, sb, o, B, T, [sp * T, T, 1], W, W, W, [0] * sp, [0] * sp, [0] * sp)
+        y = torch.empty(B * T, Hq * D, device=o.device, dtype=torch.bfloat16)
+        C.ul_exchange(gid, off, sb, y, B, T, [T, 0, 1], W, W)
+        ctx.cfg = (ex, B, T, Hq, D, sp)
+        return y
+
+    @staticmethod
+    def backward(ctx, g_y):
+        ex, B, T, Hq, D, sp = ctx.cfg
+        hq_l = Hq // sp
+        W = hq_l * D
+        g_y = g_y.to(torch.bfloat16).contiguous()
+        gid, off, sb = ex.ensure(sp * B * T * W * 2)
+        C = _C()
+        C.ul_pack(gid, off, sb, g_y, B, T, [T, 0, 1], W, W, W, [c * W for c in range(sp)], [0] * sp, [0] * sp)
+        do = torch.empty(B * sp * T, W, device=g_y.device, dtype=torch.bfloat16)
+        C.ul_exchange(gid, off, sb, do, B, T, [sp * T, T, 1], 0, W)
+        return do, None, None, None, None, None, None
+
+
+def _fused_ok(x: torch.Tensor, group, sp: int, Hq: int, Hkv: int, D: int):
+    if not x.is_cuda or x.dtype != torch.bfloat16 or sp > 8 or D % 8:
+        return None
+    if not native_gqa_routing(sp, Hq, Hkv):
+        return None
+    from .symm import ulysses_exchange_for
+
+    return ulysses_exchange_for(group)
+
+
 def route_heads_to_ranks(qkv: torch.Tensor, B: int, T_loc: int, Hq: int, Hkv: int, D: int, sp: int, group):
     """qkv [B*T_loc, (Hq+2Hkv)*D] (this rank's sequence chunk, all heads) ->
     [B*T_full, (Hq_l + 2*Hkv_l)*D] (full sequence, this rank's heads)."""
     hq_l = Hq // sp
+    ex = _fused_ok(qkv, group, sp, Hq, Hkv, D)
+    if ex is not None:
+        k0, k1 = kv_heads_for_rank(0, sp, Hq, Hkv)
+        hkv_l = k1 - k0
+        full = _FusedHeadsFn.apply(qkv.contiguous(), ex, B, T_loc, Hq, Hkv, D, sp, hq_l, hkv_l)
+        return full, hq_l, hkv_l
     x = qkv.view(B, T_loc, Hq + 2 * Hkv, D)
     if native_gqa_routing(sp, Hq, Hkv):
         parts = []
@@ -93,6 +185,9 @@ def route_heads_to_ranks(qkv: torch.Tensor, B: int, T_loc: int, Hq: int, Hkv: in
 def gather_heads_from_ranks(o: torch.Tensor, B: int, T_loc: int, Hq: int, D: int, sp: int, group) -> torch.Tensor:
     """o [B*T_full, Hq_l*D] (full sequence, local heads) -> [B, T_loc, Hq*D] (local chunk, all heads)."""
     hq_l = Hq // sp
+    ex = _fused_ok(o, group, sp, Hq, Hq, D)
+    if ex is not None:
+        return _FusedTokensFn.apply(o.contiguous(), ex, B, T_loc, Hq, D, sp).view(B, T_loc, Hq * D)
     send = o.view(B, sp, T_loc, hq_l * D).permute(1, 0, 2, 3).contiguous()  # [dst chunk, B, T_loc, hq_l*D]
     recv = ulysses_all_to_all(send, group)  # [src rank (head block), B, T_loc, hq_l*D]
     return recv.permute(1, 2, 0, 3).reshape(B, T_loc, Hq * D)
