@@ -4,6 +4,8 @@ import os
 import subprocess
 import sys
 
+import torch
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -37,3 +39,71 @@ def test_pretrain_entry_point_cpu(tmp_path):
     out = subprocess.run(cmd, cwd=ROOT, env=env, capture_output=True, text=True, timeout=600)
     assert out.returncode == 0, out.stderr[-2000:]
     assert out.stdout.count("tok/sec:") == 3, out.stdout[-2000:]
+
+
+def test_token_shard_dataset_split_and_resume(tmp_path):
+    import numpy as np
+
+    from tinytron_b200.training.streaming import TokenShardDataset, write_token_shards
+
+    toks = np.arange(1000) % 997
+    write_token_shards(str(tmp_path), toks, tokens_per_chunk=123)  # samples span shard boundaries
+    seq = 16
+    full = [s["input_ids"].tolist() for s in TokenShardDataset(str(tmp_path), seq)]
+    assert len(full) == (1000 - 1) // seq and full[3] == list(range(48, 64))
+    ranks = [[s["input_ids"].tolist() for s in TokenShardDataset(str(tmp_path), seq, r, 2)] for r in range(2)]
+    assert ranks[0] == full[0::2] and ranks[1] == full[1::2]  # DP ranks interleave samples
+    resumed = [s["labels"].tolist() for s in TokenShardDataset(str(tmp_path), seq, 1, 2, global_skip=10)]
+    assert resumed[0] == list(range(11 * seq + 1, 12 * seq + 1))
+
+
+def test_streaming_trainer_checkpoint_resume_cpu(tmp_path):
+    """Train 4 steps with checkpoints, then resume from step 1: the resumed run sees the
+    same batches as the uninterrupted one from step 2 on."""
+    import numpy as np
+
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT"):
+        os.environ.pop(k, None)
+    from tinytron_b200.training import build_config, parse_args
+    from tinytron_b200.training.streaming import StreamingTrainer, write_token_shards
+
+    data = tmp_path / "shards"
+    write_token_shards(str(data), np.random.default_rng(0).integers(0, 256, 40000), tokens_per_chunk=5000)
+
+    def make(log_dir, steps):
+        argv = ["--dataset_path", str(data), "--log_dir", str(log_dir), "--total_batch_size", str(2 * 32 * 2),
+                "--batch_size", "2", "--seq_len", "32", "--max_steps", str(steps), "--warmup_steps", "1",
+                "--num_layer", "1", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+                "--intermediate_size", "96", "--vocab_size", "256", "--block_size", "32", "--backend", "gloo",
+                "--do_save", "--save_every_steps", "1", "--log_every", "100"]
+        return StreamingTrainer(build_config(parse_args(argv)))
+
+    seen_a = []
+    a = make(tmp_path / "a", 4)
+    orig = a._next_train_batch
+    a._next_train_batch = lambda: (lambda b: (seen_a.append(b["input_ids"].clone()), b)[1])(orig())
+    a.train()
+    import shutil
+
+    ck = sorted(p for p in os.listdir(a.log_dir) if p.endswith("_meta.pt"))
+    assert ck, os.listdir(a.log_dir)
+    for p in os.listdir(a.log_dir):  # keep only the step-1 checkpoint
+        if not p.startswith("00001") and p != "log.txt":
+            full = os.path.join(a.log_dir, p)
+            shutil.rmtree(full) if os.path.isdir(full) else os.remove(full)
+    seen_b = []
+    b = make(tmp_path / "a", 4)
+    orig_b = b._next_train_batch
+    b._next_train_batch = lambda: (lambda x: (seen_b.append(x["input_ids"].clone()), x)[1])(orig_b())
+    b.train()
+    assert b.start_step == 2
+    ga = 2
+    assert len(seen_b) == 2 * ga
+    for x, y in zip(seen_b, seen_a[2 * ga:]):
+        assert torch.equal(x, y)
+
+
+def test_shell_launchers_parse():
+    for name in ("pretrain.sh", "inference.sh", "rl.sh"):
+        out = subprocess.run(["bash", "-n", os.path.join(ROOT, "tinytron_b200", "launch", name)], capture_output=True)
+        assert out.returncode == 0, (name, out.stderr)

@@ -25,7 +25,14 @@ SEQ_LEN=${SEQ_LEN:-4096}
 GBS=${GBS:-1024}
 TOTAL_BATCH_SIZE=$((GBS * SEQ_LEN))
 SEP_SIZE=${SEP_SIZE:-1}
-BATCH_SIZE_PER_DP_RANK=$((BATCH_SIZE * SEP_SIZE))
+BATCH_SIZE_SCALE_WITH_SEP=${BATCH_SIZE_SCALE_WITH_SEP:-1}
+if [ "$BATCH_SIZE_SCALE_WITH_SEP" -eq 1 ]; then
+  BATCH_SIZE_PER_DP_RANK=$((BATCH_SIZE * SEP_SIZE))
+else
+  BATCH_SIZE_PER_DP_RANK=$BATCH_SIZE
+fi
+PRECISION=${PRECISION:-bf16}
+STREAMING_DATA_DIR=${STREAMING_DATA_DIR:-}
 DEBUG=${DEBUG:-1}
 DETER_MODE=${DETER_MODE:-1}
 MODEL_SIZE=${MODEL_SIZE:-0.25B}
@@ -33,11 +40,16 @@ MOE_BALANCE_LOSS_WEIGHT=${MOE_BALANCE_LOSS_WEIGHT:-}
 MAX_STEPS=${MAX_STEPS:-}
 LOG_DIR=${LOG_DIR:-"$REPO_ROOT/logs/debug_gpt_${MODEL_SIZE}"}
 
-ARGS=(--preset "$MODEL_SIZE" --seed "$SEED" --use_mock_data --mock_data_num_samples 12800 --log_dir "$LOG_DIR"
+ARGS=(--preset "$MODEL_SIZE" --seed "$SEED" --precision "$PRECISION" --log_dir "$LOG_DIR"
       --total_batch_size "$TOTAL_BATCH_SIZE" --batch_size "$BATCH_SIZE_PER_DP_RANK" --seq_len "$SEQ_LEN"
       --block_size "$SEQ_LEN" --max_lr "$MAX_LR" --min_lr "$MIN_LR" --weight_decay 0.1 --grad_clip_value 1.0
       --warmup_steps "$LR_WARMUP_STEPS" --max_epochs 1 --do_save --save_every_steps 500
       --sep_size "$SEP_SIZE" --use_distributed_optimizer)
+if [ -n "$STREAMING_DATA_DIR" ]; then
+  ARGS+=(--streaming_data_dir "$STREAMING_DATA_DIR")
+else
+  ARGS+=(--use_mock_data --mock_data_num_samples 12800)
+fi
 [ "$DEBUG" -eq 1 ] && ARGS+=(--debug)
 [ "$DETER_MODE" -eq 1 ] && ARGS+=(--deterministic)
 [ -n "$MOE_BALANCE_LOSS_WEIGHT" ] && ARGS+=(--moe_balance_loss_weight "$MOE_BALANCE_LOSS_WEIGHT")

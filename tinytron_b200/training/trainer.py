@@ -549,10 +549,15 @@ class Trainer:
                 "sampler_state": {"epoch": self.train_sampler_epoch, "iter_idx": self.train_loader_iter_idx},
                 "rng_state": rng,
             }
+            meta.update(self._checkpoint_extra_meta())
             torch.save(meta, ck.checkpoint_meta_path(prefix))
             ck.write_checksums(prefix)
         if dist.is_initialized():
             dist.barrier()
+
+    def _checkpoint_extra_meta(self) -> dict:
+        """Extra entries for the checkpoint's ``_meta.pt`` (subclass hook, e.g. a data position)."""
+        return {}
 
     def _resume_from_checkpoint(self):
         from . import checkpoint as ck
@@ -563,6 +568,7 @@ class Trainer:
             self.start_step = 0
             return
         meta = torch.load(ck.checkpoint_meta_path(prefix), map_location="cpu", weights_only=False)
+        self._resumed_meta = meta
         sd = ck.load_model_state_dict_for_training(prefix, self.model_config, self.rank, meta)
         self.raw_model.load_state_dict(sd)
         if self.device.type == "cuda":
@@ -574,8 +580,9 @@ class Trainer:
         ss = meta.get("sampler_state", {})
         epoch, it = int(ss.get("epoch", 0)), int(ss.get("iter_idx", 0))
         self.train_sampler_epoch, self.train_loader_iter_idx = epoch, it
-        self.train_sampler.set_epoch(epoch)
-        self.train_loader_iter = enumerate(islice(self.train_loader, it, None), start=it)
+        if self.train_sampler is not None:
+            self.train_sampler.set_epoch(epoch)
+            self.train_loader_iter = enumerate(islice(self.train_loader, it, None), start=it)
         step = meta.get("step")
         self.start_step = (step + 1) if step is not None else 0
         if self.master_process:
