@@ -90,10 +90,13 @@ int64_t comm_heap_base(int64_t gid);
 void comm_barrier(int64_t gid, bool signal);
 void comm_all_reduce(int64_t gid, int64_t in_offset, torch::Tensor out, c10::optional<torch::Tensor> residual);
 void comm_reduce_scatter_sumsq(int64_t gid, int64_t grad_offset, int64_t lo, int64_t hi, int64_t split, double scale);
+void comm_reduce_scatter_bucket(int64_t gid, int64_t grad_offset, int64_t lo, int64_t hi, int64_t split,
+                                double scale, torch::Tensor sq_local, int64_t max_blocks);
+int64_t comm_publish_sumsq(int64_t gid, torch::Tensor sq);
 void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset, c10::optional<torch::Tensor> p16,
                           torch::Tensor m, torch::Tensor v, int64_t lo, int64_t hi, double lr, double beta1,
                           double beta2, double eps, double wd, int64_t step, double max_norm,
-                          c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out);
+                          c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out, int64_t pads_epoch);
 void comm_shadow_refresh(int64_t gid, int64_t data_offset, torch::Tensor p16, int64_t lo, int64_t hi);
 void comm_all_to_all(int64_t gid, int64_t slot_offset, torch::Tensor out);
 int64_t comm_epoch(int64_t gid);
@@ -214,7 +217,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_reduce_scatter_sumsq", &tt::comm::comm_reduce_scatter_sumsq,
         "ZeRO-1 fp32 gradient reduce-scatter in place + published sums of squares");
   m.def("comm_adamw_allgather", &tt::comm::comm_adamw_allgather,
-        "ZeRO-1 clip + AdamW on the owned shard + fp32 all-gather by peer stores");
+        "ZeRO-1 clip + AdamW on the owned shard + fp32 all-gather by peer stores", py::arg("gid"),
+        py::arg("data_offset"), py::arg("grad_offset"), py::arg("p16"), py::arg("m"), py::arg("v"), py::arg("lo"),
+        py::arg("hi"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("wd"),
+        py::arg("step"), py::arg("max_norm"), py::arg("extra_sq") = py::none(), py::arg("norm_out") = py::none(),
+        py::arg("pads_epoch") = -1);
+  m.def("comm_reduce_scatter_bucket", &tt::comm::comm_reduce_scatter_bucket,
+        "one bucket of a reduce-scatter overlapped with the backward (sums of squares kept local)");
+  m.def("comm_publish_sumsq", &tt::comm::comm_publish_sumsq,
+        "publish the per-bucket sums of squares to every peer's pad; returns the epoch to wait for");
   m.def("comm_shadow_refresh", &tt::comm::comm_shadow_refresh, "wait for the all-gather; refresh bf16 shadow");
   m.def("comm_all_to_all", &tt::comm::comm_all_to_all, "equal-split all-to-all of a heap slot by peer loads");
   m.def("comm_epoch", &tt::comm::comm_epoch);

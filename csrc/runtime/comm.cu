@@ -120,8 +120,12 @@ __global__ void alltoall_kernel(PeerTable t, size_t slot_off, long long chunk_by
 // reduced shard split at `split` (elements < split: dense parameters; >= split:
 // expert parameters), reduced deterministically over blocks and stored into
 // pads[my_rank][0..1] of every peer before signalling epoch e_done.
+// sq_local != nullptr (bucketed reduce-scatter, overlapped with the backward): the block
+// sums go to sq_local[0..1] on this rank only, and no completion epoch is signalled;
+// publish_sumsq_kernel later publishes the total over all buckets.
 __global__ void rs_sumsq_kernel(PeerTable t, size_t grad_off, long long lo, long long hi, long long split,
-                                float scale, uint64_t e_start, uint64_t e_done, int* status, uint64_t timeout_ns) {
+                                float scale, uint64_t e_start, uint64_t e_done, int* status, uint64_t timeout_ns,
+                                float* sq_local) {
   if (blockIdx.x == 0 && threadIdx.x == 0) signal_peers(t, e_start);  // our grads are final (stream order)
   if (!block_wait_peers(t, e_start, status, timeout_ns)) return;
   float sd = 0.f, se = 0.f;
@@ -158,6 +162,11 @@ __global__ void rs_sumsq_kernel(PeerTable t, size_t grad_off, long long lo, long
       d += partial[2 * b];
       x += partial[2 * b + 1];
     }
+    if (sq_local != nullptr) {
+      sq_local[0] = d;
+      sq_local[1] = x;
+      return;
+    }
     for (int p = 0; p < t.world; ++p) {
       float* pad = pad_ptr(t, p, t.rank);
       pad[0] = d;
@@ -165,6 +174,23 @@ __global__ void rs_sumsq_kernel(PeerTable t, size_t grad_off, long long lo, long
     }
     signal_peers(t, e_done);
   });
+}
+
+// One thread: total the per-bucket sums of squares (fixed order), publish them into every
+// peer's pad and signal epoch e.
+__global__ void publish_sumsq_kernel(PeerTable t, const float* __restrict__ sq, int n_buckets, uint64_t e) {
+  if (threadIdx.x != 0) return;
+  float d = 0.f, x = 0.f;
+  for (int b = 0; b < n_buckets; ++b) {
+    d += sq[2 * b];
+    x += sq[2 * b + 1];
+  }
+  for (int p = 0; p < t.world; ++p) {
+    float* pad = pad_ptr(t, p, t.rank);
+    pad[0] = d;
+    pad[1] = x;
+  }
+  signal_peers(t, e);
 }
 
 struct AdamArgs {
@@ -551,8 +577,44 @@ void comm_reduce_scatter_sumsq(int64_t gid, int64_t grad_offset, int64_t lo, int
   rs_sumsq_kernel<<<grid, threads, 0, cur_stream()>>>(table(g), static_cast<size_t>(grad_offset), lo, hi, split,
                                                        static_cast<float>(scale), g.emulated ? 0ull : e0,
                                                        g.emulated ? 0ull : e1, device_status_ptr(g.device),
-                                                       timeout_ns());
+                                                       timeout_ns(), nullptr);
   TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// One bucket of a reduce-scatter that overlaps the backward: grad[lo:hi] = scale * sum over
+// ranks (in place), its sums of squares into sq_local (fp32 [2], this rank's memory).  The
+// grid is capped at max_blocks so the kernel shares the GPU with the backward's GEMMs.
+void comm_reduce_scatter_bucket(int64_t gid, int64_t grad_offset, int64_t lo, int64_t hi, int64_t split,
+                                double scale, torch::Tensor sq_local, int64_t max_blocks) {
+  Group& g = get(gid);
+  TT_CHECK(lo % 4 == 0 && hi % 4 == 0 && split % 4 == 0 && lo <= hi, "comm_rs: lo/hi/split must be multiples of 4");
+  TT_CHECK(grad_offset % 256 == 0 && grad_offset + hi * 4 <= static_cast<int64_t>(g.bytes), "comm_rs: bad region");
+  TT_CHECK(sq_local.is_cuda() && sq_local.scalar_type() == torch::kFloat32 && sq_local.numel() >= 2,
+           "comm_rs: sq_local fp32 [2]");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
+  const uint64_t e0 = next_epoch(g);
+  const int threads = 512;
+  const int grid = std::max(1, std::min<int>(grid_for(g.device, std::max<long long>(1, (hi - lo) / 4), threads),
+                                             static_cast<int>(max_blocks)));
+  rs_sumsq_kernel<<<grid, threads, 0, cur_stream()>>>(table(g), static_cast<size_t>(grad_offset), lo, hi, split,
+                                                       static_cast<float>(scale), g.emulated ? 0ull : e0, 0ull,
+                                                       device_status_ptr(g.device), timeout_ns(),
+                                                       sq_local.data_ptr<float>());
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
+// Publish the total of per-bucket sums of squares (fp32 [n_buckets, 2]) to every peer's pad;
+// returns the epoch the adamw_allgather calls of this step wait for.
+int64_t comm_publish_sumsq(int64_t gid, torch::Tensor sq) {
+  Group& g = get(gid);
+  TT_CHECK(sq.is_cuda() && sq.scalar_type() == torch::kFloat32 && sq.is_contiguous() && sq.numel() % 2 == 0,
+           "comm_publish_sumsq: fp32 [n, 2]");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
+  const uint64_t e = next_epoch(g);
+  publish_sumsq_kernel<<<1, 32, 0, cur_stream()>>>(table(g), sq.data_ptr<float>(), static_cast<int>(sq.numel() / 2),
+                                                  g.emulated ? 0ull : e);
+  TT_CUDA_CHECK(cudaGetLastError());
+  return static_cast<int64_t>(e);
 }
 
 // ZeRO-1: clip + AdamW on [lo, hi) + fp32 all-gather into every rank's buffer at data_offset.
@@ -560,7 +622,8 @@ void comm_reduce_scatter_sumsq(int64_t gid, int64_t grad_offset, int64_t lo, int
 void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset, c10::optional<torch::Tensor> p16,
                           torch::Tensor m, torch::Tensor v, int64_t lo, int64_t hi, double lr, double beta1,
                           double beta2, double eps, double wd, int64_t step, double max_norm,
-                          c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out) {
+                          c10::optional<torch::Tensor> extra_sq, c10::optional<torch::Tensor> norm_out,
+                          int64_t pads_epoch) {
   Group& g = get(gid);
   TT_CHECK(lo % 4 == 0 && hi % 4 == 0 && lo <= hi, "comm_adamw: lo/hi must be multiples of 4");
   TT_CHECK(m.scalar_type() == torch::kFloat32 && v.scalar_type() == torch::kFloat32 && m.numel() == hi - lo &&
@@ -593,8 +656,9 @@ void comm_adamw_allgather(int64_t gid, int64_t data_offset, int64_t grad_offset,
   a.bc2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
   a.max_norm = static_cast<float>(max_norm);
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(g.device));
-  // The pads were published with the reduce-scatter's second epoch (the current one).
-  const uint64_t e_pads = g.epoch;
+  // The pads were published with the reduce-scatter's second epoch (the current one), or,
+  // for the bucketed path, with the epoch comm_publish_sumsq returned (pads_epoch).
+  const uint64_t e_pads = pads_epoch >= 0 ? static_cast<uint64_t>(pads_epoch) : g.epoch;
   const uint64_t e_done = next_epoch(g);
   const int threads = 512;
   const int grid = grid_for(g.device, std::max<long long>(1, (hi - lo) / 4), threads);

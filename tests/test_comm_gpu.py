@@ -235,3 +235,65 @@ def test_two_rank_ipc_collectives_match_nccl():
         assert ar_err < 2e-2, (rank, ar_err)
         assert z_err < 1e-5, (rank, z_err)
         assert shadow_ok, rank
+
+
+@pytest.mark.parametrize("W", [2, 4, 8])
+def test_emulated_bucketed_zero1_step(W):
+    """The overlapped-reduce-scatter layout: buckets of the flat buffer, rank r owning the
+    r-th slice of every bucket (reduce per bucket with the sums of squares kept local, one
+    publish, AdamW per slice, full shadow refresh) == the fp32 reference update."""
+    from tinytron_b200.parallel.symm import SymmetricHeap
+
+    n = 64 * W * 37
+    split = 64 * 11 * W
+    bounds = [0, 64 * W * 5, 64 * W * 20, n]  # three buckets
+    buckets = list(zip(bounds[:-1], bounds[1:]))
+    lr, b1, b2, eps, wd, max_norm = 1e-2, 0.9, 0.95, 1e-8, 0.1, 0.5
+    heaps = SymmetricHeap.create_emulated(SymmetricHeap.bytes_needed((n, torch.float32), (n, torch.float32),
+                                                                     (n, torch.bfloat16)), W)
+    g0 = torch.Generator(device="cuda").manual_seed(2)
+    p0 = torch.randn(n, device="cuda", generator=g0)
+    bufs = []
+    for h in heaps:
+        data, grad, p16 = h.alloc(n, torch.float32), h.alloc(n, torch.float32), h.alloc(n, torch.bfloat16)
+        data.copy_(p0)
+        p16.copy_(p0)
+        bufs.append(dict(data=data, grad=grad, p16=p16, m=torch.zeros(n // W, device="cuda"),
+                         v=torch.zeros(n // W, device="cuda"), norm=torch.zeros(2, device="cuda"),
+                         sq=torch.zeros(len(buckets), 2, device="cuda")))
+
+    def my_slices(r):
+        out, off = [], 0
+        for lo, hi in buckets:
+            k = (hi - lo) // W
+            out.append(((lo + r * k, lo + (r + 1) * k), (off, off + k)))
+            off += k
+        return out
+
+    p_ref, m_ref, v_ref = p0.clone().double(), torch.zeros(n, device="cuda").double(), torch.zeros(n, device="cuda").double()
+    for step in (1, 2):
+        grads = [torch.randn(n, device="cuda", generator=g0) for _ in range(W)]
+        for b, gr in zip(bufs, grads):
+            b["grad"].copy_(gr)
+        for bi in range(len(buckets)):  # bucket by bucket, every rank (launch order = overlap order)
+            for r, (h, b) in enumerate(zip(heaps, bufs)):
+                (lo, hi), _ = my_slices(r)[bi]
+                h.reduce_scatter_bucket(b["grad"], lo, hi, split, 1.0 / W, b["sq"][bi])
+        pads = [h.publish_sumsq(b["sq"]) for h, b in zip(heaps, bufs)]
+        for r, (h, b) in enumerate(zip(heaps, bufs)):
+            for (lo, hi), (m0, m1) in my_slices(r):
+                h.adamw_allgather(b["data"], b["grad"], b["p16"], b["m"][m0:m1], b["v"][m0:m1], lo, hi, lr, (b1, b2),
+                                  eps, wd, step, max_norm, norm_out=b["norm"], pads_epoch=pads[r])
+        for h, b in zip(heaps, bufs):
+            h.shadow_refresh(b["data"], b["p16"], 0, 0)
+        torch.cuda.synchronize()
+        gbar = torch.stack(grads).double().mean(0)
+        norm = gbar.norm().item()
+        coef = min(max_norm / (norm + 1e-6), 1.0)
+        p_ref, m_ref, v_ref = _ref_adamw(p_ref, gbar * coef, m_ref, v_ref, lr, b1, b2, eps, wd, step)
+        for b in bufs:
+            assert abs(b["norm"][0].item() - norm) < 1e-4 * norm
+            assert (b["data"].double() - p_ref).abs().max().item() < 1e-5
+            assert torch.equal(b["p16"], b["data"].bfloat16())
+    for h in heaps:
+        h.close()

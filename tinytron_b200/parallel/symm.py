@@ -154,10 +154,22 @@ class SymmetricHeap:
     def adamw_allgather(self, data: torch.Tensor, grad: torch.Tensor, p16: torch.Tensor | None, m: torch.Tensor,
                         v: torch.Tensor, lo: int, hi: int, lr: float, betas, eps: float, wd: float, step: int,
                         max_norm: float, norm_out: torch.Tensor | None = None,
-                        extra_sq: torch.Tensor | None = None) -> None:
+                        extra_sq: torch.Tensor | None = None, pads_epoch: int = -1) -> None:
         _C().comm_adamw_allgather(self.gid, self.offset_of(data), self.offset_of(grad), p16, m, v, int(lo), int(hi),
                                   float(lr), float(betas[0]), float(betas[1]), float(eps), float(wd), int(step),
-                                  float(max_norm), extra_sq, norm_out)
+                                  float(max_norm), extra_sq, norm_out, int(pads_epoch))
+
+    def reduce_scatter_bucket(self, grad: torch.Tensor, lo: int, hi: int, split: int, scale: float,
+                              sq_local: torch.Tensor, max_blocks: int = 32) -> None:
+        """One bucket of an overlapped reduce-scatter: grad[lo:hi] = scale * sum over ranks
+        (in place); the slice's sums of squares go to ``sq_local`` (fp32 [2]) on this rank."""
+        _C().comm_reduce_scatter_bucket(self.gid, self.offset_of(grad), int(lo), int(hi), int(split), float(scale),
+                                        sq_local, int(max_blocks))
+
+    def publish_sumsq(self, sq: torch.Tensor) -> int:
+        """Publish the total of per-bucket sums of squares ([n, 2]) to every peer; returns
+        the epoch the update kernels must wait for."""
+        return int(_C().comm_publish_sumsq(self.gid, sq))
 
     def all_to_all(self, slot: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """out[c] = chunk ``rank`` of rank c's ``slot`` (both [world, ...], equal chunks)."""

@@ -23,6 +23,12 @@ Two implementations:
   coefficient from the pads, applies AdamW to the owned shard and stores the new
   fp32 shard straight into every peer's parameter buffer; a third waits for the
   peers' stores and refreshes the local bf16 shadow of their shards.
+
+  With ``bucket_bytes`` (``--grad_bucket_mb``, DP only) the reduce-scatter overlaps the
+  last micro-step's backward: the buffer is cut into buckets of whole parameters in
+  reverse order, every rank owns one slice of every bucket, and each bucket's
+  reduce-scatter kernel starts on a side stream (a few CTAs, next to the GEMMs) as soon
+  as the wgrad epilogues of its last parameter have run.
 """
 from __future__ import annotations
 
@@ -137,7 +143,7 @@ class FlatZeRO1:
     parameters."""
 
     def __init__(self, flat, dp_group=None, sp_group=None, lr=1e-3, betas=(0.9, 0.95), eps=1e-8,
-                 weight_decay=0.0):
+                 weight_decay=0.0, bucket_bytes: int = 0):
         self.flat = flat
         self.dp_group = dp_group
         self.sp_group = sp_group
@@ -165,11 +171,108 @@ class FlatZeRO1:
                        and (self.sp == 1 or flat.dense_numel == flat.numel) and self.shard % 4 == 0)
         self._max_norm = 0.0
         self._normc = torch.zeros(2, device=dev)
+        self.buckets = None
+        if self.native and bucket_bytes > 0 and self.sp == 1 and 16 % self.dp == 0 and dev.type == "cuda":
+            self._init_buckets(int(bucket_bytes))
+
+    # ---------------------------------------------------------------- overlapped reduce-scatter
+    def _init_buckets(self, bucket_bytes: int) -> None:
+        """Buckets of whole parameters in reverse buffer order (the order their gradients
+        become final in the backward).  Ownership is interleaved: rank r owns the r-th of
+        ``dp`` equal slices of EVERY bucket, so each bucket's reduce-scatter spreads over all
+        ranks and can start as soon as that bucket is final everywhere."""
+        flat = self.flat
+        bounds = [flat.numel]
+        for i in range(len(flat.params) - 1, 0, -1):
+            if (bounds[-1] - flat.offsets[i]) * 4 >= bucket_bytes:
+                bounds.append(flat.offsets[i])
+        if bounds[-1] != 0:
+            bounds.append(0)
+        self.buckets = [(bounds[i + 1], bounds[i]) for i in range(len(bounds) - 1)]  # reverse buffer order
+        self.slices, self.state_off = [], []
+        off = 0
+        for lo, hi in self.buckets:
+            n = (hi - lo) // self.dp
+            assert (hi - lo) % (4 * self.dp) == 0, (lo, hi, self.dp)
+            self.slices.append((lo + self.dp_rank * n, lo + (self.dp_rank + 1) * n))
+            self.state_off.append((off, off + n))
+            off += n
+        assert off == self.shard
+        self._bucket_of = {}
+        self._bucket_params = [[] for _ in self.buckets]
+        for p, o in zip(flat.params, flat.offsets):
+            b = next(i for i, (lo, hi) in enumerate(self.buckets) if lo <= o < hi)
+            self._bucket_of[id(p)] = b
+            self._bucket_params[b].append(p)
+        self._expected = None     # notifications per parameter in one micro-step (learned)
+        self._counts = {}
+        self._armed = False
+        self._launched = 0
+        self._pads_epoch = -1
+        self._sq = torch.zeros(len(self.buckets), 2, device=flat.device)
+        self.comm_stream = torch.cuda.Stream(device=flat.device)
+        self.lo, self.hi = 0, 0  # the owned elements are self.slices, not one range
+        for p in flat.params:
+            p.__dict__["_tt_grad_ready"] = self._on_grad_ready
+
+    def begin_micro_step(self, last: bool) -> None:
+        """Trainer hook before each micro-step's forward.  The last micro-step of a step
+        launches each bucket's reduce-scatter as soon as its gradients are final; the
+        others count the gradient notifications so the last one knows when that is."""
+        if self.buckets is None:
+            return
+        if last and self._counts:
+            self._expected = dict(self._counts)
+        self._armed = last and self._expected is not None
+        self._counts = {}
+        self._launched = 0
+        self._ready = [False] * len(self.buckets)
+
+    def _on_grad_ready(self, p) -> None:
+        k = id(p)
+        self._counts[k] = self._counts.get(k, 0) + 1
+        if not self._armed:
+            return
+        b = self._bucket_of[k]
+        if all(self._counts.get(id(q), 0) >= self._expected.get(id(q), 1) for q in self._bucket_params[b]):
+            self._ready[b] = True
+            while self._launched < len(self.buckets) and self._ready[self._launched]:
+                self._launch_bucket(self._launched, overlap=True)
+                self._launched += 1
+
+    def _launch_bucket(self, b: int, overlap: bool) -> None:
+        lo, hi = self.slices[b]
+        heap = self.flat.heap
+        if not overlap:
+            heap.reduce_scatter_bucket(self.flat.grad, lo, hi, self.flat.dense_numel, 1.0 / self.dp, self._sq[b],
+                                       max_blocks=1 << 30)
+            return
+        main = torch.cuda.current_stream(self.flat.device)
+        self.comm_stream.wait_stream(main)  # this bucket's gradients are written (stream order)
+        with torch.cuda.stream(self.comm_stream):
+            heap.reduce_scatter_bucket(self.flat.grad, lo, hi, self.flat.dense_numel, 1.0 / self.dp, self._sq[b],
+                                       max_blocks=32)
+
+    def _finish_buckets(self) -> None:
+        main = torch.cuda.current_stream(self.flat.device)
+        if self._armed:
+            while self._launched < len(self.buckets):  # anything the notifications did not cover
+                self._launch_bucket(self._launched, overlap=True)
+                self._launched += 1
+            main.wait_stream(self.comm_stream)
+        else:
+            for b in range(len(self.buckets)):
+                self._launch_bucket(b, overlap=False)
+        self._armed = False
+        self._pads_epoch = self.flat.heap.publish_sumsq(self._sq)
 
     # ---------------------------------------------------------------- gradient sync
     @torch.no_grad()
     def reduce_gradients(self):
         g = self.flat.grad
+        if self.buckets is not None:
+            self._finish_buckets()
+            return
         if self.sp > 1 and self.flat.dense_numel > 0:
             dist.all_reduce(g[:self.flat.dense_numel], op=dist.ReduceOp.SUM, group=self.sp_group)
         if self.native:
@@ -223,6 +326,17 @@ class FlatZeRO1:
         b1, b2 = grp["betas"]
         self.step_count += 1
         lo, hi = self.lo, self.hi
+        if self.buckets is not None:
+            heap = self.flat.heap
+            for (slo, shi), (m0, m1) in zip(self.slices, self.state_off):
+                heap.adamw_allgather(self.flat.data, self.flat.grad, self.flat.bf16, self.exp_avg[m0:m1],
+                                     self.exp_avg_sq[m0:m1], slo, shi, lr, (b1, b2), grp["eps"], grp["weight_decay"],
+                                     self.step_count, self._max_norm, norm_out=self._normc,
+                                     pads_epoch=self._pads_epoch)
+            if self.flat.bf16 is not None:  # waits for every peer's stores, then all shadows
+                heap.shadow_refresh(self.flat.data, self.flat.bf16, 0, 0)
+            self.flat.mark_shadows_fresh()
+            return
         if self.native:
             heap = self.flat.heap
             heap.adamw_allgather(self.flat.data, self.flat.grad, self.flat.bf16, self.exp_avg, self.exp_avg_sq, lo, hi,
@@ -268,13 +382,16 @@ class FlatZeRO1:
         self.flat.zero_grad()
 
     # ---------------------------------------------------------------- state
+    def _owned(self) -> list:
+        return [list(x) for x in self.slices] if self.buckets is not None else [[self.lo, self.hi]]
+
     def state_dict(self):
         return {"step": self.step_count, "exp_avg": self.exp_avg, "exp_avg_sq": self.exp_avg_sq,
-                "param_groups": [dict(g) for g in self.param_groups], "shard": [self.lo, self.hi],
-                "numel": self.flat.numel, "format": "tinytron_b200.flat_zero1.v1"}
+                "param_groups": [dict(g) for g in self.param_groups], "shard": self._owned(),
+                "numel": self.flat.numel, "format": "tinytron_b200.flat_zero1.v2"}
 
     def load_state_dict(self, sd):
-        if sd.get("numel") != self.flat.numel or list(sd.get("shard", [])) != [self.lo, self.hi]:
+        if sd.get("numel") != self.flat.numel or [list(x) for x in sd.get("shard", [])] != self._owned():
             raise ValueError("optimizer state layout does not match the current flat layout")
         self.step_count = int(sd["step"])
         self.exp_avg.copy_(sd["exp_avg"])

@@ -1,5 +1,5 @@
 """Training CLI (reference: tinytron/training/arguments.py:8-120): same flag names,
-groups and defaults, plus a few B200 extensions (``--comm_impl``, ``--rms_norm_eps``,
+groups and defaults, plus a few B200 extensions (``--comm_impl``, ``--grad_bucket_mb``, ``--rms_norm_eps``,
 ``--rope_theta``, ``--model_preset``)."""
 from __future__ import annotations
 
@@ -96,6 +96,9 @@ def _parallel(p):
     g.add_argument("--ddp_find_unused_parameters", action="store_true")
     g.add_argument("--ddp_gradient_as_bucket_view", action=argparse.BooleanOptionalAction, default=True)
     g.add_argument("--use_distributed_optimizer", action=argparse.BooleanOptionalAction, default=True)
+    g.add_argument("--grad_bucket_mb", type=int, default=256,
+                   help="native ZeRO-1 (DP, no SEP): fp32 gradient bucket size whose reduce-scatter overlaps "
+                        "the last micro-step's backward; 0 reduce-scatters everything after the backward")
     g.add_argument("--comm_impl", type=str, default="native", choices=["native", "nccl"],
                    help="native: ZeRO-1, EP and Ulysses collectives as NVLink peer loads/stores on symmetric "
                         "heaps (one node); nccl: every collective on NCCL")

@@ -89,6 +89,8 @@ class ParallelConfig:
     # ext: collective implementation of the hot paths: "native" (peer loads/stores on symmetric
     # heaps inside one node) or "nccl".
     comm_impl: str = "native"
+    # ext: fp32 gradient bucket (MB) of the reduce-scatter overlapped with the backward (0: off).
+    grad_bucket_mb: int = 256
 
 
 @dataclass(frozen=True)
@@ -144,7 +146,7 @@ def build_config(args: argparse.Namespace) -> Config:
         ddp_find_unused_parameters=args.ddp_find_unused_parameters,
         ddp_gradient_as_bucket_view=args.ddp_gradient_as_bucket_view,
         use_distributed_optimizer=args.use_distributed_optimizer,
-        comm_impl=getattr(args, "comm_impl", "native"),
+        comm_impl=getattr(args, "comm_impl", "native"), grad_bucket_mb=getattr(args, "grad_bucket_mb", 256),
     )
     model_cfg = build_model_config(args, seed=args.seed)
     cfg = Config(logging=logging_cfg, seed=seed_cfg, data=data_cfg, train=train_cfg, optim=optim_cfg,

@@ -180,7 +180,8 @@ class Trainer:
             shard = config.parallel.use_distributed_optimizer
             self.optimizer = FlatZeRO1(self.flat, dp_group=self.dp_group if shard else None, sp_group=self.sp_group,
                                        lr=o.max_lr, betas=(o.adam_beta1, o.adam_beta2), eps=o.adam_eps,
-                                       weight_decay=o.weight_decay)
+                                       weight_decay=o.weight_decay,
+                                       bucket_bytes=max(0, config.parallel.grad_bucket_mb) << 20)
             self.raw_optimizer = self.optimizer
             self._replicated_dp = (not shard) and self.dp_world_size > 1
             return
@@ -351,7 +352,11 @@ class Trainer:
         self.flat.zero_grad()
         loss_accum = torch.zeros((), device=self.device)
         valid_accum = torch.zeros((), device=self.device, dtype=torch.long)
-        for micro in range(self.training_info["grad_accum_steps"]):
+        ga = self.training_info["grad_accum_steps"]
+        begin = getattr(self.optimizer, "begin_micro_step", None)
+        for micro in range(ga):
+            if begin is not None:  # overlapped reduce-scatter: armed for the last micro-step
+                begin(micro == ga - 1)
             batch = self._next_train_batch()
             ll, v = self._one_training_micro_step(config, micro, batch)
             loss_accum += ll
