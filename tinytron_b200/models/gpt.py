@@ -13,6 +13,8 @@ the return value is ``(logits, loss + aux_loss, logging_loss)`` like the referen
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 import torch.nn as nn
@@ -70,6 +72,9 @@ class GPT(nn.Module):
         if config.tied_lm_head:
             self.lm_head.weight = self.wte.weight
         self.loss_fn = CrossEntropyLoss()
+        # TT_LM_HEAD_CHUNK_ROWS=n: LM head + CE in chunks of n rows recomputed in the backward
+        # (no [tokens, vocab] logits buffer); 0 keeps the single fused pass (fastest).
+        self.lm_head_chunk_rows = int(os.environ.get("TT_LM_HEAD_CHUNK_ROWS", "0") or 0)
         self.expert_loss_fn = (
             ExpertLoadBalancingLoss(config.num_experts, config.num_experts_per_tok, alpha=config.moe_balance_loss_weight)
             if config.use_moe and config.moe_balance_loss_weight > 0.0 else None)
@@ -100,7 +105,8 @@ class GPT(nn.Module):
                 return ops.linear(h, self.lm_head.weight)
             return ops.lm_logits(h, self.lm_head.weight)
         valid = targets != self.loss_fn.ignore_index
-        loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index)
+        loss_sum = ops.lm_head_ce_sum(h, self.lm_head.weight, targets, self.loss_fn.ignore_index,
+                                      chunk_rows=self.lm_head_chunk_rows)
         loss, logging_loss, total_aux = self._reduce_step_stats(loss_sum, valid.sum(), aux_stats)
         logits = None
         if return_logits:

@@ -133,9 +133,14 @@ def embedding(idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
     return F.embedding(idx, weight)
 
 
-def lm_head_ce_sum(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100):
-    """Sum of token cross-entropies over valid targets of logits = h @ weight^T."""
+def lm_head_ce_sum(h: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
+                   chunk_rows: int = 0):
+    """Sum of token cross-entropies over valid targets of logits = h @ weight^T.
+    ``chunk_rows`` > 0 (CUDA): no full logits buffer; chunks of rows are recomputed in
+    the backward (one extra LM-head GEMM)."""
     if h.is_cuda:
+        if chunk_rows > 0:
+            return _cuda_fn().ChunkedLMHeadCrossEntropyFn.apply(h, weight, targets, ignore_index, int(chunk_rows))
         return _cuda_fn().LMHeadCrossEntropyFn.apply(h, weight, targets, ignore_index)
     logits = F.linear(h, weight)
     per = F.cross_entropy(logits.view(-1, logits.size(-1)).float(), targets.reshape(-1), ignore_index=ignore_index,

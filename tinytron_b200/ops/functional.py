@@ -472,6 +472,59 @@ class LMHeadCrossEntropyFn(torch.autograd.Function):
         return dh, gw, None, None
 
 
+class ChunkedLMHeadCrossEntropyFn(torch.autograd.Function):
+    """Sum over valid tokens of CE(h @ W^T, targets) without a full logits buffer.
+
+    Rows are processed in chunks of ``rows``: the forward computes each chunk's logits
+    into one reused [rows, V] bf16 buffer and keeps only the per-row loss; the backward
+    recomputes the chunk's logits, the CE kernel turns them into (softmax - onehot) in
+    place, and the two GEMMs (scaled by the incoming loss gradient read on the device)
+    accumulate dh and dW.  Costs one extra LM-head GEMM per micro-step and saves the
+    [tokens, V] logits buffer (1.65 GB at 16 K tokens x 50 K vocab)."""
+
+    @staticmethod
+    def forward(ctx, h, weight, targets, ignore_index, rows):
+        h2d = _bf16(h.reshape(-1, h.shape[-1]))
+        w16 = bf16_of(weight)
+        N, V = h2d.shape[0], w16.shape[0]
+        t = targets.reshape(-1).contiguous()
+        loss_rows = torch.empty(N, device=h.device, dtype=torch.float32)
+        buf = torch.empty(min(rows, N), V, device=h.device, dtype=torch.bfloat16)
+        for r0 in range(0, N, rows):
+            r1 = min(N, r0 + rows)
+            lg = buf[:r1 - r0]
+            C().gemm(h2d[r0:r1], w16, lg, False, False, False, 1.0, None, 0)
+            C().cross_entropy_fwd(lg, t[r0:r1], loss_rows[r0:r1], None, ignore_index, False)
+        ctx.save_for_backward(h2d, w16, t)
+        ctx.weight, ctx.h_shape, ctx.h_dtype = weight, h.shape, h.dtype
+        ctx.ignore_index, ctx.rows = ignore_index, rows
+        return loss_rows.sum()
+
+    @staticmethod
+    def backward(ctx, g_loss):
+        h2d, w16, t = ctx.saved_tensors
+        rows = ctx.rows
+        N, V = h2d.shape[0], w16.shape[0]
+        alpha = g_loss.detach().reshape(1).float().contiguous()
+        dh = torch.empty(N, h2d.shape[1], device=h2d.device, dtype=torch.bfloat16)
+        buf = torch.empty(min(rows, N), V, device=h2d.device, dtype=torch.bfloat16)
+        scratch = torch.empty(min(rows, N), device=h2d.device, dtype=torch.float32)
+        gw_total = None
+        for r0 in range(0, N, rows):
+            r1 = min(N, r0 + rows)
+            lg = buf[:r1 - r0]
+            C().gemm(h2d[r0:r1], w16, lg, False, False, False, 1.0, None, 0)
+            C().cross_entropy_fwd(lg, t[r0:r1], scratch[:r1 - r0], None, ctx.ignore_index, True)
+            C().gemm(lg, w16, dh[r0:r1], False, True, False, 1.0, alpha, 0)
+            (gw,) = weight_grads([ctx.weight], lg, h2d[r0:r1], alpha_t=alpha)
+            if gw is not None:
+                gw_total = gw if gw_total is None else gw_total.add_(gw)
+        dh = dh.view(ctx.h_shape)
+        if ctx.h_dtype != torch.bfloat16:
+            dh = dh.to(ctx.h_dtype)
+        return dh, gw_total, None, None, None
+
+
 class LMHeadTokenLogProbFn(torch.autograd.Function):
     """Per-token log-probabilities -CE(h @ W^T, targets) (fp32 [N]).
 
