@@ -259,7 +259,7 @@ def run(args, impl: str):
         from tinytron_b200.training.trainer import Trainer
 
         _ext.load()
-        cfg = build_config(parse_args(_train_argv(world, total_steps, log_dir)))
+        cfg = build_config(parse_args(_train_argv(world, total_steps, log_dir) + args.train_args.split()))
         trainer = Trainer(cfg)
         own_marker = "tt::"
     trainer.model.train()
@@ -465,6 +465,8 @@ def main():
     ap.add_argument("--config", choices=["dense", "moe", "longctx", "decode"], default="dense",
                     help="dense: BASELINE config 2 (headline); moe: config 3 (SEP = #GPUs); longctx: config 4 "
                          "(Muon, SEP = #GPUs, seq 32768); decode: config 5")
+    ap.add_argument("--train-args", type=str, default="",
+                    help="extra trainer flags for this framework's arm (A/B runs, e.g. '--grad_bucket_mb 0')")
     ap.add_argument("--decode-steps", type=int, default=512)
     ap.add_argument("--page-size", type=int, default=16, help="decode: KV page size (0 = contiguous cache)")
     args = ap.parse_args()
