@@ -87,6 +87,9 @@ __global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_b
 // ROWS rows per CTA so dw partials are per CTA (deterministic two-stage reduction).
 constexpr int BWD_ROWS = 16;
 
+// Rows are software-pipelined: the loads of row rr + 1 (x, gh and the residual gradient)
+// are issued before row rr's block reduction, so each CTA keeps two rows of traffic in
+// flight instead of stalling on every row's reduction.  Arithmetic order is unchanged.
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const float* __restrict__ x,
                                    const float* __restrict__ rstd, const float* __restrict__ w,
                                    const float* __restrict__ g_res, float* __restrict__ gx,
@@ -98,16 +101,21 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const f
   float dw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
   if (active) load8_f32(w + c, wv);
   const int row0 = blockIdx.x * BWD_ROWS;
-  for (int rr = 0; rr < BWD_ROWS; ++rr) {
+  const int rows = min(BWD_ROWS, M - row0);
+  float xv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, g[8] = {0, 0, 0, 0, 0, 0, 0, 0}, res[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  auto fetch = [&](int row, float (&xa)[8], float (&ga)[8], float (&ra)[8]) {
+    const size_t off = static_cast<size_t>(row) * D + c;
+    load8_f32(x + off, xa);
+    load8_bf16(gh + off, ga);
+    if (g_res != nullptr) load8_f32(g_res + off, ra);
+  };
+  if (active && rows > 0) fetch(row0, xv, g, res);
+  for (int rr = 0; rr < rows; ++rr) {  // `rows` is uniform across the CTA
     const int row = row0 + rr;
-    if (row >= M) break;  // uniform across the CTA
     const size_t off = static_cast<size_t>(row) * D + c;
     const float r = rstd[row];
-    float xv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     float dot = 0.0f;
     if (active) {
-      load8_f32(x + off, xv);
-      load8_bf16(gh + off, g);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const float xh = xv[i] * r;
@@ -117,15 +125,21 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const f
         xv[i] = xh;
       }
     }
+    float xn[8] = {0, 0, 0, 0, 0, 0, 0, 0}, gn[8] = {0, 0, 0, 0, 0, 0, 0, 0}, rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (active && rr + 1 < rows) fetch(row + 1, xn, gn, rn);  // in flight during the reduction
     const float mean_dot = block_sum(dot, red) / static_cast<float>(D);
     if (active) {
       float o[8];
-      float res[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (g_res != nullptr) load8_f32(g_res + off, res);
 #pragma unroll
       for (int i = 0; i < 8; ++i) o[i] = res[i] + r * (g[i] - xv[i] * mean_dot);
       if (gx != nullptr) store8_f32(gx + off, o);
       if (g_delta != nullptr) store8_bf16(g_delta + off, o);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      xv[i] = xn[i];
+      g[i] = gn[i];
+      res[i] = rn[i];
     }
   }
   if (active && dw_part != nullptr) store8_f32(dw_part + static_cast<size_t>(blockIdx.x) * D + c, dw);
