@@ -248,3 +248,40 @@ def test_muon_batched_step_matches_cpu():
     for a, b, t0 in zip(res["cpu"], res["cuda"], init):
         da, db = a - t0, b - t0
         assert ((da - db).norm() / da.norm()).item() < 3e-2
+
+
+def _muon_moe_dp_rank(rank, world, port, tmp, out):
+    import os
+
+    os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                      MASTER_PORT=str(port))
+    torch.set_num_threads(1)
+    from tinytron_b200.training import build_config, parse_args
+    from tinytron_b200.training.trainer import Trainer
+
+    argv = ["--use_mock_data", "--deterministic", "--mock_data_num_samples", "16", "--log_dir", tmp,
+            "--total_batch_size", str(2 * 32 * 2), "--batch_size", "2", "--seq_len", "32", "--max_steps", "4",
+            "--warmup_steps", "1", "--max_lr", "2e-2", "--min_lr", "2e-3", "--optimizer", "muon",
+            "--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--vocab_size", "128", "--block_size", "32", "--backend", "gloo",
+            "--use_moe", "--num_experts", "4", "--num_experts_per_tok", "2", "--moe_intermediate_size", "32"]
+    tr = Trainer(build_config(parse_args(argv)))
+    for s in range(2):
+        tr.train_step(s)
+    owned = sum(len(g["params"]) for g in tr.raw_optimizer.param_groups)
+    torch.save({"data": tr.flat.data.clone(), "owned": owned}, os.path.join(out, f"r{rank}.pt"))
+    tr.close()
+
+
+def test_trainer_with_distributed_muon_moe_dp2_gloo(tmp_path):
+    """DP=2 with MoE: dense and expert matrices are split between the two replicas, and
+    the broadcasts leave both replicas with identical parameters."""
+    import os
+
+    import torch.multiprocessing as mp
+    from test_rl_trainer import _port
+
+    mp.spawn(_muon_moe_dp_rank, args=(2, _port(), str(tmp_path / "logs"), str(tmp_path)), nprocs=2, join=True)
+    r0, r1 = (torch.load(os.path.join(tmp_path, f"r{i}.pt")) for i in range(2))
+    assert torch.equal(r0["data"], r1["data"])
+    assert r0["owned"] > 0 and r1["owned"] > 0
