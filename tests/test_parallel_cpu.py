@@ -165,3 +165,22 @@ def test_dp2_zero1_matches_single_rank_adamw():
     for n, p in m.named_parameters():
         for r in range(2):
             assert torch.allclose(res[r][n], p.detach(), atol=2e-5, rtol=1e-4), (n, r)
+
+
+def test_grad_bucket_plan_tiles_buffer_and_interleaves_ownership():
+    from tinytron_b200.parallel.zero1 import plan_grad_buckets
+
+    offsets = [0, 64 * 10, 64 * 500, 64 * 900, 64 * 2000, 64 * 2100]
+    numel = 64 * 2400
+    for dp in (1, 2, 4, 8, 16):
+        per_rank = []
+        for r in range(dp):
+            buckets, slices, state = plan_grad_buckets(offsets, numel, 64 * 700 * 4, dp, r)
+            assert buckets[0][1] == numel and buckets[-1][0] == 0  # reverse order, tiles [0, numel)
+            assert all(buckets[i][0] == buckets[i + 1][1] for i in range(len(buckets) - 1))
+            assert all(lo in offsets or lo == 0 for lo, _ in buckets)  # whole parameters
+            assert state[-1][1] == numel // dp and all(s1 - s0 == hi - lo for (s0, s1), (lo, hi) in zip(state, slices))
+            per_rank.append(slices)
+        cover = sorted(sl for sls in per_rank for sl in sls)  # the ranks' slices tile the buffer
+        assert cover[0][0] == 0 and cover[-1][1] == numel
+        assert all(cover[i][1] == cover[i + 1][0] for i in range(len(cover) - 1))

@@ -134,6 +134,31 @@ def partition_tensors(tensor_dict, ranks_map=None, num_parts=None, verbose=False
 
 
 # ============================================================================ fast flat path
+def plan_grad_buckets(offsets, numel: int, bucket_bytes: int, dp: int, dp_rank: int):
+    """Buckets of whole parameters for the overlapped reduce-scatter, in REVERSE buffer
+    order (the order gradients become final), each at least ``bucket_bytes`` of fp32
+    gradients except possibly the last; they tile [0, numel).  Returns (buckets,
+    this rank's slice of each bucket, the slice's offsets in the rank's optimizer state).
+    Every bucket length is a multiple of 4 * dp (parameter offsets are multiples of 64
+    and dp divides 16), so every slice is float4-aligned."""
+    bounds = [numel]
+    for o in sorted(offsets, reverse=True):
+        if o > 0 and (bounds[-1] - o) * 4 >= bucket_bytes:
+            bounds.append(o)
+    if bounds[-1] != 0:
+        bounds.append(0)
+    buckets = [(bounds[i + 1], bounds[i]) for i in range(len(bounds) - 1)]
+    slices, state_off, off = [], [], 0
+    for lo, hi in buckets:
+        if (hi - lo) % (4 * dp):
+            raise ValueError(f"bucket [{lo}, {hi}) cannot be split into {dp} float4-aligned slices")
+        n = (hi - lo) // dp
+        slices.append((lo + dp_rank * n, lo + (dp_rank + 1) * n))
+        state_off.append((off, off + n))
+        off += n
+    return buckets, slices, state_off
+
+
 class FlatZeRO1:
     """Gradient sync + clip + fused AdamW + parameter all-gather over FlatParams.
 
@@ -182,22 +207,9 @@ class FlatZeRO1:
         ``dp`` equal slices of EVERY bucket, so each bucket's reduce-scatter spreads over all
         ranks and can start as soon as that bucket is final everywhere."""
         flat = self.flat
-        bounds = [flat.numel]
-        for i in range(len(flat.params) - 1, 0, -1):
-            if (bounds[-1] - flat.offsets[i]) * 4 >= bucket_bytes:
-                bounds.append(flat.offsets[i])
-        if bounds[-1] != 0:
-            bounds.append(0)
-        self.buckets = [(bounds[i + 1], bounds[i]) for i in range(len(bounds) - 1)]  # reverse buffer order
-        self.slices, self.state_off = [], []
-        off = 0
-        for lo, hi in self.buckets:
-            n = (hi - lo) // self.dp
-            assert (hi - lo) % (4 * self.dp) == 0, (lo, hi, self.dp)
-            self.slices.append((lo + self.dp_rank * n, lo + (self.dp_rank + 1) * n))
-            self.state_off.append((off, off + n))
-            off += n
-        assert off == self.shard
+        self.buckets, self.slices, self.state_off = plan_grad_buckets(flat.offsets, flat.numel, bucket_bytes,
+                                                                      self.dp, self.dp_rank)
+        assert self.state_off[-1][1] == self.shard
         self._bucket_of = {}
         self._bucket_params = [[] for _ in self.buckets]
         for p, o in zip(flat.params, flat.offsets):
