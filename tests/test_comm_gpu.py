@@ -293,7 +293,11 @@ def test_emulated_bucketed_zero1_step(W):
         p_ref, m_ref, v_ref = _ref_adamw(p_ref, gbar * coef, m_ref, v_ref, lr, b1, b2, eps, wd, step)
         for b in bufs:
             assert abs(b["norm"][0].item() - norm) < 1e-4 * norm
-            assert (b["data"].double() - p_ref).abs().max().item() < 1e-5
+            # fp32 AdamW against the fp64 reference: elements whose gradient is near eps
+            # differ by a few 1e-5 after two steps; a wrong slice or state offset is O(lr)
+            assert (b["data"].double() - p_ref).abs().max().item() < 5e-5
             assert torch.equal(b["p16"], b["data"].bfloat16())
+        for b in bufs[1:]:
+            assert torch.equal(b["data"], bufs[0]["data"])  # every rank holds the same parameters
     for h in heaps:
         h.close()

@@ -334,9 +334,36 @@ def _case_muon_torch(layers: int = 16, H: int = 2048, kv: int = 256, I: int = 55
     return run, (lambda: None)
 
 
+def _case_norm(M: int = 16384, D: int = 2048):
+    """Fused residual-add + RMSNorm forward and backward of one dense-1.3B micro-batch
+    (M tokens, fp32 residual stream); 670 MB of algorithmic traffic per iteration."""
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(M, D, device="cuda", generator=g)
+    delta = torch.randn(M, D, device="cuda", generator=g).bfloat16()
+    w = torch.rand(D, device="cuda", generator=g) + 0.5
+    x_out = torch.empty_like(x)
+    h = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    rstd = torch.empty(M, device="cuda")
+    gh = torch.randn(M, D, device="cuda", generator=g).bfloat16()
+    gres = torch.randn(M, D, device="cuda", generator=g)
+    gx = torch.empty_like(x)
+    gd = torch.empty(M, D, device="cuda", dtype=torch.bfloat16)
+    dw = torch.zeros(D, device="cuda")
+    scratch = torch.empty(C.rmsnorm_bwd_scratch_numel(M, D), device="cuda")
+
+    def run():
+        C.add_rmsnorm_fwd(x, delta, w, x_out, h, rstd, 1e-5)
+        C.rmsnorm_bwd(gh, x_out, rstd, w, gres, gx, gd, dw, True, scratch)
+
+    return run, check_status
+
+
 KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
                 "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "muon": _case_muon,
-                "muon_torch": _case_muon_torch}
+                "muon_torch": _case_muon_torch, "norm": _case_norm}
 
 
 def bench_case(name: str, iters: int, warmup: int) -> list[dict]:
