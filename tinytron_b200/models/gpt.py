@@ -126,8 +126,10 @@ class GPT(nn.Module):
         group = parallel_state._DP_SP_GROUP
         world = parallel_state.get_dp_sp_world_size()
         me = parallel_state.get_dp_sp_rank()
-        sp_ranks = parallel_state.get_sep_ranks() if group is not None else [0]
-        sp_idx = torch.tensor(sp_ranks, device=loss_sum.device)
+        # the SEP group is a contiguous block of ranks (parallel_state's layout): a slice, so
+        # no index tensor is built (a host-to-device copy would synchronise every micro-step)
+        sp_ranks = parallel_state.get_sep_ranks() if group is not None else [me]
+        sp_idx = slice(sp_ranks[0], sp_ranks[-1] + 1)
         E = self.config.num_experts if aux_stats else 0
         n_layers = len(aux_stats) if aux_stats else 0
         with torch.no_grad():
