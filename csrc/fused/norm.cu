@@ -8,6 +8,7 @@
 // backward: g = g_x_out + rstd * (w*gh - xhat * mean(w*gh*xhat));   gx = g (fp32),
 //           g_delta = bf16(g);  dw partial sums per row-group, reduced deterministically.
 #include "common/host_utils.h"
+#include <cstdlib>
 #include "common/ptx.cuh"
 #include "fused/rmsnorm_bwd_noalloc.h"
 
@@ -145,6 +146,52 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const f
   if (active && dw_part != nullptr) store8_f32(dw_part + static_cast<size_t>(blockIdx.x) * D + c, dw);
 }
 
+// One row after another (no prefetch): fewer registers (61 vs 88), so four CTAs fit per
+// SM instead of two.  TT_NORM_BWD_VARIANT selects it (0) or the prefetching kernel (1).
+__global__ void rmsnorm_bwd_serial_kernel(const __nv_bfloat16* __restrict__ gh, const float* __restrict__ x,
+                                   const float* __restrict__ rstd, const float* __restrict__ w,
+                                   const float* __restrict__ g_res, float* __restrict__ gx,
+                                   __nv_bfloat16* __restrict__ g_delta, float* __restrict__ dw_part, int M, int D) {
+  __shared__ float red[32];
+  const int c = threadIdx.x * EPT;
+  const bool active = c < D;
+  float wv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float dw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (active) load8_f32(w + c, wv);
+  const int row0 = blockIdx.x * BWD_ROWS;
+  for (int rr = 0; rr < BWD_ROWS; ++rr) {
+    const int row = row0 + rr;
+    if (row >= M) break;  // uniform across the CTA
+    const size_t off = static_cast<size_t>(row) * D + c;
+    const float r = rstd[row];
+    float xv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, g[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    float dot = 0.0f;
+    if (active) {
+      load8_f32(x + off, xv);
+      load8_bf16(gh + off, g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float xh = xv[i] * r;
+        dw[i] += g[i] * xh;
+        g[i] *= wv[i];
+        dot += g[i] * xh;
+        xv[i] = xh;
+      }
+    }
+    const float mean_dot = block_sum(dot, red) / static_cast<float>(D);
+    if (active) {
+      float o[8];
+      float res[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (g_res != nullptr) load8_f32(g_res + off, res);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = res[i] + r * (g[i] - xv[i] * mean_dot);
+      if (gx != nullptr) store8_f32(gx + off, o);
+      if (g_delta != nullptr) store8_bf16(g_delta + off, o);
+    }
+  }
+  if (active && dw_part != nullptr) store8_f32(dw_part + static_cast<size_t>(blockIdx.x) * D + c, dw);
+}
+
 // dw[d] (+)= sum_g part[g, d]   (fixed summation order -> deterministic).
 // Block = 32 columns x 8 row lanes (256 threads): row lane r sums rows g = r (mod 8) with
 // four independent accumulators, then the 8 lane sums are added in lane order.
@@ -232,7 +279,12 @@ void rmsnorm_bwd(torch::Tensor gh, torch::Tensor x, torch::Tensor rstd, torch::T
   const float* gr = g_res.has_value() ? g_res->data_ptr<float>() : nullptr;
   float* gxp = gx.has_value() ? gx->data_ptr<float>() : nullptr;
   __nv_bfloat16* gdp = g_delta.has_value() ? reinterpret_cast<__nv_bfloat16*>(g_delta->data_ptr()) : nullptr;
-  rmsnorm_bwd_kernel<<<G, norm_threads(static_cast<int>(D)), 0, st>>>(
+  static const int variant = [] {
+    const char* e = std::getenv("TT_NORM_BWD_VARIANT");
+    return e ? std::atoi(e) : 0;
+  }();
+  auto kern = variant == 1 ? rmsnorm_bwd_kernel : rmsnorm_bwd_serial_kernel;
+  kern<<<G, norm_threads(static_cast<int>(D)), 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(gh.data_ptr()), x.data_ptr<float>(), rstd.data_ptr<float>(),
       w.data_ptr<float>(), gr, gxp, gdp, scratch.data_ptr<float>(), static_cast<int>(M), static_cast<int>(D));
   TT_CUDA_CHECK(cudaGetLastError());

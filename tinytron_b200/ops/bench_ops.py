@@ -363,7 +363,8 @@ def _case_norm(M: int = 16384, D: int = 2048):
 
 KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
                 "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "muon": _case_muon,
-                "muon_torch": _case_muon_torch, "norm": _case_norm}
+                "muon_torch": _case_muon_torch, "norm": _case_norm,
+                "muon_2layers": lambda: _case_muon(layers=2)}
 
 
 def bench_case(name: str, iters: int, warmup: int) -> list[dict]:
