@@ -8,7 +8,6 @@
 // backward: g = g_x_out + rstd * (w*gh - xhat * mean(w*gh*xhat));   gx = g (fp32),
 //           g_delta = bf16(g);  dw partial sums per row-group, reduced deterministically.
 #include "common/host_utils.h"
-#include <cstdlib>
 #include "common/ptx.cuh"
 #include "fused/rmsnorm_bwd_noalloc.h"
 
@@ -88,67 +87,7 @@ __global__ void add_rmsnorm_fwd_kernel(const float* __restrict__ x, const __nv_b
 // ROWS rows per CTA so dw partials are per CTA (deterministic two-stage reduction).
 constexpr int BWD_ROWS = 16;
 
-// Rows are software-pipelined: the loads of row rr + 1 (x, gh and the residual gradient)
-// are issued before row rr's block reduction, so each CTA keeps two rows of traffic in
-// flight instead of stalling on every row's reduction.  Arithmetic order is unchanged.
 __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ gh, const float* __restrict__ x,
-                                   const float* __restrict__ rstd, const float* __restrict__ w,
-                                   const float* __restrict__ g_res, float* __restrict__ gx,
-                                   __nv_bfloat16* __restrict__ g_delta, float* __restrict__ dw_part, int M, int D) {
-  __shared__ float red[32];
-  const int c = threadIdx.x * EPT;
-  const bool active = c < D;
-  float wv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  float dw[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (active) load8_f32(w + c, wv);
-  const int row0 = blockIdx.x * BWD_ROWS;
-  const int rows = min(BWD_ROWS, M - row0);
-  float xv[8] = {0, 0, 0, 0, 0, 0, 0, 0}, g[8] = {0, 0, 0, 0, 0, 0, 0, 0}, res[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  auto fetch = [&](int row, float (&xa)[8], float (&ga)[8], float (&ra)[8]) {
-    const size_t off = static_cast<size_t>(row) * D + c;
-    load8_f32(x + off, xa);
-    load8_bf16(gh + off, ga);
-    if (g_res != nullptr) load8_f32(g_res + off, ra);
-  };
-  if (active && rows > 0) fetch(row0, xv, g, res);
-  for (int rr = 0; rr < rows; ++rr) {  // `rows` is uniform across the CTA
-    const int row = row0 + rr;
-    const size_t off = static_cast<size_t>(row) * D + c;
-    const float r = rstd[row];
-    float dot = 0.0f;
-    if (active) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float xh = xv[i] * r;
-        dw[i] += g[i] * xh;
-        g[i] *= wv[i];
-        dot += g[i] * xh;
-        xv[i] = xh;
-      }
-    }
-    float xn[8] = {0, 0, 0, 0, 0, 0, 0, 0}, gn[8] = {0, 0, 0, 0, 0, 0, 0, 0}, rn[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (active && rr + 1 < rows) fetch(row + 1, xn, gn, rn);  // in flight during the reduction
-    const float mean_dot = block_sum(dot, red) / static_cast<float>(D);
-    if (active) {
-      float o[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[i] = res[i] + r * (g[i] - xv[i] * mean_dot);
-      if (gx != nullptr) store8_f32(gx + off, o);
-      if (g_delta != nullptr) store8_bf16(g_delta + off, o);
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      xv[i] = xn[i];
-      g[i] = gn[i];
-      res[i] = rn[i];
-    }
-  }
-  if (active && dw_part != nullptr) store8_f32(dw_part + static_cast<size_t>(blockIdx.x) * D + c, dw);
-}
-
-// One row after another (no prefetch): fewer registers (61 vs 88), so four CTAs fit per
-// SM instead of two.  TT_NORM_BWD_VARIANT selects it (0) or the prefetching kernel (1).
-__global__ void rmsnorm_bwd_serial_kernel(const __nv_bfloat16* __restrict__ gh, const float* __restrict__ x,
                                    const float* __restrict__ rstd, const float* __restrict__ w,
                                    const float* __restrict__ g_res, float* __restrict__ gx,
                                    __nv_bfloat16* __restrict__ g_delta, float* __restrict__ dw_part, int M, int D) {
@@ -279,12 +218,7 @@ void rmsnorm_bwd(torch::Tensor gh, torch::Tensor x, torch::Tensor rstd, torch::T
   const float* gr = g_res.has_value() ? g_res->data_ptr<float>() : nullptr;
   float* gxp = gx.has_value() ? gx->data_ptr<float>() : nullptr;
   __nv_bfloat16* gdp = g_delta.has_value() ? reinterpret_cast<__nv_bfloat16*>(g_delta->data_ptr()) : nullptr;
-  static const int variant = [] {
-    const char* e = std::getenv("TT_NORM_BWD_VARIANT");
-    return e ? std::atoi(e) : 0;
-  }();
-  auto kern = variant == 1 ? rmsnorm_bwd_kernel : rmsnorm_bwd_serial_kernel;
-  kern<<<G, norm_threads(static_cast<int>(D)), 0, st>>>(
+  rmsnorm_bwd_kernel<<<G, norm_threads(static_cast<int>(D)), 0, st>>>(
       reinterpret_cast<const __nv_bfloat16*>(gh.data_ptr()), x.data_ptr<float>(), rstd.data_ptr<float>(),
       w.data_ptr<float>(), gr, gxp, gdp, scratch.data_ptr<float>(), static_cast<int>(M), static_cast<int>(D));
   TT_CUDA_CHECK(cudaGetLastError());
