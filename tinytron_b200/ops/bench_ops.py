@@ -361,10 +361,64 @@ def _case_norm(M: int = 16384, D: int = 2048):
     return run, check_status
 
 
+def _case_ce(M: int = 4096, V: int = 50304):
+    """Fused cross-entropy over bf16 logits with the in-place (softmax - onehot) gradient
+    (one dense-1.3B micro-batch quarter: 412 MB read + written)."""
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = torch.randn(M, V, device="cuda", generator=g).bfloat16()
+    t = torch.randint(0, V, (M,), device="cuda", generator=g)
+    loss = torch.empty(M, device="cuda")
+    return (lambda: C.cross_entropy_fwd(logits, t, loss, None, -100, True)), check_status
+
+
+def _case_router(N: int = 8192, E: int = 64, k: int = 8, H: int = 2048):
+    """MoE routing of one SEP=8 micro-batch per rank: router top-k + softmax, expert
+    layout (segments, slots), row gather for the grouped GEMMs."""
+    from tinytron_b200.ops import _ext, check_status
+    from tinytron_b200.ops.functional import moe_align
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = torch.randn(N, E, device="cuda", generator=g).bfloat16()
+    x = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    w = torch.empty(N, k, device="cuda")
+    sel = torch.empty(N, k, device="cuda", dtype=torch.int32)
+    P = N * k
+    align = moe_align(P, E)
+    cap = C.moe_row_capacity(P, E, align)
+    grp = torch.empty(E + 1, device="cuda", dtype=torch.int32)
+    slot = torch.empty(P, device="cuda", dtype=torch.int32)
+    row_pair = torch.empty(cap, device="cuda", dtype=torch.int32)
+    xr = torch.empty(cap, H, device="cuda", dtype=torch.bfloat16)
+
+    def run():
+        C.moe_topk_softmax(logits, k, w, sel)
+        C.moe_layout(sel.view(-1), E, grp, slot, row_pair, align)
+        C.moe_gather_rows(x, row_pair, grp, k, xr)
+
+    return run, check_status
+
+
+def _case_sample(B: int = 32, V: int = 50304):
+    """One decode step's sampling: temperature, top-k 50, top-p 0.9, Philox draw, log-prob."""
+    from tinytron_b200.ops import _ext, check_status
+
+    C = _ext.load()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = (torch.randn(B, V, device="cuda", generator=g) * 3).bfloat16()
+    tok = torch.empty(B, device="cuda", dtype=torch.long)
+    lp = torch.empty(B, device="cuda")
+    return (lambda: C.sample_tokens(logits, 0.8, 50, 0.9, 1234, 0, tok, lp)), check_status
+
+
 KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
                 "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "muon": _case_muon,
                 "muon_torch": _case_muon_torch, "norm": _case_norm,
-                "muon_2layers": lambda: _case_muon(layers=2)}
+                "muon_2layers": lambda: _case_muon(layers=2), "ce": _case_ce, "router": _case_router,
+                "sample": _case_sample}
 
 
 def bench_case(name: str, iters: int, warmup: int) -> list[dict]:
