@@ -124,6 +124,31 @@ def test_sep2_head_parallel_decode_matches_single_rank(kv):
         assert torch.allclose(res[r]["l2"], l2, atol=1e-5)
 
 
+def _sample_worker(rank, world, c, out_dir):
+    from tinytron_b200.inference import InferenceEngine
+    from tinytron_b200.parallel import parallel_state
+
+    parallel_state.initialize_model_parallel(sep_size=world)
+    eng = InferenceEngine(c, device="cpu", use_paged_kv_cache=False)
+    torch.manual_seed(100 + rank)  # ranks' own RNG streams differ on purpose
+    x, _ = data(B=3, T=8, V=c.vocab_size)
+    toks, info = eng.generate(x, 10, temperature=1.0, top_k=20, return_logprobs=True)
+    torch.save({"toks": toks, "lp": info["token_log_probs"]}, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_sep2_temperature_sampling_is_replicated_across_ranks():
+    """Head-parallel ranks hold identical logits; with temperature > 0 they must also draw
+    identical tokens (one seed sent by the group's first rank), or their KV caches would
+    diverge after the first sampled step."""
+    c = cfg()
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_sample_worker, 2, c, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    assert torch.equal(res[0]["toks"], res[1]["toks"])
+    assert torch.allclose(res[0]["lp"], res[1]["lp"], atol=1e-6)
+    assert res[0]["toks"].shape == (3, 18)
+
+
 # ---------------------------------------------------------------- DP + ZeRO-1
 def _dp_worker(rank, world, c, out_dir):
     from tinytron_b200.parallel import parallel_state
