@@ -16,6 +16,8 @@
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
 
+#include <type_traits>
+
 namespace tt {
 namespace decode {
 
@@ -114,35 +116,75 @@ struct DecodeParams {
   int* status;
 };
 
+// 16-byte global -> shared copy without registers (LDGSTS); zero-fills when !valid.
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem)), "l"(gmem),
+               "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+// Four 8x8 bf16 matrices from shared memory (row addresses from lanes 0-7, 8-15, 16-23, 24-31).
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+// c[16x8] += a[16x16] b[16x8], bf16 in, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+constexpr int kRowPad = 8;  // bf16 padding per shared row: the 8 rows of an ldmatrix hit distinct banks
+
 // One CTA per (split of 64 keys, kv head, sequence); G (q heads per kv head) is a template
-// parameter so no register or instruction is spent on absent heads.  Every phase has at
-// most one dependent round trip to memory, so a CTA's life is a few memory latencies and
-// the many small CTAs (4x more than 256-key splits) keep HBM busy:
-//   scores: two threads per key, each dotting alternate 16-byte pieces of the key's row
-//           (all of the chunk's K loads in flight at once) with the G query heads held in
-//           shared memory (16-byte broadcast reads), then one shuffle;
-//   softmax: chunk max and sum per head (block reductions);
-//   P.V:    each warp takes every 4th key; a lane owns D/32 dims, so a warp reads whole V
-//           rows; 16 keys per warp = the whole chunk in one step, all loads in flight; the
-//           4 warp partials are summed in warp order.  Key rows come from a per-chunk table
-//           in shared memory filled during the score pass (one page-table lookup per key).
+// parameter.  A CTA's life is two dependent trips to memory, so the many small CTAs keep
+// HBM busy:
+//   1. the page-pool row of every key of the chunk (one page-table lookup per key, into
+//      shared memory) and the G query heads (asynchronous copies);
+//   2. the chunk's K and V rows (32 KB at D = 128), all in flight at once as 16-byte
+//      asynchronous copies into padded shared rows (keys past the length read as zeros).
+// The two products run on the tensor cores as 16x8x16 warp MMAs with the G query heads as
+// the rows of a 16-row tile (rows >= G are never read back, so they need no zeroing):
+//   S = Q K^T: warp w takes keys [16w, 16w + 16) over all of D;
+//   softmax:   warp w owns heads w, w + 4, ...: chunk max, 2^(s - m) rounded to bf16 (the
+//              P operand) and the sum of the rounded values;
+//   O = P V:   warp w takes dims [wD/4, (w+1)D/4) over the 64 keys (V through transposing
+//              ldmatrix), so each output element has exactly one owner and no partials
+//              are summed.
+// A warp MMA is the right size here: the M side is G <= 8 heads, below the 64-row minimum
+// of a tcgen05 tile, and the kernel is bound by the K/V bytes, not by tensor throughput.
 template <int D, int G>
 __global__ void __launch_bounds__(kThreads, 4) decode_split_kernel(const DecodeParams p) {
   static_assert(D == 64 || D == 128, "head_dim 64 or 128");
-  static_assert(kChunk * 2 == kThreads, "two threads per key");
-  constexpr int NV = D / 8;  // uint4 per K row
+  static_assert(G <= 8, "at most 8 q heads per kv head (one 16-row tile, upper half unused)");
+  constexpr int NV = D / 8;          // 16-byte pieces per row
+  constexpr int RS = D + kRowPad;    // shared K/V/Q row stride (bf16)
+  constexpr int PS = kChunk + kRowPad;
   constexpr int NW = kThreads / 32;
-  constexpr int KPW = kChunk / NW;  // keys per warp in P.V
+  static_assert(NW * 16 == kChunk, "one 16-key slice per warp");
+  constexpr int DW = D / NW;         // output dims per warp
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int L = (p.len_dev != nullptr ? *p.len_dev : 0) + p.len_host;
   const int j0 = split * kChunk;
   const int n = max(0, min(kChunk, L - j0));
-  __shared__ __align__(16) float q_s[G][D];
+  __shared__ __align__(16) __nv_bfloat16 k_s[kChunk][RS];
+  __shared__ __align__(16) __nv_bfloat16 v_s[kChunk][RS];
+  __shared__ __align__(16) __nv_bfloat16 q_s[16][RS];
+  __shared__ __align__(16) __nv_bfloat16 p_s[16][PS];
   __shared__ float s_s[G][kChunk];
-  __shared__ float red_s[NW][G];
   __shared__ float m_s[G], l_s[G];
-  __shared__ __align__(16) float o_s[NW][G][D];
-  __shared__ long long rows_s[kChunk];  // page-pool row of each key of the chunk (-1: unmapped)
+  __shared__ long long rows_s[kChunk];  // page-pool row of each key of the chunk (-1: none)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (n == 0) {  // split past the current length (uniform per CTA): an empty partial
     if (tid < G) {
@@ -152,152 +194,110 @@ __global__ void __launch_bounds__(kThreads, 4) decode_split_kernel(const DecodeP
     }
     return;
   }
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, d = i % D;
-    q_s[g][d] = __bfloat162float(p.q[(static_cast<long long>(b) * p.Hq + kvh * G + g) * D + d]);
-  }
-  __syncthreads();
-  // ---- scores: thread pair (2j, 2j+1) takes key j; thread hh dots 16-byte pieces hh, hh+2, ...
-  {
-    const int j = tid >> 1, hh = tid & 1;
-    float acc[G];
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] = 0.f;
-    if (j < n) {
-      const int key = j0 + j;
+  // ---- trip 1: key rows and query heads
+  if (tid < kChunk) {
+    long long row = -1;
+    if (tid < n) {
+      const int key = j0 + tid;
       const int pi = key / p.page_size;
       const int page = pi < p.pages_per_seq ? p.page_table[static_cast<long long>(b) * p.pages_per_seq + pi] : -1;
-      const long long row =
-          (page < 0 || page >= p.num_pages) ? -1ll : static_cast<long long>(page) * p.page_size + key % p.page_size;
-      if (hh == 0) rows_s[j] = row;
-      if (row >= 0) {
-        const uint4* kr = reinterpret_cast<const uint4*>(p.k_pages + (row * p.Hkv + kvh) * D);
-        uint4 kv[NV / 2];
+      if (page >= 0 && page < p.num_pages) row = static_cast<long long>(page) * p.page_size + key % p.page_size;
+      else atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
+    }
+    rows_s[tid] = row;
+  }
+  const __nv_bfloat16* qg = p.q + (static_cast<long long>(b) * p.Hq + kvh * G) * D;
+  for (int i = tid; i < G * NV; i += kThreads) cp_async16(&q_s[i / NV][8 * (i % NV)], qg + 8 * i, true);
+  cp_async_wait_all();
+  __syncthreads();
+  // ---- trip 2: the chunk's K and V rows (consecutive threads copy consecutive pieces of a row)
+#pragma unroll 4
+  for (int i = tid; i < kChunk * NV; i += kThreads) {
+    const int r = i / NV, c = i % NV;
+    const long long row = rows_s[r];
+    const long long off = row >= 0 ? (row * p.Hkv + kvh) * D + 8 * c : 0;
+    cp_async16(&k_s[r][8 * c], p.k_pages + off, row >= 0);
+    cp_async16(&v_s[r][8 * c], p.v_pages + off, row >= 0);
+  }
+  cp_async_wait_all();
+  __syncthreads();
+  const int lr = lane & 7, lm = lane >> 3;  // row within an 8x8 matrix, matrix index
+  // ---- S = Q K^T for keys [16w, 16w + 16)
+  {
+    float sacc[2][4] = {};
+    const int kb = warp * 16;
 #pragma unroll
-        for (int c = 0; c < NV / 2; ++c) kv[c] = kr[2 * c + hh];
+    for (int k0 = 0; k0 < D; k0 += 16) {
+      uint32_t a[4], bk[4];
+      ldsm_x4(a, &q_s[lane & 15][k0 + (lane >> 4) * 8]);
+      // matrices: (keys kb..+7, dims k0..+7), (kb..+7, k0+8..), (kb+8..+15, k0..), (kb+8.., k0+8..)
+      ldsm_x4(bk, &k_s[kb + (lm >> 1) * 8 + lr][k0 + (lm & 1) * 8]);
+      mma_bf16_16816(sacc[0], a, bk[0], bk[1]);
+      mma_bf16_16816(sacc[1], a, bk[2], bk[3]);
+    }
+    const int g = lane >> 2;
+    if (g < G) {
 #pragma unroll
-        for (int c = 0; c < NV / 2; ++c) {
-          const int d0 = 8 * (2 * c + hh);
-          const uint32_t* w = reinterpret_cast<const uint32_t*>(&kv[c]);
-          float kf[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = unpack_bf16x2(w[e]);
-            kf[2 * e] = f.x;
-            kf[2 * e + 1] = f.y;
-          }
-#pragma unroll
-          for (int g = 0; g < G; ++g) {
-            const float4 qa = *reinterpret_cast<const float4*>(&q_s[g][d0]);
-            const float4 qb = *reinterpret_cast<const float4*>(&q_s[g][d0 + 4]);
-            acc[g] += kf[0] * qa.x + kf[1] * qa.y + kf[2] * qa.z + kf[3] * qa.w + kf[4] * qb.x + kf[5] * qb.y +
-                      kf[6] * qb.z + kf[7] * qb.w;
-          }
-        }
-      } else if (hh == 0) {
-        atomicCAS(p.status, 0, static_cast<int>(kBadIndex));
+      for (int t = 0; t < 2; ++t) {
+        const int j = kb + t * 8 + 2 * (lane & 3);
+        s_s[g][j] = sacc[t][0] * p.scale_log2;
+        s_s[g][j + 1] = sacc[t][1] * p.scale_log2;
       }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) acc[g] += __shfl_xor_sync(0xffffffffu, acc[g], 1);
-    if (j < n && hh == 0) {
-#pragma unroll
-      for (int g = 0; g < G; ++g) s_s[g][j] = acc[g] * p.scale_log2;
-    }
   }
   __syncthreads();
-  // ---- chunk max per head (warp w < G reduces head w over the chunk)
-  if (warp < G) {
+  // ---- softmax of the chunk per head: P (bf16, zero past the length) and its sum
+  for (int g = warp; g < G; g += NW) {
     float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, s_s[warp][j]);
+    for (int jj = lane; jj < n; jj += 32) m = fmaxf(m, s_s[g][jj]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if (lane == 0) m_s[warp] = m;
-  }
-  if constexpr (G > NW) {
-    for (int g = NW + warp; g < G; g += NW) {
-      float m = -INFINITY;
-      for (int j = lane; j < n; j += 32) m = fmaxf(m, s_s[g][j]);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      if (lane == 0) m_s[g] = m;
-    }
-  }
-  __syncthreads();
-  // ---- probabilities (in place) and their sums
-  for (int g = warp; g < G; g += NW) {
-    const float m = m_s[g];
     float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float e = exp2f(s_s[g][j] - m);
-      s_s[g][j] = e;
-      l += e;
+#pragma unroll
+    for (int jj = lane; jj < kChunk; jj += 32) {
+      const __nv_bfloat16 e = __float2bfloat16_rn(jj < n ? exp2f(s_s[g][jj] - m) : 0.f);
+      p_s[g][jj] = e;
+      l += __bfloat162float(e);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) l_s[g] = l;
+    if (lane == 0) {
+      m_s[g] = m;
+      l_s[g] = l;
+    }
   }
   __syncthreads();
-  // ---- P.V: warp w takes keys w, w+4, ...; lane owns D/32 consecutive dims (one 8- or
-  // 4-byte load per key, a warp reads whole V rows); the chunk in one step, all loads in flight.
-  constexpr int DPL = D / 32;
-  float oacc[G][DPL];
-#pragma unroll
-  for (int g = 0; g < G; ++g)
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) oacc[g][e] = 0.f;
+  // ---- O = P V for dims [w DW, (w + 1) DW)
   {
-    float vv[KPW][DPL];
+    constexpr int NT = DW / 8;  // 8-dim n-tiles per warp
+    static_assert(NT % 2 == 0, "n-tiles are loaded in pairs");
+    float oacc[NT][4] = {};
+    const int db = warp * DW;
 #pragma unroll
-    for (int u = 0; u < KPW; ++u) {
-      const int j = warp + u * NW;
-      const long long row = j < n ? rows_s[j] : -1;
-      if (row >= 0) {
-        const __nv_bfloat16* vr = p.v_pages + (row * p.Hkv + kvh) * D + lane * DPL;
-        if constexpr (DPL == 4) {
-          const uint2 w = *reinterpret_cast<const uint2*>(vr);
-          const float2 a = unpack_bf16x2(w.x), c = unpack_bf16x2(w.y);
-          vv[u][0] = a.x; vv[u][1] = a.y; vv[u][2] = c.x; vv[u][3] = c.y;
-        } else {
-          const float2 a = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(vr));
-          vv[u][0] = a.x; vv[u][1] = a.y;
-        }
-      } else {
+    for (int k0 = 0; k0 < kChunk; k0 += 16) {
+      uint32_t a[4];
+      ldsm_x4(a, &p_s[lane & 15][k0 + (lane >> 4) * 8]);
 #pragma unroll
-        for (int e = 0; e < DPL; ++e) vv[u][e] = 0.f;
+      for (int t = 0; t < NT; t += 2) {
+        uint32_t bv[4];
+        // matrices: (keys k0..+7, dims t), (k0+8..+15, dims t), (k0..+7, dims t+1), (k0+8.., dims t+1)
+        ldsm_x4_t(bv, &v_s[k0 + (lm & 1) * 8 + lr][db + (t + (lm >> 1)) * 8]);
+        mma_bf16_16816(oacc[t], a, bv[0], bv[1]);
+        mma_bf16_16816(oacc[t + 1], a, bv[2], bv[3]);
       }
     }
+    const int g = lane >> 2;
+    if (g < G) {
+      const long long rowo = (static_cast<long long>(b) * p.Hq + kvh * G + g) * p.splits + split;
+      float* o = p.o_part + rowo * D + db + 2 * (lane & 3);
 #pragma unroll
-    for (int u = 0; u < KPW; ++u) {
-      const int j = warp + u * NW;
-      if (j < n) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          const float pr = s_s[g][j];
-#pragma unroll
-          for (int e = 0; e < DPL; ++e) oacc[g][e] += pr * vv[u][e];
-        }
-      }
+      for (int t = 0; t < NT; ++t) *reinterpret_cast<float2*>(o + t * 8) = make_float2(oacc[t][0], oacc[t][1]);
     }
   }
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-#pragma unroll
-    for (int e = 0; e < DPL; ++e) o_s[warp][g][lane * DPL + e] = oacc[g][e];
-  }
-  __syncthreads();
-  // sum the NW partitions in warp order: thread handles (g, d) pairs
-  for (int i = tid; i < G * D; i += kThreads) {
-    const int g = i / D, d = i % D;
-    float o = 0.f;
-#pragma unroll
-    for (int w = 0; w < NW; ++w) o += o_s[w][g][d];
-    const long long rowo = (static_cast<long long>(b) * p.Hq + kvh * G + g) * p.splits + split;
-    p.o_part[rowo * D + d] = o;
-    if (d == 0) {
-      p.ml_part[rowo * 2] = n > 0 ? m_s[g] : -INFINITY;
-      p.ml_part[rowo * 2 + 1] = n > 0 ? l_s[g] : 0.f;
-    }
+  if (tid < G) {
+    const long long rowo = (static_cast<long long>(b) * p.Hq + kvh * G + tid) * p.splits + split;
+    p.ml_part[rowo * 2] = m_s[tid];
+    p.ml_part[rowo * 2 + 1] = l_s[tid];
   }
 }
 
@@ -318,6 +318,19 @@ __global__ void decode_combine_kernel(const float* __restrict__ o_part, const fl
       if (ml[2 * s + 1] > 0.f) acc += exp2f(ml[2 * s] - M) * o_part[(row * splits + s) * D + d];
     out[row * D + d] = __float2bfloat16_rn(acc * inv);
   }
+}
+
+// The split kernel's ~40 KB of static shared memory allows 5 CTAs per SM only with the
+// largest shared-memory carveout, so ask for it (a per-kernel attribute, set once).
+template <int D, int G>
+void launch_split(const DecodeParams& p, dim3 grid, cudaStream_t stream) {
+  static const bool carveout_set = [] {
+    cudaFuncSetAttribute(decode_split_kernel<D, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    return true;
+  }();
+  (void)carveout_set;
+  decode_split_kernel<D, G><<<grid, kThreads, 0, stream>>>(p);
 }
 
 }  // namespace decode
@@ -374,11 +387,14 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
                       torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out) {
   check_cuda_bf16(q, "q");
   check_cuda_bf16(out, "out");
-  TT_CHECK(q.dim() == 3 && q.is_contiguous(), "decode_attention: q must be [B, Hq, D]");
+  TT_CHECK(q.dim() == 3 && q.is_contiguous() && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+           "decode_attention: q must be a 16-byte aligned contiguous [B, Hq, D]");
   const int64_t B = q.size(0), Hq = q.size(1), D = q.size(2);
   TT_CHECK(k_pages.dim() == 4 && k_pages.size(3) == D && v_pages.sizes() == k_pages.sizes() &&
-               k_pages.is_contiguous() && v_pages.is_contiguous(),
-           "decode_attention: pages [num_pages, page_size, Hkv, D]");
+               k_pages.is_contiguous() && v_pages.is_contiguous() &&
+               reinterpret_cast<uintptr_t>(k_pages.data_ptr()) % 16 == 0 &&
+               reinterpret_cast<uintptr_t>(v_pages.data_ptr()) % 16 == 0,
+           "decode_attention: pages [num_pages, page_size, Hkv, D], 16-byte aligned");
   const int64_t Hkv = k_pages.size(2);
   TT_CHECK(Hq % Hkv == 0 && Hq / Hkv <= decode::kMaxG, "decode_attention: Hq/Hkv must be an integer <= 8");
   TT_CHECK((Hq / Hkv) == 1 || (Hq / Hkv) == 2 || (Hq / Hkv) == 4 || (Hq / Hkv) == 8,
@@ -419,7 +435,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
   const c10::cuda::CUDAGuard guard(q.device());
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
   const int G = static_cast<int>(Hq / Hkv);
-#define TT_DECODE(DV, GV) decode::decode_split_kernel<DV, GV><<<grid, decode::kThreads, 0, cur_stream()>>>(p)
+#define TT_DECODE(DV, GV) decode::launch_split<DV, GV>(p, grid, cur_stream())
   if (D == 128) {
     switch (G) {
       case 1: TT_DECODE(128, 1); break;
