@@ -327,9 +327,10 @@ void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor se
 }
 
 // Capacity of the padded row space for P pairs over E experts, segments aligned to
-// `align` rows (128, or 256 for the CTA-pair grouped GEMM whose tiles span 256 rows).
+// `align` rows (128, or 256 for the CTA-pair grouped GEMM whose tiles span 256 rows; 1 for
+// the unpadded segments of the decode-sized weight-streaming path).
 int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align) {
-  TT_CHECK(align == 128 || align == 256, "moe: segment alignment must be 128 or 256");
+  TT_CHECK(align == 1 || align == 128 || align == 256, "moe: segment alignment must be 1, 128 or 256");
   return (P + E * (align - 1) + align - 1) / align * align;
 }
 

@@ -100,7 +100,12 @@ def moe_experts(x: torch.Tensor, sel: torch.Tensor, weights: torch.Tensor | None
 
     x [N, H]; expert weights [E, I, H], [E, I, H], [E, H, I]; sel holds local expert ids."""
     if x.is_cuda:
-        return _cuda_fn().MoEExpertsFn.apply(x, sel, weights, w_gate, w_up, w_down)
+        fn = _cuda_fn()
+        needs_grad = torch.is_grad_enabled() and any(
+            t is not None and t.requires_grad for t in (x, weights, w_gate, w_up, w_down))
+        if not needs_grad and x.shape[0] <= fn.SKINNY_MAX_ROWS and fn.skinny_enabled():
+            return fn.moe_experts_decode(x, sel, weights, w_gate, w_up, w_down)
+        return fn.MoEExpertsFn.apply(x, sel, weights, w_gate, w_up, w_down)
     N, k = sel.shape
     flat = sel.reshape(-1)
     rep = x.repeat_interleave(k, dim=0)

@@ -23,6 +23,7 @@ SOURCES = [
     "runtime/comm.cu",
     "runtime/ulysses.cu",
     "gemm/gemm.cu",
+    "gemm/skinny.cu",
     "fused/norm.cu",
     "fused/elementwise.cu",
     "fused/sample.cu",

@@ -10,6 +10,7 @@ Dtype contract (matches the reference's fp32-master + bf16-autocast numerics):
 from __future__ import annotations
 
 import math
+import os
 
 import torch
 
@@ -28,10 +29,25 @@ def _bf16(x: torch.Tensor) -> torch.Tensor:
 
 
 # ----------------------------------------------------------------------------- GEMM helpers
+# Decode-sized products (<= 32 token rows) against a large weight run on the
+# weight-streaming split-K kernel (csrc/gemm/skinny.cu); TT_SKINNY=0 keeps them on the
+# tile GEMM (for comparisons).
+SKINNY_MAX_ROWS = 32
+_SKINNY_MIN_WEIGHT = 1 << 21  # weight elements (4 MB in bf16)
+
+
+def skinny_enabled() -> bool:
+    return os.environ.get("TT_SKINNY", "1") != "0"
+
+
 def gemm_nt(a: torch.Tensor, w16: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
     """a [M, K] @ w16[N, K]^T."""
     out = torch.empty(a.shape[0], w16.shape[0], device=a.device, dtype=out_dtype)
-    C().gemm(a, w16, out, False, False, False, 1.0, None, 0)
+    if (out_dtype == torch.bfloat16 and a.shape[0] <= SKINNY_MAX_ROWS and w16.numel() >= _SKINNY_MIN_WEIGHT
+            and w16.shape[0] % 4 == 0 and skinny_enabled()):
+        C().skinny_linear(a, w16, out)
+    else:
+        C().gemm(a, w16, out, False, False, False, 1.0, None, 0)
     return out
 
 
@@ -177,6 +193,44 @@ def moe_align(pairs: int, experts: int) -> int:
 
 
 @torch.no_grad()
+def moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo: int | None = None, out=None):
+    """Routed experts for a decode-sized batch (<= 32 tokens, no autograd) on the
+    weight-streaming kernels: every expert's weights are read once by all SMs, token rows
+    sit in unpadded expert segments, and the down projection's split sums are combined
+    with the top-k weights in one pass.  ``e_lo`` set: only the experts [e_lo, e_lo + E)
+    held by this rank (the others' pairs go to an extra segment that is never computed),
+    as in :func:`moe_experts_local`."""
+    x2d = _bf16(x.reshape(-1, x.shape[-1]))
+    N, H = x2d.shape
+    E, I = w_gate.shape[0], w_gate.shape[1]
+    k = sel.shape[-1]
+    c = C()
+    dev = x.device
+    ids = sel.reshape(-1).to(torch.int32)
+    if e_lo is None:
+        groups, local = E, ids.contiguous()
+    else:
+        groups = E + 1
+        local = ids - int(e_lo)
+        local = torch.where((local >= 0) & (local < E), local, torch.full_like(local, E)).contiguous()
+    P = local.numel()
+    cap = c.moe_row_capacity(P, groups, 1)
+    grp_off = torch.empty(groups + 1, device=dev, dtype=torch.int32)
+    slot = torch.empty(P, device=dev, dtype=torch.int32)
+    row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
+    c.moe_layout(local, groups, grp_off, slot, row_pair, 1)
+    g_loc = grp_off[:E + 1]
+    xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
+    c.moe_gather_rows(x2d, row_pair, g_loc, k, xr)
+    w_gu = concat_rows_cached(w_gate, "_tt_gu_cat", [bf16_of(w_gate).view(E * I, H), bf16_of(w_up).view(E * I, H)])
+    act = torch.empty(cap, I, device=dev, dtype=torch.bfloat16)
+    c.moe_skinny_swiglu(xr, w_gu, g_loc, E, act)
+    out = torch.empty(N, H, device=dev, dtype=torch.bfloat16) if out is None else out
+    w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
+    c.moe_skinny_down_combine(act, bf16_of(w_down).view(E * H, I), g_loc, E, slot, w32, k, out, g_loc[E:E + 1])
+    return out
+
+
 def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None):
     """Expert-parallel inference: the weighted partial sum over the experts
     [e_lo, e_lo + E_local) held by this rank, for every token (zeros where none of a
@@ -184,6 +238,8 @@ def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None
     so a decode step containing it can be captured in a CUDA graph): pairs routed
     elsewhere go to an extra "remote" segment that the grouped GEMMs never compute, and
     the combine stops at the local row count read on the device."""
+    if x.reshape(-1, x.shape[-1]).shape[0] <= SKINNY_MAX_ROWS and skinny_enabled():
+        return moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo, out)
     x2d = _bf16(x.reshape(-1, x.shape[-1]))
     N, H = x2d.shape
     E, I = w_gate.shape[0], w_gate.shape[1]
