@@ -26,7 +26,7 @@ void moe_skinny_down_combine_op(torch::Tensor act, torch::Tensor wd, torch::Tens
 void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor sel, torch::Tensor dlogits);
 int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align);
 void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair,
-                   int64_t align);
+                   int64_t align, int64_t remap_lo);
 void moe_gather_rows_op(torch::Tensor x, torch::Tensor row_pair, torch::Tensor grp_off, int64_t k, torch::Tensor out);
 void moe_combine_op(torch::Tensor y_rows, torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k,
                     torch::Tensor out, c10::optional<torch::Tensor> row_limit);
@@ -157,8 +157,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_topk_softmax_bwd", &tt::moe_topk_softmax_bwd_op, "backward of moe_topk_softmax");
   m.def("moe_row_capacity", &tt::moe_row_capacity, "padded expert-row capacity for P pairs and E experts",
         py::arg("P"), py::arg("E"), py::arg("align") = 128);
-  m.def("moe_layout", &tt::moe_layout_op, "expert segments (128- or 256-row aligned, stable) for the grouped GEMMs",
-        py::arg("sel"), py::arg("E"), py::arg("grp_off"), py::arg("slot"), py::arg("row_pair"), py::arg("align") = 128);
+  m.def("moe_layout", &tt::moe_layout_op,
+        "expert segments (1-, 128- or 256-row aligned, stable) for the grouped GEMMs; remap_lo >= 0: ids "
+        "sel - remap_lo in [0, E - 1) are local experts, all others go to group E - 1",
+        py::arg("sel"), py::arg("E"), py::arg("grp_off"), py::arg("slot"), py::arg("row_pair"), py::arg("align") = 128,
+        py::arg("remap_lo") = -1);
   m.def("moe_gather_rows", &tt::moe_gather_rows_op, "x_rows[r] = x[token of row r], zero pad rows");
   m.def("moe_combine", &tt::moe_combine_op, "out[t] = sum_j w[t,j] y_rows[slot[t,j]] (slots below row_limit)",
         py::arg("y_rows"), py::arg("slot"), py::arg("w"), py::arg("k"), py::arg("out"),

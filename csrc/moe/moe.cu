@@ -117,12 +117,23 @@ __global__ void topk_softmax_bwd_kernel(const float* __restrict__ dw, const floa
   }
 }
 
+// Expert id of pair i: sel[i], or with remap_lo >= 0 the local id sel[i] - remap_lo when
+// that lies in [0, E - 1) and E - 1 (the "remote" group of pairs another rank computes)
+// otherwise (expert-parallel inference).
+__device__ __forceinline__ int layout_id(const int* __restrict__ sel, int i, int E, int remap_lo) {
+  const int x = sel[i];
+  if (remap_lo < 0) return x;
+  const int l = x - remap_lo;
+  return (l >= 0 && l < E - 1) ? l : E - 1;
+}
+
 // Grid: one block per expert (1024 threads).  Every block builds the full histogram
 // (cheap: the pair list is a few hundred KB and stays in L2), so all offsets are known
 // without a second launch; block e then places its own pairs in token order.
 __global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ sel, int P, int E, int align,
                                                      int* __restrict__ grp_off, int* __restrict__ slot,
-                                                     int* __restrict__ row_pair, int* __restrict__ status) {
+                                                     int* __restrict__ row_pair, int* __restrict__ status,
+                                                     int remap_lo) {
   __shared__ int hist[kMaxExperts];
   __shared__ int off[kMaxExperts + 1];
   __shared__ int warp_cnt[32];
@@ -131,7 +142,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ se
   for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
   __syncthreads();
   for (int i = threadIdx.x; i < P; i += blockDim.x) {
-    const int x = sel[i];
+    const int x = layout_id(sel, i, E, remap_lo);
     if (x >= 0 && x < E) atomicAdd(&hist[x], 1);
     else if (e == 0) atomicCAS(status, 0, static_cast<int>(kBadIndex));  // out-of-range expert id: pair dropped
   }
@@ -153,7 +164,7 @@ __global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ se
   const int nwarps = blockDim.x >> 5;
   for (int c0 = 0; c0 < P; c0 += blockDim.x) {
     const int i = c0 + threadIdx.x;
-    const bool mine = i < P && sel[i] == e;
+    const bool mine = i < P && layout_id(sel, i, E, remap_lo) == e;
     const unsigned bal = __ballot_sync(0xffffffffu, mine);
     if (lane == 0) warp_cnt[warp] = __popc(bal);
     __syncthreads();
@@ -173,6 +184,106 @@ __global__ void __launch_bounds__(1024) layout_kernel(const int* __restrict__ se
     __syncthreads();
   }
   for (int r = base + hist[e] + threadIdx.x; r < off[e + 1]; r += blockDim.x) row_pair[r] = -1;
+}
+
+// The same layout for large pair counts (prefill, training micro-batches) in three
+// launches that use the whole GPU instead of one block per expert scanning every pair:
+//   1. layout_count_kernel: block b counts the experts of pairs [b*C, (b+1)*C) (shared
+//      histogram);
+//   2. layout_scan_kernel (one block, a thread per expert): the expert totals, the
+//      aligned segment starts (grp_off), each chunk's first row within every expert
+//      segment, and the padding rows' row_pair = -1;
+//   3. layout_place_kernel: block b walks its chunk 256 pairs at a time; a pair's row is
+//      its expert's running count + the same-expert pairs of earlier warps (per-warp
+//      counts from __match_any_sync) + its rank among equal lanes of its own warp.
+// Rows keep token order within each expert (stable), exactly as the one-block kernel.
+constexpr int kLayoutChunk = 4096;
+constexpr int kLayoutThreads = 256;
+
+__global__ void __launch_bounds__(kLayoutThreads) layout_count_kernel(const int* __restrict__ sel, int P, int E,
+                                                                      int* __restrict__ cnt, int* __restrict__ status,
+                                                                      int remap_lo) {
+  __shared__ int hist[kMaxExperts];
+  for (int i = threadIdx.x; i < E; i += blockDim.x) hist[i] = 0;
+  __syncthreads();
+  const int i0 = blockIdx.x * kLayoutChunk, i1 = min(P, i0 + kLayoutChunk);
+  for (int i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+    const int x = layout_id(sel, i, E, remap_lo);
+    if (x >= 0 && x < E) atomicAdd(&hist[x], 1);
+    else atomicCAS(status, 0, static_cast<int>(kBadIndex));  // out-of-range expert id: pair dropped
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) cnt[static_cast<size_t>(blockIdx.x) * E + e] = hist[e];
+}
+
+__global__ void __launch_bounds__(kMaxExperts) layout_scan_kernel(const int* __restrict__ cnt, int nb, int E,
+                                                                  int align, int* __restrict__ grp_off,
+                                                                  int* __restrict__ blk_off,
+                                                                  int* __restrict__ row_pair) {
+  __shared__ int seg[kMaxExperts];
+  const int e = threadIdx.x;
+  int total = 0;
+  if (e < E)
+    for (int b = 0; b < nb; ++b) total += cnt[static_cast<size_t>(b) * E + e];
+  seg[e] = e < E ? (total + align - 1) / align * align : 0;
+  __syncthreads();
+  // inclusive scan of the padded segment sizes (Hillis-Steele over kMaxExperts entries)
+  for (int d = 1; d < kMaxExperts; d <<= 1) {
+    const int v = e >= d ? seg[e - d] : 0;
+    __syncthreads();
+    seg[e] += v;
+    __syncthreads();
+  }
+  if (e < E) {
+    const int start = seg[e] - (total + align - 1) / align * align;
+    grp_off[e] = start;
+    if (e == E - 1) grp_off[E] = seg[e];
+    int run = start;
+    for (int b = 0; b < nb; ++b) {
+      blk_off[static_cast<size_t>(b) * E + e] = run;
+      run += cnt[static_cast<size_t>(b) * E + e];
+    }
+    for (int r = start + total; r < seg[e]; ++r) row_pair[r] = -1;
+  }
+}
+
+__global__ void __launch_bounds__(kLayoutThreads) layout_place_kernel(const int* __restrict__ sel, int P, int E,
+                                                                      const int* __restrict__ blk_off,
+                                                                      int* __restrict__ slot,
+                                                                      int* __restrict__ row_pair, int remap_lo) {
+  constexpr int NW = kLayoutThreads / 32;
+  __shared__ int running[kMaxExperts];
+  __shared__ int wcnt[NW][kMaxExperts];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) running[e] = blk_off[static_cast<size_t>(blockIdx.x) * E + e];
+  const int i0 = blockIdx.x * kLayoutChunk, i1 = min(P, i0 + kLayoutChunk);
+  for (int c0 = i0; c0 < i1; c0 += kLayoutThreads) {
+    for (int j = threadIdx.x; j < NW * E; j += blockDim.x) wcnt[j / E][j % E] = 0;
+    __syncthreads();
+    const int i = c0 + threadIdx.x;
+    const int x = i < i1 ? layout_id(sel, i, E, remap_lo) : -1;
+    const bool ok = x >= 0 && x < E;
+    const unsigned peers = __match_any_sync(0xffffffffu, ok ? x : -1);
+    const int rank = __popc(peers & ((1u << lane) - 1u));
+    if (ok && rank == 0) wcnt[warp][x] = __popc(peers);
+    __syncthreads();
+    if (ok) {
+      int r = running[x] + rank;
+      for (int w = 0; w < warp; ++w) r += wcnt[w][x];
+      slot[i] = r;
+      row_pair[r] = i;
+    } else if (i < i1) {
+      slot[i] = -1;
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int add = 0;
+#pragma unroll
+      for (int w = 0; w < NW; ++w) add += wcnt[w][e];
+      running[e] += add;
+    }
+    __syncthreads();
+  }
 }
 
 // One warp per padded row; rows at or past the device-side total are skipped.
@@ -210,7 +321,7 @@ __global__ void combine_kernel(const __nv_bfloat16* __restrict__ y_rows, const i
     int kk = 0;
     for (int j = 0; j < k; ++j) {
       const int sl = slot[static_cast<size_t>(t) * k + j];
-      if (sl < lim) {
+      if (sl >= 0 && sl < lim) {
         s_slot[kk] = sl;
         s_w[kk] = w ? w[static_cast<size_t>(t) * k + j] : 1.0f;
         ++kk;
@@ -335,7 +446,7 @@ int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align) {
 }
 
 void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair,
-                   int64_t align) {
+                   int64_t align, int64_t remap_lo) {
   TT_CHECK(sel.is_cuda() && sel.scalar_type() == torch::kInt32 && sel.is_contiguous(), "layout: sel int32");
   const int P = static_cast<int>(sel.numel());
   TT_CHECK(E >= 1 && E <= moe::kMaxExperts, "layout: 1 <= E <= 256");
@@ -343,9 +454,26 @@ void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::T
                slot.scalar_type() == torch::kInt32 && row_pair.scalar_type() == torch::kInt32 &&
                row_pair.numel() >= moe_row_capacity(P, E, align), "layout: bad outputs");
   const c10::cuda::CUDAGuard guard(sel.device());
-  moe::layout_kernel<<<static_cast<unsigned>(E), 1024, 0, cur_stream()>>>(
-      sel.data_ptr<int>(), P, static_cast<int>(E), static_cast<int>(align), grp_off.data_ptr<int>(), slot.data_ptr<int>(),
-      row_pair.data_ptr<int>(), device_status_ptr(sel.get_device()));
+  int* status = device_status_ptr(sel.get_device());
+  if (P <= 2 * moe::kLayoutChunk) {  // decode and small batches: one launch
+    moe::layout_kernel<<<static_cast<unsigned>(E), 1024, 0, cur_stream()>>>(
+        sel.data_ptr<int>(), P, static_cast<int>(E), static_cast<int>(align), grp_off.data_ptr<int>(),
+        slot.data_ptr<int>(), row_pair.data_ptr<int>(), status, static_cast<int>(remap_lo));
+    TT_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
+  const int nb = (P + moe::kLayoutChunk - 1) / moe::kLayoutChunk;
+  torch::Tensor scratch = torch::empty({2, nb, E}, sel.options());
+  int* cnt = scratch.data_ptr<int>();
+  int* blk_off = cnt + static_cast<size_t>(nb) * E;
+  moe::layout_count_kernel<<<nb, moe::kLayoutThreads, 0, cur_stream()>>>(sel.data_ptr<int>(), P, static_cast<int>(E),
+                                                                         cnt, status, static_cast<int>(remap_lo));
+  moe::layout_scan_kernel<<<1, moe::kMaxExperts, 0, cur_stream()>>>(cnt, nb, static_cast<int>(E),
+                                                                    static_cast<int>(align), grp_off.data_ptr<int>(),
+                                                                    blk_off, row_pair.data_ptr<int>());
+  moe::layout_place_kernel<<<nb, moe::kLayoutThreads, 0, cur_stream()>>>(
+      sel.data_ptr<int>(), P, static_cast<int>(E), blk_off, slot.data_ptr<int>(), row_pair.data_ptr<int>(),
+      static_cast<int>(remap_lo));
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -53,10 +53,12 @@ def test_topk_softmax_matches_torch(E, k):
     assert torch.allclose(dl, lg.grad, atol=1e-6)
 
 
-def test_layout_segments_are_aligned_stable_and_complete():
-    E, k = 16, 4
-    _, _, sel = _route(3000, E, k, skew=2.0)
-    cap, grp_off, slot, row_pair = _layout(sel, E)
+@pytest.mark.parametrize("N,E,k,align", [(3000, 16, 4, 128), (1000, 16, 4, 128), (40000, 64, 8, 256),
+                                         (20000, 256, 2, 1), (9000, 64, 8, 128), (24, 64, 8, 1)])
+def test_layout_segments_are_aligned_stable_and_complete(N, E, k, align):
+    # pair counts <= 8192 take the one-launch kernel, larger ones the count/scan/place kernels
+    _, _, sel = _route(N, E, k, skew=2.0)
+    cap, grp_off, slot, row_pair = _layout(sel, E, align)
     off = grp_off.cpu().tolist()
     counts = torch.bincount(sel.reshape(-1).long(), minlength=E).cpu().tolist()
     flat = sel.reshape(-1).cpu()
@@ -64,12 +66,35 @@ def test_layout_segments_are_aligned_stable_and_complete():
     rp = row_pair.cpu()
     assert off[0] == 0 and off[-1] <= cap
     for e in range(E):
-        assert off[e] % 128 == 0
-        assert off[e + 1] - off[e] == (counts[e] + 127) // 128 * 128
+        assert off[e] % align == 0
+        assert off[e + 1] - off[e] == (counts[e] + align - 1) // align * align
         pairs = torch.nonzero(flat == e).squeeze(-1)
         assert torch.equal(sl[pairs], torch.arange(off[e], off[e] + counts[e], dtype=torch.int32))  # stable
         assert torch.equal(rp[off[e]:off[e] + counts[e]].long(), pairs)
         assert (rp[off[e] + counts[e]:off[e + 1]] == -1).all()
+    assert ext().status_read(0) == 0
+
+
+@pytest.mark.parametrize("N,lo", [(32, 8), (3000, 24)])
+def test_layout_remap_matches_precomputed_local_ids(N, lo):
+    """remap_lo: ids in [lo, lo + E_l) become local experts, all others the last group."""
+    C = ext()
+    E, k, E_l = 64, 8, 8
+    _, _, sel = _route(N, E, k)
+    flat = sel.reshape(-1)
+    local = flat - lo
+    local = torch.where((local >= 0) & (local < E_l), local, torch.full_like(local, E_l)).contiguous()
+    outs = []
+    for ids, remap in ((local, -1), (flat.contiguous(), lo)):
+        P = ids.numel()
+        cap = C.moe_row_capacity(P, E_l + 1, 1)
+        grp = torch.empty(E_l + 2, device="cuda", dtype=torch.int32)
+        slot = torch.empty(P, device="cuda", dtype=torch.int32)
+        rp = torch.empty(cap, device="cuda", dtype=torch.int32)
+        C.moe_layout(ids, E_l + 1, grp, slot, rp, 1, remap)
+        outs.append((grp, slot, rp[:int(grp[-1])]))
+    for a, b in zip(*outs):
+        assert torch.equal(a, b)
     assert ext().status_read(0) == 0
 
 

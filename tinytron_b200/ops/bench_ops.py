@@ -290,6 +290,28 @@ def _case_moe_decode(N: int = 32, E: int = 64, k: int = 8, H: int = 2048, I: int
     return run, check_status
 
 
+def _case_moe_decode_ep8(N: int = 32, E: int = 64, k: int = 8, H: int = 2048, I: int = 1408, ranks: int = 8):
+    """The same decode step for one rank of an EP=8 group: its 8 local experts' share of
+    the 32 tokens' pairs (the others go to the never-computed remote segment)."""
+    from tinytron_b200 import ops
+    from tinytron_b200.ops import check_status
+
+    E_l = E // ranks
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = torch.randn(N, H, device="cuda", generator=g).bfloat16()
+    wg = (torch.randn(E_l, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wu = (torch.randn(E_l, I, H, device="cuda", generator=g) * 0.02).bfloat16()
+    wd = (torch.randn(E_l, H, I, device="cuda", generator=g) * 0.02).bfloat16()
+    sel = torch.topk(torch.randn(N, E, device="cuda", generator=g), k, -1).indices.to(torch.int32)
+    w = torch.softmax(torch.randn(N, k, device="cuda", generator=g), -1)
+
+    def run():
+        with torch.no_grad():
+            ops.moe_experts_local(x, sel, w, wg, wu, wd, 0)
+
+    return run, check_status
+
+
 def _case_muon(layers: int = 16, H: int = 2048, kv: int = 256, I: int = 5504):
     """One Muon step over the matrices of the long-context preset (16 layers, d2048,
     2 kv heads, SwiGLU 5504) on one GPU: momentum, tcgen05 Newton-Schulz (symmetric
@@ -415,7 +437,7 @@ def _case_sample(B: int = 32, V: int = 50304):
 
 
 KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "attn_bwd_b4": _case_attn_bwd_b4,
-                "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "muon": _case_muon,
+                "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "moe_decode_ep8": _case_moe_decode_ep8, "muon": _case_muon,
                 "muon_torch": _case_muon_torch, "norm": _case_norm,
                 "muon_2layers": lambda: _case_muon(layers=2), "ce": _case_ce, "router": _case_router,
                 "sample": _case_sample}

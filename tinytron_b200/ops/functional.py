@@ -206,19 +206,14 @@ def moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo: int | None =
     k = sel.shape[-1]
     c = C()
     dev = x.device
-    ids = sel.reshape(-1).to(torch.int32)
-    if e_lo is None:
-        groups, local = E, ids.contiguous()
-    else:
-        groups = E + 1
-        local = ids - int(e_lo)
-        local = torch.where((local >= 0) & (local < E), local, torch.full_like(local, E)).contiguous()
-    P = local.numel()
+    ids = sel.reshape(-1).to(torch.int32).contiguous()
+    groups = E if e_lo is None else E + 1  # + the never-computed group of other ranks' pairs
+    P = ids.numel()
     cap = c.moe_row_capacity(P, groups, 1)
     grp_off = torch.empty(groups + 1, device=dev, dtype=torch.int32)
     slot = torch.empty(P, device=dev, dtype=torch.int32)
     row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
-    c.moe_layout(local, groups, grp_off, slot, row_pair, 1)
+    c.moe_layout(ids, groups, grp_off, slot, row_pair, 1, -1 if e_lo is None else int(e_lo))
     g_loc = grp_off[:E + 1]
     xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
     c.moe_gather_rows(x2d, row_pair, g_loc, k, xr)
@@ -246,8 +241,7 @@ def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None
     k = sel.shape[-1]
     c = C()
     dev = x.device
-    local = sel.reshape(-1).to(torch.int32) - int(e_lo)
-    local = torch.where((local >= 0) & (local < E), local, torch.full_like(local, E)).contiguous()
+    local = sel.reshape(-1).to(torch.int32).contiguous()
     P = local.numel()
     align = moe_align(P, E + 1)
     pair = align == 256
@@ -255,7 +249,7 @@ def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None
     grp_off = torch.empty(E + 2, device=dev, dtype=torch.int32)
     slot = torch.empty(P, device=dev, dtype=torch.int32)
     row_pair = torch.empty(cap, device=dev, dtype=torch.int32)
-    c.moe_layout(local, E + 1, grp_off, slot, row_pair, align)
+    c.moe_layout(local, E + 1, grp_off, slot, row_pair, align, int(e_lo))
     g_loc = grp_off[:E + 1]  # local expert segments; g_loc[E] = rows computed on this rank
     xr = torch.empty(cap, H, device=dev, dtype=torch.bfloat16)
     c.moe_gather_rows(x2d, row_pair, g_loc, k, xr)
