@@ -13,6 +13,9 @@ GB/s per GPU and its fraction of the measured 770 GB/s per-direction peer bandwi
   reduce_scatter_tensor + all_gather_into_tensor (+ the fused AdamW kernel).
 * one-shot all-reduce (bf16) at the decode size (32 x 2048) and a bulk size (64 MB).
 * equal-split all-to-all (Ulysses exchange) of 64 MB.
+* the fused Ulysses head<->sequence exchange of the long-context preset (4096 tokens per
+  rank, 16 q / 2 kv heads of 128), both directions, vs the same layout change around NCCL.
+* the graph-safe two-kernel all-reduce (device epochs) at the decode size.
 """
 from __future__ import annotations
 
@@ -144,6 +147,45 @@ def main():
     b = 2 * numel * (W - 1) / W
     rows.append(_row("alltoall_64MB_ttcomm", _timed(heap_a2a, 10), b))
     rows.append(_row("alltoall_64MB_nccl", _timed(lambda: dist.all_to_all_single(out, src), 10), b))
+    # ---------------------------------------------------------------- Ulysses (SEP attention)
+    # Long-context preset: one 4096-token chunk per rank, 16 q / 2 kv heads of 128.  Fused:
+    # pack + peer-load exchange kernels on a symmetric heap; baseline: the same layout
+    # change with torch copies around NCCL all_to_all_single (a separate, unregistered group).
+    from tinytron_b200.parallel.symm import enable_heap_all_to_all
+    from tinytron_b200.parallel.ulysses import gather_heads_from_ranks, route_heads_to_ranks
+
+    Bu, Tl, Hq, Hkv, D = 1, 4096, 16, 2, 128
+    if Hq % W == 0:
+        enable_heap_all_to_all(None, torch.device("cuda", local))
+        plain = dist.new_group(list(range(W)))
+        qkv = torch.randn(Bu * Tl, (Hq + 2 * Hkv) * D, device="cuda").bfloat16()
+        full, hq_l, hkv_l = route_heads_to_ranks(qkv, Bu, Tl, Hq, Hkv, D, W, None)
+        b_in = full.numel() * 2 * (W - 1) / W  # bytes each rank receives from peers
+        rows.append(_row("ulysses_qkv_to_heads_fused", _timed(
+            lambda: route_heads_to_ranks(qkv, Bu, Tl, Hq, Hkv, D, W, None), 20), b_in))
+        rows.append(_row("ulysses_qkv_to_heads_nccl", _timed(
+            lambda: route_heads_to_ranks(qkv, Bu, Tl, Hq, Hkv, D, W, plain), 20), b_in))
+        o = torch.randn(Bu * W * Tl, hq_l * D, device="cuda").bfloat16()
+        b_out = o.numel() * 2 * (W - 1) / W
+        rows.append(_row("ulysses_o_to_tokens_fused", _timed(
+            lambda: gather_heads_from_ranks(o, Bu, Tl, Hq, D, W, None), 20), b_out))
+        rows.append(_row("ulysses_o_to_tokens_nccl", _timed(
+            lambda: gather_heads_from_ranks(o, Bu, Tl, Hq, D, W, plain), 20), b_out))
+    # ---------------------------------------------------------------- graph-safe all-reduce
+    # decode-sized (32 x 2048 bf16) two-kernel all-reduce with device epochs, as replayed
+    # inside the SEP decode graph, against NCCL
+    numel = 32 * 2048
+    h = SymmetricHeap.create(2 * numel * 2 + 4096)
+    slot_buf, slot_bytes = h.replay_slots(numel * 2)
+    xin = torch.randn(numel, device="cuda").bfloat16()
+    xout = torch.empty_like(xin)
+
+    def replay_ar():
+        h.replay_publish(slot_buf, slot_bytes, xin)
+        h.replay_reduce(slot_buf, slot_bytes, xout)
+
+    rows.append(_row("allreduce_decode_32x2048_replay", _timed(replay_ar, 200), 2 * numel * (W - 1)))
+    h.close()
     check_status()
     if rank == 0:
         if args.json:
