@@ -69,7 +69,10 @@ void decode_rope_append(torch::Tensor qkv, int64_t B, int64_t T, int64_t Hq, int
                         torch::Tensor page_table);
 int64_t decode_num_splits(int64_t max_len);
 void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, double top_p, int64_t seed,
-                   int64_t offset, torch::Tensor tokens, c10::optional<torch::Tensor> logprob);
+                   int64_t offset, torch::Tensor tokens, c10::optional<torch::Tensor> logprob,
+                   c10::optional<torch::Tensor> rng);
+void decode_advance(torch::Tensor nxt, torch::Tensor tokens, int64_t P, torch::Tensor tok_in, torch::Tensor rng,
+                    c10::optional<torch::Tensor> lp, c10::optional<torch::Tensor> lp_all);
 void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pages, torch::Tensor page_table,
                       c10::optional<torch::Tensor> len_dev, int64_t len_host, int64_t splits, double scale,
                       torch::Tensor o_part, torch::Tensor ml_part, torch::Tensor out);
@@ -190,7 +193,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_rope_append", &tt::decode_rope_append, "RoPE on q/k + paged KV-cache append (device position)");
   m.def("sample_tokens", &tt::sample_tokens, "temperature/top-k/top-p sampling in one kernel (Philox draw)",
         py::arg("logits"), py::arg("temperature"), py::arg("top_k"), py::arg("top_p"), py::arg("seed"),
-        py::arg("offset"), py::arg("tokens"), py::arg("logprob") = py::none());
+        py::arg("offset"), py::arg("tokens"), py::arg("logprob") = py::none(), py::arg("rng") = py::none());
+  m.def("decode_advance", &tt::decode_advance,
+        "decode step bookkeeping on the device: tokens[:, P + step] = nxt, token input = nxt, log-prob column "
+        "step, step += 1 (step = rng[1])",
+        py::arg("nxt"), py::arg("tokens"), py::arg("P"), py::arg("tok_in"), py::arg("rng"), py::arg("lp") = py::none(),
+        py::arg("lp_all") = py::none());
   m.def("decode_num_splits", &tt::decode_num_splits, "split-KV CTAs per (sequence, kv head) for a max length");
   m.def("decode_attention", &tt::decode_attention, "split-KV paged decode attention (GQA-native) + combine");
   m.def("ep_allgather_counts", &tt::ep_allgather_counts, "EP: all-gather per-expert counts into the heap");

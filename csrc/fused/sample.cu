@@ -109,6 +109,7 @@ template <typename T>
 __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ logits, int V, long long ld,
                                                         float inv_t, int top_k, float top_p,
                                                         unsigned long long seed, unsigned long long offset,
+                                                        const long long* __restrict__ rng,
                                                         int64_t* __restrict__ tokens, float* __restrict__ logprob) {
   __shared__ float sh[36];
   __shared__ float hist[256];
@@ -186,6 +187,10 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
     picked = argmax;
     if (top_k != 1) {
       curandStatePhilox4_32_10_t st;
+      if (rng != nullptr) {  // seed and offset from the device (a captured decode step)
+        seed = static_cast<unsigned long long>(rng[0]);
+        offset = static_cast<unsigned long long>(rng[1]);
+      }
       curand_init(seed, static_cast<unsigned long long>(r), offset, &st);
       sh[34] = curand_uniform(&st) * zk;  // (0, zk]
     } else {
@@ -219,11 +224,58 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
   }
 }
 
+// One decode step's bookkeeping on the device, so that sampling and the next step's input
+// live inside the captured decode graph: tokens[b, P + step] = nxt[b], the graph's token
+// input = nxt, the log-prob into column `step`, then step += 1 (rng[1] is the step and the
+// Philox offset of the next draw).  One block of B threads.
+__global__ void decode_advance_kernel(const int64_t* __restrict__ nxt, int B, int64_t* __restrict__ tokens,
+                                      long long ld_tokens, int P, int64_t* __restrict__ tok_in,
+                                      long long* __restrict__ rng, const float* __restrict__ lp,
+                                      float* __restrict__ lp_all, long long ld_lp) {
+  const long long step = rng[1];
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    const int64_t t = nxt[b];
+    tokens[b * ld_tokens + P + step] = t;
+    tok_in[b] = t;
+    if (lp != nullptr) lp_all[b * ld_lp + step] = lp[b];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) rng[1] = step + 1;
+}
+
 }  // namespace sample
 
+void decode_advance(torch::Tensor nxt, torch::Tensor tokens, int64_t P, torch::Tensor tok_in, torch::Tensor rng,
+                    c10::optional<torch::Tensor> lp, c10::optional<torch::Tensor> lp_all) {
+  TT_CHECK(nxt.is_cuda() && nxt.scalar_type() == torch::kInt64 && nxt.is_contiguous(), "decode_advance: nxt int64");
+  const int64_t B = nxt.numel();
+  TT_CHECK(tokens.scalar_type() == torch::kInt64 && tokens.dim() == 2 && tokens.size(0) == B && tokens.stride(1) == 1,
+           "decode_advance: tokens int64 [B, total]");
+  TT_CHECK(tok_in.scalar_type() == torch::kInt64 && tok_in.numel() == B && tok_in.is_contiguous(),
+           "decode_advance: token input int64 [B]");
+  TT_CHECK(rng.scalar_type() == torch::kInt64 && rng.numel() >= 2 && rng.is_cuda(), "decode_advance: rng int64 [2]");
+  TT_CHECK(lp.has_value() == lp_all.has_value(), "decode_advance: lp and lp_all together");
+  if (lp.has_value())
+    TT_CHECK(lp->scalar_type() == torch::kFloat32 && lp->numel() == B && lp_all->scalar_type() == torch::kFloat32 &&
+                 lp_all->dim() == 2 && lp_all->size(0) == B && lp_all->stride(1) == 1,
+             "decode_advance: lp fp32 [B], lp_all fp32 [B, steps]");
+  if (B == 0) return;
+  const c10::cuda::CUDAGuard guard(nxt.device());
+  sample::decode_advance_kernel<<<1, static_cast<unsigned>(std::min<int64_t>(1024, ((B + 31) / 32) * 32)), 0,
+                                  cur_stream()>>>(
+      nxt.data_ptr<int64_t>(), static_cast<int>(B), tokens.data_ptr<int64_t>(), tokens.stride(0), static_cast<int>(P),
+      tok_in.data_ptr<int64_t>(), reinterpret_cast<long long*>(rng.data_ptr<int64_t>()),
+      lp.has_value() ? lp->data_ptr<float>() : nullptr, lp.has_value() ? lp_all->data_ptr<float>() : nullptr,
+      lp.has_value() ? lp_all->stride(0) : 0);
+  TT_CUDA_CHECK(cudaGetLastError());
+}
+
 // tokens int64 [B]; logprob fp32 [B] (optional).  top_k <= 0: off; top_p outside (0, 1): off.
+// rng (optional, int64 [2] on the device): seed and offset read by the kernel instead of the
+// host values, so a captured graph draws a new number on every replay.
 void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, double top_p, int64_t seed,
-                   int64_t offset, torch::Tensor tokens, c10::optional<torch::Tensor> logprob) {
+                   int64_t offset, torch::Tensor tokens, c10::optional<torch::Tensor> logprob,
+                   c10::optional<torch::Tensor> rng) {
   TT_CHECK(logits.is_cuda() && logits.dim() == 2 && logits.stride(1) == 1, "sample: logits must be CUDA [B, V]");
   TT_CHECK(temperature > 0, "sample: temperature must be > 0");
   TT_CHECK(tokens.scalar_type() == torch::kInt64 && tokens.numel() == logits.size(0) && tokens.is_contiguous(),
@@ -232,6 +284,11 @@ void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, doub
   if (logprob.has_value()) {
     TT_CHECK(logprob->scalar_type() == torch::kFloat32 && logprob->numel() == logits.size(0), "sample: logprob [B]");
     lp = logprob->data_ptr<float>();
+  }
+  const long long* rng_p = nullptr;
+  if (rng.has_value()) {
+    TT_CHECK(rng->is_cuda() && rng->scalar_type() == torch::kInt64 && rng->numel() >= 2, "sample: rng int64 [2]");
+    rng_p = reinterpret_cast<const long long*>(rng->data_ptr<int64_t>());
   }
   const int64_t B = logits.size(0), V = logits.size(1);
   if (B == 0) return;
@@ -242,12 +299,13 @@ void sample_tokens(torch::Tensor logits, double temperature, int64_t top_k, doub
     sample::sample_kernel<__nv_bfloat16><<<static_cast<unsigned>(B), sample::THREADS, 0, cur_stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), static_cast<int>(V), logits.stride(0), inv_t, k,
         static_cast<float>(top_p), static_cast<unsigned long long>(seed), static_cast<unsigned long long>(offset),
-        tokens.data_ptr<int64_t>(), lp);
+        rng_p, tokens.data_ptr<int64_t>(), lp);
   } else {
     TT_CHECK(logits.scalar_type() == torch::kFloat32, "sample: logits bf16 or fp32");
     sample::sample_kernel<float><<<static_cast<unsigned>(B), sample::THREADS, 0, cur_stream()>>>(
         logits.data_ptr<float>(), static_cast<int>(V), logits.stride(0), inv_t, k, static_cast<float>(top_p),
-        static_cast<unsigned long long>(seed), static_cast<unsigned long long>(offset), tokens.data_ptr<int64_t>(), lp);
+        static_cast<unsigned long long>(seed), static_cast<unsigned long long>(offset), rng_p, tokens.data_ptr<int64_t>(),
+        lp);
   }
   TT_CUDA_CHECK(cudaGetLastError());
 }

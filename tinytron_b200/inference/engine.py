@@ -93,6 +93,49 @@ class InferenceEngine:
         torch.cuda.synchronize()
         return g, static_tok, static_logits
 
+    def _decode_graph_loop(self, logits, cache, tokens, B: int, P: int, n_new: int, temperature, top_k, top_p,
+                           want_lp: bool, gen):
+        """Every decode step as ONE graph replay: the forward of the last token, the draw and
+        the token write all run on the device (the draw's seed and Philox offset live in a
+        device tensor that the step advances), so the host only launches the graph.  The
+        first token is drawn eagerly from the prefill logits with the same kernels.
+        Returns (steps, log-probs [B, steps] or None, the graph; the caller releases it after
+        synchronising)."""
+        from tinytron_b200.ops import _ext
+
+        from .sampler import _cuda_sample
+
+        C = _ext.load()
+        dev = self.device
+        base = int(torch.randint(0, 2 ** 62, (1,), generator=gen).item())  # same on every SEP rank
+        rng = torch.tensor([base, 0], dtype=torch.long, device=dev)
+        tok_in = torch.zeros(B, 1, dtype=torch.long, device=dev)
+        nxt = torch.empty(B, dtype=torch.long, device=dev)
+        lp = torch.empty(B, dtype=torch.float32, device=dev) if want_lp else None
+        lp_all = torch.empty(B, n_new, dtype=torch.float32, device=dev) if want_lp else None
+
+        def draw(lg):
+            _cuda_sample(lg[:, -1, :], temperature, top_k, top_p, want_lp, rng=rng, out=(nxt, lp))
+            C.decode_advance(nxt, tokens, P, tok_in.view(-1), rng, lp, lp_all)
+
+        draw(logits)  # token 0
+        L = cache.current_length
+        # one eager forward outside the graph (allocations, lazy tables), then rewind
+        self.model._forward_cached(tok_in, cache, True, L, last_only=True)
+        cache.set_length(L)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            lg, _ = self.model._forward_cached(tok_in, cache, True, L, last_only=True)
+            draw(lg)
+        cache.set_length(L)  # capture advanced the host length without running anything
+        for _ in range(n_new - 1):
+            g.replay()
+        for c in cache._layer_caches:  # the replays advanced the device lengths
+            c.current_length += n_new - 1
+            c.seq_lens = [c.current_length] * c.batch_size
+        return n_new, lp_all, g
+
     # ------------------------------------------------------------------ SEP-synced sampling
     def _sep(self):
         g = parallel_state.get_sp_group_or_none()
@@ -166,7 +209,14 @@ class InferenceEngine:
         cur = P
         steps = 0
         stop_at = None
-        for i in range(max_new_tokens):
+        lp_graph = None
+        graph_loop = (cuda and eos_token_id is None and max_new_tokens > 2 and self._graph_ok()
+                      and tokens.dtype == torch.long)
+        if graph_loop:
+            steps, lp_graph, graph = self._decode_graph_loop(logits, cache, tokens, B, P, max_new_tokens, temperature,
+                                                             top_k, top_p, return_logprobs, gen)
+            cur = P + steps
+        for i in range(0 if graph_loop else max_new_tokens):
             last = logits[:, -1, :]
             if return_logprobs:
                 nxt, lp = self._sample_next_token_with_log_prob_synced(last, temperature, top_k, top_p, gen)
@@ -221,7 +271,10 @@ class InferenceEngine:
                                "prefill_tokens_per_sec_device": B * P / max(dp_ms, 1e-6) * 1e3,
                                "decode_tokens_per_sec_device": (B * steps / max(dd_ms, 1e-6) * 1e3) if steps else 0.0})
         if return_logprobs:
-            lp = torch.stack(logp_steps, 1) if logp_steps else torch.empty(B, 0, device=self.device)
+            if lp_graph is not None:
+                lp = lp_graph
+            else:
+                lp = torch.stack(logp_steps, 1) if logp_steps else torch.empty(B, 0, device=self.device)
             extras.update({"prompt_len": float(P), "decode_steps": float(steps), "token_log_probs": lp,
                            "response_mask": torch.ones_like(lp, dtype=torch.float32)})
         return tokens, extras

@@ -26,7 +26,8 @@ def filter_logits(logits: torch.Tensor, temperature: float = 1.0, top_k: int | N
     return logits
 
 
-def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_log_prob: bool, generator=None):
+def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_log_prob: bool, generator=None,
+                 rng: torch.Tensor | None = None, out=None):
     """One fused kernel (csrc/fused/sample.cu): temperature, top-k / top-p thresholds by
     radix selection, Philox draw.  The seed comes from a CPU generator (torch's global one
     unless ``generator`` is given), so ``set_seed`` makes sampling reproducible, ranks that
@@ -39,10 +40,15 @@ def _cuda_sample(logits: torch.Tensor, temperature: float, top_k, top_p, with_lo
     if x.dtype not in (torch.bfloat16, torch.float32):
         x = x.float()
     B = x.shape[0]
-    tok = torch.empty(B, dtype=torch.long, device=x.device)
-    lp = torch.empty(B, dtype=torch.float32, device=x.device) if with_log_prob else None
-    seed = int(torch.randint(0, 2 ** 62, (1,), generator=generator).item())
-    _ext.load().sample_tokens(x, float(temperature), int(top_k or 0), float(top_p or 0.0), seed, 0, tok, lp)
+    if out is not None:  # caller-owned outputs (a captured decode step)
+        tok, lp = out
+    else:
+        tok = torch.empty(B, dtype=torch.long, device=x.device)
+        lp = torch.empty(B, dtype=torch.float32, device=x.device) if with_log_prob else None
+    # rng (device int64 [seed, offset]): the kernel reads the seed there, so a CUDA graph
+    # replay draws fresh numbers; otherwise one seed per call from the CPU generator
+    seed = 0 if rng is not None else int(torch.randint(0, 2 ** 62, (1,), generator=generator).item())
+    _ext.load().sample_tokens(x, float(temperature), int(top_k or 0), float(top_p or 0.0), seed, 0, tok, lp, rng)
     return tok, lp
 
 
