@@ -198,16 +198,76 @@ def _count_launches(step_fn, step: int, own_marker: str) -> tuple[int, int]:
     """(our kernels, all kernels) launched by one step, from the torch profiler (untimed)."""
     import torch
 
-    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+    mode = os.environ.get("TT_BENCH_PROFILE", "0")
+    acts = [torch.profiler.ProfilerActivity.CUDA]
+    if mode == "2":  # also CPU ops, to name the op that launched each kernel
+        acts.append(torch.profiler.ProfilerActivity.CPU)
+    with torch.profiler.profile(activities=acts) as prof:
         step_fn(step)
         torch.cuda.synchronize()
+    if mode == "2":
+        _print_kernel_origins(prof, own_marker)
     ours = total = 0
+    spans = []
     for ev in prof.events():
         if ev.device_type == torch.autograd.DeviceType.CUDA:
             total += 1
             if own_marker and own_marker in ev.name:
                 ours += 1
+            spans.append((ev.time_range.start, ev.time_range.end, ev.name))
+    if mode in ("1", "2") and spans:
+        _print_kernel_table(spans)
     return ours, total
+
+
+def _print_kernel_origins(prof, own_marker: str, top: int = 15) -> None:
+    """For the kernels not launched by this framework, the outermost profiled op that
+    launched them (an autograd node or a top-level aten op), with counts (stderr)."""
+    import collections
+
+    per = collections.defaultdict(lambda: [0.0, collections.Counter()])
+    for ev in prof.events():
+        for k in getattr(ev, "kernels", []) or []:
+            if own_marker and own_marker in k.name:
+                continue
+            root, chain = ev, [ev.name]
+            while root.cpu_parent is not None:
+                root = root.cpu_parent
+                chain.append(root.name)
+            origin = next((c for c in chain if c.startswith("autograd::engine::evaluate_function")), chain[-1])
+            per[k.name][0] += k.duration / 1e3
+            per[k.name][1][f"{origin} <- {chain[0]}"] += 1
+    rank = os.environ.get("RANK", "0")
+    for name, (ms, origins) in sorted(per.items(), key=lambda kv: -kv[1][0])[:top]:
+        print(f"[rank {rank}] origin {ms:8.3f} ms {name[:80]}: {dict(origins.most_common(3))}", file=sys.stderr)
+
+
+def _print_kernel_table(spans, top: int = 40) -> None:
+    """Per-kernel device time of the profiled step (stderr, this rank): total, share,
+    launches, and how much of the step's span had no kernel running at all (idle gaps:
+    host synchronisation, launch latency)."""
+    import collections
+
+    per = collections.defaultdict(lambda: [0.0, 0])
+    for a, b, name in spans:
+        per[name][0] += (b - a) / 1e3
+        per[name][1] += 1
+    spans = sorted(spans)
+    busy, cur_a, cur_b = 0.0, spans[0][0], spans[0][1]
+    for a, b, _ in spans[1:]:  # union of kernel intervals
+        if a > cur_b:
+            busy += cur_b - cur_a
+            cur_a, cur_b = a, b
+        else:
+            cur_b = max(cur_b, b)
+    busy += cur_b - cur_a
+    span = spans[-1][1] - spans[0][0]
+    tot = sum(v[0] for v in per.values())
+    rank = os.environ.get("RANK", "0")
+    print(f"[rank {rank}] profiled step: span {span / 1e3:.2f} ms, some kernel running {busy / 1e3:.2f} ms "
+          f"({busy / max(span, 1e-9):.3f}), kernel time {tot:.2f} ms", file=sys.stderr)
+    for name, (ms, n) in sorted(per.items(), key=lambda kv: -kv[1][0])[:top]:
+        print(f"[rank {rank}] {ms:9.3f} ms {ms / tot:6.1%} n={n:6d}  {name[:110]}", file=sys.stderr)
 
 
 def _make_device_batches(vocab: int, n: int, seed: int):

@@ -83,6 +83,6 @@ def test_buffer_layout_includes_return_records():
 
 def test_push_combine_switch(monkeypatch):
     monkeypatch.delenv("TT_EP_PUSH_COMBINE", raising=False)
+    assert not epc.push_combine_enabled()  # pull-combine by default (measured faster)
+    monkeypatch.setenv("TT_EP_PUSH_COMBINE", "1")
     assert epc.push_combine_enabled()
-    monkeypatch.setenv("TT_EP_PUSH_COMBINE", "0")
-    assert not epc.push_combine_enabled()

@@ -181,10 +181,12 @@ class MoE(nn.Module):
             # dispatch/combine by NVLink peer stores/loads around the grouped GEMMs
             from tinytron_b200.parallel.ep_comm import ep_moe
 
+            # The expert weights are inputs of the EP autograd function, which writes their
+            # gradients into the fp32 main grads itself (even for experts that received no
+            # rows), so no zero-valued dependency on them is added: its backward would build
+            # a full-size fp32 zero gradient per weight every micro-step that nothing reads.
             y = ep_moe(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
                        self.experts_down_weights, ep_group)
-            if self.training:
-                y = y + self._zero_expert_weight_dependency().to(y.dtype)
             return y.view(B, T, D), gate_logits.view(B, T, -1)
         rep_x = flat_x.repeat_interleave(self.top_k, dim=0)
         exp_ids = sel.reshape(-1).long()
