@@ -86,6 +86,8 @@ void ep_resolve_rows(int64_t gid, int64_t ret_off, int64_t rows, int64_t H, torc
 void ep_pull_combine(int64_t gid, int64_t y_off, int64_t cap, torch::Tensor tgt, torch::Tensor dst, int64_t k,
                      c10::optional<torch::Tensor> w, torch::Tensor out, c10::optional<torch::Tensor> y_save);
 void ep_zero_pad(torch::Tensor buf, torch::Tensor seg_off, torch::Tensor seg_cnt);
+void ep_plan_rows(torch::Tensor sel, torch::Tensor slot, torch::Tensor delta, int64_t E_l, torch::Tensor dst,
+                  torch::Tensor tgt);
 namespace comm {
 int64_t comm_create(int64_t device, int64_t bytes);
 torch::Tensor comm_ipc_handle(int64_t gid);
@@ -216,6 +218,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("gid"), py::arg("y_off"), py::arg("cap"), py::arg("tgt"), py::arg("dst"), py::arg("k"),
         py::arg("w"), py::arg("out"), py::arg("y_save") = py::none());
   m.def("ep_zero_pad", &tt::ep_zero_pad, "zero the padding rows of expert segments");
+  m.def("ep_plan_rows", &tt::ep_plan_rows,
+        "EP pair destinations: dst = slot + delta[e], tgt = e / E_l (slot: position in the stable expert order)");
   // tt_comm: symmetric heap over CUDA IPC + device-initiated collectives (csrc/runtime/comm.cu)
   m.def("comm_create", &tt::comm::comm_create, "allocate a symmetric heap on a device; returns a group id");
   m.def("comm_ipc_handle", &tt::comm::comm_ipc_handle, "64-byte CUDA IPC handle of the group's heap");

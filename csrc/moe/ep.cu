@@ -204,6 +204,26 @@ __global__ void zero_pad_kernel(__nv_bfloat16* __restrict__ buf, const int* __re
   }
 }
 
+// Destination of every (token, slot) pair of this rank: dst = slot + delta[e], tgt = e / E_l,
+// where slot is the pair's position in this rank's expert-sorted (stable) order and
+// delta[e] = (owner row of expert e's first pair from this rank) - (expert e's first
+// position in that order).  Out-of-range expert ids are recorded and sent to row 0 of rank 0.
+__global__ void plan_rows_kernel(const int* __restrict__ sel, const int* __restrict__ slot,
+                                 const int* __restrict__ delta, int P, int E, int E_l, int* __restrict__ dst,
+                                 int* __restrict__ tgt, int* __restrict__ status) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < P; i += gridDim.x * blockDim.x) {
+    const int e = sel[i];
+    if (e < 0 || e >= E) {
+      atomicCAS(status, 0, static_cast<int>(kBadIndex));
+      dst[i] = 0;
+      tgt[i] = 0;
+      continue;
+    }
+    dst[i] = slot[i] + delta[e];
+    tgt[i] = e / E_l;
+  }
+}
+
 }  // namespace ep
 
 namespace {
@@ -213,6 +233,26 @@ void check_pairs(const torch::Tensor& tgt, const torch::Tensor& dst, int64_t P) 
            "ep: tgt/dst must be contiguous CUDA int32 [pairs]");
 }
 }  // namespace
+
+// Pair destinations from the stable expert order (see plan_rows_kernel).
+void ep_plan_rows(torch::Tensor sel, torch::Tensor slot, torch::Tensor delta, int64_t E_l, torch::Tensor dst,
+                  torch::Tensor tgt) {
+  const int64_t P = sel.numel();
+  TT_CHECK(sel.is_cuda() && sel.scalar_type() == torch::kInt32 && sel.is_contiguous() && slot.numel() == P &&
+               slot.scalar_type() == torch::kInt32 && delta.scalar_type() == torch::kInt32 && delta.is_contiguous(),
+           "ep_plan_rows: sel, slot int32 [P], delta int32 [E]");
+  check_pairs(tgt, dst, P);
+  const int64_t E = delta.numel();
+  TT_CHECK(E_l >= 1 && E % E_l == 0, "ep_plan_rows: E must be a multiple of E_l");
+  if (P == 0) return;
+  const c10::cuda::CUDAGuard guard(sel.device());
+  const int threads = 256;
+  const int blocks = static_cast<int>(std::min<int64_t>((P + threads - 1) / threads, 4 * num_sms(sel.get_device())));
+  ep::plan_rows_kernel<<<blocks, threads, 0, cur_stream()>>>(
+      sel.data_ptr<int>(), slot.data_ptr<int>(), delta.data_ptr<int>(), static_cast<int>(P), static_cast<int>(E),
+      static_cast<int>(E_l), dst.data_ptr<int>(), tgt.data_ptr<int>(), device_status_ptr(sel.get_device()));
+  TT_CUDA_CHECK(cudaGetLastError());
+}
 
 // counts int32 [E] -> row `rank` of the [world, E] matrix at heap offset dst_off on every rank.
 void ep_allgather_counts(int64_t gid, torch::Tensor counts, int64_t dst_off) {

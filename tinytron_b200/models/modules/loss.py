@@ -73,8 +73,10 @@ class ExpertLoadBalancingLoss(nn.Module):
             if selected_experts is None:
                 selected_experts = torch.topk(flat, self.top_k, dim=-1).indices
             sel = selected_experts.reshape(-1, self.top_k).long()
-            f_sum = torch.zeros(E, dtype=torch.float32, device=flat.device)
-            f_sum.index_add_(0, sel.reshape(-1), keep.repeat_interleave(self.top_k))
+            # selections of valid tokens: masked ones go to an extra bin (an integer count,
+            # deterministic, no sort; index_add_ runs a sort-based kernel in deterministic mode)
+            ids = torch.where(valid_mask.reshape(-1, 1).bool(), sel, torch.full_like(sel, E))
+            f_sum = torch.bincount(ids.reshape(-1), minlength=E + 1)[:E].float()
             n_local = keep.sum()
         else:
             p_sum = F.softmax(flat.float(), dim=-1).sum(0)

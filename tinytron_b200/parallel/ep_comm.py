@@ -157,19 +157,39 @@ def plan_finish(bufs: EPBuffers, sel: torch.Tensor, counts: torch.Tensor, M: np.
     if int(seg.sum(1).max()) > bufs.cap:
         raise RuntimeError(f"EP receive buffer too small ({int(seg.sum(1).max())} > {bufs.cap} rows)")
     dev = sel.device
+    p = Plan()
+    p.total, p.k, p.N, p.E_local = total, k, N, E_l
+    p.pair = align == 256
+    if sel.is_cuda:
+        # stable position of every pair within its expert from the layout kernel (unpadded
+        # segments), then one kernel for dst/tgt; the per-expert offsets and the receive
+        # segments travel to the device in one copy
+        c = _C()
+        sel32 = sel.reshape(-1).to(torch.int32).contiguous()
+        P = sel32.numel()
+        lay = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        slot = torch.empty(P, dtype=torch.int32, device=dev)
+        rows = torch.empty(max(P, 1), dtype=torch.int32, device=dev)
+        c.moe_layout(sel32, E, lay, slot, rows, 1)
+        mine = M[rank]
+        start = np.cumsum(mine) - mine  # first position of each expert in the sorted order
+        meta = np.concatenate([base - start, seg_off[rank], [total], n[rank]]).astype(np.int32)
+        meta = torch.from_numpy(meta).pin_memory().to(dev, non_blocking=True)
+        p.grp_off, p.seg_cnt = meta[E:E + E_l + 1], meta[E + E_l + 1:]
+        p.dst = torch.empty(P, dtype=torch.int32, device=dev)
+        p.tgt = torch.empty(P, dtype=torch.int32, device=dev)
+        c.ep_plan_rows(sel32, slot, meta[:E], E_l, p.dst, p.tgt)
+        return p
     flat = sel.reshape(-1).long()
     P = flat.numel()
     order = torch.argsort(flat, stable=True)
     start = torch.cumsum(counts.long(), 0) - counts.long()
     rank_in_e = torch.empty(P, dtype=torch.long, device=dev)
     rank_in_e[order] = torch.arange(P, device=dev) - start[flat[order]]
-    p = Plan()
     p.dst = (torch.from_numpy(base).to(dev)[flat] + rank_in_e).to(torch.int32).contiguous()
     p.tgt = (flat // E_l).to(torch.int32).contiguous()
     p.grp_off = torch.tensor(list(seg_off[rank]) + [total], dtype=torch.int32, device=dev)
     p.seg_cnt = torch.tensor(n[rank], dtype=torch.int32, device=dev)
-    p.total, p.k, p.N, p.E_local = total, k, N, E_l
-    p.pair = align == 256
     return p
 
 
