@@ -18,11 +18,13 @@ void moe_gemm_swiglu_op(torch::Tensor x, torch::Tensor w_gu, torch::Tensor out, 
 void moe_gemm_dswiglu_op(torch::Tensor dy, torch::Tensor w_down, torch::Tensor gu, torch::Tensor dgu,
                          torch::Tensor grp_off, int64_t n_groups, bool pair);
 void moe_topk_softmax_op(torch::Tensor logits, int64_t k, torch::Tensor w, torch::Tensor sel);
-void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out);
+void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t publish_gid, int64_t slot_off,
+                      int64_t slot_bytes);
 void moe_skinny_swiglu_op(torch::Tensor xr, torch::Tensor w_gu, torch::Tensor grp_off, int64_t E, torch::Tensor act);
 void moe_skinny_down_combine_op(torch::Tensor act, torch::Tensor wd, torch::Tensor grp_off, int64_t E,
                                 torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k, torch::Tensor out,
-                                c10::optional<torch::Tensor> row_limit);
+                                c10::optional<torch::Tensor> row_limit, int64_t publish_gid, int64_t slot_off,
+                                int64_t slot_bytes);
 void moe_topk_softmax_bwd_op(torch::Tensor dw, torch::Tensor w, torch::Tensor sel, torch::Tensor dlogits);
 int64_t moe_row_capacity(int64_t P, int64_t E, int64_t align);
 void moe_layout_op(torch::Tensor sel, int64_t E, torch::Tensor grp_off, torch::Tensor slot, torch::Tensor row_pair,
@@ -135,15 +137,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("addend") = py::none(), py::arg("beta") = 0.0, py::arg("symmetric") = false,
         py::arg("batch") = 1);
   m.def("skinny_linear", &tt::skinny_linear_op,
-        "y[M, N] = x[M, K] w[N, K]^T for M <= 32: weight-streaming split-K tcgen05 GEMM (decode)", py::arg("x"),
-        py::arg("w"), py::arg("out"));
+        "y[M, N] = x[M, K] w[N, K]^T for M <= 32: weight-streaming split-K tcgen05 GEMM (decode); publish_gid >= 0: "
+        "y goes to that heap's all-reduce slot (published to the peers) instead of out",
+        py::arg("x"), py::arg("w"), py::arg("out"), py::arg("publish_gid") = -1, py::arg("slot_off") = 0,
+        py::arg("slot_bytes") = 0);
   m.def("moe_skinny_swiglu", &tt::moe_skinny_swiglu_op,
         "decode experts: act = silu(x Wg_e^T) * (x Wu_e^T) over unpadded expert segments", py::arg("xr"),
         py::arg("w_gu"), py::arg("grp_off"), py::arg("E"), py::arg("act"));
   m.def("moe_skinny_down_combine", &tt::moe_skinny_down_combine_op,
         "decode experts: out[n] = sum_j w[n,j] act_{slot[n,j]} Wd_e^T (pairs at or past *row_limit skipped)",
         py::arg("act"), py::arg("wd"), py::arg("grp_off"), py::arg("E"), py::arg("slot"), py::arg("w"), py::arg("k"),
-        py::arg("out"), py::arg("row_limit") = py::none());
+        py::arg("out"), py::arg("row_limit") = py::none(), py::arg("publish_gid") = -1, py::arg("slot_off") = 0,
+        py::arg("slot_bytes") = 0);
   m.def("gemm_set_pair_mode", &tt::gemm_set_pair_mode, "CTA-pair GEMM: 0 never, 1 when faster, 2 always");
   m.def("gemm_pair_mode", &tt::gemm_pair_mode);
   m.def("moe_gemm", &tt::moe_gemm_op, "grouped GEMM over expert row segments (bf16 out)", py::arg("a"),

@@ -29,6 +29,7 @@
 // Every wait is bounded (status word + early exit), as in the tile GEMM.
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
+#include "runtime/comm_common.cuh"
 
 #include <algorithm>
 #include <mutex>
@@ -62,6 +63,28 @@ struct Params {
   int rows_cap, ld_part;
   int* status;
 };
+
+// Optional fused publish of a row-parallel all-reduce (SEP inference): the split-sum
+// kernel writes its bf16 result straight into this rank's symmetric-heap slot of the
+// graph-safe all-reduce (slot = device epoch parity) and its last block signals the peers,
+// so only the reducing kernel remains (it waits for every peer's epoch and sums the slots).
+struct Publish {
+  comm::PeerTable t;
+  size_t slot_off;
+  long long slot_bytes;
+  int on;
+};
+
+// Destination of the split-sum kernel's bf16 output: `out` (row stride ld_out), or with a
+// publish the heap slot of the coming epoch (contiguous rows of N).
+__device__ __forceinline__ __nv_bfloat16* publish_dst(const Publish& pub, __nv_bfloat16* out, int& ld_out, int N,
+                                                      uint64_t& e) {
+  if (!pub.on) return out;
+  e = comm::dev_epoch_next(pub.t);
+  ld_out = N;
+  return reinterpret_cast<__nv_bfloat16*>(pub.t.base[pub.t.rank] + pub.slot_off +
+                                          static_cast<size_t>(e & 1ull) * static_cast<size_t>(pub.slot_bytes));
+}
 
 struct Unit {
   int g, h, rb, s;
@@ -260,7 +283,9 @@ __device__ __forceinline__ float4 sum_splits4(const float* part, int splits, siz
 
 // out[r, n] = bf16(sum_s part[s, r, n]), r < M, n < N (N % 4 == 0).
 __global__ void reduce_bf16_kernel(const float* __restrict__ part, int splits, int rows_cap, int ld, int M, int N,
-                                   __nv_bfloat16* __restrict__ out, int ld_out) {
+                                   __nv_bfloat16* __restrict__ out, int ld_out, const Publish pub) {
+  uint64_t e = 0;
+  out = publish_dst(pub, out, ld_out, N, e);
   const int n4 = N / 4;
   const size_t total = static_cast<size_t>(M) * n4;
   const size_t ss = static_cast<size_t>(rows_cap) * ld;
@@ -273,6 +298,7 @@ __global__ void reduce_bf16_kernel(const float* __restrict__ part, int splits, i
     o.y = pack_bf16x2(v.z, v.w);
     *reinterpret_cast<uint2*>(out + static_cast<size_t>(r) * ld_out + c) = o;
   }
+  if (pub.on) comm::grid_last_block(pub.t, [&]() { comm::signal_peers(pub.t, e); });
 }
 
 // act[r, j] = bf16(silu(g) * u) with g, u the split sums of columns j and I + j; rows below
@@ -302,7 +328,10 @@ __global__ void reduce_swiglu_kernel(const float* __restrict__ part, int splits,
 // One CTA per token, a thread per 4 columns.
 __global__ void reduce_combine_kernel(const float* __restrict__ part, int splits, int rows_cap, int H,
                                       const int* __restrict__ slot, const float* __restrict__ w, int k,
-                                      const int* __restrict__ row_limit, __nv_bfloat16* __restrict__ out, int ld_out) {
+                                      const int* __restrict__ row_limit, __nv_bfloat16* __restrict__ out, int ld_out,
+                                      const Publish pub) {
+  uint64_t e = 0;
+  out = publish_dst(pub, out, ld_out, H, e);
   const int n = blockIdx.x;
   const int limit = row_limit != nullptr ? *row_limit : 0x7fffffff;
   const size_t ss = static_cast<size_t>(rows_cap) * H;
@@ -323,6 +352,7 @@ __global__ void reduce_combine_kernel(const float* __restrict__ part, int splits
     o.y = pack_bf16x2(acc.z, acc.w);
     *reinterpret_cast<uint2*>(out + static_cast<size_t>(n) * ld_out + c) = o;
   }
+  if (pub.on) comm::grid_last_block(pub.t, [&]() { comm::signal_peers(pub.t, e); });
 }
 
 // ---------------------------------------------------------------------------- host side
@@ -359,6 +389,22 @@ static void check_operand(const torch::Tensor& t, const char* name) {
            std::string(name) + ": rows of a 16-byte aligned row-major matrix expected");
 }
 
+// Publish target (gid >= 0): a heap slot pair of a graph-safe all-reduce (see Publish);
+// `bytes` is the size of the output that will be written there.
+static Publish make_publish(int64_t gid, int64_t slot_off, int64_t slot_bytes, int64_t bytes, int device) {
+  Publish pub{};
+  if (gid < 0) return pub;
+  TT_CHECK(comm::group_device(gid) == device, "skinny publish: heap on another device");
+  TT_CHECK(slot_off % 16 == 0 && slot_bytes % 16 == 0 && bytes <= slot_bytes &&
+               slot_off + 2 * slot_bytes <= static_cast<int64_t>(comm::group_bytes(gid)),
+           "skinny publish: slot outside the heap or too small");
+  pub.t = comm::group_table(gid);
+  pub.slot_off = static_cast<size_t>(slot_off);
+  pub.slot_bytes = slot_bytes;
+  pub.on = 1;
+  return pub;
+}
+
 static Params base_params(int K, int device) {
   Params p{};
   p.K = K;
@@ -370,7 +416,8 @@ static Params base_params(int K, int device) {
 }  // namespace skinny
 
 // y[M, N] = x[M, K] w[N, K]^T for M <= 32 (decode-sized batches).
-void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
+void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t publish_gid, int64_t slot_off,
+                      int64_t slot_bytes) {
   using namespace skinny;
   check_operand(x, "x");
   check_operand(w, "w");
@@ -401,9 +448,10 @@ void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out) {
   launch(w, x, p, device);
   const int threads = 256;
   const int blocks = std::max(1, std::min(num_sms(device) * 4, (M * N / 4 + threads - 1) / threads));
+  const Publish pub = make_publish(publish_gid, slot_off, slot_bytes, static_cast<int64_t>(M) * N * 2, device);
   reduce_bf16_kernel<<<blocks, threads, 0, cur_stream()>>>(p.part, p.splits, M, N, M, N,
                                                            reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                           static_cast<int>(out.stride(0)));
+                                                           static_cast<int>(out.stride(0)), pub);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -452,7 +500,8 @@ void moe_skinny_swiglu_op(torch::Tensor xr, torch::Tensor w_gu, torch::Tensor gr
 // past *row_limit (experts held by other ranks).  wd = [Wd of all E experts] ([E*H, I]).
 void moe_skinny_down_combine_op(torch::Tensor act, torch::Tensor wd, torch::Tensor grp_off, int64_t E,
                                 torch::Tensor slot, c10::optional<torch::Tensor> w, int64_t k, torch::Tensor out,
-                                c10::optional<torch::Tensor> row_limit) {
+                                c10::optional<torch::Tensor> row_limit, int64_t publish_gid, int64_t slot_off,
+                                int64_t slot_bytes) {
   using namespace skinny;
   check_operand(act, "act");
   check_operand(wd, "wd");
@@ -485,10 +534,11 @@ void moe_skinny_down_combine_op(torch::Tensor act, torch::Tensor wd, torch::Tens
   p.rows_cap = std::max(cap, 1);
   p.ld_part = H;
   if (cap > 0) launch(wd, act, p, device);
+  const Publish pub = make_publish(publish_gid, slot_off, slot_bytes, static_cast<int64_t>(N) * H * 2, device);
   reduce_combine_kernel<<<N, std::min(256, std::max(32, H / 4)), 0, cur_stream()>>>(
       p.part, p.splits, p.rows_cap, H, slot.data_ptr<int>(), w.has_value() ? w->data_ptr<float>() : nullptr,
       static_cast<int>(k), row_limit.has_value() ? row_limit->data_ptr<int>() : p.grp_off + E,
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), static_cast<int>(out.stride(0)));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), static_cast<int>(out.stride(0)), pub);
   TT_CUDA_CHECK(cudaGetLastError());
 }
 

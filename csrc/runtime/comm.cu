@@ -293,9 +293,6 @@ __global__ void shadow_refresh_kernel(PeerTable t, size_t data_off, __nv_bfloat1
 // Slots alternate with the epoch's parity: a rank rewrites slot (e & 1) at call e + 2 only
 // after its reduce of call e + 1 saw every peer's publish of e + 1, which each peer issued
 // after finishing its reduce of call e (stream order), i.e. after reading that slot.
-__device__ __forceinline__ uint64_t dev_epoch_next(const PeerTable& t) {
-  return *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) + 1;
-}
 
 __global__ void replay_publish_kernel(PeerTable t, size_t slot_off, long long slot_bytes, const char* __restrict__ in,
                                       long long bytes) {

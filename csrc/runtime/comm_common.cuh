@@ -54,6 +54,12 @@ __device__ __forceinline__ void signal_peers(const PeerTable& t, uint64_t e) {
   st_release_sys_u64(flag_ptr(t, t.rank, t.rank), e);
 }
 
+// Epoch of the next replayable collective step (the device-side counter + 1); the last
+// kernel of the step stores it back (see kDevEpochOff).
+__device__ __forceinline__ uint64_t dev_epoch_next(const PeerTable& t) {
+  return *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) + 1;
+}
+
 // One thread: wait until every peer published epoch >= e.  Bounded.
 __device__ __forceinline__ bool wait_peers(const PeerTable& t, uint64_t e, int* status, uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer();

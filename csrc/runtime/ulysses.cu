@@ -47,14 +47,11 @@ struct UlExch {
   int W;
 };
 
-__device__ __forceinline__ uint64_t ul_epoch_next(const PeerTable& t) {
-  return *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) + 1;
-}
 
 __global__ void __launch_bounds__(kUlThreads) ul_pack_kernel(PeerTable t, size_t slot_off, long long slot_bytes,
                                                             const __nv_bfloat16* __restrict__ src, int B, int T,
                                                             UlPack d) {
-  const uint64_t e = ul_epoch_next(t);
+  const uint64_t e = dev_epoch_next(t);
   __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(t.base[t.rank] + slot_off +
                                                         static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes));
   const int wv = d.W / 8;
@@ -78,7 +75,7 @@ __global__ void __launch_bounds__(kUlThreads) ul_pack_kernel(PeerTable t, size_t
 __global__ void __launch_bounds__(kUlThreads) ul_exchange_kernel(PeerTable t, size_t slot_off, long long slot_bytes,
                                                                 __nv_bfloat16* __restrict__ out, int B, int T,
                                                                 UlExch d, int* status, uint64_t timeout_ns) {
-  const uint64_t e = ul_epoch_next(t);
+  const uint64_t e = dev_epoch_next(t);
   if (block_wait_peers(t, e, status, timeout_ns)) {
     const size_t off = slot_off + static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes);
     const int wv = d.W / 8;
@@ -105,7 +102,7 @@ __global__ void __launch_bounds__(kUlThreads) ul_exchange_kernel(PeerTable t, si
 __global__ void __launch_bounds__(kUlThreads) ul_exchange_qkv_grad_kernel(
     PeerTable t, size_t slot_off, long long slot_bytes, __nv_bfloat16* __restrict__ dqkv, int B, int T, int Hq,
     int Hkv, int D, int hq_l, int hkv_l, UlPack kv, int* status, uint64_t timeout_ns) {
-  const uint64_t e = ul_epoch_next(t);
+  const uint64_t e = dev_epoch_next(t);
   if (block_wait_peers(t, e, status, timeout_ns)) {
     const size_t off = slot_off + static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes);
     const int W = (hq_l + 2 * hkv_l) * D;

@@ -86,6 +86,101 @@ def test_moe_experts_local_matches_masked_full(N, E, k, W):
     assert _rel(total, full) < 2e-2
 
 
+class _DeferredReduce:
+    """A heap all-reduce target whose reduction the test runs later: on one GPU every
+    emulated rank must publish before any rank reduces."""
+
+    def __init__(self, heap, numel):
+        self.heap = heap
+        self.slots, self.slot_bytes = heap.replay_slots(numel * 2)
+        self.pending = None
+
+    def fits(self, numel):
+        return numel * 2 <= self.slot_bytes and numel % 8 == 0
+
+    def publish_target(self):
+        return self.heap.gid, self.heap.offset_of(self.slots), self.slot_bytes
+
+    def reduce_into(self, out):
+        self.pending = out
+
+    def finish(self):
+        self.heap.replay_reduce(self.slots, self.slot_bytes, self.pending.view(-1))
+
+
+@pytest.mark.parametrize("W", [2, 4])
+def test_fused_publish_row_parallel_emulated(W):
+    """The decode-sized GEMM / MoE combine publish their results into the heap slot of the
+    graph-safe all-reduce themselves; only the reducing kernel follows."""
+    from tinytron_b200.ops import check_status
+    from tinytron_b200.ops import functional as Fn
+    from tinytron_b200.parallel.symm import SymmetricHeap
+
+    C = Fn.C()
+    M, K, N = 32, 256, 2048
+    heaps = SymmetricHeap.create_emulated(2 * M * N * 2 + 8192, W)
+    targets = [_DeferredReduce(h, M * N) for h in heaps]
+    g = torch.Generator(device="cuda").manual_seed(W)
+    xs = [torch.randn(M, K, device="cuda", generator=g).bfloat16() for _ in range(W)]
+    ws = [(torch.randn(N, K, device="cuda", generator=g) * 0.05).bfloat16() for _ in range(W)]
+    outs = [torch.full((M, N), float("nan"), device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+    want = sum(x.float() @ w.float().t() for x, w in zip(xs, ws))
+
+    def step():
+        for t, x, w, o in zip(targets, xs, ws, outs):
+            C.skinny_linear(x, w, o, *t.publish_target())
+            t.reduce_into(o)
+        for t in targets:
+            t.finish()
+
+    for _ in range(2):  # both slot parities
+        step()
+        torch.cuda.synchronize()
+        check_status()
+        for o in outs:
+            assert _rel(o, want) < 1e-2
+        assert all(torch.equal(o, outs[0]) for o in outs)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for it in range(3):
+        for x in xs:
+            x.copy_(torch.randn(M, K, device="cuda", generator=g))
+        graph.replay()
+        torch.cuda.synchronize()
+        check_status()
+        want = sum(x.float() @ w.float().t() for x, w in zip(xs, ws))
+        for o in outs:
+            assert _rel(o, want) < 1e-2, it
+    del graph
+    # MoE: each rank's local experts, combine published into the slot
+    E, k, H, I = 16, 4, 256, 384
+    E_l = E // W
+    x = torch.randn(M, H, device="cuda", generator=g).bfloat16()
+    sel = torch.topk(torch.randn(M, E, device="cuda", generator=g), k, -1).indices.to(torch.int32)
+    wt = torch.softmax(torch.randn(M, k, device="cuda", generator=g), -1)
+    Wg = (torch.randn(E, I, H, device="cuda", generator=g) * 0.05).bfloat16()
+    Wu = (torch.randn(E, I, H, device="cuda", generator=g) * 0.05).bfloat16()
+    Wd = (torch.randn(E, H, I, device="cuda", generator=g) * 0.05).bfloat16()
+    ys = []
+    with torch.no_grad():
+        for r, t in enumerate(targets):
+            lo = r * E_l
+            y, reduced = Fn.moe_experts_local(x, sel, wt, Wg[lo:lo + E_l], Wu[lo:lo + E_l], Wd[lo:lo + E_l], lo,
+                                              publish=t)
+            assert reduced
+            ys.append(y)
+        for t in targets:
+            t.finish()
+        full = Fn.MoEExpertsFn.apply(x, sel, wt, Wg, Wu, Wd)
+    torch.cuda.synchronize()
+    check_status()
+    for y in ys:
+        assert _rel(y, full) < 2e-2
+    for h in heaps:
+        h.close()
+
+
 def _free_port():
     s = socket.socket()
     s.bind(("127.0.0.1", 0))

@@ -235,9 +235,17 @@ class Attention(nn.Module):
             y = o.view(B, T, hq_l * hd)
         past_kv.advance(T)
         if sp > 1:
-            from tinytron_b200.parallel.symm import row_parallel_all_reduce
+            from tinytron_b200.ops.weights import bf16_of
+            from tinytron_b200.parallel.symm import row_parallel_all_reduce, row_parallel_target
 
-            y = row_parallel_all_reduce(ops.linear(y, self.c_proj.weight[:, q0 * hd:q1 * hd]), sp_group)
+            ar = row_parallel_target(sp_group)
+            fused = None
+            if ar is not None:  # c_proj's split sums published straight into the all-reduce slot
+                fused = ops.linear_row_parallel(y, bf16_of(self.c_proj.weight)[:, q0 * hd:q1 * hd], ar)
+            if fused is not None:
+                y = fused
+            else:
+                y = row_parallel_all_reduce(ops.linear(y, self.c_proj.weight[:, q0 * hd:q1 * hd]), sp_group)
         else:
             y = ops.linear(y, self.c_proj.weight)
         return y, (past_kv if use_cache else None)

@@ -147,12 +147,14 @@ class MoE(nn.Module):
         all-reduced.  On CUDA this is device-only (grouped GEMMs over the local segments,
         graph-capturable heap all-reduce); the CPU path selects the local pairs eagerly."""
         D = self.hidden_size
-        from tinytron_b200.parallel.symm import row_parallel_all_reduce
+        from tinytron_b200.parallel.symm import row_parallel_all_reduce, row_parallel_target
 
         if flat_x.is_cuda:
-            partial = ops.moe_experts_local(flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights,
-                                            self.experts_down_weights, ep_rank * self.num_local_experts)
-            return row_parallel_all_reduce(partial, ep_group).reshape(B, T, D)
+            # decode-sized batches: the combine publishes straight into the heap all-reduce
+            y, reduced = ops.moe_experts_local_published(
+                flat_x, sel, weights, self.experts_gate_weights, self.experts_up_weights, self.experts_down_weights,
+                ep_rank * self.num_local_experts, row_parallel_target(ep_group))
+            return (y if reduced else row_parallel_all_reduce(y, ep_group)).reshape(B, T, D)
         tgt = sel // self.num_local_experts
         mask = tgt == ep_rank
         partial = flat_x.new_zeros((flat_x.size(0), D))

@@ -124,12 +124,26 @@ def moe_experts_local(x: torch.Tensor, sel: torch.Tensor, weights: torch.Tensor,
     SwiGLU_{sel[t, j]}(x[t]) restricted to the experts [e_lo, e_lo + E_local) held here
     (``sel`` holds global expert ids; the caller all-reduces the partial sums)."""
     if x.is_cuda:
-        return _cuda_fn().moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo)
+        return _cuda_fn().moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo)[0]
     E = w_gate.shape[0]
     local = sel - e_lo
     mine = (local >= 0) & (local < E)
     y = moe_experts(x, local.clamp(0, E - 1), weights * mine.to(weights.dtype), w_gate, w_up, w_down)
     return y
+
+
+def moe_experts_local_published(x, sel, weights, w_gate, w_up, w_down, e_lo: int, ar):
+    """CUDA inference with experts sharded over an EP group whose graph-safe heap
+    all-reduce is ``ar``: (output, reduced).  For a decode-sized batch the combine publishes
+    the partial sums into ``ar`` and the output is already the group sum (reduced True);
+    otherwise it is this rank's partial sum."""
+    return _cuda_fn().moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo, publish=ar)
+
+
+def linear_row_parallel(x: torch.Tensor, w16: torch.Tensor, ar):
+    """CUDA inference: x @ w16^T summed over the SEP group of the heap all-reduce ``ar``,
+    with the publish fused into the GEMM's split-sum kernel; None when not applicable."""
+    return _cuda_fn().linear_row_parallel(x, w16, ar) if x.is_cuda else None
 
 
 def embedding(idx: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:

@@ -51,6 +51,22 @@ def gemm_nt(a: torch.Tensor, w16: torch.Tensor, out_dtype=torch.bfloat16) -> tor
     return out
 
 
+@torch.no_grad()
+def linear_row_parallel(x: torch.Tensor, w16: torch.Tensor, ar) -> torch.Tensor | None:
+    """x [..., K] @ w16[N, K]^T summed over the SEP group whose graph-safe heap all-reduce
+    is ``ar`` (inference): the decode-sized product's split-sum kernel writes its result
+    straight into ``ar``'s slot and signals the peers, so only the reducing kernel follows
+    (no separate publish copy).  None when the shape does not take this path."""
+    x2d = _bf16(x.reshape(-1, x.shape[-1]))
+    M, N = x2d.shape[0], w16.shape[0]
+    if M > SKINNY_MAX_ROWS or N % 4 or not skinny_enabled() or not ar.fits(M * N):
+        return None
+    out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    C().skinny_linear(x2d, w16, out, *ar.publish_target())
+    ar.reduce_into(out)
+    return out.view(*x.shape[:-1], N)
+
+
 def gemm_nn(a: torch.Tensor, w16: torch.Tensor, alpha_t=None) -> torch.Tensor:
     """a [M, N] @ w16[N, K]  (dgrad)."""
     out = torch.empty(a.shape[0], w16.shape[1], device=a.device, dtype=torch.bfloat16)
@@ -193,13 +209,15 @@ def moe_align(pairs: int, experts: int) -> int:
 
 
 @torch.no_grad()
-def moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo: int | None = None, out=None):
+def moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo: int | None = None, out=None, publish=None):
     """Routed experts for a decode-sized batch (<= 32 tokens, no autograd) on the
     weight-streaming kernels: every expert's weights are read once by all SMs, token rows
     sit in unpadded expert segments, and the down projection's split sums are combined
     with the top-k weights in one pass.  ``e_lo`` set: only the experts [e_lo, e_lo + E)
     held by this rank (the others' pairs go to an extra segment that is never computed),
-    as in :func:`moe_experts_local`."""
+    as in :func:`moe_experts_local`.  ``publish`` (a graph-safe heap all-reduce of the EP
+    group): the combine writes the partial sums into its slot and signals the peers, and
+    the returned tensor is already the sum over the group."""
     x2d = _bf16(x.reshape(-1, x.shape[-1]))
     N, H = x2d.shape
     E, I = w_gate.shape[0], w_gate.shape[1]
@@ -222,19 +240,29 @@ def moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo: int | None =
     c.moe_skinny_swiglu(xr, w_gu, g_loc, E, act)
     out = torch.empty(N, H, device=dev, dtype=torch.bfloat16) if out is None else out
     w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
-    c.moe_skinny_down_combine(act, bf16_of(w_down).view(E * H, I), g_loc, E, slot, w32, k, out, g_loc[E:E + 1])
+    target = publish.publish_target() if publish is not None else (-1, 0, 0)
+    c.moe_skinny_down_combine(act, bf16_of(w_down).view(E * H, I), g_loc, E, slot, w32, k, out, g_loc[E:E + 1],
+                              *target)
+    if publish is not None:
+        publish.reduce_into(out)
     return out
 
 
-def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None):
+def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None, publish=None):
     """Expert-parallel inference: the weighted partial sum over the experts
     [e_lo, e_lo + E_local) held by this rank, for every token (zeros where none of a
     token's experts is here).  Everything stays on the device (no host synchronisation,
     so a decode step containing it can be captured in a CUDA graph): pairs routed
     elsewhere go to an extra "remote" segment that the grouped GEMMs never compute, and
-    the combine stops at the local row count read on the device."""
-    if x.reshape(-1, x.shape[-1]).shape[0] <= SKINNY_MAX_ROWS and skinny_enabled():
-        return moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo, out)
+    the combine stops at the local row count read on the device.  Returns (output,
+    reduced): with ``publish`` (the EP group's heap all-reduce) a decode-sized batch is
+    summed over the group by the fused publish (reduced True); otherwise the caller
+    all-reduces the partial sums."""
+    N = x.reshape(-1, x.shape[-1]).shape[0]
+    if N <= SKINNY_MAX_ROWS and skinny_enabled():
+        if publish is not None and not publish.fits(N * x.shape[-1]):
+            publish = None
+        return moe_experts_decode(x, sel, weights, w_gate, w_up, w_down, e_lo, out, publish), publish is not None
     x2d = _bf16(x.reshape(-1, x.shape[-1]))
     N, H = x2d.shape
     E, I = w_gate.shape[0], w_gate.shape[1]
@@ -262,7 +290,7 @@ def moe_experts_local(x, sel, weights, w_gate, w_up, w_down, e_lo: int, out=None
     out = torch.empty(N, H, device=dev, dtype=torch.bfloat16) if out is None else out
     w32 = weights.reshape(-1).float().contiguous() if weights is not None else None
     c.moe_combine(yr, slot, w32, k, out, grp_off[E:E + 1])
-    return out
+    return out, False
 
 
 class MoEExpertsFn(torch.autograd.Function):

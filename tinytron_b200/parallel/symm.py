@@ -224,6 +224,18 @@ class RowParallelAllReduce:
         self.heap = SymmetricHeap.create(2 * ((nbytes + ALIGN - 1) // ALIGN * ALIGN), group, device)
         self.slots, self.slot_bytes = self.heap.replay_slots(nbytes)
 
+    def fits(self, numel: int) -> bool:
+        return numel <= self.max_numel and numel % 8 == 0
+
+    def publish_target(self) -> tuple[int, int, int]:
+        """(heap id, slot offset, slot bytes) for a producer kernel that writes its result
+        into this rank's slot and signals the peers itself (the fused publish); only
+        :meth:`reduce_into` has to follow."""
+        return self.heap.gid, self.heap.offset_of(self.slots), self.slot_bytes
+
+    def reduce_into(self, out: torch.Tensor) -> None:
+        self.heap.replay_reduce(self.slots, self.slot_bytes, out.view(-1))
+
     def __call__(self, y: torch.Tensor) -> torch.Tensor | None:
         n = y.numel()
         if y.dtype != torch.bfloat16 or n > self.max_numel or not y.is_cuda or n % 8:
@@ -262,6 +274,11 @@ def disable_row_parallel_all_reduce(group) -> None:
 
 def row_parallel_heap_enabled(group) -> bool:
     return id(group) in _ROW_AR
+
+
+def row_parallel_target(group) -> RowParallelAllReduce | None:
+    """The group's heap all-reduce, for producers that publish into it themselves."""
+    return _ROW_AR.get(id(group))
 
 
 def row_parallel_all_reduce(y: torch.Tensor, group) -> torch.Tensor:
