@@ -65,42 +65,69 @@ __device__ __forceinline__ float block_sum(float v, float* sh) {
 // Radix select.  MODE 0: the key of the k-th largest element (count histogram).
 // MODE 1: the largest key K such that the mass of keys > K is <= budget and the mass of
 // keys >= K exceeds it (keys > K are the nucleus); returns 0 when everything fits.
+// Each pass builds a 256-bin histogram of the next key byte: every warp adds into its own
+// histogram (logits cluster in a few exponent bins, so one shared histogram would
+// serialise all the block's atomics on those bins), 256 threads merge the 32 warp
+// histograms, and a suffix scan over the bins picks the byte in one step.
+constexpr int kWarps = THREADS / 32;
+
 template <int MODE, typename T>
 __device__ uint32_t radix_select(const T* row, int V, float inv_t, float mx, uint32_t floor_key, float target,
-                                 float* hist, float* sh) {
+                                 float (*hist_w)[256], float* suf, float* sh) {
   uint32_t prefix = 0, prefix_mask = 0;
   float above = 0.0f;  // count / mass of keys strictly above the current prefix range
-  if (threadIdx.x == 0) sh[35] = 0.0f;
+  const int warp = threadIdx.x >> 5;
+  bool all_fit = false;
   for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int i = threadIdx.x; i < 256; i += THREADS) hist[i] = 0.0f;
+    for (int i = threadIdx.x; i < kWarps * 256; i += THREADS) hist_w[i >> 8][i & 255] = 0.0f;
     __syncthreads();
     for (int i = threadIdx.x; i < V; i += THREADS) {
       const float x = load_logit(row, i, inv_t);
       const uint32_t k = key_of(x);
       if (k < floor_key || (k & prefix_mask) != prefix) continue;
-      atomicAdd(&hist[(k >> shift) & 0xFFu], MODE == 0 ? 1.0f : __expf(x - mx));
+      atomicAdd(&hist_w[warp][(k >> shift) & 0xFFu], MODE == 0 ? 1.0f : __expf(x - mx));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int d = 255;
-      for (; d >= 0; --d) {
-        if (above + hist[d] >= target && (MODE == 0 || above + hist[d] > target)) break;
-        above += hist[d];
-      }
-      if (d < 0) {  // everything left fits the budget (top-p keeps all candidates)
-        d = 0;
-        sh[35] = 1.0f;
-      }
-      sh[33] = __uint_as_float(static_cast<uint32_t>(d));
+    // merge, then suffix sums from the top bin down (Hillis-Steele over 256 entries)
+    if (threadIdx.x < 256) {
+      float v = 0.0f;
+#pragma unroll 8
+      for (int w = 0; w < kWarps; ++w) v += hist_w[w][threadIdx.x];
+      suf[threadIdx.x] = v;
     }
     __syncthreads();
-    const uint32_t d = __float_as_uint(sh[33]);
-    prefix |= d << shift;
+    for (int o = 1; o < 256; o <<= 1) {
+      float add = 0.0f;
+      if (threadIdx.x < 256 && threadIdx.x + o < 256) add = suf[threadIdx.x + o];
+      __syncthreads();
+      if (threadIdx.x < 256) suf[threadIdx.x] += add;
+      __syncthreads();
+    }
+    // the byte d: the highest bin whose cumulative count/mass from the top reaches the target
+    if (threadIdx.x == 0) sh[33] = -1.0f;
+    __syncthreads();
+    if (threadIdx.x < 256) {
+      const int d = threadIdx.x;
+      const float incl = above + suf[d];
+      const float excl = above + (d < 255 ? suf[d + 1] : 0.0f);
+      const bool reach = MODE == 0 ? incl >= target : incl > target;
+      const bool before = MODE == 0 ? excl >= target : excl > target;
+      if (reach && !before) {
+        sh[33] = static_cast<float>(d);
+        sh[34] = excl;
+      }
+    }
+    __syncthreads();
+    const float dsel = sh[33];
+    if (dsel < 0.0f) {  // everything left fits the budget (top-p keeps all candidates)
+      all_fit = true;
+      break;
+    }
+    above = sh[34];
+    prefix |= static_cast<uint32_t>(dsel) << shift;
     prefix_mask |= 0xFFu << shift;
-    if (sh[35] != 0.0f) break;
     __syncthreads();
   }
-  const bool all_fit = sh[35] != 0.0f;
   __syncthreads();
   return all_fit ? 0u : prefix;
 }
@@ -112,7 +139,8 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
                                                         const long long* __restrict__ rng,
                                                         int64_t* __restrict__ tokens, float* __restrict__ logprob) {
   __shared__ float sh[36];
-  __shared__ float hist[256];
+  __shared__ float hist_w[kWarps][256];
+  __shared__ float suf[256];
   __shared__ float scan[THREADS];
   const int r = blockIdx.x;
   const T* row = logits + static_cast<long long>(r) * ld;
@@ -144,7 +172,7 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
   if (top_k == 1) {
     floor_key = key_of(gmax);
   } else if (top_k > 0 && top_k < V) {
-    floor_key = radix_select<0>(row, V, inv_t, gmax, 0u, static_cast<float>(top_k), hist, sh);
+    floor_key = radix_select<0>(row, V, inv_t, gmax, 0u, static_cast<float>(top_k), hist_w, suf, sh);
   }
   // ---- mass of the top-k set
   float z = 0.0f;
@@ -157,7 +185,7 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
   uint32_t excl = 0;  // 0: no top-p cut
   bool use_excl = false;
   if (top_k != 1 && top_p > 0.0f && top_p < 1.0f) {
-    excl = radix_select<1>(row, V, inv_t, gmax, floor_key, top_p * z, hist, sh);
+    excl = radix_select<1>(row, V, inv_t, gmax, floor_key, top_p * z, hist_w, suf, sh);
     use_excl = true;
   }
   auto kept = [&](uint32_t k, int i) {
