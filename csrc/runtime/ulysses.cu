@@ -48,26 +48,42 @@ struct UlExch {
 };
 
 
+// Each thread moves kUlUnroll 16-byte vectors per step, all loads issued before any store,
+// so a thread keeps several NVLink (or HBM) round trips in flight instead of one; index
+// math is 32-bit (the host checks that every vector count fits).
+constexpr int kUlUnroll = 4;
+
 __global__ void __launch_bounds__(kUlThreads) ul_pack_kernel(PeerTable t, size_t slot_off, long long slot_bytes,
                                                             const __nv_bfloat16* __restrict__ src, int B, int T,
                                                             UlPack d) {
   const uint64_t e = dev_epoch_next(t);
-  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(t.base[t.rank] + slot_off +
-                                                        static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes));
+  uint4* dst = reinterpret_cast<uint4*>(t.base[t.rank] + slot_off +
+                                        static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes));
   const int wv = d.W / 8;
-  const long long total = static_cast<long long>(t.world) * B * T * wv;
-  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-    const int v = static_cast<int>(i % wv);
-    const long long row = i / wv;  // (c, b, t)
-    const int tt = static_cast<int>(row % T);
-    const int b = static_cast<int>((row / T) % B);
-    const int c = static_cast<int>(row / (static_cast<long long>(T) * B));
-    const int w = v * 8;
-    const int col = w < d.s1 ? d.base0[c] + w : (w < d.s2 ? d.base1[c] + (w - d.s1) : d.base2[c] + (w - d.s2));
-    const long long srow = b * d.rs_b + c * d.rs_c + tt * d.rs_t;
-    reinterpret_cast<uint4*>(dst)[i] =
-        *reinterpret_cast<const uint4*>(src + static_cast<size_t>(srow) * d.ld_src + col);
+  const int total = t.world * B * T * wv;
+  const int stride = gridDim.x * blockDim.x;
+  for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * kUlUnroll) {
+    uint4 v[kUlUnroll];
+#pragma unroll
+    for (int u = 0; u < kUlUnroll; ++u) {
+      const int i = i0 + u * stride;
+      if (i < total) {
+        const int vi = i % wv;
+        const int row = i / wv;  // (c, b, t)
+        const int tt = row % T;
+        const int b = (row / T) % B;
+        const int c = row / (T * B);
+        const int w = vi * 8;
+        const int col = w < d.s1 ? d.base0[c] + w : (w < d.s2 ? d.base1[c] + (w - d.s1) : d.base2[c] + (w - d.s2));
+        const long long srow = b * d.rs_b + c * d.rs_c + tt * d.rs_t;
+        v[u] = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(srow) * d.ld_src + col);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kUlUnroll; ++u) {
+      const int i = i0 + u * stride;
+      if (i < total) dst[i] = v[u];
+    }
   }
   grid_last_block(t, [&]() { signal_peers(t, e); });
 }
@@ -79,26 +95,39 @@ __global__ void __launch_bounds__(kUlThreads) ul_exchange_kernel(PeerTable t, si
   if (block_wait_peers(t, e, status, timeout_ns)) {
     const size_t off = slot_off + static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes);
     const int wv = d.W / 8;
-    const long long chunk_vecs = static_cast<long long>(B) * T * wv;
-    const long long total = chunk_vecs * t.world;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-      const int c = static_cast<int>(i / chunk_vecs);
-      const long long j = i - c * chunk_vecs;  // (b, t, v) inside chunk `me` of rank c
-      const int v = static_cast<int>(j % wv);
-      const long long row = j / wv;
-      const int tt = static_cast<int>(row % T);
-      const int b = static_cast<int>(row / T);
-      const uint4 q = reinterpret_cast<const uint4*>(t.base[c] + off)[static_cast<long long>(t.rank) * chunk_vecs + j];
-      const long long drow = b * d.ds_b + c * d.ds_c + tt * d.ds_t;
-      *reinterpret_cast<uint4*>(out + static_cast<size_t>(drow) * d.ld_out + c * d.dcol_c + v * 8) = q;
+    const int chunk_vecs = B * T * wv;
+    const int total = chunk_vecs * t.world;
+    const int stride = gridDim.x * blockDim.x;
+    for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * kUlUnroll) {
+      uint4 q[kUlUnroll];
+#pragma unroll
+      for (int u = 0; u < kUlUnroll; ++u) {  // chunk `me` of rank c, vector j
+        const int i = i0 + u * stride;
+        if (i < total) {
+          const int c = i / chunk_vecs;
+          const int j = i - c * chunk_vecs;
+          q[u] = reinterpret_cast<const uint4*>(t.base[c] + off)[static_cast<long long>(t.rank) * chunk_vecs + j];
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUlUnroll; ++u) {
+        const int i = i0 + u * stride;
+        if (i < total) {
+          const int c = i / chunk_vecs;
+          const int j = i - c * chunk_vecs;  // (b, t, v) inside the chunk
+          const int vi = j % wv;
+          const int row = j / wv;
+          const int tt = row % T;
+          const int b = row / T;
+          const long long drow = b * d.ds_b + c * d.ds_c + tt * d.ds_t;
+          *reinterpret_cast<uint4*>(out + static_cast<size_t>(drow) * d.ld_out + c * d.dcol_c + vi * 8) = q[u];
+        }
+      }
     }
   }
   grid_last_block(t, [&]() { *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) = e; });
 }
 
-// d(q|k|v) [B*T, (Hq + 2*Hkv) * D] of this rank's tokens from the peers' gradient chunks:
-// chunk row layout [q heads of rank c (hq_l*D) | its kv heads (hkv_l*D) | (hkv_l*D)].
 __global__ void __launch_bounds__(kUlThreads) ul_exchange_qkv_grad_kernel(
     PeerTable t, size_t slot_off, long long slot_bytes, __nv_bfloat16* __restrict__ dqkv, int B, int T, int Hq,
     int Hkv, int D, int hq_l, int hkv_l, UlPack kv, int* status, uint64_t timeout_ns) {
@@ -109,50 +138,68 @@ __global__ void __launch_bounds__(kUlThreads) ul_exchange_qkv_grad_kernel(
     const int Wtot = (Hq + 2 * Hkv) * D;
     const int wv = Wtot / 8;
     const long long chunk_elems = static_cast<long long>(B) * T * W;
-    const long long total = static_cast<long long>(B) * T * wv;
-    const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
-    for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total; i += stride) {
-      const int v = static_cast<int>(i % wv);
-      const long long row = i / wv;  // b * T + t
-      const int col = v * 8;
-      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      auto add = [&](int c, int w) {
-        const __nv_bfloat16* s = reinterpret_cast<const __nv_bfloat16*>(t.base[c] + off) +
-                                 static_cast<long long>(t.rank) * chunk_elems + row * W + w;
-        const uint4 q = *reinterpret_cast<const uint4*>(s);
-        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+    const int total = B * T * wv;
+    const int stride = gridDim.x * blockDim.x;
+    auto src_of = [&](int c, int row, int w) {
+      return reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(t.base[c] + off) +
+                                            static_cast<long long>(t.rank) * chunk_elems +
+                                            static_cast<long long>(row) * W + w);
+    };
+    auto add = [](float (&acc)[8], const uint4& q) {
+      const uint32_t uw[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float2 f = unpack_bf16x2(u[k]);
-          acc[2 * k] += f.x;
-          acc[2 * k + 1] += f.y;
-        }
-      };
-      if (col < Hq * D) {  // q head h lives on rank h / hq_l only
-        const int h = col / D;
-        add(h / hq_l, (h % hq_l) * D + col % D);
-      } else {  // kv head kh: every rank whose kv range covers it, in rank order
-        const bool is_v = col >= (Hq + Hkv) * D;
-        const int kh = (col - (is_v ? (Hq + Hkv) * D : Hq * D)) / D;
-        for (int c = 0; c < t.world; ++c) {
-          const int k0 = kv.base1[c];
-          if (kh >= k0 && kh < k0 + hkv_l) add(c, (hq_l + (is_v ? hkv_l : 0) + (kh - k0)) * D + col % D);
+      for (int k = 0; k < 4; ++k) {
+        const float2 f = unpack_bf16x2(uw[k]);
+        acc[2 * k] += f.x;
+        acc[2 * k + 1] += f.y;
+      }
+    };
+    for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * kUlUnroll) {
+      // q columns: one source each, loaded for all unrolled vectors before use; kv columns:
+      // every rank whose kv range covers the head, summed in rank order (deterministic)
+      uint4 qv[kUlUnroll];
+#pragma unroll
+      for (int u = 0; u < kUlUnroll; ++u) {
+        const int i = i0 + u * stride;
+        const int col = (i % wv) * 8;
+        if (i < total && col < Hq * D) {
+          const int h = col / D;
+          qv[u] = *src_of(h / hq_l, i / wv, (h % hq_l) * D + col % D);
         }
       }
-      uint4 o;
-      o.x = pack_bf16x2(acc[0], acc[1]);
-      o.y = pack_bf16x2(acc[2], acc[3]);
-      o.z = pack_bf16x2(acc[4], acc[5]);
-      o.w = pack_bf16x2(acc[6], acc[7]);
-      reinterpret_cast<uint4*>(dqkv)[i] = o;
+#pragma unroll
+      for (int u = 0; u < kUlUnroll; ++u) {
+        const int i = i0 + u * stride;
+        if (i >= total) continue;
+        const int row = i / wv;  // b * T + t
+        const int col = (i % wv) * 8;
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (col < Hq * D) {
+          add(acc, qv[u]);
+        } else {
+          const bool is_v = col >= (Hq + Hkv) * D;
+          const int kh = (col - (is_v ? (Hq + Hkv) * D : Hq * D)) / D;
+          for (int c = 0; c < t.world; ++c) {
+            const int k0 = kv.base1[c];
+            if (kh >= k0 && kh < k0 + hkv_l) add(acc, *src_of(c, row, (hq_l + (is_v ? hkv_l : 0) + (kh - k0)) * D + col % D));
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16x2(acc[0], acc[1]);
+        o.y = pack_bf16x2(acc[2], acc[3]);
+        o.z = pack_bf16x2(acc[4], acc[5]);
+        o.w = pack_bf16x2(acc[6], acc[7]);
+        reinterpret_cast<uint4*>(dqkv)[i] = o;
+      }
     }
   }
   grid_last_block(t, [&]() { *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) = e; });
 }
 
-// ------------------------------------------------------------------ host side
 static int ul_grid(int device, long long vecs) {
-  return std::max(1, std::min(grid_blocks(device, vecs, kUlThreads), 2 * num_sms(device)));
+  TT_CHECK(vecs < (1ll << 31), "ulysses: exchange larger than 2^31 16-byte vectors");
+  const long long per_thread = (vecs + kUlUnroll - 1) / kUlUnroll;
+  return std::max(1, std::min(grid_blocks(device, per_thread, kUlThreads), 4 * num_sms(device)));
 }
 
 static void ul_check_slots(int64_t gid, int64_t slot_offset, int64_t slot_bytes, long long need) {
