@@ -542,7 +542,12 @@ def main():
         if args.impl != "reference":
             raise
         if int(os.environ.get("RANK", "0")) == 0:
-            msg = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}"[:300]
+            import traceback
+
+            frames = traceback.extract_tb(exc.__traceback__)
+            where = f" (raised at {os.path.basename(frames[-1].filename)}:{frames[-1].lineno})" if frames else ""
+            msg = f"{type(exc).__name__}: {str(exc).splitlines()[0] if str(exc) else ''}{where}"[:300]
+            traceback.print_exc()
             print(json.dumps({"impl": "reference", "config": args.config, "unavailable": msg}), flush=True)
         sys.stdout.flush()
         os._exit(0)
