@@ -53,36 +53,42 @@ struct UlExch {
 // math is 32-bit (the host checks that every vector count fits).
 constexpr int kUlUnroll = 4;
 
+__device__ __forceinline__ int ul_warp() { return static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5); }
+__device__ __forceinline__ int ul_warps() { return static_cast<int>((gridDim.x * blockDim.x) >> 5); }
+
+// Pack: one warp per row of the send slot; the row's coordinates (destination rank,
+// batch, token) are decoded once and the lanes walk its 16-byte vectors (measured faster
+// than decoding every vector).  The exchanges below keep one vector index per thread
+// step: on NVLink that interleaving of many rows measured faster than a warp per row.
 __global__ void __launch_bounds__(kUlThreads) ul_pack_kernel(PeerTable t, size_t slot_off, long long slot_bytes,
                                                             const __nv_bfloat16* __restrict__ src, int B, int T,
                                                             UlPack d) {
   const uint64_t e = dev_epoch_next(t);
   uint4* dst = reinterpret_cast<uint4*>(t.base[t.rank] + slot_off +
                                         static_cast<size_t>(e & 1ull) * static_cast<size_t>(slot_bytes));
+  const int lane = threadIdx.x & 31;
   const int wv = d.W / 8;
-  const int total = t.world * B * T * wv;
-  const int stride = gridDim.x * blockDim.x;
-  for (int i0 = blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += stride * kUlUnroll) {
-    uint4 v[kUlUnroll];
+  const int rows = t.world * B * T;  // (c, b, t)
+  for (int row = ul_warp(); row < rows; row += ul_warps()) {
+    const int tt = row % T;
+    const int b = (row / T) % B;
+    const int c = row / (T * B);
+    const __nv_bfloat16* s = src + static_cast<size_t>(b * d.rs_b + c * d.rs_c + tt * d.rs_t) * d.ld_src;
+    const int c0 = d.base0[c], c1 = d.base1[c] - d.s1, c2 = d.base2[c] - d.s2;
+    uint4* o = dst + static_cast<size_t>(row) * wv;
+    for (int v0 = lane; v0 < wv; v0 += 32 * kUlUnroll) {
+      uint4 q[kUlUnroll];
 #pragma unroll
-    for (int u = 0; u < kUlUnroll; ++u) {
-      const int i = i0 + u * stride;
-      if (i < total) {
-        const int vi = i % wv;
-        const int row = i / wv;  // (c, b, t)
-        const int tt = row % T;
-        const int b = (row / T) % B;
-        const int c = row / (T * B);
-        const int w = vi * 8;
-        const int col = w < d.s1 ? d.base0[c] + w : (w < d.s2 ? d.base1[c] + (w - d.s1) : d.base2[c] + (w - d.s2));
-        const long long srow = b * d.rs_b + c * d.rs_c + tt * d.rs_t;
-        v[u] = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(srow) * d.ld_src + col);
+      for (int u = 0; u < kUlUnroll; ++u) {
+        const int v = v0 + 32 * u;
+        if (v < wv) {
+          const int w = v * 8;
+          q[u] = *reinterpret_cast<const uint4*>(s + (w < d.s1 ? c0 : (w < d.s2 ? c1 : c2)) + w);
+        }
       }
-    }
 #pragma unroll
-    for (int u = 0; u < kUlUnroll; ++u) {
-      const int i = i0 + u * stride;
-      if (i < total) dst[i] = v[u];
+      for (int u = 0; u < kUlUnroll; ++u)
+        if (v0 + 32 * u < wv) o[v0 + 32 * u] = q[u];
     }
   }
   grid_last_block(t, [&]() { signal_peers(t, e); });
@@ -196,6 +202,13 @@ __global__ void __launch_bounds__(kUlThreads) ul_exchange_qkv_grad_kernel(
   grid_last_block(t, [&]() { *reinterpret_cast<volatile uint64_t*>(t.base[t.rank] + kDevEpochOff) = e; });
 }
 
+// Pack grid: one warp per row (8 rows per 256-thread CTA), up to eight CTAs per SM (the
+// kernel keeps no per-block scratch, only the heap's last-block counter).
+static int ul_pack_grid(int device, long long rows) {
+  const long long blocks = (rows + kUlThreads / 32 - 1) / (kUlThreads / 32);
+  return static_cast<int>(std::max<long long>(1, std::min<long long>(blocks, 8ll * num_sms(device))));
+}
+
 static int ul_grid(int device, long long vecs) {
   TT_CHECK(vecs < (1ll << 31), "ulysses: exchange larger than 2^31 16-byte vectors");
   const long long per_thread = (vecs + kUlUnroll - 1) / kUlUnroll;
@@ -242,7 +255,8 @@ void ul_pack(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor
   ul_check_slots(gid, slot_offset, slot_bytes, vecs * 16);
   const int device = group_device(gid);
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
-  ul_pack_kernel<<<ul_grid(device, vecs), kUlThreads, 0, cur_stream()>>>(
+  TT_CHECK(vecs < (1ll << 31), "ulysses: exchange larger than 2^31 16-byte vectors");
+  ul_pack_kernel<<<ul_pack_grid(device, static_cast<long long>(t.world) * B * T), kUlThreads, 0, cur_stream()>>>(
       t, static_cast<size_t>(slot_offset), slot_bytes, reinterpret_cast<const __nv_bfloat16*>(src.data_ptr()),
       static_cast<int>(B), static_cast<int>(T), d);
   TT_CUDA_CHECK(cudaGetLastError());

@@ -179,6 +179,43 @@ def _case_zero1(n: int = 64 * 1024 * 1024, W: int = 2):
     return run, close
 
 
+def _case_ulysses(B: int = 2, T: int = 4096, Hq: int = 16, Hkv: int = 2, D: int = 128, W: int = 2):
+    """Fused Ulysses q|k|v -> heads exchange of the long-context preset on W emulated ranks
+    (W heaps on one GPU; every pack is launched before any exchange): per rank a
+    [B * T, (Hq + 2 Hkv) * D] chunk in, its heads over the W chunks out."""
+    from tinytron_b200.ops import _ext, check_status
+    from tinytron_b200.parallel.symm import SymmetricHeap
+    from tinytron_b200.parallel.ulysses import kv_heads_for_rank
+
+    C = _ext.load()
+    hq_l = Hq // W
+    kv0 = [kv_heads_for_rank(r, W, Hq, Hkv)[0] for r in range(W)]
+    hkv_l = kv_heads_for_rank(0, W, Hq, Hkv)[1] - kv0[0]
+    Wc = (hq_l + 2 * hkv_l) * D
+    nbytes = W * B * T * Wc * 2
+    heaps = SymmetricHeap.create_emulated(2 * nbytes + 4096, W)
+    slots = [h.replay_slots(nbytes) for h in heaps]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    qkvs = [torch.randn(B * T, (Hq + 2 * Hkv) * D, device="cuda", generator=g).bfloat16() for _ in range(W)]
+    fulls = [torch.empty(B * W * T, Wc, device="cuda", dtype=torch.bfloat16) for _ in range(W)]
+    b0 = [c * hq_l * D for c in range(W)]
+    b1 = [Hq * D + k * D for k in kv0]
+    b2 = [(Hq + Hkv) * D + k * D for k in kv0]
+
+    def run():
+        for h, (buf, sb), src in zip(heaps, slots, qkvs):
+            C.ul_pack(h.gid, h.offset_of(buf), sb, src, B, T, [T, 0, 1], Wc, hq_l * D, (hq_l + hkv_l) * D, b0, b1, b2)
+        for h, (buf, sb), out in zip(heaps, slots, fulls):
+            C.ul_exchange(h.gid, h.offset_of(buf), sb, out, B, T, [W * T, T, 1], 0, Wc)
+
+    def close():
+        check_status()
+        for h in heaps:
+            h.close()
+
+    return run, close
+
+
 def _case_ep(N: int = 4096, W: int = 2, E: int = 64, k: int = 8, H: int = 2048, I: int = 1408):
     from tinytron_b200.ops import check_status
     from tinytron_b200.ops.weights import concat_rows
@@ -440,7 +477,7 @@ KERNEL_CASES = {"zero1": _case_zero1, "ep": _case_ep, "decode": _case_decode, "a
                 "dswiglu": _case_dswiglu, "moe_decode": _case_moe_decode, "moe_decode_ep8": _case_moe_decode_ep8, "muon": _case_muon,
                 "muon_torch": _case_muon_torch, "norm": _case_norm,
                 "muon_2layers": lambda: _case_muon(layers=2), "ce": _case_ce, "router": _case_router,
-                "sample": _case_sample}
+                "sample": _case_sample, "ulysses": _case_ulysses}
 
 
 def bench_case(name: str, iters: int, warmup: int) -> list[dict]:
