@@ -482,11 +482,14 @@ def run_decode(args, impl: str):
         eng.generate(prompt, 8, **gen_kw)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    prompt_host = prompt.pin_memory()  # the timed call copies its prompt from pinned host memory
     with ClockSampler(rank == 0 and not args.no_clocks) as clk:
         s.record()
-        _, stats = eng.generate(prompt, NEW, **gen_kw)
+        toks, stats = eng.generate(prompt_host, NEW, **gen_kw)
+        toks_host = toks.cpu()  # device -> host read of the result, inside the timed region
         e.record()
         torch.cuda.synchronize()
+    d2h = toks_host.numel() * toks_host.element_size()
     total_ms = _max_over_ranks(s.elapsed_time(e))
     dec_ms = _max_over_ranks(stats.get("decode_ms_device", stats["decode_tokens"] / max(
         stats["decode_tokens_per_sec"], 1e-9) * 1e3))
@@ -501,8 +504,11 @@ def run_decode(args, impl: str):
                       "decode_steps": NEW, "kv_cache": f"paged page={args.page_size}" if args.page_size > 0 else
                       "contiguous", "parallelism": f"sep{world}" if world > 1 else "1 GPU"},
            "prefill_tokens_per_sec": round(B * P / (pre_ms / 1e3), 1),
-           "e2e": {"value": round(value, 1), "unit": "generated tokens/s (prefill + decode, device-timed)",
-                   "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 8 * B},
+           "e2e": {"value": round(value, 1),
+                   "unit": "generated tokens/s through InferenceEngine.generate: the prompt copied from pinned host "
+                           "memory, prefill, decode and the generated tokens read back to the host (device-timed); "
+                           "byte counts are per generate() call",
+                   "h2d_bytes_per_step": prompt.numel() * prompt.element_size(), "d2h_bytes_per_step": d2h},
            "clocks": clk.summary(world)}
     if impl == "reference":
         out["impl"] = "reference"
