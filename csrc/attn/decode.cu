@@ -16,6 +16,7 @@
 #include "common/ptx.cuh"
 #include "common/host_utils.h"
 
+#include <mutex>
 #include <type_traits>
 
 namespace tt {
@@ -323,13 +324,12 @@ __global__ void decode_combine_kernel(const float* __restrict__ o_part, const fl
 // The split kernel's ~40 KB of static shared memory allows 5 CTAs per SM only with the
 // largest shared-memory carveout, so ask for it (a per-kernel attribute, set once).
 template <int D, int G>
-void launch_split(const DecodeParams& p, dim3 grid, cudaStream_t stream) {
-  static const bool carveout_set = [] {
+void launch_split(const DecodeParams& p, dim3 grid, cudaStream_t stream, int device) {
+  static std::once_flag once[64];  // the attribute belongs to the current device's context
+  std::call_once(once[device & 63], [] {
     cudaFuncSetAttribute(decode_split_kernel<D, G>, cudaFuncAttributePreferredSharedMemoryCarveout,
                          cudaSharedmemCarveoutMaxShared);
-    return true;
-  }();
-  (void)carveout_set;
+  });
   decode_split_kernel<D, G><<<grid, kThreads, 0, stream>>>(p);
 }
 
@@ -435,7 +435,7 @@ void decode_attention(torch::Tensor q, torch::Tensor k_pages, torch::Tensor v_pa
   const c10::cuda::CUDAGuard guard(q.device());
   dim3 grid(static_cast<unsigned>(splits), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
   const int G = static_cast<int>(Hq / Hkv);
-#define TT_DECODE(DV, GV) decode::launch_split<DV, GV>(p, grid, cur_stream())
+#define TT_DECODE(DV, GV) decode::launch_split<DV, GV>(p, grid, cur_stream(), q.get_device())
   if (D == 128) {
     switch (G) {
       case 1: TT_DECODE(128, 1); break;
