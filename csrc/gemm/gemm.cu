@@ -153,7 +153,12 @@ __device__ __forceinline__ TileInfo decode_tile(int tile, int num_m, int num_n, 
   return t;
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// Logistic sigmoid with the approximate exponential and the approximate division
+// (__fdividef): two special-function ops and a few FMAs, against a branchy IEEE-exact
+// division sequence per element; the results are rounded to bf16 afterwards.  For x below
+// about -88 the exponential overflows to inf and __fdividef(1, inf) gives 0, the limit.
+__device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float silu_f(float x) { return x * sigmoid_f(x); }
 
 __device__ __forceinline__ int ld_acquire_gpu_s32(const int* p) {
   int v;
@@ -386,7 +391,7 @@ __device__ __forceinline__ void epilogue_row(const Params& p, uint32_t t_row, in
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const float d = __uint_as_float(r[i]) * alpha;
-            const float sg = 1.0f / (1.0f + __expf(-gv[i]));
+            const float sg = sigmoid_f(gv[i]);
             du[i] = d * gv[i] * sg;
             dg[i] = d * uv[i] * sg * (1.0f + gv[i] * (1.0f - sg));
           }
