@@ -389,6 +389,11 @@ static void check_operand(const torch::Tensor& t, const char* name) {
            std::string(name) + ": rows of a 16-byte aligned row-major matrix expected");
 }
 
+// Every operand of one call must live on the launching device (the first operand's).
+static void check_device(const torch::Tensor& t, int device, const char* name) {
+  TT_CHECK(t.is_cuda() && t.get_device() == device, std::string(name) + ": must be on the operands' CUDA device");
+}
+
 // Publish target (gid >= 0): a heap slot pair of a graph-safe all-reduce (see Publish);
 // `bytes` is the size of the output that will be written there.
 static Publish make_publish(int64_t gid, int64_t slot_off, int64_t slot_bytes, int64_t bytes, int device) {
@@ -428,6 +433,8 @@ void skinny_linear_op(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64
   TT_CHECK(out.size(0) == M && out.size(1) == N && out.stride(1) == 1 && out.stride(0) % 4 == 0 &&
                reinterpret_cast<uintptr_t>(out.data_ptr()) % 8 == 0,
            "skinny_linear: out [M, N]");
+  check_device(w, x.get_device(), "skinny_linear w");
+  check_device(out, x.get_device(), "skinny_linear out");
   if (M == 0) return;
   const c10::cuda::CUDAGuard guard(x.device());
   const int device = x.get_device();
@@ -468,7 +475,13 @@ void moe_skinny_swiglu_op(torch::Tensor xr, torch::Tensor w_gu, torch::Tensor gr
   TT_CHECK(grp_off.is_cuda() && grp_off.scalar_type() == torch::kInt32 && grp_off.numel() >= E + 1,
            "moe_skinny_swiglu: grp_off int32 [E + 1]");
   TT_CHECK(w_gu.size(0) == 2 * E * I && w_gu.size(1) == K && I % 4 == 0, "moe_skinny_swiglu: w_gu [2*E*I, K]");
-  TT_CHECK(act.size(0) == cap && act.stride(1) == 1 && act.stride(0) % 4 == 0, "moe_skinny_swiglu: act [cap, I]");
+  // the split-sum kernel stores 4 bf16 (8 bytes) at a time
+  TT_CHECK(act.size(0) == cap && act.stride(1) == 1 && act.stride(0) % 4 == 0 &&
+               reinterpret_cast<uintptr_t>(act.data_ptr()) % 8 == 0,
+           "moe_skinny_swiglu: act [cap, I], 8-byte aligned");
+  check_device(w_gu, xr.get_device(), "moe_skinny_swiglu w_gu");
+  check_device(grp_off, xr.get_device(), "moe_skinny_swiglu grp_off");
+  check_device(act, xr.get_device(), "moe_skinny_swiglu act");
   if (cap == 0 || E == 0) return;
   const c10::cuda::CUDAGuard guard(xr.device());
   const int device = xr.get_device();
@@ -511,12 +524,22 @@ void moe_skinny_down_combine_op(torch::Tensor act, torch::Tensor wd, torch::Tens
   TT_CHECK(grp_off.is_cuda() && grp_off.scalar_type() == torch::kInt32 && grp_off.numel() >= E + 1,
            "moe_skinny_down: grp_off int32 [E + 1]");
   TT_CHECK(wd.size(0) == E * H && wd.size(1) == I && H % 4 == 0, "moe_skinny_down: wd [E*H, I]");
-  TT_CHECK(slot.is_cuda() && slot.scalar_type() == torch::kInt32 && slot.numel() == N * k,
+  TT_CHECK(slot.is_cuda() && slot.scalar_type() == torch::kInt32 && slot.is_contiguous() && slot.numel() == N * k,
            "moe_skinny_down: slot int32 [N * k]");
-  if (w.has_value()) TT_CHECK(w->scalar_type() == torch::kFloat32 && w->numel() == N * k, "moe_skinny_down: w fp32");
+  if (w.has_value())
+    TT_CHECK(w->is_cuda() && w->scalar_type() == torch::kFloat32 && w->is_contiguous() && w->numel() == N * k,
+             "moe_skinny_down: w fp32 [N * k]");
   if (row_limit.has_value())
     TT_CHECK(row_limit->is_cuda() && row_limit->scalar_type() == torch::kInt32, "moe_skinny_down: row_limit int32");
-  TT_CHECK(out.stride(1) == 1 && out.stride(0) % 4 == 0, "moe_skinny_down: out [N, H]");
+  TT_CHECK(out.stride(1) == 1 && out.stride(0) % 4 == 0 && reinterpret_cast<uintptr_t>(out.data_ptr()) % 8 == 0,
+           "moe_skinny_down: out [N, H], 8-byte aligned");
+  const int dev0 = act.get_device();
+  check_device(wd, dev0, "moe_skinny_down wd");
+  check_device(grp_off, dev0, "moe_skinny_down grp_off");
+  check_device(slot, dev0, "moe_skinny_down slot");
+  check_device(out, dev0, "moe_skinny_down out");
+  if (w.has_value()) check_device(*w, dev0, "moe_skinny_down w");
+  if (row_limit.has_value()) check_device(*row_limit, dev0, "moe_skinny_down row_limit");
   if (N == 0) return;
   const c10::cuda::CUDAGuard guard(act.device());
   const int device = act.get_device();
