@@ -255,17 +255,23 @@ __global__ void __launch_bounds__(THREADS) sample_kernel(const T* __restrict__ l
 // One decode step's bookkeeping on the device, so that sampling and the next step's input
 // live inside the captured decode graph: tokens[b, P + step] = nxt[b], the graph's token
 // input = nxt, the log-prob into column `step`, then step += 1 (rng[1] is the step and the
-// Philox offset of the next draw).  One block of B threads.
+// Philox offset of the next draw).  One block of B threads.  A step past the last column
+// of `tokens` (total columns) or of `lp_all` (lp_cols) is not written and sets kBadIndex:
+// the step lives on the device, so the host cannot bound it before the launch.
 __global__ void decode_advance_kernel(const int64_t* __restrict__ nxt, int B, int64_t* __restrict__ tokens,
-                                      long long ld_tokens, int P, int64_t* __restrict__ tok_in,
+                                      long long ld_tokens, int P, long long total, int64_t* __restrict__ tok_in,
                                       long long* __restrict__ rng, const float* __restrict__ lp,
-                                      float* __restrict__ lp_all, long long ld_lp) {
+                                      float* __restrict__ lp_all, long long ld_lp, long long lp_cols,
+                                      int* __restrict__ status) {
   const long long step = rng[1];
+  const bool tok_ok = step >= 0 && P + step < total;
+  const bool lp_ok = step >= 0 && step < lp_cols;
+  if (threadIdx.x == 0 && (!tok_ok || (lp != nullptr && !lp_ok))) atomicCAS(status, 0, static_cast<int>(kBadIndex));
   for (int b = threadIdx.x; b < B; b += blockDim.x) {
     const int64_t t = nxt[b];
-    tokens[b * ld_tokens + P + step] = t;
+    if (tok_ok) tokens[b * ld_tokens + P + step] = t;
     tok_in[b] = t;
-    if (lp != nullptr) lp_all[b * ld_lp + step] = lp[b];
+    if (lp != nullptr && lp_ok) lp_all[b * ld_lp + step] = lp[b];
   }
   __syncthreads();
   if (threadIdx.x == 0) rng[1] = step + 1;
@@ -277,24 +283,31 @@ void decode_advance(torch::Tensor nxt, torch::Tensor tokens, int64_t P, torch::T
                     c10::optional<torch::Tensor> lp, c10::optional<torch::Tensor> lp_all) {
   TT_CHECK(nxt.is_cuda() && nxt.scalar_type() == torch::kInt64 && nxt.is_contiguous(), "decode_advance: nxt int64");
   const int64_t B = nxt.numel();
-  TT_CHECK(tokens.scalar_type() == torch::kInt64 && tokens.dim() == 2 && tokens.size(0) == B && tokens.stride(1) == 1,
-           "decode_advance: tokens int64 [B, total]");
-  TT_CHECK(tok_in.scalar_type() == torch::kInt64 && tok_in.numel() == B && tok_in.is_contiguous(),
-           "decode_advance: token input int64 [B]");
-  TT_CHECK(rng.scalar_type() == torch::kInt64 && rng.numel() >= 2 && rng.is_cuda(), "decode_advance: rng int64 [2]");
+  TT_CHECK(tokens.is_cuda() && tokens.get_device() == nxt.get_device() && tokens.scalar_type() == torch::kInt64 &&
+               tokens.dim() == 2 && tokens.size(0) == B && tokens.stride(1) == 1 && P >= 0 && P < tokens.size(1),
+           "decode_advance: tokens int64 [B, total] on nxt's device, 0 <= P < total");
+  TT_CHECK(tok_in.is_cuda() && tok_in.get_device() == nxt.get_device() && tok_in.scalar_type() == torch::kInt64 &&
+               tok_in.numel() == B && tok_in.is_contiguous(),
+           "decode_advance: token input int64 [B] on nxt's device");
+  TT_CHECK(rng.scalar_type() == torch::kInt64 && rng.numel() >= 2 && rng.is_cuda() && rng.is_contiguous() &&
+               rng.get_device() == nxt.get_device(),
+           "decode_advance: rng int64 [2] on nxt's device");
   TT_CHECK(lp.has_value() == lp_all.has_value(), "decode_advance: lp and lp_all together");
   if (lp.has_value())
-    TT_CHECK(lp->scalar_type() == torch::kFloat32 && lp->numel() == B && lp_all->scalar_type() == torch::kFloat32 &&
+    TT_CHECK(lp->is_cuda() && lp_all->is_cuda() && lp->get_device() == nxt.get_device() &&
+                 lp_all->get_device() == nxt.get_device() && lp->scalar_type() == torch::kFloat32 &&
+                 lp->is_contiguous() && lp->numel() == B && lp_all->scalar_type() == torch::kFloat32 &&
                  lp_all->dim() == 2 && lp_all->size(0) == B && lp_all->stride(1) == 1,
-             "decode_advance: lp fp32 [B], lp_all fp32 [B, steps]");
+             "decode_advance: lp fp32 [B], lp_all fp32 [B, steps] on nxt's device");
   if (B == 0) return;
   const c10::cuda::CUDAGuard guard(nxt.device());
   sample::decode_advance_kernel<<<1, static_cast<unsigned>(std::min<int64_t>(1024, ((B + 31) / 32) * 32)), 0,
                                   cur_stream()>>>(
       nxt.data_ptr<int64_t>(), static_cast<int>(B), tokens.data_ptr<int64_t>(), tokens.stride(0), static_cast<int>(P),
-      tok_in.data_ptr<int64_t>(), reinterpret_cast<long long*>(rng.data_ptr<int64_t>()),
+      tokens.size(1), tok_in.data_ptr<int64_t>(), reinterpret_cast<long long*>(rng.data_ptr<int64_t>()),
       lp.has_value() ? lp->data_ptr<float>() : nullptr, lp.has_value() ? lp_all->data_ptr<float>() : nullptr,
-      lp.has_value() ? lp_all->stride(0) : 0);
+      lp.has_value() ? lp_all->stride(0) : 0, lp.has_value() ? lp_all->size(1) : 0,
+      device_status_ptr(nxt.get_device()));
   TT_CUDA_CHECK(cudaGetLastError());
 }
 
