@@ -215,6 +215,19 @@ static int ul_grid(int device, long long vecs) {
   return std::max(1, std::min(grid_blocks(device, per_thread, kUlThreads), 4 * num_sms(device)));
 }
 
+// Host bounds of the row maps: every (b, c, t) row of a pack source or an exchange
+// destination lies inside `t`'s rows, and the column ranges inside its row width.
+static void ul_check_rows(const torch::Tensor& t, int64_t B, int64_t T, int world, const std::vector<int64_t>& rows,
+                          const char* what) {
+  TT_CHECK(B >= 0 && T >= 0 && rows[0] >= 0 && rows[1] >= 0 && rows[2] >= 0,
+           std::string("ulysses: negative size or row stride in ") + what);
+  const int64_t ld = t.size(-1);
+  const int64_t n_rows = ld > 0 ? t.numel() / ld : 0;
+  if (B > 0 && T > 0)
+    TT_CHECK((B - 1) * rows[0] + static_cast<int64_t>(world - 1) * rows[1] + (T - 1) * rows[2] < n_rows,
+             std::string("ulysses: row map past the last row of ") + what);
+}
+
 static void ul_check_slots(int64_t gid, int64_t slot_offset, int64_t slot_bytes, long long need) {
   TT_CHECK(slot_offset % 256 == 0 && slot_bytes % 256 == 0 && need <= slot_bytes &&
                slot_offset + 2 * slot_bytes <= static_cast<int64_t>(group_bytes(gid)),
@@ -250,7 +263,15 @@ void ul_pack(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Tensor
   check_cuda_bf16(src, "src");
   TT_CHECK(src.is_contiguous() && reinterpret_cast<uintptr_t>(src.data_ptr()) % 16 == 0, "ulysses: src layout");
   const PeerTable t = group_table(gid);
+  TT_CHECK(src.get_device() == group_device(gid), "ulysses: src is not on the heap's device");
   const UlPack d = make_pack(rows, src.size(-1), W, s1, s2, b0, b1, b2, t.world);
+  ul_check_rows(src, B, T, t.world, rows, "src");
+  const int64_t ld = src.size(-1);
+  TT_CHECK(0 <= s1 && s1 <= s2 && s2 <= W, "ulysses: segments must satisfy 0 <= s1 <= s2 <= W");
+  for (int c = 0; c < t.world; ++c)  // the three column segments of destination c inside a source row
+    TT_CHECK(b0[c] >= 0 && b0[c] + s1 <= ld && b1[c] >= 0 && b1[c] + (s2 - s1) <= ld && b2[c] >= 0 &&
+                 b2[c] + (W - s2) <= ld,
+             "ulysses: pack columns outside the source row");
   const long long vecs = static_cast<long long>(t.world) * B * T * (W / 8);
   ul_check_slots(gid, slot_offset, slot_bytes, vecs * 16);
   const int device = group_device(gid);
@@ -269,6 +290,10 @@ void ul_exchange(int64_t gid, int64_t slot_offset, int64_t slot_bytes, torch::Te
   TT_CHECK(out.is_contiguous() && reinterpret_cast<uintptr_t>(out.data_ptr()) % 16 == 0 && out.size(-1) % 8 == 0 &&
                W % 8 == 0 && dcol_c % 8 == 0 && rows.size() == 3, "ulysses: out layout");
   const PeerTable t = group_table(gid);
+  TT_CHECK(out.get_device() == group_device(gid), "ulysses: out is not on the heap's device");
+  ul_check_rows(out, B, T, t.world, rows, "out");
+  TT_CHECK(dcol_c >= 0 && static_cast<int64_t>(t.world - 1) * dcol_c + W <= out.size(-1),
+           "ulysses: exchange columns outside the destination row");
   UlExch d{};
   d.ds_b = rows[0];
   d.ds_c = rows[1];
@@ -294,8 +319,14 @@ void ul_exchange_qkv_grad(int64_t gid, int64_t slot_offset, int64_t slot_bytes, 
   const PeerTable t = group_table(gid);
   TT_CHECK(dqkv.is_contiguous() && dqkv.numel() == B * T * (Hq + 2 * Hkv) * D && D % 8 == 0 &&
                static_cast<int>(kv0.size()) == t.world, "ulysses: dqkv layout");
+  TT_CHECK(dqkv.get_device() == group_device(gid), "ulysses: dqkv is not on the heap's device");
+  TT_CHECK(hq_l >= 1 && hq_l * t.world == Hq && hkv_l >= 1 && hkv_l <= Hkv,
+           "ulysses: q heads split evenly over the ranks, 1 <= kv heads per rank <= Hkv");
   UlPack kv{};
-  for (int c = 0; c < t.world; ++c) kv.base1[c] = static_cast<int>(kv0[c]);
+  for (int c = 0; c < t.world; ++c) {
+    TT_CHECK(kv0[c] >= 0 && kv0[c] + hkv_l <= Hkv, "ulysses: a rank's kv heads outside [0, Hkv)");
+    kv.base1[c] = static_cast<int>(kv0[c]);
+  }
   const long long W = (hq_l + 2 * hkv_l) * D;
   ul_check_slots(gid, slot_offset, slot_bytes, static_cast<long long>(t.world) * B * T * W * 2);
   const long long vecs = B * T * (Hq + 2 * Hkv) * D / 8;
