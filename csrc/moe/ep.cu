@@ -239,9 +239,14 @@ void ep_plan_rows(torch::Tensor sel, torch::Tensor slot, torch::Tensor delta, in
                   torch::Tensor tgt) {
   const int64_t P = sel.numel();
   TT_CHECK(sel.is_cuda() && sel.scalar_type() == torch::kInt32 && sel.is_contiguous() && slot.numel() == P &&
-               slot.scalar_type() == torch::kInt32 && delta.scalar_type() == torch::kInt32 && delta.is_contiguous(),
+               slot.scalar_type() == torch::kInt32 && slot.is_contiguous() && delta.scalar_type() == torch::kInt32 &&
+               delta.is_contiguous(),
            "ep_plan_rows: sel, slot int32 [P], delta int32 [E]");
   check_pairs(tgt, dst, P);
+  const int dev = sel.get_device();
+  TT_CHECK(slot.is_cuda() && slot.get_device() == dev && delta.is_cuda() && delta.get_device() == dev &&
+               dst.get_device() == dev && tgt.get_device() == dev,
+           "ep_plan_rows: every operand on sel's device");
   const int64_t E = delta.numel();
   TT_CHECK(E_l >= 1 && E % E_l == 0, "ep_plan_rows: E must be a multiple of E_l");
   if (P == 0) return;
