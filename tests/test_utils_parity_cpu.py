@@ -1,0 +1,76 @@
+"""The `utils` helpers return what the reference's return for the same inputs: training
+budget (gradient accumulation, steps, epochs, and the error when budgets disagree),
+parameter counts of dense and MoE configs, and the compiled -> uncompiled checkpoint
+key mapping.  Skipped when the reference is not installed under baseline/_ref."""
+import pytest
+import torch
+
+from ref_oracle import available, cpu_reference
+
+pytestmark = pytest.mark.skipif(not available(), reason="reference not installed under baseline/_ref")
+
+
+@pytest.mark.parametrize("kw", [
+    dict(num_samples=1000, tokens_per_sample=4096, global_token_batch_size=524288,
+         samples_per_dp_rank_per_micro_step=4, dp_world_size=8, max_steps=100),
+    dict(num_samples=5000, tokens_per_sample=1024, global_token_batch_size=65536,
+         samples_per_dp_rank_per_micro_step=2, dp_world_size=4, max_epochs=3),
+    dict(num_samples=64, tokens_per_sample=128, global_token_batch_size=2048,
+         samples_per_dp_rank_per_micro_step=1, dp_world_size=2, max_steps=16, max_epochs=4),
+])
+def test_training_info_matches_reference(kw):
+    with cpu_reference():
+        from tinytron.utils import get_training_info as ref_fn
+    from tinytron_b200.utils import get_training_info
+
+    assert get_training_info(**kw) == ref_fn(**kw)
+
+
+def test_training_info_rejects_the_same_inputs():
+    with cpu_reference():
+        from tinytron.utils import get_training_info as ref_fn
+    from tinytron_b200.utils import get_training_info
+
+    for kw in (dict(num_samples=64, tokens_per_sample=128, global_token_batch_size=2048,
+                    samples_per_dp_rank_per_micro_step=1, dp_world_size=2, max_steps=16, max_epochs=9),
+               dict(num_samples=64, tokens_per_sample=128, global_token_batch_size=2048,
+                    samples_per_dp_rank_per_micro_step=1, dp_world_size=2)):
+        with pytest.raises(ValueError):
+            ref_fn(**kw)
+        with pytest.raises(ValueError):
+            get_training_info(**kw)
+
+
+@pytest.mark.parametrize("moe", [False, True])
+def test_model_params_match_reference(moe):
+    kw = dict(block_size=4096, vocab_size=50304, num_layer=24, num_attention_heads=16, num_key_value_heads=4,
+              hidden_size=2048, intermediate_size=5504)
+    if moe:
+        kw.update(use_moe=True, num_experts=64, num_experts_per_tok=8, moe_intermediate_size=1408)
+    with cpu_reference():
+        from tinytron.model import ModelConfig as RefConfig
+        from tinytron.utils import get_model_params as ref_fn
+
+        ref = ref_fn(RefConfig(**kw))
+    from tinytron_b200.models import ModelConfig
+    from tinytron_b200.utils import get_model_params
+
+    assert get_model_params(ModelConfig(**kw)) == pytest.approx(ref)
+
+
+def test_compiled_key_mapping_matches_reference(capsys):
+    from tinytron_b200.models import GPT, ModelConfig
+    from tinytron_b200.utils import get_compiled_to_uncompiled_mapping
+
+    c = ModelConfig(block_size=32, vocab_size=64, num_layer=1, num_attention_heads=2, num_key_value_heads=1,
+                    hidden_size=32, intermediate_size=48)
+    m = GPT(c, device="cpu")
+    keys = ["_orig_mod." + k for k in list(m.state_dict())[:3]] + [list(m.state_dict())[3], "_orig_mod.not_a_key"]
+    with cpu_reference():
+        from tinytron.utils import get_compiled_to_uncompiled_mapping as ref_fn
+
+        ref = ref_fn(m, keys)
+    ours = get_compiled_to_uncompiled_mapping(m, keys)
+    assert set(ours) == set(ref)
+    for k in ref:
+        assert torch.equal(ours[k], ref[k])
