@@ -150,6 +150,7 @@ class LayerPagedKVCache:
         self._host_table = [[-1] * self.pages_per_seq for _ in range(self.batch_size)]
         self._free = list(range(self.k_pages.size(0) - 1, -1, -1))
         self.current_length = 0
+        self.seq_lens = [0] * self.batch_size
         self.len_dev.zero_()
 
 
