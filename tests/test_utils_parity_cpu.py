@@ -74,3 +74,18 @@ def test_compiled_key_mapping_matches_reference(capsys):
     assert set(ours) == set(ref)
     for k in ref:
         assert torch.equal(ours[k], ref[k])
+
+
+@pytest.mark.parametrize("path", ["ckpt/model_step_100.pt", "ckpt/model_step_100_rank0.pt", "a/b/c.pt",
+                                  "ckpt/model_step_7_meta.pt", "ckpt/model_step_7", "", "/abs/x_model.pt",
+                                  "ckpt/step_3_model_rank12.pt"])
+def test_inference_checkpoint_paths_match_reference(path):
+    with cpu_reference():
+        from tinytron.inference import checkpoint as ref
+    from tinytron_b200.inference import checkpoint as ours
+
+    assert ours.checkpoint_prefix_from_model_path(path) == ref.checkpoint_prefix_from_model_path(path)
+    prefix = "ckpt/model_step_5"
+    assert ours.checkpoint_meta_path(prefix) == ref.checkpoint_meta_path(prefix)
+    for r in (0, 3, 15):
+        assert ours.checkpoint_model_shard_path(prefix, r) == ref.checkpoint_model_shard_path(prefix, r)
