@@ -60,3 +60,38 @@ def test_reference_command_line_parses_the_same():
     ours = vars(parse_args(argv))
     for k, v in ref.items():
         assert k in ours and ours[k] == v, (k, ours.get(k), v)
+
+
+def test_config_dataclasses_keep_the_reference_fields():
+    """Every field of the reference's frozen config dataclasses exists here, and
+    build_config of a reference command line gives the same values for them."""
+    import dataclasses
+
+    argv = ["--num_layer", "2", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--batch_size", "2", "--seq_len", "32", "--block_size", "32",
+            "--vocab_size", "128", "--total_batch_size", "128", "--use_mock_data", "--max_steps", "3",
+            "--warmup_steps", "1"]
+    with cpu_reference():
+        from tinytron.training import config as ref_cfg
+        from tinytron.training.arguments import parse_args as ref_parse
+
+        ref = ref_cfg.build_config(ref_parse(argv))
+    from tinytron_b200.training import config as our_cfg
+    from tinytron_b200.training.arguments import parse_args
+
+    ours = our_cfg.build_config(parse_args(argv))
+    for name in ("Config", "TrainingConfig", "LoggingConfig", "SeedConfig", "DataConfig", "OptimConfig",
+                 "CheckpointConfig", "ParallelConfig"):
+        ref_fields = {f.name for f in dataclasses.fields(getattr(ref_cfg, name))}
+        our_fields = {f.name for f in dataclasses.fields(getattr(our_cfg, name))}
+        assert ref_fields <= our_fields, (name, sorted(ref_fields - our_fields))
+
+    def compare(r, o, path):
+        for f in dataclasses.fields(r):
+            rv, ov = getattr(r, f.name), getattr(o, f.name)
+            if dataclasses.is_dataclass(rv):
+                compare(rv, ov, f"{path}.{f.name}")
+            else:
+                assert ov == rv, (f"{path}.{f.name}", ov, rv)
+
+    compare(ref, ours, "config")
