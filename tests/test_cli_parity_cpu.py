@@ -95,3 +95,26 @@ def test_config_dataclasses_keep_the_reference_fields():
                 assert ov == rv, (f"{path}.{f.name}", ov, rv)
 
     compare(ref, ours, "config")
+
+
+@pytest.mark.parametrize("argv", [[], ["--use_moe", "--num_experts", "8", "--num_experts_per_tok", "2",
+                                       "--moe_intermediate_size", "64", "--hidden_size", "128", "--num_layer", "3"]])
+def test_model_config_builder_matches_reference(argv):
+    """add_model_config_args / build_model_config give the same ModelConfig fields (and the
+    reference's default config) for the same command line and overrides."""
+    import dataclasses
+
+    with cpu_reference():
+        from tinytron.model import add_model_config_args as ref_add
+        from tinytron.model import build_model_config as ref_build
+
+        p = argparse.ArgumentParser()
+        ref_add(p)
+        ref = ref_build(p.parse_args(argv), block_size=256)
+    from tinytron_b200.models import add_model_config_args, build_model_config
+
+    p = argparse.ArgumentParser()
+    add_model_config_args(p)
+    ours = build_model_config(p.parse_args(argv), block_size=256)
+    for f in dataclasses.fields(ref):
+        assert getattr(ours, f.name) == getattr(ref, f.name), (f.name, getattr(ours, f.name), getattr(ref, f.name))
