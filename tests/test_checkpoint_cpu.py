@@ -72,3 +72,51 @@ def test_checkpoint_files_load_in_reference_loader(tmp_path, no_dist_env):
     assert set(sd) == set(ours)
     for k, v in ours.items():
         assert sd[k].dtype == torch.float32 and torch.equal(sd[k], v.cpu()), k
+
+
+def test_reference_checkpoint_files_load_here(tmp_path, no_dist_env):
+    """The other direction: files written by the reference's own save functions (rank shard,
+    full model, meta with its training layout) load through this framework's training and
+    inference loaders, and the loaded model computes the reference model's logits."""
+    from tinytron_b200.inference import checkpoint as icp
+    from tinytron_b200.models import GPT, ModelConfig
+    from tinytron_b200.parallel import parallel_state as ps
+    from tinytron_b200.training import checkpoint as ck
+
+    cfg = ModelConfig(block_size=64, vocab_size=256, num_layer=2, num_attention_heads=4, num_key_value_heads=2,
+                      hidden_size=64, intermediate_size=96, init_std=0.02, seed=7)
+    prefix = str(tmp_path / "00002")
+    x = torch.randint(0, 256, (2, 16), generator=torch.Generator().manual_seed(1))
+    ref_oracle.ensure_gloo_world1(port=29615)
+    with ref_oracle.cpu_reference():
+        from tinytron.distributed import parallel_state
+        from tinytron.model import GPT as RefGPT
+        from tinytron.model.config import ModelConfig as RefCfg
+        from tinytron.training import checkpoint as ref_ck
+        from tinytron.training.config import ParallelConfig
+
+        parallel_state.initialize_model_parallel(ParallelConfig(sep_size=1))
+        torch.manual_seed(0)
+        rm = RefGPT(RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})).eval()
+        ref_ck.save_local_model_shard(rm, prefix, 0)
+        ref_ck.save_rank0_legacy_model(rm, prefix)
+        torch.save({"model_layout": ref_ck.model_layout_metadata(), "model_sharded": True,
+                    "model_shard_pattern": "00002_model_rank{rank:05d}.pt"}, ref_ck.checkpoint_meta_path(prefix))
+        with torch.no_grad():
+            want = rm(x)
+    own_state = not ps.model_parallel_is_initialized()
+    if own_state:
+        ps.initialize_model_parallel(sep_size=1)
+    try:
+        meta = torch.load(ck.checkpoint_meta_path(prefix), map_location="cpu", weights_only=False)
+        assert ck.find_latest_checkpoint_prefix(str(tmp_path)) == prefix
+        for sd in (ck.load_model_state_dict_for_training(prefix, cfg, 0, meta),
+                   icp.load_model_state_dict_for_inference(ck.checkpoint_model_shard_path(prefix, 0), cfg),
+                   icp.load_model_state_dict_for_inference(ck.checkpoint_model_path(prefix), cfg)):
+            m = GPT(cfg, device="cpu").eval()
+            m.load_state_dict(sd, strict=True)
+            with torch.no_grad():
+                assert torch.allclose(m(x), want, atol=1e-5)
+    finally:
+        if own_state:
+            ps.destroy_model_parallel()
