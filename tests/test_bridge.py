@@ -175,3 +175,63 @@ def test_corrupt_shard_detected():
             f.write(b"\x00\x01\x02\x03\x04\x05\x06\x07")
         with pytest.raises(tcp.CheckpointCorruptError):
             tcp.verify_checksum(path)
+
+
+def _reshard_with(api, cfg, files_prefix, src_spec, dst_layout, rank):
+    """Materialize placement `rank` of dst_layout from the source shard files with one
+    framework's bridge API (`api` is this package's or the reference's bridge module)."""
+    src = api.build_tinytron_training_layout(cfg, src_spec)
+    pl = [p for p in dst_layout.placements() if p.rank == rank][0]
+    store = api.StateDictShardFileStore(lambda p: f"{files_prefix}_model_rank{int(p.rank or 0):05d}.pt")
+    out = api.StateDictTensorStore()
+    api.RoutedMaterializer().materialize(api.LayoutPlanner().plan(src, api.localize_layout(dst_layout, pl)),
+                                         api.BridgeContext(src_store=store, dst_store=out))
+    return out.state_dict_for(pl), dst_layout.local_shards(pl)
+
+
+def test_reshard_matches_reference_bridge_and_ground_truth():
+    """SEP=4 training shards cut from one full state dict, resharded to SEP=2 training,
+    SEP=2 q/k/v-sharded inference and SEP=1 inference by this package's bridge and by the
+    reference's: every destination shard equals its slice of the full tensors in both."""
+    import ref_oracle
+    from tinytron_b200 import bridge as ours
+    from tinytron_b200.bridge.layout import to_torch_slices
+
+    if not ref_oracle.available():
+        pytest.skip("reference not installed under baseline/_ref")
+    cfg = moe_cfg()
+    g = torch.Generator().manual_seed(0)
+    full = {}
+    for s in ours.build_tinytron_canonical_layout(cfg).local_shards(
+            ours.build_tinytron_canonical_layout(cfg).placements()[0]):
+        full[s.param_name] = torch.randn(s.global_shape, generator=g)
+    src_spec = ParallelSpec(1, 4, "training")
+    src = build_tinytron_training_layout(cfg, src_spec)
+    with tempfile.TemporaryDirectory() as td, ref_oracle.cpu_reference():
+        from tinytron import bridge as ref
+        from tinytron.model.config import ModelConfig as RefCfg
+
+        rcfg = RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+        prefix = str(Path(td) / "00004")
+        for p in src.placements():  # real replicas: every rank's copy of a replicated tensor is equal
+            torch.save({s.param_name: full[s.param_name][to_torch_slices(s.global_slices)].clone()
+                        for s in src.local_shards(p)}, f"{prefix}_model_rank{p.rank:05d}.pt")
+        targets = [
+            ("train sep2", lambda api, c: api.build_tinytron_training_layout(c, api.ParallelSpec(1, 2, "training")),
+             (0, 1)),
+            ("infer sep2 qkv", lambda api, c: api.build_tinytron_inference_layout(
+                c, api.ParallelSpec(1, 2, "inference"), True), (0, 1)),
+            ("infer sep1", lambda api, c: api.build_tinytron_inference_layout(
+                c, api.ParallelSpec(1, 1, "inference"), False), (0,)),
+        ]
+        for name, make, ranks in targets:
+            for rank in ranks:
+                o_sd, o_shards = _reshard_with(ours, cfg, prefix, src_spec, make(ours, cfg), rank)
+                r_sd, _ = _reshard_with(ref, rcfg, prefix, ref.ParallelSpec(1, 4, "training"), make(ref, rcfg), rank)
+                assert set(o_sd) == set(r_sd), (name, rank)
+                names = [s.param_name for s in o_shards]
+                assert any("experts" in n for n in names) and any(".attn." in n for n in names), (name, names)
+                for s in o_shards:
+                    want = full[s.param_name][to_torch_slices(s.global_slices)]
+                    assert torch.equal(o_sd[s.param_name], want), (name, rank, s.param_name)
+                    assert torch.equal(r_sd[s.param_name], want), (name, rank, s.param_name, "reference")
