@@ -76,3 +76,29 @@ def test_kv_cache_decode_matches_reference(ref):
         rl2, _ = rm(nxt, use_cache=True, past_key_values=rkv, position_offset=10)
         ol2, _ = ours(nxt, use_cache=True, past_key_values=okv, position_offset=10)
         assert torch.allclose(ol2, rl2, atol=1e-5)
+
+
+@pytest.mark.parametrize("paged", [True, False])
+def test_engine_generate_matches_reference(ref, paged):
+    """InferenceEngine.generate on CPU in fp32, same weights: greedy tokens, their
+    log-probs and the EOS stop agree with the reference engine."""
+    from tinytron.inference import InferenceEngine as RefEngine
+    from tinytron.model.config import ModelConfig as RefCfg
+
+    from tinytron_b200.inference import InferenceEngine
+
+    cfg = _cfgs()["moe"]
+    rcfg = RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+    torch.manual_seed(0)
+    re = RefEngine(rcfg, device="cpu", dtype=torch.float32, use_paged_kv_cache=paged, kv_cache_page_size=4)
+    oe = InferenceEngine(cfg, device="cpu", dtype=torch.float32, use_paged_kv_cache=paged, kv_cache_page_size=4)
+    oe.model.load_state_dict(re.model.state_dict())
+    prompt = torch.randint(0, cfg.vocab_size, (3, 9), generator=torch.Generator().manual_seed(2))
+    rt, rinfo = re.generate(prompt, 12, temperature=1.0, top_k=1, return_logprobs=True)
+    ot, oinfo = oe.generate(prompt, 12, temperature=1.0, top_k=1, return_logprobs=True)
+    assert torch.equal(ot.cpu(), rt.cpu())
+    assert torch.allclose(oinfo["token_log_probs"].cpu(), rinfo["token_log_probs"].cpu(), atol=1e-5)
+    eos = int(rt[0, 9 + 4])  # stop when sequence 0 emits its 5th generated token
+    rt2 = re.generate(prompt, 12, temperature=1.0, top_k=1, eos_token_id=eos)
+    ot2 = oe.generate(prompt, 12, temperature=1.0, top_k=1, eos_token_id=eos)
+    assert torch.equal(ot2.cpu(), rt2.cpu())
