@@ -209,3 +209,59 @@ def test_grad_bucket_plan_tiles_buffer_and_interleaves_ownership():
         cover = sorted(sl for sls in per_rank for sl in sls)  # the ranks' slices tile the buffer
         assert cover[0][0] == 0 and cover[-1][1] == numel
         assert all(cover[i][1] == cover[i + 1][0] for i in range(len(cover) - 1))
+
+
+# ---------------------------------------------------------------- reference-compatible ZeRO-1 wrapper
+def _distopt_worker(rank, world, c, out_dir, impl):
+    import ref_oracle
+
+    from tinytron_b200.parallel import parallel_state
+
+    parallel_state.initialize_model_parallel(sep_size=1)
+    torch.manual_seed(0)
+    m = GPT(c, device="cpu")
+    base = torch.optim.AdamW(m.parameters(), lr=1e-2, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8)
+    if impl == "reference":
+        with ref_oracle.cpu_reference():
+            from tinytron.distributed import DistributedOptimizer
+    else:
+        from tinytron_b200.parallel import DistributedOptimizer
+    opt = DistributedOptimizer(base, dist.group.WORLD)
+    x, y = data(B=4, V=c.vocab_size)
+    for step in range(3):
+        opt.zero_grad()
+        _, loss, _ = m(x[rank * 2:(rank + 1) * 2], y[rank * 2:(rank + 1) * 2])
+        loss.backward()
+        for p in m.parameters():  # data-parallel gradient mean, as the trainers do before step()
+            dist.all_reduce(p.grad)
+            p.grad /= world
+        opt.step()
+    torch.save({n: p.detach().clone() for n, p in m.named_parameters()}, os.path.join(out_dir, f"{impl}{rank}.pt"))
+
+
+def test_distributed_optimizer_matches_reference_and_adamw():
+    """The reference-compatible ZeRO-1 wrapper (each rank updates the tensors it owns and
+    broadcasts them) gives the reference wrapper's parameters, equal on both ranks and
+    equal to single-process AdamW on the full batch."""
+    import ref_oracle
+
+    if not ref_oracle.available():
+        pytest.skip("reference not installed under baseline/_ref")
+    c = cfg()
+    with tempfile.TemporaryDirectory() as td:
+        for impl in ("ours", "reference"):
+            spawn(_distopt_worker, 2, c, td, impl)
+        res = {(i, r): torch.load(os.path.join(td, f"{i}{r}.pt")) for i in ("ours", "reference") for r in range(2)}
+    m = GPT(c, device="cpu")
+    opt = torch.optim.AdamW(m.parameters(), lr=1e-2, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8)
+    x, y = data(B=4, V=c.vocab_size)
+    for step in range(3):
+        opt.zero_grad()
+        loss = sum(m(x[r * 2:(r + 1) * 2], y[r * 2:(r + 1) * 2])[1] for r in range(2)) / 2
+        loss.backward()
+        opt.step()
+    for n, p in m.named_parameters():
+        for r in range(2):
+            assert torch.equal(res[("ours", r)][n], res[("ours", 0)][n]), (n, r)
+            assert torch.allclose(res[("ours", r)][n], res[("reference", r)][n], atol=1e-6), (n, r)
+            assert torch.allclose(res[("ours", r)][n], p.detach(), atol=2e-5, rtol=1e-4), (n, r)
