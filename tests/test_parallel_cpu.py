@@ -265,3 +265,50 @@ def test_distributed_optimizer_matches_reference_and_adamw():
             assert torch.equal(res[("ours", r)][n], res[("ours", 0)][n]), (n, r)
             assert torch.allclose(res[("ours", r)][n], res[("reference", r)][n], atol=1e-6), (n, r)
             assert torch.allclose(res[("ours", r)][n], p.detach(), atol=2e-5, rtol=1e-4), (n, r)
+
+
+# ---------------------------------------------------------------- public collective functions
+def _collectives_worker(rank, world, out_dir):
+    import ref_oracle
+
+    from tinytron_b200.parallel import ep_all_to_all, ep_all_to_all_no_grad, ulysses_all_to_all
+
+    with ref_oracle.cpu_reference():
+        from tinytron.distributed import ep_all_to_all as r_ep
+        from tinytron.distributed import ep_all_to_all_no_grad as r_ep_ng
+        from tinytron.distributed import ulysses_all_to_all as r_ul
+    g = torch.Generator().manual_seed(rank)
+    group = dist.group.WORLD
+    res = {}
+    x = torch.randn(world * 3, 5, generator=g)
+    for tag, fn in (("ours", ulysses_all_to_all), ("ref", r_ul)):
+        xi = x.clone().requires_grad_(True)
+        y = fn(xi, group)
+        (y * torch.arange(y.numel(), dtype=torch.float32).view_as(y)).sum().backward()
+        res[f"ul_{tag}"], res[f"ul_grad_{tag}"] = y.detach(), xi.grad
+    # uneven splits, including an empty one: rank r sends (r + c) % 3 rows to rank c
+    in_splits = [(rank + c) % 3 for c in range(world)]
+    out_splits = [(c + rank) % 3 for c in range(world)]
+    h = torch.randn(sum(in_splits), 4, generator=g)
+    for tag, fn, fn_ng in (("ours", ep_all_to_all, ep_all_to_all_no_grad), ("ref", r_ep, r_ep_ng)):
+        hi = h.clone().requires_grad_(True)
+        y = fn(hi, in_splits, out_splits, group)
+        (y * (1 + torch.arange(y.numel(), dtype=torch.float32).view_as(y))).sum().backward()
+        res[f"ep_{tag}"], res[f"ep_grad_{tag}"] = y.detach(), hi.grad
+        res[f"epng_{tag}"] = fn_ng(h.clone(), in_splits, out_splits, group)
+    torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_public_collectives_match_reference():
+    """ulysses_all_to_all, ep_all_to_all (uneven splits with empty ones) and
+    ep_all_to_all_no_grad give the reference's outputs and input gradients."""
+    import ref_oracle
+
+    if not ref_oracle.available():
+        pytest.skip("reference not installed under baseline/_ref")
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_collectives_worker, 3, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(3)]
+    for r in range(3):
+        for k in ("ul", "ul_grad", "ep", "ep_grad", "epng"):
+            assert torch.equal(res[r][f"{k}_ours"], res[r][f"{k}_ref"]), (r, k)
