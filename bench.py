@@ -22,7 +22,6 @@ import statistics
 import subprocess
 import sys
 import tempfile
-import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 
@@ -35,7 +34,7 @@ MODEL_NAME = "dense-1.3B (24L d2048 16q/4kv I5504 V50304)"
 PRESET = "b200-dense-1.3b"
 SEP = 1
 
-# MoE GPT, SEP = #GPUs + ZeRO-1, 16L d2048 16q/4kv, 64 experts x SwiGLU 1408,
+# MoE training config: MoE GPT, SEP = #GPUs + ZeRO-1, 16L d2048 16q/4kv, 64 experts x SwiGLU 1408,
 # top-8, aux 0.01, seq 4096, micro-batch 2 sequences per GPU (reference launcher convention
 # --batch_size = 2 x SEP: each rank holds 2 x SEP sequences x 4096/SEP tokens = 8192 tokens).
 MOE_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_heads", "16",
@@ -44,8 +43,8 @@ MOE_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_head
              "--num_experts_per_tok", "8", "--moe_intermediate_size", "1408", "--moe_balance_loss_weight", "0.01"]
 
 
-# long-context dense GPT, Muon + ZeRO-1, SEP = #GPUs, 16L d2048 16q/2kv,
-# SwiGLU 5504 (not given by the config; the same value in both arms), seq 32768 = 4096 per rank
+# Long-context config: dense GPT, Muon + ZeRO-1, SEP = #GPUs, 16L d2048 16q/2kv,
+# SwiGLU 5504 (the intermediate size is not fixed by the benchmark; the same value in both arms), seq 32768 = 4096 per rank
 # at SEP 8, micro-batch 1 sequence per GPU (--batch_size = 1 x SEP, the launcher convention).
 LONGCTX_FLAGS = ["--num_layer", "16", "--hidden_size", "2048", "--num_attention_heads", "16",
                  "--num_key_value_heads", "2", "--intermediate_size", "5504", "--vocab_size", "50304",
@@ -440,7 +439,7 @@ def run(args, impl: str):
 
 
 def run_decode(args, impl: str):
-    """KV-cache inference of the config-3 MoE model (random init),
+    """Decode config: KV-cache inference of the MoE training config's model (random init),
     batch 32 x 1024-token prompts, greedy decode; device-timed prefill and decode."""
     import torch
     import torch.distributed as dist
@@ -529,8 +528,8 @@ def main():
                     help="reference arm: run eager instead of --use_compile (compile is the faster of the two)")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--config", choices=["dense", "moe", "longctx", "decode"], default="dense",
-                    help="dense: BASELINE config 2 (headline); moe: config 3 (SEP = #GPUs); longctx: config 4 "
-                         "(Muon, SEP = #GPUs, seq 32768); decode: config 5")
+                    help="dense: 1.3B DP + ZeRO-1 (headline); moe: 16L x 64 experts, SEP = #GPUs + ZeRO-1; "
+                         "longctx: Muon, SEP = #GPUs, seq 32768; decode: KV-cache decode of the MoE model")
     ap.add_argument("--train-args", type=str, default="",
                     help="extra trainer flags for this framework's arm (A/B runs, e.g. '--grad_bucket_mb 0')")
     ap.add_argument("--decode-steps", type=int, default=512)

@@ -9,9 +9,8 @@ import pytest
 import torch
 
 from tinytron_b200.bridge import (BridgeContext, LayoutIndex, LayoutPlanner, ParallelSpec, Placement, RankCoord,
-                                  RoutedMaterializer, ShardSpec, StateDictShardFileStore, StateDictTensorStore,
-                                  build_tinytron_canonical_layout, build_tinytron_inference_layout,
-                                  build_tinytron_training_layout, localize_layout)
+                                  RoutedMaterializer, ShardSpec, StateDictTensorStore, build_tinytron_canonical_layout,
+                                  build_tinytron_inference_layout, build_tinytron_training_layout)
 from tinytron_b200.bridge.layout import intersect_slices, local_slices
 from tinytron_b200.models.config import ModelConfig
 

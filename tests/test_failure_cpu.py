@@ -5,7 +5,6 @@ import socket
 import time
 
 import pytest
-import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 

@@ -1,8 +1,7 @@
 """CPU training parity: framework Trainer (fp32 CPU path, flat ZeRO-1 AdamW) vs the
 reference model + torch AdamW + reference LR schedule, same weights and batches
-(BASELINE config 1 shape, shortened)."""
+(a shortened dense configuration)."""
 import math
-import os
 
 import pytest
 import torch

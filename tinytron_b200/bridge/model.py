@@ -11,7 +11,7 @@ import torch.distributed as dist
 from tinytron_b200.parallel import parallel_state
 
 from .layout import LayoutIndex, Placement
-from .materializers import BridgeContext, LocalCopyRoute, RoutedMaterializer
+from .materializers import BridgeContext, RoutedMaterializer
 from .planner import LayoutPlanner
 from .rules import (EXPERT_SUFFIXES, ParallelSpec, build_tinytron_canonical_layout, build_tinytron_inference_layout,
                     build_tinytron_training_layout)

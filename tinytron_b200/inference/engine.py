@@ -21,7 +21,6 @@ Differences that matter for speed:
 from __future__ import annotations
 
 import time
-from contextlib import nullcontext
 
 import torch
 import torch.distributed as dist

@@ -24,7 +24,7 @@ from tinytron_b200.utils.profile import nvtx_range
 from tinytron_b200.parallel import parallel_state
 
 from .config import ModelConfig
-from .modules.attn import Attention, sp_context
+from .modules.attn import Attention
 from .modules.loss import CrossEntropyLoss, ExpertLoadBalancingLoss
 from .modules.mlp import MLP, MoE
 from .modules.norm import LayerNorm, default_device

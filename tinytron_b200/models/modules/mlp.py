@@ -20,7 +20,6 @@ import time
 import torch
 import torch.distributed as dist
 import torch.nn as nn
-import torch.nn.functional as F
 
 from tinytron_b200 import ops
 from tinytron_b200.parallel import parallel_state

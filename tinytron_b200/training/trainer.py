@@ -28,10 +28,9 @@ from torch.utils.data import DataLoader
 from torch.utils.data.distributed import DistributedSampler
 
 from tinytron_b200.models import GPT
-from tinytron_b200.models.gpt import EXPERT_LOCAL_PARAM_SUFFIXES
 from tinytron_b200.parallel import parallel_state
 from tinytron_b200.parallel.buffers import FlatParams
-from tinytron_b200.parallel.zero1 import DistributedOptimizer, FlatZeRO1
+from tinytron_b200.parallel.zero1 import FlatZeRO1
 from tinytron_b200.utils import compute_mfu, get_model_params, get_training_info, set_seed
 from tinytron_b200.utils.profile import nvtx_range
 

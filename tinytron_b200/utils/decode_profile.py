@@ -1,4 +1,4 @@
-"""Per-kernel device-time breakdown of decode steps (BASELINE config 5 model).
+"""Per-kernel device-time breakdown of decode steps (the 16-layer x 64-expert MoE decode benchmark model).
 
     python -m tinytron_b200.utils.decode_profile [--layers 16] [--batch 32] [--prompt 1024] [--steps 8] [--dense]
 

@@ -22,7 +22,7 @@ def main():
     ap.add_argument("--grad-accum", type=int, default=4)
     ap.add_argument("--top", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=2)
-    ap.add_argument("--moe", action="store_true", help="MoE model of BASELINE config 3 (64 experts x 1408, top-8)")
+    ap.add_argument("--moe", action="store_true", help="the MoE benchmark model (16 layers, 64 experts x 1408, top-8)")
     args = ap.parse_args()
     import torch
 
