@@ -108,3 +108,46 @@ def test_losses_match(ref_rl, adv_shape):
     c, r, rc, rr = (torch.randn(B, generator=g) for _ in range(4))
     for beta in (0.1, 0.5):
         _same_output(rl.dpo_loss(c, r, rc, rr, beta=beta), ref_rl.dpo_loss(c, r, rc, rr, beta=beta))
+
+
+def test_rl_config_and_sync_helpers_match(ref_rl):
+    """RLConfig keeps the reference's fields and defaults; inference_model_config and
+    unwrap_model behave the same; the actor -> rollout state dict at SEP=1 holds the same
+    tensors."""
+    import dataclasses
+
+    import torch.nn as nn
+
+    import ref_oracle
+    import tinytron_b200.rl as rl
+    from tinytron_b200.models import GPT, ModelConfig
+
+    ref_fields = {f.name: f.default for f in dataclasses.fields(ref_rl.RLConfig)}
+    our_fields = {f.name: f.default for f in dataclasses.fields(rl.RLConfig)}
+    for k, v in ref_fields.items():
+        assert k in our_fields and our_fields[k] == v, (k, our_fields.get(k), v)
+    cfg = ModelConfig(block_size=32, vocab_size=64, num_layer=1, num_attention_heads=4, num_key_value_heads=2,
+                      hidden_size=32, intermediate_size=48)
+    with cpu_reference():
+        from tinytron.model.config import ModelConfig as RefCfg
+
+        rcfg = RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+    for shard in (True, False):
+        assert rl.inference_model_config(cfg, shard).inference_shard_qkv == \
+            ref_rl.inference_model_config(rcfg, shard).inference_shard_qkv == shard
+    m = nn.Linear(2, 2)
+    wrapped = nn.Module()
+    wrapped.module = m
+    assert rl.unwrap_model(wrapped) is m and ref_rl.unwrap_model(wrapped) is m and rl.unwrap_model(m) is m
+    ref_oracle.ensure_gloo_world1(port=29617)
+    model = GPT(cfg, device="cpu")
+    ours = rl.training_state_dict_to_inference(model, rl.inference_model_config(cfg, False))
+    with cpu_reference():
+        from tinytron.distributed import parallel_state
+        from tinytron.training.config import ParallelConfig
+
+        parallel_state.initialize_model_parallel(ParallelConfig(sep_size=1))
+        theirs = ref_rl.training_state_dict_to_inference(model, ref_rl.inference_model_config(rcfg, False))
+    assert set(ours) == set(theirs)
+    for k in theirs:
+        assert torch.equal(ours[k].cpu(), theirs[k].cpu()), k
