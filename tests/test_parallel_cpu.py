@@ -108,9 +108,10 @@ def _decode_worker(rank, world, c, out_dir):
     torch.save({"l1": l1, "l2": l2}, os.path.join(out_dir, f"r{rank}.pt"))
 
 
-@pytest.mark.parametrize("kv", [2, 1])
-def test_sep2_head_parallel_decode_matches_single_rank(kv):
-    c = cfg(num_key_value_heads=kv)
+@pytest.mark.parametrize("kv,moe", [(2, False), (1, False), (2, True)])
+def test_sep2_head_parallel_decode_matches_single_rank(kv, moe):
+    extra = dict(use_moe=True, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32) if moe else {}
+    c = cfg(num_key_value_heads=kv, **extra)
     with tempfile.TemporaryDirectory() as td:
         spawn(_decode_worker, 2, c, td)
         res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
