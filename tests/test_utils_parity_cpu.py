@@ -89,3 +89,27 @@ def test_inference_checkpoint_paths_match_reference(path):
     assert ours.checkpoint_meta_path(prefix) == ref.checkpoint_meta_path(prefix)
     for r in (0, 3, 15):
         assert ours.checkpoint_model_shard_path(prefix, r) == ref.checkpoint_model_shard_path(prefix, r)
+
+
+@pytest.mark.parametrize("gpu", ["NVIDIA H100 80GB HBM3", "NVIDIA A100-SXM4-80GB", "NVIDIA L40S", "Tesla V100"])
+def test_peak_flops_and_mfu_match_reference(monkeypatch, gpu):
+    """With the device name faked: the same peak for every dtype and both per-device
+    modes, and compute_mfu's (mfu, achieved, peak) for the same model FLOP count."""
+    monkeypatch.setattr(torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(torch.cuda, "get_device_name", lambda *a, **k: gpu)
+    monkeypatch.setattr(torch.cuda, "device_count", lambda: 8)
+    with cpu_reference():
+        from tinytron.utils import compute_mfu as ref_mfu
+        from tinytron.utils import get_gpu_peak_flops as ref_peak
+    from tinytron_b200.utils import compute_mfu, get_gpu_peak_flops
+
+    for dtype in ("bf16", "fp16", "fp32", "BF16"):
+        for per_device in (True, False):
+            assert get_gpu_peak_flops(dtype, per_device) == ref_peak(dtype, per_device), (dtype, per_device)
+
+    class _Model:
+        def get_flops_per_fwd_bwd(self, batch_size, seq_len):
+            return 6.0 * 1.3e9 * batch_size * seq_len
+
+    for ga in (1, 4):
+        assert compute_mfu(_Model(), 4, 4096, 0.6, ga=ga) == pytest.approx(ref_mfu(_Model(), 4, 4096, 0.6, ga=ga))
