@@ -113,3 +113,22 @@ def test_peak_flops_and_mfu_match_reference(monkeypatch, gpu):
 
     for ga in (1, 4):
         assert compute_mfu(_Model(), 4, 4096, 0.6, ga=ga) == pytest.approx(ref_mfu(_Model(), 4, 4096, 0.6, ga=ga))
+
+
+@pytest.mark.parametrize("parts,ranks_map", [(1, None), (3, None), (4, None), (None, [5, 1, 3])])
+def test_partition_tensors_matches_reference(parts, ranks_map):
+    """The ZeRO-1 whole-tensor partition (largest first onto the least-loaded part, ties by
+    key) assigns every tensor to the same part as the reference's."""
+    from collections import OrderedDict
+
+    from tinytron_b200.parallel.zero1 import partition_tensors
+
+    g = torch.Generator().manual_seed(4)
+    sizes = [int(x) for x in torch.randint(1, 50, (23,), generator=g)] + [7, 7, 7, 7]  # with ties
+    td = OrderedDict(((i // 10, i % 10), torch.empty(n)) for i, n in enumerate(sizes))
+    with cpu_reference():
+        from tinytron.distributed.zero1.distributed_optimizer import partition_tensors as ref_fn
+
+        ref, _ = ref_fn(td, ranks_map=ranks_map, num_parts=parts)
+    ours, _ = partition_tensors(td, ranks_map=ranks_map, num_parts=parts)
+    assert ours == ref
