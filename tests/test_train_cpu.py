@@ -103,3 +103,52 @@ def test_lm_collator_pads_to_sep_multiple_and_shifts():
     import pickle
 
     pickle.dumps(c)  # DataLoader workers can receive it
+
+
+@pytest.mark.skipif(not ref_oracle.available(), reason="reference not installed under baseline/_ref")
+@pytest.mark.parametrize("deterministic", [True, False])
+def test_mock_data_loader_matches_reference(tmp_path, monkeypatch, deterministic):
+    """The reference's own _init_dataset (its MockDataset, DistributedSampler and collate)
+    and this trainer's loader yield the same batches: the same token stream for the
+    same seed, epoch order and shifting.  The vocabulary is 50304, the range the
+    reference always draws from (its mock data ignores the model's vocab_size; this
+    framework draws below the model's vocab_size, which is the same at 50304)."""
+    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR"):
+        monkeypatch.delenv(k, raising=False)
+    from tinytron_b200.training.trainer import Trainer
+
+    argv = ["--use_mock_data", "--mock_data_num_samples", "24", "--log_dir", str(tmp_path), "--total_batch_size",
+            str(4 * 64), "--batch_size", "4", "--seq_len", "64", "--max_steps", "6", "--warmup_steps", "2",
+            "--num_layer", "1", "--hidden_size", "64", "--num_attention_heads", "4", "--num_key_value_heads", "2",
+            "--intermediate_size", "96", "--vocab_size", "50304", "--block_size", "64", "--seed", "7",
+            "--backend", "gloo"] + (["--deterministic"] if deterministic else [])
+
+    def batches(loader, sampler, epoch, n):
+        sampler.set_epoch(epoch)
+        out = []
+        for i, b in enumerate(loader):
+            if i == n:
+                break
+            out.append({k: v.clone() for k, v in b.items()})
+        return out
+
+    torch.manual_seed(123)  # the non-deterministic mode draws from the global generator
+    tr = Trainer(build_config(parse_args(argv)))
+    torch.manual_seed(123)
+    ours = batches(tr.train_loader, tr.train_sampler, 0, 6) + batches(tr.train_loader, tr.train_sampler, 1, 2)
+    ref_oracle.ensure_gloo_world1(port=29618)
+    with ref_oracle.cpu_reference():
+        from tinytron.training.arguments import parse_args as ref_parse
+        from tinytron.training.config import build_config as ref_build
+        from tinytron.training.trainer import Trainer as RefTrainer
+
+        rt = object.__new__(RefTrainer)  # only the data pipeline: no model, no process groups
+        rt.dp_world_size, rt.dp_rank, rt.sp_world_size = 1, 0, 1
+        rt._init_dataset(ref_build(ref_parse(argv)))
+        torch.manual_seed(123)
+        ref = batches(rt.train_loader, rt.train_sampler, 0, 6) + batches(rt.train_loader, rt.train_sampler, 1, 2)
+    assert len(ours) == len(ref) == 8
+    for i, (o, r) in enumerate(zip(ours, ref)):
+        assert set(o) >= {"input_ids", "labels"}, i
+        for k in ("input_ids", "labels"):
+            assert torch.equal(o[k], r[k]), (i, k)
