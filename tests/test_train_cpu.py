@@ -152,3 +152,49 @@ def test_mock_data_loader_matches_reference(tmp_path, monkeypatch, deterministic
         assert set(o) >= {"input_ids", "labels"}, i
         for k in ("input_ids", "labels"):
             assert torch.equal(o[k], r[k]), (i, k)
+
+
+@pytest.mark.skipif(not ref_oracle.available(), reason="reference not installed under baseline/_ref")
+@pytest.mark.parametrize("sp", [1, 2, 4])
+def test_collate_matches_reference(sp):
+    """Variable-length samples (input_ids only, or pre-shifted input_ids/labels; lists or
+    tensors; longer than seq_len) collate to the reference's input_ids/labels and valid
+    token count, and raise where it raises.  One deliberate difference: the reference
+    computes a length rounded up to the SEP size but pads only to the longest sample, so
+    its batch can have a length the sequence split cannot divide; here the batch is padded
+    to the rounded length (input 0, label -100, which the loss ignores)."""
+    from tinytron_b200.training.data import build_lm_collate_fn
+
+    argv = ["--use_mock_data", "--seq_len", "12", "--batch_size", "2", "--total_batch_size", "24",
+            "--max_steps", "3", "--warmup_steps", "1", "--sep_size", str(sp)]
+    with ref_oracle.cpu_reference():
+        from tinytron.training.arguments import parse_args as ref_parse
+        from tinytron.training.config import build_config as ref_build
+        from tinytron.training.trainer import Trainer as RefTrainer
+
+        rt = object.__new__(RefTrainer)
+        rt.sp_world_size = sp
+        ref = rt._build_lm_collate_fn(ref_build(ref_parse(argv)))
+    ours = build_lm_collate_fn(seq_len=12, sp_world_size=sp)
+    g = torch.Generator().manual_seed(sp)
+    cases = [
+        [{"input_ids": list(range(1, 8))}, {"input_ids": torch.arange(20, 26)}],  # shifted here
+        [{"input_ids": torch.arange(5), "labels": torch.arange(1, 6)},
+         {"input_ids": torch.arange(9), "labels": torch.arange(1, 10)}],  # already shifted
+        [{"input_ids": torch.randint(0, 100, (30,), generator=g)}],  # cut to seq_len
+        [{"input_ids": [3, 4]}, {"input_ids": torch.randint(0, 100, (11,), generator=g)}],
+    ]
+    for i, batch in enumerate(cases):
+        try:
+            r = ref(batch)
+        except ValueError:
+            with pytest.raises(ValueError):
+                ours(batch)
+            continue
+        o = ours(batch)
+        w = r["input_ids"].shape[1]
+        assert o["input_ids"].shape[1] % sp == 0 and o["input_ids"].shape[1] - w < sp, (i, o["input_ids"].shape, w)
+        for k, pad in (("input_ids", 0), ("labels", -100)):
+            assert torch.equal(o[k][:, :w], r[k]), (i, k, o[k], r[k])
+            assert (o[k][:, w:] == pad).all(), (i, k)
+        assert int(o["valid_token_count"]) == int(r["valid_token_count"]), i
