@@ -198,3 +198,21 @@ def test_collate_matches_reference(sp):
             assert torch.equal(o[k][:, :w], r[k]), (i, k, o[k], r[k])
             assert (o[k][:, w:] == pad).all(), (i, k)
         assert int(o["valid_token_count"]) == int(r["valid_token_count"]), i
+
+
+@pytest.mark.skipif(not ref_oracle.available(), reason="reference not installed under baseline/_ref")
+def test_lr_schedule_matches_reference():
+    """Warmup, cosine decay and the floor after max_steps: the same learning rate at every
+    step as the reference trainer's scheduler."""
+    from tinytron_b200.training.trainer import Trainer
+
+    with ref_oracle.cpu_reference():
+        from tinytron.training.trainer import Trainer as RefTrainer
+
+        rt = object.__new__(RefTrainer)
+    ours = object.__new__(Trainer)
+    for max_steps, warm, hi, lo in ((100, 10, 6e-4, 6e-5), (7, 1, 1e-3, 0.0), (50, 49, 3e-4, 3e-5)):
+        for it in range(0, max_steps + 5):
+            a = ours._lr_scheduler(it, max_steps, warm, hi, lo)
+            b = rt._lr_scheduler(it, max_steps, warm, hi, lo)
+            assert a == pytest.approx(b, rel=1e-12, abs=0), (max_steps, warm, it, a, b)
