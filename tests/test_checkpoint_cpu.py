@@ -57,6 +57,11 @@ def test_checkpoint_files_load_in_reference_loader(tmp_path, no_dist_env):
     tr.save(1)
     prefix = os.path.join(tr.log_dir, "00001")
     meta = torch.load(ck.checkpoint_meta_path(prefix), map_location="cpu", weights_only=False)
+    # every key the reference trainer writes into _meta.pt and reads back on resume
+    assert {"config", "step", "this_step_results", "opt_part_assignment", "model_layout", "model_sharded",
+            "model_shard_pattern", "sampler_state", "rng_state"} <= set(meta), sorted(meta)
+    assert set(meta["sampler_state"]) >= {"epoch", "iter_idx"} and meta["step"] == 1
+    assert meta["model_shard_pattern"].format(rank=0) == os.path.basename(ck.checkpoint_model_shard_path(prefix, 0))
     ours = tr.raw_model.state_dict()
     ref_oracle.ensure_gloo_world1(port=29613)
     with ref_oracle.cpu_reference():
