@@ -313,3 +313,61 @@ def test_public_collectives_match_reference():
     for r in range(3):
         for k in ("ul", "ul_grad", "ep", "ep_grad", "epng"):
             assert torch.equal(res[r][f"{k}_ours"], res[r][f"{k}_ref"]), (r, k)
+
+
+# ---------------------------------------------------------------- live training -> inference reshard
+def _live_reshard_worker(rank, world, out_dir):
+    from dataclasses import replace
+
+    import ref_oracle
+    from tinytron_b200.bridge import (build_tinytron_canonical_layout, build_tinytron_inference_layout,
+                                      build_tinytron_training_layout, current_tinytron_parallel_spec,
+                                      current_tinytron_placement, distributed_training_state_dict_to_local_inference)
+    from tinytron_b200.bridge.layout import to_torch_slices
+    from tinytron_b200.parallel import parallel_state
+
+    c = cfg(use_moe=True, num_experts=4, num_experts_per_tok=2, moe_intermediate_size=32)
+    parallel_state.initialize_model_parallel(sep_size=world)
+    canon = build_tinytron_canonical_layout(c)
+    g = torch.Generator().manual_seed(0)  # the same full tensors on every rank
+    full = {s.param_name: torch.randn(s.global_shape, generator=g) for s in canon.local_shards(canon.placements()[0])}
+    train = build_tinytron_training_layout(c, current_tinytron_parallel_spec("training"))
+    mine = current_tinytron_placement(train)
+    sd = {s.param_name: full[s.param_name][to_torch_slices(s.global_slices)].clone() for s in train.local_shards(mine)}
+    icfg = replace(c, inference_shard_qkv=True)
+    res = {"p2p": distributed_training_state_dict_to_local_inference(sd, icfg, use_p2p=True),
+           "bcast": distributed_training_state_dict_to_local_inference(sd, icfg, use_p2p=False)}
+    dst = build_tinytron_inference_layout(icfg, current_tinytron_parallel_spec("inference"), shard_qkv=True)
+    res["want"] = {s.param_name: full[s.param_name][to_torch_slices(s.global_slices)]
+                   for s in dst.local_shards(current_tinytron_placement(dst))}
+    with ref_oracle.cpu_reference():
+        from tinytron.bridge import distributed_training_state_dict_to_local_inference as ref_fn
+        from tinytron.distributed import parallel_state as ref_ps
+        from tinytron.model.config import ModelConfig as RefCfg
+        from tinytron.training.config import ParallelConfig
+
+        ref_ps.initialize_model_parallel(ParallelConfig(sep_size=world))
+        rcfg = RefCfg(**{k: v for k, v in icfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+        res["ref"] = ref_fn(sd, rcfg)
+    torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_live_reshard_matches_reference():
+    """Every rank's SEP=2 training shard -> its q/k/v-sharded inference shard over gloo:
+    the packed per-rank-pair transfer and the broadcast mode both give the reference
+    bridge's tensors, which are the full tensors' slices."""
+    import ref_oracle
+
+    if not ref_oracle.available():
+        pytest.skip("reference not installed under baseline/_ref")
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_live_reshard_worker, 2, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(2)]
+    for r in range(2):
+        want = res[r]["want"]
+        assert any("experts" in k for k in want) and any("q_proj" in k for k in want)
+        for mode in ("p2p", "bcast", "ref"):
+            got = res[r][mode]
+            assert set(got) == set(want), (r, mode, sorted(set(got) ^ set(want)))
+            for k in want:
+                assert torch.equal(got[k], want[k]), (r, mode, k)
