@@ -297,12 +297,29 @@ def _collectives_worker(rank, world, out_dir):
         (y * (1 + torch.arange(y.numel(), dtype=torch.float32).view_as(y))).sum().backward()
         res[f"ep_{tag}"], res[f"ep_grad_{tag}"] = y.detach(), hi.grad
         res[f"epng_{tag}"] = fn_ng(h.clone(), in_splits, out_splits, group)
+    # SP gradient sum of the non-expert parameters (expert gradients stay local), with a
+    # bucket size that splits the parameters over several buckets
+    from tinytron_b200.models.gpt import EXPERT_LOCAL_PARAM_SUFFIXES
+    from tinytron_b200.parallel import allreduce_non_expert_grads_across_sp as ours_sp
+
+    with ref_oracle.cpu_reference():
+        from tinytron.distributed import allreduce_non_expert_grads_across_sp as ref_sp
+    c = cfg(use_moe=True, num_experts=3, num_experts_per_tok=1, moe_intermediate_size=16)
+    for tag, fn in (("ours", ours_sp), ("ref", ref_sp)):
+        torch.manual_seed(0)
+        m = GPT(c, device="cpu")
+        gg = torch.Generator().manual_seed(100 + rank)
+        for p in m.parameters():
+            p.grad = torch.randn(p.shape, generator=gg)
+        fn(m, group, world, EXPERT_LOCAL_PARAM_SUFFIXES, bucket_size_mb=0)
+        res[f"sp_{tag}"] = {n: p.grad.clone() for n, p in m.named_parameters()}
     torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
 
 
 def test_public_collectives_match_reference():
     """ulysses_all_to_all, ep_all_to_all (uneven splits with empty ones) and
-    ep_all_to_all_no_grad give the reference's outputs and input gradients."""
+    ep_all_to_all_no_grad give the reference's outputs and input gradients, and
+    allreduce_non_expert_grads_across_sp its gradients (expert ones left local)."""
     import ref_oracle
 
     if not ref_oracle.available():
@@ -313,6 +330,8 @@ def test_public_collectives_match_reference():
     for r in range(3):
         for k in ("ul", "ul_grad", "ep", "ep_grad", "epng"):
             assert torch.equal(res[r][f"{k}_ours"], res[r][f"{k}_ref"]), (r, k)
+        for n, g in res[r]["sp_ref"].items():
+            assert torch.allclose(res[r]["sp_ours"][n], g, atol=1e-6), (r, n)
 
 
 # ---------------------------------------------------------------- live training -> inference reshard
