@@ -390,3 +390,48 @@ def test_live_reshard_matches_reference():
             assert set(got) == set(want), (r, mode, sorted(set(got) ^ set(want)))
             for k in want:
                 assert torch.equal(got[k], want[k]), (r, mode, k)
+
+
+# ---------------------------------------------------------------- parallel_state getters
+_GETTERS = ["dp_world_size", "dp_rank", "dp_global_rank", "sep_world_size", "sep_rank", "sep_global_rank",
+            "sp_world_size", "sp_rank", "sp_global_rank", "ep_world_size", "ep_rank", "ep_global_rank",
+            "dp_sp_world_size", "dp_sp_rank", "dp_sp_global_rank"]
+
+
+def _state_worker(rank, world, out_dir):
+    import ref_oracle
+    from tinytron_b200.parallel import parallel_state as ours
+
+    def snapshot(ps):
+        out = {}
+        for n in _GETTERS:
+            fn = getattr(ps, f"get_{n}")
+            out[n] = fn(0) if n.endswith("global_rank") else fn()
+        for grp in ("dp", "sep", "sp", "ep", "dp_sp"):
+            out[f"{grp}_members"] = sorted(dist.get_process_group_ranks(getattr(ps, f"get_{grp}_group")()))
+        return out
+
+    ours.initialize_model_parallel(sep_size=2)
+    res = {"ours": snapshot(ours)}
+    with ref_oracle.cpu_reference():
+        from tinytron.distributed import parallel_state as ref
+        from tinytron.training.config import ParallelConfig
+
+        ref.initialize_model_parallel(ParallelConfig(sep_size=2))
+        res["ref"] = snapshot(ref)
+    torch.save(res, os.path.join(out_dir, f"r{rank}.pt"))
+
+
+def test_parallel_state_getters_match_reference():
+    """Four gloo ranks at SEP=2: every rank/world-size getter and the member ranks of the
+    DP, SEP (SP, EP) and DP x SEP groups equal the reference's."""
+    import ref_oracle
+
+    if not ref_oracle.available():
+        pytest.skip("reference not installed under baseline/_ref")
+    with tempfile.TemporaryDirectory() as td:
+        spawn(_state_worker, 4, td)
+        res = [torch.load(os.path.join(td, f"r{r}.pt")) for r in range(4)]
+    for r in range(4):
+        assert res[r]["ours"] == res[r]["ref"], (r, res[r])
+    assert res[1]["ours"]["sep_members"] == [0, 1] and res[1]["ours"]["dp_members"] == [1, 3]
