@@ -102,3 +102,29 @@ def test_engine_generate_matches_reference(ref, paged):
     rt2 = re.generate(prompt, 12, temperature=1.0, top_k=1, eos_token_id=eos)
     ot2 = oe.generate(prompt, 12, temperature=1.0, top_k=1, eos_token_id=eos)
     assert torch.equal(ot2.cpu(), rt2.cpu())
+
+
+def test_engine_extras_match_reference(ref):
+    """generate(..., return_stats=True, return_logprobs=True) returns the reference's extra
+    keys; the counts (prompt length, decode steps, token counts) and the response mask
+    agree, the throughput fields are positive."""
+    from tinytron.inference import InferenceEngine as RefEngine
+    from tinytron.model.config import ModelConfig as RefCfg
+
+    from tinytron_b200.inference import InferenceEngine
+
+    cfg = _cfgs()["dense"]
+    rcfg = RefCfg(**{k: v for k, v in cfg.__dict__.items() if k in RefCfg.__dataclass_fields__})
+    torch.manual_seed(0)
+    re = RefEngine(rcfg, device="cpu", dtype=torch.float32, use_paged_kv_cache=True, kv_cache_page_size=4)
+    oe = InferenceEngine(cfg, device="cpu", dtype=torch.float32, use_paged_kv_cache=True, kv_cache_page_size=4)
+    oe.model.load_state_dict(re.model.state_dict())
+    prompt = torch.randint(0, cfg.vocab_size, (2, 6), generator=torch.Generator().manual_seed(5))
+    for n_new in (1, 5):
+        _, r = re.generate(prompt, n_new, top_k=1, return_stats=True, return_logprobs=True)
+        _, o = oe.generate(prompt, n_new, top_k=1, return_stats=True, return_logprobs=True)
+        assert set(r) <= set(o), sorted(set(r) - set(o))
+        for k in ("prompt_len", "decode_steps", "prefill_tokens", "decode_tokens"):
+            assert float(o[k]) == float(r[k]), (n_new, k, o[k], r[k])
+        assert torch.equal(o["response_mask"].cpu(), r["response_mask"].cpu())
+        assert o["prefill_tokens_per_sec"] > 0 and (o["decode_tokens_per_sec"] > 0) == (r["decode_tokens_per_sec"] > 0)
