@@ -107,3 +107,35 @@ def test_shell_launchers_parse():
     for name in ("pretrain.sh", "inference.sh", "rl.sh"):
         out = subprocess.run(["bash", "-n", os.path.join(ROOT, "tinytron_b200", "launch", name)], capture_output=True)
         assert out.returncode == 0, (name, out.stderr)
+
+
+def _launcher_args(tmp_path, env_extra):
+    """Run launch/pretrain.sh with `python` replaced by a stub that prints its arguments."""
+    stub = tmp_path / "bin"
+    stub.mkdir(exist_ok=True)
+    (stub / "python").write_text('#!/bin/bash\nprintf "%s\\n" "$@"\n')
+    (stub / "python").chmod(0o755)
+    env = {k: v for k, v in os.environ.items() if k not in ("MAX_STEPS", "DO_SAVE", "USE_DISTRIBUTED_OPTIMIZER")}
+    env.update(PATH=f"{stub}:{env['PATH']}", LOG_DIR=str(tmp_path / "logs"), **env_extra)
+    out = subprocess.run(["bash", os.path.join(ROOT, "tinytron_b200", "launch", "pretrain.sh")], env=env,
+                         capture_output=True, text=True, check=True)
+    args = out.stdout.split("\n")
+    return args[args.index("tinytron_b200.launch.pretrain") + 1:-1]
+
+
+def test_pretrain_launcher_budget_and_switches(tmp_path):
+    """MAX_STEPS replaces the epoch budget (both together are rejected when they
+    disagree); DO_SAVE / USE_DISTRIBUTED_OPTIMIZER / LOG_EVERY / SAVE_EVERY_STEPS map to
+    their flags; the produced command line parses."""
+    from tinytron_b200.launch._presets import expand_preset
+    from tinytron_b200.training import parse_args
+
+    a = _launcher_args(tmp_path, {})
+    assert "--max_epochs" in a and "--max_steps" not in a and "--do_save" in a and "--use_distributed_optimizer" in a
+    b = _launcher_args(tmp_path, {"MAX_STEPS": "10", "DO_SAVE": "0", "USE_DISTRIBUTED_OPTIMIZER": "0",
+                                  "LOG_EVERY": "3", "SAVE_EVERY_STEPS": "7"})
+    assert b[b.index("--max_steps") + 1] == "10" and "--max_epochs" not in b
+    assert "--do_save" not in b and "--use_distributed_optimizer" not in b
+    assert b[b.index("--log_every") + 1] == "3" and b[b.index("--save_every_steps") + 1] == "7"
+    ns = parse_args(expand_preset(b))
+    assert ns.max_steps == 10 and ns.max_epochs is None and not ns.do_save and ns.log_every == 3
