@@ -4,6 +4,7 @@ import os
 import subprocess
 import sys
 
+import pytest
 import torch
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
@@ -139,3 +140,39 @@ def test_pretrain_launcher_budget_and_switches(tmp_path):
     assert b[b.index("--log_every") + 1] == "3" and b[b.index("--save_every_steps") + 1] == "7"
     ns = parse_args(expand_preset(b))
     assert ns.max_steps == 10 and ns.max_epochs is None and not ns.do_save and ns.log_every == 3
+    from tinytron_b200.training import build_config
+
+    build_config(ns)  # the static validation (warmup < max_steps, ...) passes
+    build_config(parse_args(expand_preset(a)))
+
+
+def _launcher_module_args(tmp_path, script, module, env_extra):
+    stub = tmp_path / "bin"
+    stub.mkdir(exist_ok=True)
+    (stub / "python").write_text('#!/bin/bash\nprintf "%s\\n" "$@"\n')
+    (stub / "python").chmod(0o755)
+    env = dict(os.environ)
+    env.update(PATH=f"{stub}:{env['PATH']}", LOG_DIR=str(tmp_path / "logs"), **env_extra)
+    out = subprocess.run(["bash", os.path.join(ROOT, "tinytron_b200", "launch", script)], env=env,
+                         capture_output=True, text=True, check=True)
+    args = out.stdout.split("\n")
+    return args[args.index(module) + 1:-1]
+
+
+@pytest.mark.parametrize("sep", ["1", "2"])
+def test_inference_and_rl_launchers_produce_parsable_command_lines(tmp_path, sep):
+    """The inference and RL shell launchers (single process and torchrun forms) hand their
+    entry points command lines that those entry points' parsers accept."""
+    from tinytron_b200.inference.arguments import build_parser
+    from tinytron_b200.launch._presets import expand_preset
+    import argparse
+
+    from tinytron_b200.launch.rl import add_all_arguments, add_rl_args
+    from tinytron_b200.training import build_config
+
+    a = _launcher_module_args(tmp_path, "inference.sh", "tinytron_b200.launch.inference",
+                              {"SEP_SIZE": sep, "MODEL_SIZE": "0.1B"})
+    build_parser().parse_args(expand_preset(a))
+    b = _launcher_module_args(tmp_path, "rl.sh", "tinytron_b200.launch.rl", {"SEP_SIZE": sep, "MODEL_SIZE": "0.03B"})
+    ns = add_rl_args(add_all_arguments(argparse.ArgumentParser("rl", allow_abbrev=False))).parse_args(expand_preset(b))
+    build_config(ns)  # the static validation of the training config passes
