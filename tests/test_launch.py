@@ -105,7 +105,7 @@ def test_streaming_trainer_checkpoint_resume_cpu(tmp_path):
 
 
 def test_shell_launchers_parse():
-    for name in ("pretrain.sh", "inference.sh", "rl.sh"):
+    for name in ("pretrain.sh", "inference.sh", "rl.sh", "autotune.sh"):
         out = subprocess.run(["bash", "-n", os.path.join(ROOT, "tinytron_b200", "launch", name)], capture_output=True)
         assert out.returncode == 0, (name, out.stderr)
 
@@ -176,3 +176,21 @@ def test_inference_and_rl_launchers_produce_parsable_command_lines(tmp_path, sep
     b = _launcher_module_args(tmp_path, "rl.sh", "tinytron_b200.launch.rl", {"SEP_SIZE": sep, "MODEL_SIZE": "0.03B"})
     ns = add_rl_args(add_all_arguments(argparse.ArgumentParser("rl", allow_abbrev=False))).parse_args(expand_preset(b))
     build_config(ns)  # the static validation of the training config passes
+
+
+def test_autotune_reads_the_reference_environment(monkeypatch):
+    """The reference autotune script's variables set the tuner's defaults; flags win."""
+    from tinytron_b200.launch.autotune import build_arg_parser
+
+    for k, v in {"SEP_SIZES": "1 2", "BATCH_SIZES": "4 8 16", "TARGET_STEPS": "30", "WARMUP_STEPS": "5",
+                 "DEBUG": "1", "MODEL_SIZE": "0.1B", "NUM_GPUS": "2"}.items():
+        monkeypatch.setenv(k, v)
+    a = build_arg_parser().parse_args([])
+    assert (a.sep_sizes, a.batch_sizes, a.target_steps, a.warmup_steps, a.debug, a.preset, a.nproc) == \
+        ([1, 2], [4, 8, 16], 30, 5, True, "0.1B", 2)
+    b = build_arg_parser().parse_args(["--sep-sizes", "4", "--target-steps", "9"])
+    assert b.sep_sizes == [4] and b.target_steps == 9 and b.batch_sizes == [4, 8, 16]
+    monkeypatch.delenv("SEP_SIZES")
+    monkeypatch.delenv("DEBUG")
+    c = build_arg_parser().parse_args([])
+    assert c.sep_sizes == [1, 2, 4, 8] and c.debug is False

@@ -9,6 +9,12 @@ started in its own process group and only that group is ever signalled.
 
     python -m tinytron_b200.launch.autotune --preset 0.25B --nproc 8 --sep-sizes 1 2 4 8 \\
         --batch-sizes 1 2 4 8 16 32 --target-steps 100 --warmup-steps 20 [-- extra pretrain flags]
+
+The reference script's environment variables set the defaults of the same flags
+(``SEP_SIZES`` / ``BATCH_SIZES`` as space-separated lists, ``TARGET_STEPS``,
+``WARMUP_STEPS``, ``DEBUG=1``; ``MODEL_SIZE`` and ``NUM_GPUS`` as its pretraining launcher
+reads them), so ``SEP_SIZES="1 2" bash tinytron_b200/launch/autotune.sh`` works as before;
+``RUN_SCRIPT`` has no counterpart (the runs always use this framework's pretraining entry).
 """
 from __future__ import annotations
 
@@ -85,21 +91,32 @@ def run_one(cmd: list[str], timeout_s: float, echo: bool) -> list[str]:
     return lines
 
 
-def main(argv: list[str] | None = None) -> None:
+def _env_ints(name: str, default: list[int]) -> list[int]:
+    v = os.environ.get(name, "").split()
+    return [int(x) for x in v] if v else default
+
+
+def build_arg_parser() -> argparse.ArgumentParser:
+    env = os.environ.get
     ap = argparse.ArgumentParser("autotune")
-    ap.add_argument("--preset", default="0.25B")
-    ap.add_argument("--nproc", type=int, default=8)
-    ap.add_argument("--sep-sizes", type=int, nargs="+", default=[1, 2, 4, 8])
-    ap.add_argument("--batch-sizes", type=int, nargs="+", default=[1, 2, 4, 8, 16, 32])
+    ap.add_argument("--preset", default=env("MODEL_SIZE", "0.25B"))
+    ap.add_argument("--nproc", type=int, default=int(env("NUM_GPUS", "8")))
+    ap.add_argument("--sep-sizes", type=int, nargs="+", default=_env_ints("SEP_SIZES", [1, 2, 4, 8]))
+    ap.add_argument("--batch-sizes", type=int, nargs="+", default=_env_ints("BATCH_SIZES", [1, 2, 4, 8, 16, 32]))
     ap.add_argument("--seq-len", type=int, default=4096)
-    ap.add_argument("--target-steps", type=int, default=100)
-    ap.add_argument("--warmup-steps", type=int, default=20)
+    ap.add_argument("--target-steps", type=int, default=int(env("TARGET_STEPS", "100")))
+    ap.add_argument("--warmup-steps", type=int, default=int(env("WARMUP_STEPS", "20")))
     ap.add_argument("--timeout", type=float, default=1800.0, help="seconds per run")
     ap.add_argument("--results", default="autotune_results.csv")
     ap.add_argument("--log-dir", default="logs/autotune")
-    ap.add_argument("--debug", action="store_true", help="echo every run's output")
+    ap.add_argument("--debug", action="store_true", default=env("DEBUG", "0") == "1",
+                    help="echo every run's output")
     ap.add_argument("extra", nargs=argparse.REMAINDER, help="after --: extra pretrain flags")
-    args = ap.parse_args(argv)
+    return ap
+
+
+def main(argv: list[str] | None = None) -> None:
+    args = build_arg_parser().parse_args(argv)
     if args.extra and args.extra[0] == "--":
         args.extra = args.extra[1:]
     best = (0.0, None)
